@@ -1,0 +1,184 @@
+/* envgemm.h -- C ABI of libenvgemm.so, the B200 (sm_100a) dense-linear engine for Envision.
+ *
+ * Envision (hshatti/Invision) runs every Linear of its FLUX.2 / Z-Image transformers and Qwen3
+ * encoder, and every im2col convolution of its VAE, through one CPU GEMM.  This library replaces
+ * that path with hand-written tcgen05/TMA kernels.  The Pascal host binds it at run time with
+ * LoadLibrary/GetProcAddress (the reference's rule for optional libraries, README.md:102-104, and
+ * the OpenBLAS binding block in src/quicknncpu.pas:3951-3996); every entry point therefore uses
+ * plain C types, the cdecl convention (= Pascal `winapi` on x86-64 Linux) and returns a status.
+ *
+ * Conventions shared by every entry point (paths below are Envision source files):
+ *   - Row-major throughout.  X fp32 [M, K]; W bf16 [N, K] (PyTorch Linear / safetensors order);
+ *     Y fp32 [M, N].  alpha = 1 and beta = 0 for linears; Y is overwritten, never accumulated
+ *     (quicknncpu.pas:1807-1828), except ENVG_EPI_GATED_RESIDUAL which reads Y as the residual.
+ *   - The activation X is rounded fp32 -> bf16 with round-to-nearest-even on the device and
+ *     multiplied with fp32 accumulation.  (The reference widens W to fp32 and runs an fp32 GEMM,
+ *     quicknncpu.pas:1830-1847; the difference is bounded by the tests at max|d|/max|ref| <= 1e-2
+ *     and sum|d|/sum|ref| <= 2e-3.)
+ *   - M == 0 is a no-op returning ENVG_OK.  dst must not alias x.
+ *   - Errors never throw: a negative ENVG_ERR_* code is returned and envg_last_error() gives a
+ *     thread-local message.  The Pascal shim turns a non-zero code into assert(false, msg), which
+ *     is how the reference reports bad arguments (e.g. quicknn_kernels.pas:484-486).
+ *   - Calls made from one host thread are serialised on the library's stream for the current
+ *     device.  Host-pointer calls are synchronous (the Pascal caller reads dst right after the
+ *     call); ENVG_DEVICE_PTRS calls are stream-ordered and return before completion when
+ *     ENVG_ASYNC is also set (envg_sync() waits).
+ */
+#ifndef ENVGEMM_H
+#define ENVGEMM_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------------------------- */
+#define ENVG_OK 0
+#define ENVG_ERR_ARG (-1)         /* bad shape, null pointer, unsupported combination          */
+#define ENVG_ERR_OOM (-2)         /* device or pinned-host allocation failed                    */
+#define ENVG_ERR_CUDA (-3)        /* a CUDA runtime/driver call failed                          */
+#define ENVG_ERR_NCCL (-4)        /* reserved for the multi-GPU gather                           */
+#define ENVG_ERR_TIMEOUT (-5)     /* a bounded device-side wait gave up (see ENVG_WAIT_CAP)     */
+#define ENVG_ERR_STATE (-6)       /* library not initialised / handle freed / wrong device      */
+#define ENVG_ERR_UNSUPPORTED (-7) /* valid request this build does not implement                */
+
+/* ---- weight layouts (envg_weight_upload.layout_flags) -------------------------------------- */
+#define ENVG_LAYOUT_PLAIN 0   /* W [N, K]                                                     */
+#define ENVG_LAYOUT_GATE_UP 1 /* W [N, K], rows [0, N/2) = gate, [N/2, N) = up (the fused     */
+                              /* FLUX linear_in / Qwen3 gate+up tensor, quicknn_transformers.pas */
+                              /* :595-597); re-laid out once at upload for ENVG_EPI_SILU_GATE   */
+
+/* ---- epilogues (envg_linear.epilogue, envg_conv2d.epilogue) -------------------------------- */
+#define ENVG_EPI_NONE 0           /* Y = X.W^T (+ bias if bias != NULL)                         */
+#define ENVG_EPI_BIAS 1           /* Y = X.W^T + bias           (QNNLinear, quicknncpu.pas:1807) */
+#define ENVG_EPI_SILU_GATE 2      /* Y[:, j] = silu(g_j) * u_j, g/u the gate/up halves          */
+                                  /*   (QNNSiluMul, quicknncpu.pas:2404-2419); Y is [M, N/2]      */
+#define ENVG_EPI_GATED_RESIDUAL 3 /* Y = Y + gate (.) (X.W^T + bias)  (QNNGatedAdd, :853-859)     */
+#define ENVG_EPI_SILU 4           /* conv only: Y = silu(conv + bias)                            */
+
+/* ---- call flags ----------------------------------------------------------------------------- */
+#define ENVG_HOST_PTRS 0    /* x, dst, bias, gate are host pointers (pinned or pageable)       */
+#define ENVG_DEVICE_PTRS 1  /* x, dst, bias, gate are device pointers on the current device   */
+#define ENVG_ASYNC 2        /* with ENVG_DEVICE_PTRS: do not wait for completion               */
+
+/* Opaque device-resident weight (bf16 in HBM, laid out for the kernels). */
+typedef struct envg_weight_s* envg_weight;
+
+typedef struct envg_stats {
+  uint64_t calls;            /* linear + conv + sgemm calls since init                     */
+  uint64_t kernel_launches;  /* kernels launched by the library                            */
+  double flops;              /* 2*M*N*K summed over calls                                  */
+  double h2d_bytes;          /* host->device bytes copied by host-pointer calls            */
+  double d2h_bytes;          /* device->host bytes                                         */
+  uint64_t weight_bytes;     /* device bytes held by live weight handles                   */
+  uint64_t workspace_bytes;  /* device scratch currently held by the library               */
+  int32_t device;            /* current CUDA device                                        */
+  int32_t last_status;       /* last non-zero status (0 if none)                           */
+} envg_stats;
+
+/* Select the device used by this host thread and create its stream and workspace.
+ * ndev must be 1 in this build (one process per GPU; multi-GPU runs shard W across processes,
+ * see envg_weight_upload_shard).  dev_ids may be NULL (device 0).  Replaces the library
+ * detection in quicknncpu.pas:3951-3996 (`isUsingBlas`).  Fails with ENVG_ERR_CUDA when no
+ * sm_100 device is present, so the caller keeps its CPU path. */
+int envg_init(int ndev, const int* dev_ids);
+
+/* Release the workspace and stream of the current device.  Weight handles must be freed first. */
+int envg_shutdown(void);
+
+/* Upload a weight once into HBM (replaces the per-call widening of QNNLinearNoBias_BF16,
+ * quicknncpu.pas:1830-1847, and the per-step mmap re-reads of quicknn_transformers.pas:1581-1602).
+ * Exactly one of w_bf16 (raw bf16 bits, the safetensors dtype BF16) or w_f32 (rounded to bf16
+ * with RNE) is non-NULL; both are host pointers to W[N, K] row-major.  After return the host
+ * memory may be unmapped (safetensor.pas mmap views). */
+int envg_weight_upload(const uint16_t* w_bf16, const float* w_f32, int64_t N, int64_t K,
+                       int layout_flags, envg_weight* out);
+
+/* Upload only the output-column shard [n0, n1) of W[N, K] (the N-split used when several
+ * processes share one linear, one GPU each).  For ENVG_LAYOUT_GATE_UP the shard is taken in
+ * gate/up pairs: rows [n0, n1) of the gate half and the same rows of the up half, so the SiLU
+ * gate stays shard-local.  The handle then behaves like a W of n1 - n0 (x2 for GATE_UP) rows. */
+int envg_weight_upload_shard(const uint16_t* w_bf16, const float* w_f32, int64_t N, int64_t K,
+                             int64_t n0, int64_t n1, int layout_flags, envg_weight* out);
+
+/* Upload a convolution weight W[out_ch, in_ch, kH, kW] (the layout QNNConv2d reads,
+ * quicknncpu.pas:1958-2132) for envg_conv2d. */
+int envg_conv_weight_upload(const uint16_t* w_bf16, const float* w_f32, int out_ch, int in_ch,
+                            int kH, int kW, envg_weight* out);
+
+int envg_weight_free(envg_weight w);
+
+/* Y = epilogue(X . W^T).  Mirrors QNNLinear(dst, x, W, B, seqLen, inDIM, outDIM)
+ * (quicknn_kernels.pas:897-911 -> quicknncpu.pas:1807-1820) with M = seqLen, K = inDIM,
+ * N = outDIM, and QNNLINEAR_BF16_OR_F32 / QNNLinearNoBias (quicknn_kernels.pas:2093-2103,
+ * :913-927) with bias = NULL.  N is the number of W rows held by the handle; for
+ * ENVG_EPI_SILU_GATE dst has N/2 columns.  bias: fp32 [N] or NULL.  gate: fp32 [N] for
+ * ENVG_EPI_GATED_RESIDUAL, else NULL. */
+int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, int64_t M,
+                int64_t K, int64_t N, int epilogue, const float* gate, int flags);
+
+/* dst[batch, out_ch, outH, outW] = conv(src[batch, in_ch, H, W], W) + bias, NCHW, as
+ * QNNConv2d (quicknn_kernels.pas:984-1010 -> quicknncpu.pas:1958-2132); outH/outW follow
+ * QNNConv2DShape (quicknn_kernels.pas:984-988).  epilogue: ENVG_EPI_NONE/BIAS or ENVG_EPI_SILU. */
+int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, int in_ch,
+                int out_ch, int H, int W_, int kH, int kW, int stride, int pad, int batch,
+                int epilogue, int flags);
+
+/* cblas_sgemm-compatible fp32 GEMM on host pointers: the signature of the function-pointer
+ * slot TQNNSingleOPS.cblas_sgemm (quicknncpu.pas:102-109; enums quicknn_common.pas:54-58:
+ * RowMajor = 101, NoTrans = 111, Trans = 112).  Re-pointing that slot to this entry moves
+ * every cblas_gemm call (attention products included) to the GPU without model edits.  Both
+ * operands are rounded to bf16 (RNE) on the device; C = alpha*A.op(B) + beta*C.  RowMajor,
+ * NN/NT/TN only (as qgemm, quicknncpu.pas:1476). */
+int envg_sgemm(int order, int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,
+               const float* A, int64_t lda, const float* B, int64_t ldb, float beta, float* C,
+               int64_t ldc);
+
+/* Make the library launch on a caller-owned stream (a cudaStream_t passed as void*), or back on
+ * its own stream with NULL.  Lets a PyTorch or CUDA-graph caller order the kernels itself. */
+int envg_set_stream(void* stream);
+
+/* Wait for all work queued by this thread's calls. */
+int envg_sync(void);
+
+/* Thread-local text of the last error ("" if none). */
+const char* envg_last_error(void);
+
+int envg_get_stats(envg_stats* out);
+
+/* Bound (nanoseconds) for every device-side spin wait; 0 restores the default (2 s, or the
+ * ENVG_WAIT_CAP environment variable in ms).  A wait that runs out makes the call return
+ * ENVG_ERR_TIMEOUT instead of hanging the GPU. */
+int envg_set_wait_cap_ns(uint64_t ns);
+
+/* Self-test of the bounded-wait path: launches one CTA that waits on an mbarrier nothing
+ * arrives at, with cap_ns as the bound.  Returns ENVG_ERR_TIMEOUT when the bound works.  Used
+ * by the fault-handling tests; faults nothing. */
+int envg_selftest_wait_timeout(uint64_t cap_ns);
+
+/* Per-kernel timing, measured with CUDA events recorded around each launch on the stream the
+ * kernel runs on (used by the benchmark for the roofline figures; off by default). */
+typedef struct envg_kernel_stat {
+  char name[32];      /* kernel family, e.g. "k1_gemm", "k2_skinny", "k_cast_rows"           */
+  uint64_t launches;
+  double ms;          /* summed device time of those launches                                 */
+  double flops;       /* algorithmic 2*M*N*K summed over the launches                         */
+  double bytes;       /* algorithmic HBM bytes summed over the launches (operands read once,  */
+                      /* outputs written once)                                                */
+} envg_kernel_stat;
+
+/* enable = 1: reset the counters and start recording; 0: stop recording. */
+int envg_profile(int enable);
+
+/* Synchronise, resolve pending events and copy up to max records; *count = records written. */
+int envg_profile_read(envg_kernel_stat* out, int max, int* count);
+
+/* Build/version string, e.g. "envgemm 0.1 sm_100a". */
+const char* envg_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ENVGEMM_H */

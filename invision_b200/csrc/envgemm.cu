@@ -1,0 +1,997 @@
+// envgemm.cu -- host side of libenvgemm.so: the C ABI declared in include/envgemm.h, the
+// device-resident weight registry, TMA descriptor construction and kernel dispatch.
+//
+// Call path of one Envision Linear (quicknn_kernels.pas:2093 QNNLINEAR_BF16_OR_F32 ->
+// quicknncpu.pas:1822 QNNLinearNoBias -> cblas_gemm NT) through this library:
+//   envg_linear(dst, x, W, bias, M, K, N, ...)
+//     [host pointers] x, bias (and the residual) -> device workspace
+//     k_cast_rows     X fp32 -> Xb bf16 (RNE), K padded to a multiple of 8
+//     k1_gemm         M > 64: persistent tcgen05 GEMM, fused epilogue writes Y fp32
+//     k2_skinny       M <= 64: swap-AB split-K GEMM, fused epilogue
+//     [host pointers] Y -> dst, stream synchronised, device status checked
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/envgemm.h"
+#include "kernels.cuh"
+
+using namespace envg;
+
+namespace {
+
+constexpr uint32_t WEIGHT_MAGIC = 0xE17A9E11u;
+constexpr int K1_BN = 256;
+constexpr int K1_STAGES = 4;
+constexpr int SKINNY_MAX = 64;
+constexpr uint64_t DEFAULT_WAIT_CAP_NS = 2000000000ull;  // 2 s
+
+thread_local std::string t_err;
+thread_local char t_buf[1024];
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_buf, sizeof(t_buf), fmt, ap);
+  va_end(ap);
+  t_err = t_buf;
+  return code;
+}
+
+#define ENVG_CUDA(call)                                                                                \
+  do {                                                                                                 \
+    cudaError_t e_ = (call);                                                                           \
+    if (e_ != cudaSuccess)                                                                             \
+      return fail(ENVG_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+  } while (0)
+
+#define ENVG_TRY(...)       \
+  do {                      \
+    int rc_ = (__VA_ARGS__); \
+    if (rc_ != ENVG_OK) return rc_; \
+  } while (0)
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+struct Buf {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+struct Dev {
+  bool ready = false;
+  int id = -1;
+  int sms = 0;
+  cudaStream_t own = nullptr;
+  cudaStream_t user = nullptr;
+  Buf x, y, xb, wb, part, cnt, bias, gate, act, col, b32;
+  int* h_status = nullptr;  // mapped pinned: [0] status code, [1] wait site
+  int* d_status = nullptr;
+  uint64_t wait_cap_ns = DEFAULT_WAIT_CAP_NS;
+  int skinny_max = SKINNY_MAX;
+  envg_stats st{};
+  size_t ws_bytes() const {
+    return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
+           col.bytes + b32.bytes;
+  }
+};
+
+std::recursive_mutex g_mu;
+Dev g_dev[64];
+int g_cur = -1;
+
+// ---- optional per-launch timing (envg_profile) ---------------------------------------------
+enum KernelId { KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_CAST, KID_TRANSPOSE, KID_IM2COL, KID_SELFTEST, KID_COUNT };
+const char* const kKernelNames[KID_COUNT] = {"k1_gemm", "k1_gemm_silu_gate", "k1_gemm_conv", "k2_skinny",
+                                             "k_cast_rows", "k_transpose_cast", "k_im2col_nhwc", "k_wait_selftest"};
+struct KAcc {
+  uint64_t launches = 0;
+  double ms = 0, flops = 0, bytes = 0;
+};
+struct Pending {
+  int kid;
+  cudaEvent_t a, b;
+  double flops, bytes;
+};
+bool g_prof_on = false;
+KAcc g_prof[KID_COUNT];
+std::vector<Pending> g_pending;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t take_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Brackets one launch with events on `s` when profiling is on.
+struct ProfScope {
+  bool on;
+  Pending p;
+  cudaStream_t s;
+  ProfScope(cudaStream_t s_, int kid, double flops, double bytes) : on(g_prof_on), s(s_) {
+    if (!on) return;
+    p.kid = kid;
+    p.flops = flops;
+    p.bytes = bytes;
+    p.a = take_event();
+    p.b = take_event();
+    cudaEventRecord(p.a, s);
+  }
+  ~ProfScope() {
+    if (!on) return;
+    cudaEventRecord(p.b, s);
+    g_pending.push_back(p);
+  }
+};
+
+void resolve_pending() {
+  for (auto& p : g_pending) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, p.a, p.b) == cudaSuccess) {
+      KAcc& k = g_prof[p.kid];
+      k.launches++;
+      k.ms += ms;
+      k.flops += p.flops;
+      k.bytes += p.bytes;
+    }
+    g_event_pool.push_back(p.a);
+    g_event_pool.push_back(p.b);
+  }
+  g_pending.clear();
+}
+
+Dev* cur() { return (g_cur >= 0 && g_dev[g_cur].ready) ? &g_dev[g_cur] : nullptr; }
+cudaStream_t stream_of(Dev* d) { return d->user ? d->user : d->own; }
+
+int ensure(Dev* d, Buf& b, size_t bytes, bool zero = false) {
+  if (bytes == 0) bytes = 256;
+  if (b.bytes >= bytes) return ENVG_OK;
+  size_t want = (bytes + (2u << 20) - 1) & ~size_t((2u << 20) - 1);
+  if (b.p) {
+    ENVG_CUDA(cudaStreamSynchronize(stream_of(d)));
+    cudaFree(b.p);
+    b.p = nullptr;
+    b.bytes = 0;
+  }
+  if (cudaMalloc(&b.p, want) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(ENVG_ERR_OOM, "device workspace allocation of %zu bytes failed", want);
+  }
+  if (zero) ENVG_CUDA(cudaMemset(b.p, 0, want));
+  b.bytes = want;
+  d->st.workspace_bytes = d->ws_bytes();
+  return ENVG_OK;
+}
+
+int get_encode() {
+  if (g_encode) return ENVG_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  ENVG_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (!fn || q != cudaDriverEntryPointSuccess) return fail(ENVG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return ENVG_OK;
+}
+
+// 2D bf16 K-major map: dims {inner, rows}, 64 x box_rows boxes, 128-byte swizzle, zero fill.
+int tmap_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16)
+    return fail(ENVG_ERR_ARG, "TMA operand misaligned (base %p, inner %llu)", base, (unsigned long long)inner);
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ENVG_ERR_CUDA, "cuTensorMapEncodeTiled(2D) failed: %d", (int)r);
+  return ENVG_OK;
+}
+
+// 4D map over an NHWC bf16 activation [B][H][W][Cp]: dims {Cp, W, H, B}, box {64, tw, th, 1}.
+int tmap_nhwc(CUtensorMap* tm, const void* base, int Cp, int W, int H, int B, int tw, int th) {
+  cuuint64_t dims[4] = {(cuuint64_t)Cp, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)Cp * 2, (cuuint64_t)W * Cp * 2, (cuuint64_t)H * W * Cp * 2};
+  cuuint32_t box[4] = {(cuuint32_t)BK, (cuuint32_t)tw, (cuuint32_t)th, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ENVG_ERR_CUDA, "cuTensorMapEncodeTiled(4D) failed: %d", (int)r);
+  return ENVG_OK;
+}
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t rup(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+
+uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return (uint16_t)((u >> 16) | 0x40);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+// Reads element (r, k) of the caller's weight as bf16 bits.
+struct WSrc {
+  const uint16_t* b;
+  const float* f;
+  int64_t ld;
+  uint16_t at(int64_t r, int64_t k) const { return b ? b[r * ld + k] : f32_to_bf16_rne(f[r * ld + k]); }
+};
+
+}  // namespace
+
+struct envg_weight_s {
+  uint32_t magic;
+  int dev;
+  uint16_t* d;
+  size_t bytes;
+  int64_t rows;   // rows stored on the device (padding included)
+  int64_t N;      // rows seen by envg_linear (N argument)
+  int64_t K, Kp;  // logical and padded reduction length
+  int layout;
+  int64_t half;   // GATE_UP: gate rows (N/2)
+  bool conv;
+  int out_ch, in_ch, kH, kW, Cp;
+  CUtensorMap tm256;  // box 64 x 256 rows: B operand of k1_gemm
+  CUtensorMap tm128;  // box 64 x 128 rows: A operand of k2_skinny and of convolutions
+};
+
+namespace {
+
+int check_weight(Dev* d, envg_weight w) {
+  if (!w || w->magic != WEIGHT_MAGIC) return fail(ENVG_ERR_STATE, "invalid or freed weight handle");
+  if (w->dev != d->id) return fail(ENVG_ERR_STATE, "weight lives on device %d, current device is %d", w->dev, d->id);
+  return ENVG_OK;
+}
+
+int finish_weight(Dev* d, envg_weight w, const std::vector<uint16_t>& host) {
+  w->bytes = host.size() * 2;
+  if (cudaMalloc(reinterpret_cast<void**>(&w->d), std::max<size_t>(w->bytes, 256)) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(ENVG_ERR_OOM, "weight allocation of %zu bytes failed", w->bytes);
+  }
+  ENVG_CUDA(cudaMemcpy(w->d, host.data(), w->bytes, cudaMemcpyHostToDevice));
+  ENVG_TRY(tmap_2d(&w->tm256, w->d, w->Kp, w->rows, 256));
+  ENVG_TRY(tmap_2d(&w->tm128, w->d, w->Kp, w->rows, 128));
+  d->st.weight_bytes += w->bytes;
+  return ENVG_OK;
+}
+
+// Status word written by bounded device waits; reset after reading.
+int check_status(Dev* d) {
+  volatile int* hs = d->h_status;
+  int st = hs[0];
+  if (st != 0) {
+    int site = hs[1];
+    hs[0] = 0;
+    hs[1] = 0;
+    if (d->cnt.p) cudaMemsetAsync(d->cnt.p, 0, d->cnt.bytes, stream_of(d));  // re-arm split-K counters
+    d->st.last_status = st;
+    return fail(st, "device-side wait exceeded its bound (site %d); pipeline abandoned", site);
+  }
+  return ENVG_OK;
+}
+
+int sync_and_check(Dev* d) {
+  ENVG_CUDA(cudaStreamSynchronize(stream_of(d)));
+  return check_status(d);
+}
+
+// ---- kernel launchers ----------------------------------------------------------------------
+
+template <bool CONV_B, bool SILU_GATE>
+int launch_k1(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, GemmArgs& a, double flops, double bytes) {
+  using L = K1Smem<K1_BN, K1_STAGES>;
+  auto kern = k1_gemm<K1_BN, K1_STAGES, CONV_B, SILU_GATE>;
+  static bool attr = false;
+  if (!attr) {
+    ENVG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    attr = true;
+  }
+  a.status = d->d_status;
+  a.wait_cap_ns = d->wait_cap_ns;
+  const int grid = (int)std::min<int64_t>(a.num_tiles, d->sms);
+  if (grid <= 0) return ENVG_OK;
+  ProfScope ps(stream_of(d), CONV_B ? KID_K1_CONV : (SILU_GATE ? KID_K1_SILU_GATE : KID_K1), flops, bytes);
+  kern<<<grid, K1_THREADS, L::TOTAL, stream_of(d)>>>(tA, tB, a);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
+template <int MPAD, int R>
+int launch_k2_t(Dev* d, const CUtensorMap& tW, const CUtensorMap& tX, SkinnyArgs& a, double flops, double bytes) {
+  constexpr int STAGE_BYTES = K2Smem<MPAD, R, 1>::STAGE_BYTES;
+  constexpr int ST = (110 * 1024) / STAGE_BYTES < 2 ? 2 : (110 * 1024) / STAGE_BYTES;  // two CTAs per SM
+  using L = K2Smem<MPAD, R, ST>;
+  auto kern = k2_skinny<MPAD, R, ST>;
+  static bool attr = false;
+  if (!attr) {
+    ENVG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    attr = true;
+  }
+  a.status = d->d_status;
+  a.wait_cap_ns = d->wait_cap_ns;
+  ProfScope ps(stream_of(d), KID_K2, flops, bytes);
+  kern<<<a.n_tiles * a.splits, K1_THREADS, L::TOTAL, stream_of(d)>>>(tW, tX, a);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
+int launch_k2(Dev* d, int mpad, int R, const CUtensorMap& tW, const CUtensorMap& tX, SkinnyArgs& a, double flops,
+              double bytes) {
+  if (R == 1) {
+    switch (mpad) {
+      case 16: return launch_k2_t<16, 1>(d, tW, tX, a, flops, bytes);
+      case 32: return launch_k2_t<32, 1>(d, tW, tX, a, flops, bytes);
+      case 48: return launch_k2_t<48, 1>(d, tW, tX, a, flops, bytes);
+      case 64: return launch_k2_t<64, 1>(d, tW, tX, a, flops, bytes);
+    }
+  } else {
+    switch (mpad) {
+      case 16: return launch_k2_t<16, 2>(d, tW, tX, a, flops, bytes);
+      case 32: return launch_k2_t<32, 2>(d, tW, tX, a, flops, bytes);
+      case 48: return launch_k2_t<48, 2>(d, tW, tX, a, flops, bytes);
+      case 64: return launch_k2_t<64, 2>(d, tW, tX, a, flops, bytes);
+    }
+  }
+  return fail(ENVG_ERR_ARG, "skinny path: unsupported padded M %d", mpad);
+}
+
+int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t K, int64_t Kp, void* xb) {
+  if (rows == 0) return ENVG_OK;
+  const int vec8 = (K == Kp && K % 8 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
+  const int64_t work = vec8 ? rows * K / 8 : rows * Kp;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)d->sms * 8));
+  ProfScope ps(stream_of(d), KID_CAST, 0.0, (double)rows * K * 4 + (double)rows * Kp * 2);
+  k_cast_rows<<<blocks, 256, 0, stream_of(d)>>>(x, ldx, (int)rows, (int)K, (int)Kp,
+                                                  reinterpret_cast<__nv_bfloat16*>(xb), vec8);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
+// fp32 [batch][R][C] -> bf16 [batch][C][Rp]
+int launch_transpose_cast(Dev* d, const float* src, int64_t lds, int64_t sbs, int R, int C, void* dst, int64_t ldd,
+                          int64_t dbs, int Rp, int batch) {
+  dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(Rp, 64), (unsigned)batch);
+  ProfScope ps(stream_of(d), KID_TRANSPOSE, 0.0, (double)batch * ((double)R * C * 4 + (double)C * Rp * 2));
+  k_transpose_cast<<<grid, 256, 0, stream_of(d)>>>(src, lds, sbs, R, C, reinterpret_cast<__nv_bfloat16*>(dst), ldd,
+                                                   dbs, Rp);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
+// Core GEMM on device operands: Y = epilogue(A[M, Kp] . B[rows, Kp]^T).
+//   A: bf16 activations (M rows);  B: bf16 weights (rows_b rows), with maps for both boxes.
+int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap& b256, const CUtensorMap& b128,
+                int64_t rows_b, bool silu_gate, EpiArgs e, double flops, double bytes) {
+  const int64_t num_kb = cdiv(Kp, BK);
+  if (M <= d->skinny_max) {
+    const int mpad = (int)rup(std::max<int64_t>(M, 1), 16);
+    const int R = silu_gate ? 2 : 1;
+    CUtensorMap tX;
+    ENVG_TRY(tmap_2d(&tX, A, Kp, M, mpad));
+    SkinnyArgs s{};
+    s.n_tiles = (int)cdiv(rows_b, (int64_t)R * BM);
+    s.num_kb = (int)num_kb;
+    int splits = std::max(1, (2 * d->sms) / s.n_tiles);
+    splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 2));
+    s.kb_per_split = (int)cdiv(num_kb, splits);
+    s.splits = (int)cdiv(num_kb, s.kb_per_split);
+    s.epi = e;
+    if (s.splits > 1) {
+      ENVG_TRY(ensure(d, d->part, (size_t)s.n_tiles * s.splits * R * BM * mpad * sizeof(float)));
+      ENVG_TRY(ensure(d, d->cnt, (size_t)s.n_tiles * sizeof(int), true));
+      s.partial = reinterpret_cast<float*>(d->part.p);
+      s.counters = reinterpret_cast<int*>(d->cnt.p);
+    }
+    return launch_k2(d, mpad, R, b128, tX, s, flops, bytes);
+  }
+  CUtensorMap tA;
+  ENVG_TRY(tmap_2d(&tA, A, Kp, M, BM));
+  GemmArgs g{};
+  g.num_kb = (int)num_kb;
+  g.tiles_m = (int)cdiv(M, BM);
+  g.tiles_n = (int)cdiv(rows_b, K1_BN);
+  g.num_tiles = g.tiles_m * g.tiles_n;
+  g.group_m = 8;
+  g.epi = e;
+  if (silu_gate) return launch_k1<false, true>(d, tA, b256, g, flops, bytes);
+  return launch_k1<false, false>(d, tA, b256, g, flops, bytes);
+}
+
+int upload_common(Dev* d, WSrc src, int64_t N, int64_t K, int64_t n0, int64_t n1, int layout, envg_weight* out) {
+  if (!out) return fail(ENVG_ERR_ARG, "out handle pointer is NULL");
+  *out = nullptr;
+  if (N <= 0 || K <= 0) return fail(ENVG_ERR_ARG, "weight shape [%lld, %lld] invalid", (long long)N, (long long)K);
+  if (layout != ENVG_LAYOUT_PLAIN && layout != ENVG_LAYOUT_GATE_UP)
+    return fail(ENVG_ERR_ARG, "unknown layout flag %d", layout);
+  const bool gu = layout == ENVG_LAYOUT_GATE_UP;
+  if (gu && (N % 2)) return fail(ENVG_ERR_ARG, "GATE_UP weight needs an even row count, got %lld", (long long)N);
+  const int64_t lim = gu ? N / 2 : N;
+  if (n0 < 0 || n1 > lim || n0 >= n1)
+    return fail(ENVG_ERR_ARG, "shard [%lld, %lld) outside [0, %lld)", (long long)n0, (long long)n1, (long long)lim);
+  auto* w = new envg_weight_s();
+  w->magic = WEIGHT_MAGIC;
+  w->dev = d->id;
+  w->K = K;
+  w->Kp = rup(K, 8);
+  w->layout = layout;
+  w->conv = false;
+  std::vector<uint16_t> host;
+  const int64_t cnt = n1 - n0;
+  if (!gu) {
+    w->N = cnt;
+    w->rows = cnt;
+    host.assign((size_t)(w->rows * w->Kp), 0);
+    for (int64_t r = 0; r < cnt; ++r)
+      for (int64_t k = 0; k < K; ++k) host[(size_t)(r * w->Kp + k)] = src.at(n0 + r, k);
+  } else {
+    // Interleave per 128-row block: device rows [256t, 256t+128) = gate rows [128t, 128t+128),
+    // rows [256t+128, 256t+256) = the matching up rows; missing rows are zero.
+    const int64_t half = N / 2;
+    w->half = cnt;
+    w->N = 2 * cnt;
+    const int64_t hp = rup(cnt, BM);
+    w->rows = 2 * hp;
+    host.assign((size_t)(w->rows * w->Kp), 0);
+    for (int64_t j = 0; j < cnt; ++j) {
+      const int64_t t = j / BM, i = j % BM;
+      const int64_t rg = 2 * BM * t + i, ru = rg + BM;
+      for (int64_t k = 0; k < K; ++k) {
+        host[(size_t)(rg * w->Kp + k)] = src.at(n0 + j, k);
+        host[(size_t)(ru * w->Kp + k)] = src.at(half + n0 + j, k);
+      }
+    }
+  }
+  int rc = finish_weight(d, w, host);
+  if (rc != ENVG_OK) {
+    if (w->d) cudaFree(w->d);
+    w->magic = 0;
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return ENVG_OK;
+}
+
+const char* epi_name(int e) {
+  switch (e) {
+    case ENVG_EPI_NONE: return "NONE";
+    case ENVG_EPI_BIAS: return "BIAS";
+    case ENVG_EPI_SILU_GATE: return "SILU_GATE";
+    case ENVG_EPI_GATED_RESIDUAL: return "GATED_RESIDUAL";
+    case ENVG_EPI_SILU: return "SILU";
+  }
+  return "?";
+}
+
+}  // namespace
+
+// =============================================================================================
+// C ABI
+// =============================================================================================
+extern "C" {
+
+const char* envg_version(void) { return "envgemm 0.1 sm_100a (tcgen05/TMA)"; }
+
+const char* envg_last_error(void) { return t_err.c_str(); }
+
+int envg_init(int ndev, const int* dev_ids) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (ndev != 1)
+    return fail(ENVG_ERR_UNSUPPORTED, "envg_init: ndev=%d; this build drives one device per process", ndev);
+  const int id = dev_ids ? dev_ids[0] : 0;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(ENVG_ERR_CUDA, "no CUDA device visible");
+  }
+  if (id < 0 || id >= count || id >= 64) return fail(ENVG_ERR_ARG, "device id %d out of range (%d devices)", id, count);
+  ENVG_CUDA(cudaSetDevice(id));
+  Dev* d = &g_dev[id];
+  g_cur = id;
+  if (d->ready) return ENVG_OK;
+  cudaDeviceProp prop;
+  ENVG_CUDA(cudaGetDeviceProperties(&prop, id));
+  if (prop.major != 10)
+    return fail(ENVG_ERR_UNSUPPORTED, "device %d is sm_%d%d; libenvgemm is built for sm_100a", id, prop.major, prop.minor);
+  ENVG_TRY(get_encode());
+  d->id = id;
+  d->sms = prop.multiProcessorCount;
+  ENVG_CUDA(cudaStreamCreateWithFlags(&d->own, cudaStreamNonBlocking));
+  ENVG_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&d->h_status), 2 * sizeof(int), cudaHostAllocMapped));
+  d->h_status[0] = d->h_status[1] = 0;
+  ENVG_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d->d_status), d->h_status, 0));
+  if (const char* s = getenv("ENVG_WAIT_CAP")) {
+    long long ms = atoll(s);
+    if (ms > 0) d->wait_cap_ns = (uint64_t)ms * 1000000ull;
+  }
+  if (const char* s = getenv("ENVG_SKINNY_M_MAX")) {
+    int v = atoi(s);
+    if (v >= 0 && v <= SKINNY_MAX) d->skinny_max = v;
+  }
+  d->st = envg_stats{};
+  d->st.device = id;
+  d->ready = true;
+  return ENVG_OK;
+}
+
+int envg_shutdown(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return ENVG_OK;
+  cudaStreamSynchronize(stream_of(d));
+  Buf* bufs[] = {&d->x, &d->y, &d->xb, &d->wb, &d->part, &d->cnt, &d->bias, &d->gate, &d->act, &d->col, &d->b32};
+  for (Buf* b : bufs) {
+    if (b->p) cudaFree(b->p);
+    *b = Buf{};
+  }
+  if (d->own) cudaStreamDestroy(d->own);
+  if (d->h_status) cudaFreeHost(d->h_status);
+  d->own = nullptr;
+  d->user = nullptr;
+  d->h_status = d->d_status = nullptr;
+  d->ready = false;
+  g_cur = -1;
+  return ENVG_OK;
+}
+
+int envg_set_stream(void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  d->user = reinterpret_cast<cudaStream_t>(stream);
+  return ENVG_OK;
+}
+
+int envg_sync(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  return sync_and_check(d);
+}
+
+int envg_set_wait_cap_ns(uint64_t ns) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  d->wait_cap_ns = ns ? ns : DEFAULT_WAIT_CAP_NS;
+  return ENVG_OK;
+}
+
+int envg_get_stats(envg_stats* out) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!out) return fail(ENVG_ERR_ARG, "stats pointer is NULL");
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  d->st.workspace_bytes = d->ws_bytes();
+  *out = d->st;
+  return ENVG_OK;
+}
+
+int envg_weight_upload(const uint16_t* w_bf16, const float* w_f32, int64_t N, int64_t K, int layout_flags,
+                       envg_weight* out) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if ((w_bf16 == nullptr) == (w_f32 == nullptr)) return fail(ENVG_ERR_ARG, "exactly one of w_bf16 / w_f32 must be set");
+  const int64_t lim = (layout_flags == ENVG_LAYOUT_GATE_UP) ? N / 2 : N;
+  return upload_common(d, WSrc{w_bf16, w_f32, K}, N, K, 0, lim, layout_flags, out);
+}
+
+int envg_weight_upload_shard(const uint16_t* w_bf16, const float* w_f32, int64_t N, int64_t K, int64_t n0, int64_t n1,
+                             int layout_flags, envg_weight* out) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if ((w_bf16 == nullptr) == (w_f32 == nullptr)) return fail(ENVG_ERR_ARG, "exactly one of w_bf16 / w_f32 must be set");
+  return upload_common(d, WSrc{w_bf16, w_f32, K}, N, K, n0, n1, layout_flags, out);
+}
+
+int envg_conv_weight_upload(const uint16_t* w_bf16, const float* w_f32, int out_ch, int in_ch, int kH, int kW,
+                            envg_weight* out) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (!out) return fail(ENVG_ERR_ARG, "out handle pointer is NULL");
+  *out = nullptr;
+  if ((w_bf16 == nullptr) == (w_f32 == nullptr)) return fail(ENVG_ERR_ARG, "exactly one of w_bf16 / w_f32 must be set");
+  if (out_ch <= 0 || in_ch <= 0 || kH <= 0 || kW <= 0)
+    return fail(ENVG_ERR_ARG, "conv weight shape [%d, %d, %d, %d] invalid", out_ch, in_ch, kH, kW);
+  // Device layout W'[out_ch][kH][kW][Cp] (Cp = in_ch rounded up to 64, zero filled): the
+  // reduction index becomes (kh, kw, c), matching the NHWC activation tiles.
+  auto* w = new envg_weight_s();
+  w->magic = WEIGHT_MAGIC;
+  w->dev = d->id;
+  w->conv = true;
+  w->out_ch = out_ch;
+  w->in_ch = in_ch;
+  w->kH = kH;
+  w->kW = kW;
+  w->Cp = (int)rup(in_ch, BK);
+  w->K = (int64_t)in_ch * kH * kW;
+  w->Kp = (int64_t)kH * kW * w->Cp;
+  w->N = out_ch;
+  w->rows = out_ch;
+  w->layout = ENVG_LAYOUT_PLAIN;
+  std::vector<uint16_t> host((size_t)(w->rows * w->Kp), 0);
+  WSrc src{w_bf16, w_f32, w->K};
+  for (int o = 0; o < out_ch; ++o)
+    for (int c = 0; c < in_ch; ++c)
+      for (int kh = 0; kh < kH; ++kh)
+        for (int kw = 0; kw < kW; ++kw)
+          host[(size_t)(o * w->Kp + ((int64_t)kh * kW + kw) * w->Cp + c)] = src.at(o, ((int64_t)c * kH + kh) * kW + kw);
+  int rc = finish_weight(d, w, host);
+  if (rc != ENVG_OK) {
+    if (w->d) cudaFree(w->d);
+    w->magic = 0;
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return ENVG_OK;
+}
+
+int envg_weight_free(envg_weight w) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!w || w->magic != WEIGHT_MAGIC) return fail(ENVG_ERR_STATE, "invalid or already freed weight handle");
+  Dev* d = (w->dev >= 0 && w->dev < 64 && g_dev[w->dev].ready) ? &g_dev[w->dev] : nullptr;
+  if (d) cudaStreamSynchronize(stream_of(d));
+  cudaFree(w->d);
+  if (d) d->st.weight_bytes -= std::min<uint64_t>(d->st.weight_bytes, w->bytes);
+  w->magic = 0;
+  delete w;
+  return ENVG_OK;
+}
+
+int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,
+                int epilogue, const float* gate, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  ENVG_TRY(check_weight(d, W));
+  if (W->conv) return fail(ENVG_ERR_ARG, "envg_linear: handle holds a convolution weight");
+  if (M < 0) return fail(ENVG_ERR_ARG, "envg_linear: M=%lld < 0", (long long)M);
+  if (K != W->K || N != W->N)
+    return fail(ENVG_ERR_ARG, "envg_linear: [K=%lld, N=%lld] does not match the weight [N=%lld, K=%lld]", (long long)K,
+                (long long)N, (long long)W->N, (long long)W->K);
+  if (M > INT32_MAX / 2) return fail(ENVG_ERR_ARG, "envg_linear: M=%lld too large", (long long)M);
+  const bool gu = W->layout == ENVG_LAYOUT_GATE_UP;
+  if (epilogue == ENVG_EPI_SILU_GATE && !gu)
+    return fail(ENVG_ERR_ARG, "envg_linear: SILU_GATE needs a weight uploaded with ENVG_LAYOUT_GATE_UP");
+  if (gu && epilogue != ENVG_EPI_SILU_GATE)
+    return fail(ENVG_ERR_ARG, "envg_linear: a GATE_UP weight only supports the SILU_GATE epilogue");
+  if (epilogue != ENVG_EPI_NONE && epilogue != ENVG_EPI_BIAS && epilogue != ENVG_EPI_SILU_GATE &&
+      epilogue != ENVG_EPI_GATED_RESIDUAL)
+    return fail(ENVG_ERR_ARG, "envg_linear: epilogue %s (%d) not valid for a linear", epi_name(epilogue), epilogue);
+  if (epilogue == ENVG_EPI_BIAS && !bias) return fail(ENVG_ERR_ARG, "envg_linear: BIAS epilogue without bias");
+  if (epilogue == ENVG_EPI_GATED_RESIDUAL && !gate)
+    return fail(ENVG_ERR_ARG, "envg_linear: GATED_RESIDUAL epilogue without gate");
+  if (M == 0) return ENVG_OK;
+  if (!dst || !x) return fail(ENVG_ERR_ARG, "envg_linear: dst or x is NULL");
+  if ((const void*)dst == (const void*)x) return fail(ENVG_ERR_ARG, "envg_linear: dst aliases x");
+  const bool devp = (flags & ENVG_DEVICE_PTRS) != 0;
+  const int64_t n_out = gu ? N / 2 : N;
+  cudaStream_t s = stream_of(d);
+
+  const float *dx = x, *dbias = bias, *dgate = gate;
+  float* dy = dst;
+  if (!devp) {
+    ENVG_TRY(ensure(d, d->x, (size_t)(M * K) * 4));
+    ENVG_TRY(ensure(d, d->y, (size_t)(M * n_out) * 4));
+    ENVG_CUDA(cudaMemcpyAsync(d->x.p, x, (size_t)(M * K) * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)(M * K) * 4;
+    dx = reinterpret_cast<float*>(d->x.p);
+    dy = reinterpret_cast<float*>(d->y.p);
+    if (bias) {
+      ENVG_TRY(ensure(d, d->bias, (size_t)N * 4));
+      ENVG_CUDA(cudaMemcpyAsync(d->bias.p, bias, (size_t)N * 4, cudaMemcpyHostToDevice, s));
+      d->st.h2d_bytes += (double)N * 4;
+      dbias = reinterpret_cast<float*>(d->bias.p);
+    }
+    if (epilogue == ENVG_EPI_GATED_RESIDUAL) {
+      ENVG_TRY(ensure(d, d->gate, (size_t)N * 4));
+      ENVG_CUDA(cudaMemcpyAsync(d->gate.p, gate, (size_t)N * 4, cudaMemcpyHostToDevice, s));
+      ENVG_CUDA(cudaMemcpyAsync(dy, dst, (size_t)(M * n_out) * 4, cudaMemcpyHostToDevice, s));
+      d->st.h2d_bytes += (double)N * 4 + (double)(M * n_out) * 4;
+      dgate = reinterpret_cast<float*>(d->gate.p);
+    }
+  }
+  ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
+  ENVG_TRY(launch_cast_rows(d, dx, K, M, K, W->Kp, d->xb.p));
+
+  EpiArgs e{};
+  e.Y = dy;
+  e.ldy = n_out;
+  e.bias = dbias;
+  e.bias_mode = dbias ? 1 : 0;
+  e.act = 0;
+  e.mode = (epilogue == ENVG_EPI_GATED_RESIDUAL) ? EPI_GATED_RES : EPI_PLAIN;
+  e.gate = dgate;
+  e.alpha = 1.0f;
+  e.beta = 0.0f;
+  e.n_out = (int)n_out;
+  e.m_valid = (int)M;
+  e.half_n = (int)(gu ? W->half : 0);
+  e.vec_ok = ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && n_out % 4 == 0) ? 1 : 0;
+  const double lin_flops = 2.0 * (double)M * (double)N * (double)K;
+  const double lin_bytes = 2.0 * (double)N * K + 2.0 * (double)M * W->Kp + 4.0 * (double)M * n_out +
+                           (dbias ? 4.0 * N : 0.0) +
+                           (epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)M * n_out + 4.0 * N : 0.0);
+  ENVG_TRY(gemm_device(d, d->xb.p, M, W->Kp, W->tm256, W->tm128, W->rows, gu, e, lin_flops, lin_bytes));
+
+  d->st.calls++;
+  d->st.flops += 2.0 * (double)M * (double)N * (double)K;
+  if (!devp) {
+    ENVG_CUDA(cudaMemcpyAsync(dst, dy, (size_t)(M * n_out) * 4, cudaMemcpyDeviceToHost, s));
+    d->st.d2h_bytes += (double)(M * n_out) * 4;
+    return sync_and_check(d);
+  }
+  if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
+  return ENVG_OK;
+}
+
+int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, int in_ch, int out_ch, int H, int W_,
+                int kH, int kW, int stride, int pad, int batch, int epilogue, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  ENVG_TRY(check_weight(d, W));
+  if (!W->conv) return fail(ENVG_ERR_ARG, "envg_conv2d: handle holds a linear weight");
+  if (in_ch != W->in_ch || out_ch != W->out_ch || kH != W->kH || kW != W->kW)
+    return fail(ENVG_ERR_ARG, "envg_conv2d: geometry [%d,%d,%d,%d] does not match the weight [%d,%d,%d,%d]", out_ch,
+                in_ch, kH, kW, W->out_ch, W->in_ch, W->kH, W->kW);
+  if (stride <= 0 || pad < 0 || H <= 0 || W_ <= 0 || batch < 0)
+    return fail(ENVG_ERR_ARG, "envg_conv2d: invalid stride/pad/size");
+  if (epilogue != ENVG_EPI_NONE && epilogue != ENVG_EPI_BIAS && epilogue != ENVG_EPI_SILU)
+    return fail(ENVG_ERR_ARG, "envg_conv2d: epilogue %s (%d) not valid for a convolution", epi_name(epilogue), epilogue);
+  if (epilogue == ENVG_EPI_BIAS && !bias) return fail(ENVG_ERR_ARG, "envg_conv2d: BIAS epilogue without bias");
+  const int outH = (H + 2 * pad - kH) / stride + 1;
+  const int outW = (W_ + 2 * pad - kW) / stride + 1;
+  if (outH <= 0 || outW <= 0) return fail(ENVG_ERR_ARG, "envg_conv2d: empty output");
+  if (batch == 0) return ENVG_OK;
+  if (!dst || !src) return fail(ENVG_ERR_ARG, "envg_conv2d: dst or src is NULL");
+  const bool devp = (flags & ENVG_DEVICE_PTRS) != 0;
+  cudaStream_t s = stream_of(d);
+  const int64_t in_elems = (int64_t)batch * in_ch * H * W_;
+  const int64_t plane = (int64_t)outH * outW;
+  const int64_t out_elems = (int64_t)batch * out_ch * plane;
+  const float* dsrc = src;
+  const float* dbias = bias;
+  float* dy = dst;
+  if (!devp) {
+    ENVG_TRY(ensure(d, d->x, (size_t)in_elems * 4));
+    ENVG_TRY(ensure(d, d->y, (size_t)out_elems * 4));
+    ENVG_CUDA(cudaMemcpyAsync(d->x.p, src, (size_t)in_elems * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)in_elems * 4;
+    dsrc = reinterpret_cast<float*>(d->x.p);
+    dy = reinterpret_cast<float*>(d->y.p);
+    if (bias) {
+      ENVG_TRY(ensure(d, d->bias, (size_t)out_ch * 4));
+      ENVG_CUDA(cudaMemcpyAsync(d->bias.p, bias, (size_t)out_ch * 4, cudaMemcpyHostToDevice, s));
+      d->st.h2d_bytes += (double)out_ch * 4;
+      dbias = reinterpret_cast<float*>(d->bias.p);
+    }
+  }
+  // NCHW fp32 -> NHWC bf16 with channels padded to Cp.
+  const int Cp = W->Cp;
+  ENVG_TRY(ensure(d, d->act, (size_t)batch * H * W_ * Cp * 2));
+  ENVG_TRY(launch_transpose_cast(d, dsrc, (int64_t)H * W_, (int64_t)in_ch * H * W_, in_ch, H * W_, d->act.p, Cp,
+                                 (int64_t)H * W_ * Cp, Cp, batch));
+  EpiArgs e{};
+  e.Y = dy;
+  e.bias = dbias;
+  e.bias_mode = dbias ? 2 : 0;
+  e.act = (epilogue == ENVG_EPI_SILU) ? 1 : 0;
+  e.mode = EPI_PLAIN;
+  e.alpha = 1.0f;
+  e.m_valid = out_ch;
+  if (stride == 1) {
+    // Implicit im2col: each B tile is one 4D TMA box of the NHWC activation.
+    int tw = 1;
+    while (tw < outW && tw < 256) tw <<= 1;
+    const int th = 256 / tw;
+    CUtensorMap tB;
+    ENVG_TRY(tmap_nhwc(&tB, d->act.p, Cp, W_, H, batch, tw, th));
+    GemmArgs g{};
+    g.num_kb = (int)(W->Kp / BK);
+    g.tiles_m = (int)cdiv(out_ch, BM);
+    g.conv.tileW = tw;
+    g.conv.tileH = th;
+    g.conv.outH = outH;
+    g.conv.outW = outW;
+    g.conv.tiles_w = (int)cdiv(outW, tw);
+    g.conv.tiles_h = (int)cdiv(outH, th);
+    g.conv.KW = kW;
+    g.conv.pad = pad;
+    g.conv.cblocks = Cp / BK;
+    g.conv.img_stride = (int64_t)out_ch * plane;
+    g.conv.plane = plane;
+    g.tiles_n = batch * g.conv.tiles_w * g.conv.tiles_h;
+    g.num_tiles = g.tiles_m * g.tiles_n;
+    g.group_m = 1;
+    e.ldy = plane;
+    e.n_out = (int)plane;
+    e.vec_ok = ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 4 == 0) ? 1 : 0;
+    g.epi = e;
+    const double cflops = 2.0 * out_ch * (double)plane * batch * (double)W->K;
+    const double cbytes = 2.0 * (double)batch * H * W_ * Cp + 2.0 * out_ch * (double)W->Kp + 4.0 * (double)out_elems +
+                          (dbias ? 4.0 * out_ch : 0.0);
+    ENVG_TRY(launch_k1<true, false>(d, W->tm128, tB, g, cflops, cbytes));
+  } else {
+    // Strided convolution: explicit bf16 im2col, then one GEMM per image.
+    const int64_t colK = W->Kp;
+    ENVG_TRY(ensure(d, d->col, (size_t)batch * plane * colK * 2));
+    const int64_t total = (int64_t)batch * plane * kH * kW * (Cp / 8);
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(total, 256), (int64_t)d->sms * 16));
+    ProfScope ps_im(s, KID_IM2COL, 0.0, 2.0 * (double)batch * H * W_ * Cp + 2.0 * (double)batch * plane * colK);
+    k_im2col_nhwc<<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(d->act.p), batch, H, W_, Cp, kH, kW,
+                                         stride, pad, outH, outW, reinterpret_cast<__nv_bfloat16*>(d->col.p));
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches++;
+    for (int b = 0; b < batch; ++b) {
+      const void* colb = reinterpret_cast<const uint8_t*>(d->col.p) + (size_t)b * plane * colK * 2;
+      CUtensorMap tB;
+      ENVG_TRY(tmap_2d(&tB, colb, colK, plane, 256));
+      CUtensorMap tA = W->tm128;
+      GemmArgs g{};
+      g.num_kb = (int)(colK / BK);
+      g.tiles_m = (int)cdiv(out_ch, BM);
+      g.tiles_n = (int)cdiv(plane, K1_BN);
+      g.num_tiles = g.tiles_m * g.tiles_n;
+      g.group_m = 8;
+      EpiArgs eb = e;
+      eb.Y = dy + (int64_t)b * out_ch * plane;
+      eb.ldy = plane;
+      eb.n_out = (int)plane;
+      eb.vec_ok = ((reinterpret_cast<uintptr_t>(eb.Y) & 15) == 0 && plane % 4 == 0) ? 1 : 0;
+      g.epi = eb;
+      ENVG_TRY(launch_k1<false, false>(d, tA, tB, g, 2.0 * out_ch * (double)plane * (double)W->K,
+                                       2.0 * (double)plane * colK + 2.0 * out_ch * (double)colK + 4.0 * out_ch * (double)plane));
+    }
+  }
+  d->st.calls++;
+  d->st.flops += 2.0 * (double)out_ch * (double)plane * (double)batch * (double)W->K;
+  if (!devp) {
+    ENVG_CUDA(cudaMemcpyAsync(dst, dy, (size_t)out_elems * 4, cudaMemcpyDeviceToHost, s));
+    d->st.d2h_bytes += (double)out_elems * 4;
+    return sync_and_check(d);
+  }
+  if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
+  return ENVG_OK;
+}
+
+int envg_sgemm(int order, int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
+               int64_t lda, const float* B, int64_t ldb, float beta, float* C, int64_t ldc) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  const int RowMajor = 101, NoTrans = 111, Trans = 112;
+  if (order != RowMajor) return fail(ENVG_ERR_ARG, "ERROR : Operation is not supported using the provided arguments!");
+  if ((transA != NoTrans && transA != Trans) || (transB != NoTrans && transB != Trans) ||
+      (transA == Trans && transB == Trans))
+    return fail(ENVG_ERR_ARG, "ERROR : Operation is not supported using the provided arguments!");
+  if (M < 0 || N < 0 || K < 0) return fail(ENVG_ERR_ARG, "envg_sgemm: negative size");
+  if (M == 0 || N == 0) return ENVG_OK;
+  if (!A || !B || !C) return fail(ENVG_ERR_ARG, "envg_sgemm: NULL operand");
+  const bool ta = transA == Trans, tb = transB == Trans;
+  const int64_t arows = ta ? K : M, acols = ta ? M : K;
+  const int64_t brows = tb ? N : K, bcols = tb ? K : N;
+  if (lda < std::max<int64_t>(1, acols) || ldb < std::max<int64_t>(1, bcols) || ldc < std::max<int64_t>(1, N))
+    return fail(ENVG_ERR_ARG, "envg_sgemm: leading dimension too small");
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return fail(ENVG_ERR_ARG, "envg_sgemm: size too large");
+  cudaStream_t s = stream_of(d);
+  const int64_t Kp = rup(std::max<int64_t>(K, 1), 8);
+  ENVG_TRY(ensure(d, d->x, (size_t)(arows * acols) * 4));
+  ENVG_TRY(ensure(d, d->b32, (size_t)(brows * bcols) * 4));
+  ENVG_TRY(ensure(d, d->y, (size_t)(M * N) * 4));
+  ENVG_TRY(ensure(d, d->xb, (size_t)(M * Kp) * 2));
+  ENVG_TRY(ensure(d, d->wb, (size_t)(N * Kp) * 2));
+  if (K > 0) {
+    ENVG_CUDA(cudaMemcpy2DAsync(d->x.p, acols * 4, A, lda * 4, acols * 4, arows, cudaMemcpyHostToDevice, s));
+    ENVG_CUDA(cudaMemcpy2DAsync(d->b32.p, bcols * 4, B, ldb * 4, bcols * 4, brows, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)(arows * acols + brows * bcols) * 4;
+  }
+  if (beta != 0.0f) {
+    ENVG_CUDA(cudaMemcpy2DAsync(d->y.p, N * 4, C, ldc * 4, N * 4, M, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)(M * N) * 4;
+  }
+  const float* a32 = reinterpret_cast<const float*>(d->x.p);
+  const float* b32 = reinterpret_cast<const float*>(d->b32.p);
+  if (K == 0) {
+    ENVG_CUDA(cudaMemsetAsync(d->xb.p, 0, (size_t)(M * Kp) * 2, s));
+    ENVG_CUDA(cudaMemsetAsync(d->wb.p, 0, (size_t)(N * Kp) * 2, s));
+  } else {
+    if (!ta) ENVG_TRY(launch_cast_rows(d, a32, K, M, K, Kp, d->xb.p));
+    else ENVG_TRY(launch_transpose_cast(d, a32, M, 0, (int)K, (int)M, d->xb.p, Kp, 0, (int)Kp, 1));
+    if (tb) ENVG_TRY(launch_cast_rows(d, b32, K, N, K, Kp, d->wb.p));
+    else ENVG_TRY(launch_transpose_cast(d, b32, N, 0, (int)K, (int)N, d->wb.p, Kp, 0, (int)Kp, 1));
+  }
+  CUtensorMap b256, b128;
+  ENVG_TRY(tmap_2d(&b256, d->wb.p, Kp, N, 256));
+  ENVG_TRY(tmap_2d(&b128, d->wb.p, Kp, N, 128));
+  EpiArgs e{};
+  e.Y = reinterpret_cast<float*>(d->y.p);
+  e.ldy = N;
+  e.mode = EPI_ALPHA_BETA;
+  e.alpha = alpha;
+  e.beta = beta;
+  e.n_out = (int)N;
+  e.m_valid = (int)M;
+  e.vec_ok = (N % 4 == 0) ? 1 : 0;
+  ENVG_TRY(gemm_device(d, d->xb.p, M, Kp, b256, b128, N, false, e, 2.0 * (double)M * N * K,
+                       2.0 * (double)(M + N) * Kp + (beta != 0.0f ? 8.0 : 4.0) * (double)M * N));
+  ENVG_CUDA(cudaMemcpy2DAsync(C, ldc * 4, d->y.p, N * 4, N * 4, M, cudaMemcpyDeviceToHost, s));
+  d->st.d2h_bytes += (double)(M * N) * 4;
+  d->st.calls++;
+  d->st.flops += 2.0 * (double)M * (double)N * (double)K;
+  return sync_and_check(d);
+}
+
+int envg_profile(int enable) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (enable) {
+    ENVG_CUDA(cudaStreamSynchronize(stream_of(d)));
+    resolve_pending();
+    for (auto& k : g_prof) k = KAcc{};
+  }
+  g_prof_on = enable != 0;
+  return ENVG_OK;
+}
+
+int envg_profile_read(envg_kernel_stat* out, int max, int* count) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (!out || !count || max < 0) return fail(ENVG_ERR_ARG, "envg_profile_read: bad arguments");
+  ENVG_CUDA(cudaStreamSynchronize(stream_of(d)));
+  resolve_pending();
+  int n = 0;
+  for (int k = 0; k < KID_COUNT && n < max; ++k) {
+    if (!g_prof[k].launches) continue;
+    envg_kernel_stat& o = out[n++];
+    memset(&o, 0, sizeof(o));
+    strncpy(o.name, kKernelNames[k], sizeof(o.name) - 1);
+    o.launches = g_prof[k].launches;
+    o.ms = g_prof[k].ms;
+    o.flops = g_prof[k].flops;
+    o.bytes = g_prof[k].bytes;
+  }
+  *count = n;
+  return ENVG_OK;
+}
+
+int envg_selftest_wait_timeout(uint64_t cap_ns) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  k_wait_selftest<<<1, 32, 0, stream_of(d)>>>(d->d_status, cap_ns);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return sync_and_check(d);
+}
+
+}  // extern "C"

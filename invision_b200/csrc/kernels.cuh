@@ -1,0 +1,735 @@
+// kernels.cuh -- the sm_100a kernels of libenvgemm:
+//
+//   k1_gemm      large-M GEMM: persistent, warp-specialised (TMA warp / UMMA warp / 4 epilogue
+//                warps), 128 x BN x 64 tiles in a STAGES-deep shared-memory ring, fp32
+//                accumulators double-buffered in TMEM so the epilogue of tile i overlaps the
+//                main loop of tile i+1.  The B operand is either a plain K-major matrix (2D TMA)
+//                or, for convolutions, an implicit im2col tile fetched straight from an NHWC
+//                activation with a 4D TMA box (no col buffer is ever written).
+//   k2_skinny    M <= 64: swap-AB (D^T = W . X^T, W rows on the 128-lane M side of the MMA,
+//                tokens on N), split-K across CTAs with a deterministic last-CTA reduction.
+//   k_cast_rows  fp32 -> bf16 (round-to-nearest-even) row copy with zero K padding.
+//   k_transpose_cast  fp32 [R][C] -> bf16 [C][Rp]: NCHW -> NHWC for convolutions, and the
+//                transposed operands of envg_sgemm.
+//   k_im2col_nhwc  explicit bf16 im2col, only for strided convolutions.
+//
+// Arithmetic of every GEMM: bf16 x bf16 products accumulated in fp32 by tcgen05.mma; the
+// epilogue applies bias / SiLU / SiLU-gate / gated residual in fp32.  Envision's CPU path
+// (src/quicknncpu.pas:1241-1337) accumulates fp32 x fp32 in fp32; the tests bound the
+// difference.
+#pragma once
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "ptx.cuh"
+
+namespace envg {
+
+constexpr int BM = 128;                       // rows of a UMMA tile (TMEM lanes)
+constexpr int BK = 64;                        // bf16 per 128-byte swizzled row
+constexpr int TILE_A_BYTES = BM * BK * 2;     // 16 KB
+constexpr int K1_THREADS = 192;               // warp 0 TMA, warp 1 UMMA, warps 2-5 epilogue
+
+enum EpiMode : int { EPI_PLAIN = 0, EPI_SILU_GATE = 1, EPI_GATED_RES = 2, EPI_ALPHA_BETA = 3 };
+
+struct EpiArgs {
+  float* Y;           // output base
+  int64_t ldy;        // row stride of Y (floats)
+  const float* bias;  // fp32 or null
+  int bias_mode;      // 0 none, 1 per output column, 2 per output row
+  int act;            // 1: SiLU after the bias
+  int mode;           // EpiMode
+  const float* gate;  // EPI_GATED_RES: per-column gate
+  float alpha, beta;  // EPI_ALPHA_BETA: Y = alpha*acc + beta*Y
+  int n_out;          // valid output columns
+  int m_valid;        // valid output rows
+  int half_n;         // EPI_SILU_GATE: gate rows of the original W (up bias at half_n + col)
+  int vec_ok;         // Y 16-byte aligned and ldy % 4 == 0
+};
+
+struct ConvGeom {
+  int tileW, tileH;   // pixel tile, tileW * tileH == BN
+  int outH, outW;
+  int tiles_w, tiles_h;
+  int KW, pad, cblocks;
+  int64_t img_stride; // floats between images of Y
+  int64_t plane;      // outH * outW
+};
+
+struct GemmArgs {
+  int num_kb;
+  int tiles_m, tiles_n, num_tiles;
+  int group_m;
+  EpiArgs epi;
+  ConvGeom conv;
+  int* status;
+  uint64_t wait_cap_ns;
+};
+
+struct SkinnyArgs {
+  int n_tiles, splits, kb_per_split, num_kb;
+  EpiArgs epi;
+  float* partial;
+  int* counters;
+  int* status;
+  uint64_t wait_cap_ns;
+};
+
+ENVG_DEV float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// One output element of a GEMM-shaped epilogue.  GATED_RES restates QNNGatedAdd
+// (quicknncpu.pas:853-859): y + (gate * proj), product and sum rounded separately.
+ENVG_DEV float epi_value(const EpiArgs& e, float acc, int row, int col, const float* yp) {
+  float v = acc;
+  if (e.bias_mode == 1) v = __fadd_rn(v, __ldg(e.bias + col));
+  else if (e.bias_mode == 2) v = __fadd_rn(v, __ldg(e.bias + row));
+  if (e.act) v = silu_f(v);
+  if (e.mode == EPI_GATED_RES) {
+    v = __fadd_rn(*yp, __fmul_rn(__ldg(e.gate + col), v));
+  } else if (e.mode == EPI_ALPHA_BETA) {
+    v = (e.beta == 0.0f) ? __fmul_rn(e.alpha, v) : __fadd_rn(__fmul_rn(e.alpha, v), __fmul_rn(e.beta, *yp));
+  }
+  return v;
+}
+
+// Store 32 consecutive output columns [col0, col0+32) of one row.
+ENVG_DEV void epi_store_row32(const EpiArgs& e, int row, int col0, const float (&v)[32]) {
+  if (row >= e.m_valid) return;
+  float* yrow = e.Y + (int64_t)row * e.ldy;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const int col = col0 + j;
+    if (e.vec_ok && col + 3 < e.n_out) {
+      float4 o;
+      const float* yp = yrow + col;
+      float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e.mode == EPI_GATED_RES || (e.mode == EPI_ALPHA_BETA && e.beta != 0.0f))
+        old = *reinterpret_cast<const float4*>(yp);
+      o.x = epi_value(e, v[j + 0], row, col + 0, &old.x);
+      o.y = epi_value(e, v[j + 1], row, col + 1, &old.y);
+      o.z = epi_value(e, v[j + 2], row, col + 2, &old.z);
+      o.w = epi_value(e, v[j + 3], row, col + 3, &old.w);
+      *reinterpret_cast<float4*>(yrow + col) = o;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        if (col + t < e.n_out) yrow[col + t] = epi_value(e, v[j + t], row, col + t, yrow + col + t);
+    }
+  }
+}
+
+// Store 32 accumulator columns of a convolution tile: column jj -> pixel (h0 + jj / tileW,
+// w0 + jj % tileW) of image b; Y is NCHW, row = output channel.
+ENVG_DEV void epi_store_conv32(const EpiArgs& e, const ConvGeom& g, int b, int oc, int h0, int w0, int jj0,
+                               const float (&v)[32]) {
+  if (oc >= e.m_valid) return;
+  float* yplane = e.Y + (int64_t)b * g.img_stride + (int64_t)oc * g.plane;
+  const float bv = (e.bias_mode == 2) ? __ldg(e.bias + oc) : 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const int jj = jj0 + j;
+    const int h = h0 + jj / g.tileW;
+    const int w = w0 + jj % g.tileW;
+    if (h >= g.outH) continue;
+    float o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      float x = __fadd_rn(v[j + t], bv);
+      o[t] = e.act ? silu_f(x) : x;
+    }
+    float* yp = yplane + (int64_t)h * g.outW + w;
+    if (e.vec_ok && (g.tileW % 4) == 0 && w + 3 < g.outW) {
+      *reinterpret_cast<float4*>(yp) = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int jt = jj + t;
+        const int ht = h0 + jt / g.tileW, wt = w0 + jt % g.tileW;
+        if (ht < g.outH && wt < g.outW) yplane[(int64_t)ht * g.outW + wt] = o[t];
+      }
+    }
+  }
+}
+
+// Tile order: groups of `group_m` M-tiles sweep all N-tiles, so CTAs that run together share
+// A rows and B rows in L2.
+ENVG_DEV void map_tile(int tile, const GemmArgs& a, int& m_blk, int& n_blk) {
+  const int group = a.group_m * a.tiles_n;
+  const int g = tile / group;
+  const int first_m = g * a.group_m;
+  const int gm = min(a.tiles_m - first_m, a.group_m);
+  const int r = tile - g * group;
+  m_blk = first_m + r % gm;
+  n_blk = r / gm;
+}
+
+template <int BN, int STAGES>
+struct K1Smem {
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = TILE_A_BYTES + B_BYTES;
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int TOTAL = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+};
+
+// ------------------------------------------------------------------------------------------
+// K1: persistent tcgen05 GEMM.  D[128 x BN] tiles of A[M, K] . B[N, K]^T.
+// ------------------------------------------------------------------------------------------
+template <int BN, int STAGES, bool CONV_B, bool SILU_GATE>
+__global__ void __launch_bounds__(K1_THREADS, 1)
+    k1_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using L = K1Smem<BN, STAGES>;
+  constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(!SILU_GATE || BN == 256, "SiLU-gate tiles hold 128 gate + 128 up columns");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * TILE_A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * L::B_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * STAGES;
+  const uint32_t tfull0 = empty0 + 8 * STAGES;
+  const uint32_t tempty0 = tfull0 + 16;
+  const uint32_t drain = tempty0 + 16;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 4);
+    }
+    mbar_init(drain, 1);
+    *abort_s = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtl wc{args.wait_cap_ns, args.status, abort_s, 0};
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t pending = 0;   // stages whose last load may still be in flight
+      uint32_t issue_ph = 0;  // parity of that load's phase, per stage
+      for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+        int m_blk, n_blk;
+        int b = 0, h0 = 0, w0 = 0;
+        if (CONV_B) {
+          m_blk = tile % args.tiles_m;  // output-channel blocks of one pixel tile run together
+          n_blk = tile / args.tiles_m;
+          const int per_img = args.conv.tiles_w * args.conv.tiles_h;
+          b = n_blk / per_img;
+          const int r = n_blk - b * per_img;
+          h0 = (r / args.conv.tiles_w) * args.conv.tileH;
+          w0 = (r % args.conv.tiles_w) * args.conv.tileW;
+        } else {
+          map_tile(tile, args, m_blk, n_blk);
+        }
+        const int m0 = m_blk * BM;
+        const int n0 = n_blk * BN;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!wait_bounded(empty0 + 8 * stage, ph ^ 1, wc, 1)) goto producer_done;
+          const uint32_t fb = full0 + 8 * stage;
+          mbar_arrive_expect_tx(fb, L::STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + stage * TILE_A_BYTES), &tmA, fb, kb * BK, m0);
+          if (CONV_B) {
+            const int kpos = kb / args.conv.cblocks;
+            const int cb = kb - kpos * args.conv.cblocks;
+            const int kh = kpos / args.conv.KW;
+            const int kw = kpos - kh * args.conv.KW;
+            tma_load_4d(smem_u32(sB + stage * L::B_BYTES), &tmB, fb, cb * BK, w0 + kw - args.conv.pad,
+                        h0 + kh - args.conv.pad, b);
+          } else {
+            tma_load_2d(smem_u32(sB + stage * L::B_BYTES), &tmB, fb, kb * BK, n0);
+          }
+          pending |= 1u << stage;
+          issue_ph = (issue_ph & ~(1u << stage)) | (ph << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    producer_done:
+      if (*abort_s) {
+        // Let every copy this thread started land before the CTA's shared memory is released.
+        for (int s = 0; s < STAGES; ++s)
+          if (pending & (1u << s)) wait_drain(full0 + 8 * s, (issue_ph >> s) & 1u, args.wait_cap_ns);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+        if (!wait_bounded(tempty0 + 8 * acc, aph ^ 1, wc, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!wait_bounded(full0 + 8 * stage, ph, wc, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_kmajor_desc(smem_u32(sA + stage * TILE_A_BYTES));
+          const uint64_t bd = sw128_kmajor_desc(smem_u32(sB + stage * L::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(empty0 + 8 * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull0 + 8 * acc);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
+      }
+      if (*abort_s) {
+        // Every UMMA issued so far must finish before TMEM is released.
+        umma_commit(drain);
+        wait_drain(drain, 0, args.wait_cap_ns);
+      }
+    }
+  } else {
+    // ---------------- epilogue: 4 warps, one TMEM lane quadrant each ----------------
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+      int m_blk, n_blk;
+      int b = 0, h0 = 0, w0 = 0;
+      if (CONV_B) {
+        m_blk = tile % args.tiles_m;
+        n_blk = tile / args.tiles_m;
+        const int per_img = args.conv.tiles_w * args.conv.tiles_h;
+        b = n_blk / per_img;
+        const int r = n_blk - b * per_img;
+        h0 = (r / args.conv.tiles_w) * args.conv.tileH;
+        w0 = (r % args.conv.tiles_w) * args.conv.tileW;
+      } else {
+        map_tile(tile, args, m_blk, n_blk);
+      }
+      if (!wait_bounded_warp(tfull0 + 8 * acc, aph, wc, 4)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const int row = m_blk * BM + q * 32 + lane;
+      if (SILU_GATE) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(trow + c * 32, g);
+          tmem_ld32(trow + BN / 2 + c * 32, u);
+          float v[32];
+          const int col0 = n_blk * (BN / 2) + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float gv = __uint_as_float(g[j]);
+            float uv = __uint_as_float(u[j]);
+            const int col = col0 + j;
+            if (args.epi.bias_mode == 1 && col < args.epi.n_out) {
+              gv = __fadd_rn(gv, __ldg(args.epi.bias + col));
+              uv = __fadd_rn(uv, __ldg(args.epi.bias + args.epi.half_n + col));
+            }
+            v[j] = __fmul_rn(silu_f(gv), uv);
+          }
+          EpiArgs e2 = args.epi;
+          e2.bias_mode = 0;
+          e2.act = 0;
+          epi_store_row32(e2, row, col0, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + c * 32, r);
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (CONV_B)
+            epi_store_conv32(args.epi, args.conv, b, row, h0, w0, c * 32, v);
+          else
+            epi_store_row32(args.epi, row, n_blk * BN + c * 32, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+template <int MPAD, int R, int STAGES>
+struct K2Smem {
+  static constexpr int W_BYTES = R * TILE_A_BYTES;
+  static constexpr int X_BYTES = MPAD * BK * 2;
+  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+  static constexpr int BAR_BYTES = (2 * STAGES + 3) * 8 + 32;
+  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr uint32_t TMEM_COLS = (R * MPAD <= 32) ? 32 : (R * MPAD <= 64) ? 64 : 128;
+};
+
+// ------------------------------------------------------------------------------------------
+// K2: skinny-M GEMM (M <= 64), HBM-bound on W.  CTA (tile, split) multiplies R*128 rows of W
+// by all M tokens over one contiguous K range; R = 2 pairs a gate tile with its up tile.
+// ------------------------------------------------------------------------------------------
+template <int MPAD, int R, int STAGES>
+__global__ void __launch_bounds__(K1_THREADS, 1)
+    k2_skinny(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const SkinnyArgs args) {
+  using L = K2Smem<MPAD, R, STAGES>;
+  constexpr uint32_t IDESC = idesc_bf16_f32(BM, MPAD);
+  static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 64, "MPAD");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + STAGES * L::W_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sX + STAGES * L::X_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 3);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_s = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* ok_s = reinterpret_cast<volatile int*>(tmem_slot + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * STAGES;
+  const uint32_t tfull = empty0 + 8 * STAGES;
+  const uint32_t drain = tfull + 8;
+
+  const int tile = blockIdx.x / args.splits;
+  const int split = blockIdx.x - tile * args.splits;
+  const int kb0 = split * args.kb_per_split;
+  const int kb1 = min(kb0 + args.kb_per_split, args.num_kb);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(drain, 1);
+    *abort_s = 0;
+    *last_s = 0;
+    *ok_s = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtl wc{args.wait_cap_ns, args.status, abort_s, 0};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t pending = 0, issue_ph = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait_bounded(empty0 + 8 * stage, ph ^ 1, wc, 11)) break;
+        const uint32_t fb = full0 + 8 * stage;
+        mbar_arrive_expect_tx(fb, L::STAGE_BYTES);
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          tma_load_2d(smem_u32(sW + stage * L::W_BYTES + r * TILE_A_BYTES), &tmW, fb, kb * BK,
+                      (tile * R + r) * BM);
+        tma_load_2d(smem_u32(sX + stage * L::X_BYTES), &tmX, fb, kb * BK, 0);
+        pending |= 1u << stage;
+        issue_ph = (issue_ph & ~(1u << stage)) | (ph << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          ph ^= 1;
+        }
+      }
+      if (*abort_s)
+        for (int s = 0; s < STAGES; ++s)
+          if (pending & (1u << s)) wait_drain(full0 + 8 * s, (issue_ph >> s) & 1u, args.wait_cap_ns);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait_bounded(full0 + 8 * stage, ph, wc, 12)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t xd = sw128_kmajor_desc(smem_u32(sX + stage * L::X_BYTES));
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const uint64_t wd = sw128_kmajor_desc(smem_u32(sW + stage * L::W_BYTES + r * TILE_A_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16(tmem_base + (uint32_t)(r * MPAD), wd + 2 * k, xd + 2 * k, IDESC,
+                      (kb > kb0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(empty0 + 8 * stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          ph ^= 1;
+        }
+      }
+      if (ok) umma_commit(tfull);
+      if (*abort_s) {
+        umma_commit(drain);
+        wait_drain(drain, 0, args.wait_cap_ns);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int rowin = q * 32 + lane;  // W row within a 128-row tile
+    const int et = threadIdx.x - 64;  // 0..127
+    if (et == 0) *ok_s = wait_bounded(tfull, 0, wc, 13) ? 1 : 0;
+    named_bar_sync(1, 128);
+    if (*ok_s) {
+      tc_fence_after();
+      float acc[R][MPAD];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint32_t ta = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(r * MPAD);
+#pragma unroll
+        for (int c = 0; c < MPAD / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(ta + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[r][c * 32 + j] = __uint_as_float(v[j]);
+        }
+        if (MPAD % 32) {
+          uint32_t v[16];
+          tmem_ld16(ta + (MPAD / 32) * 32, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[r][(MPAD / 32) * 32 + j] = __uint_as_float(v[j]);
+        }
+      }
+      bool finalize = true;
+      if (args.splits > 1) {
+        // Deterministic split-K: every split stores its partial; the CTA that arrives last sums
+        // the partials in split order 0..S-1 and runs the epilogue.
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float* p = args.partial + ((((int64_t)tile * args.splits + split) * R + r) * BM + rowin) * MPAD;
+#pragma unroll
+          for (int m = 0; m < MPAD; m += 4)
+            __stcg(reinterpret_cast<float4*>(p + m), make_float4(acc[r][m], acc[r][m + 1], acc[r][m + 2], acc[r][m + 3]));
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          const int old = atomicAdd(args.counters + tile, 1);
+          *last_s = (old == args.splits - 1) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        finalize = (*last_s != 0);
+        if (finalize) {
+          __threadfence();
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+#pragma unroll
+            for (int m = 0; m < MPAD; ++m) acc[r][m] = 0.0f;
+            for (int s = 0; s < args.splits; ++s) {
+              const float* p = args.partial + ((((int64_t)tile * args.splits + s) * R + r) * BM + rowin) * MPAD;
+#pragma unroll
+              for (int m = 0; m < MPAD; m += 4) {
+                const float4 t = __ldcg(reinterpret_cast<const float4*>(p + m));
+                acc[r][m] += t.x;
+                acc[r][m + 1] += t.y;
+                acc[r][m + 2] += t.z;
+                acc[r][m + 3] += t.w;
+              }
+            }
+          }
+          if (et == 0) args.counters[tile] = 0;  // re-arm for the next launch
+        }
+      }
+      if (finalize) {
+        const EpiArgs& e = args.epi;
+        const int col = tile * BM + rowin;  // output column
+        if (col < e.n_out) {
+#pragma unroll
+          for (int m = 0; m < MPAD; ++m) {
+            if (m >= e.m_valid) break;
+            float* yp = e.Y + (int64_t)m * e.ldy + col;
+            float v;
+            if (R == 2) {
+              float gv = acc[0][m], uv = acc[R - 1][m];
+              if (e.bias_mode == 1) {
+                gv = __fadd_rn(gv, __ldg(e.bias + col));
+                uv = __fadd_rn(uv, __ldg(e.bias + e.half_n + col));
+              }
+              v = __fmul_rn(silu_f(gv), uv);
+            } else {
+              v = epi_value(e, acc[0][m], m, col, yp);
+            }
+            *yp = v;
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncwarp();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Casts
+// ------------------------------------------------------------------------------------------
+
+// X fp32 [rows][K] (row stride ldx) -> Xb bf16 [rows][Kp] with zeros in [K, Kp).  RNE.
+__global__ void k_cast_rows(const float* __restrict__ X, int64_t ldx, int rows, int K, int Kp,
+                            __nv_bfloat16* __restrict__ Xb, int vec8) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec8) {
+    // K == Kp, K % 8 == 0, ldx % 4 == 0, 16-byte aligned rows.
+    const int kv = K / 8;
+    const int64_t total = (int64_t)rows * kv;
+    for (int64_t i = tid; i < total; i += stride) {
+      const int64_t r = i / kv;
+      const int c = (int)(i - r * kv) * 8;
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(X + r * ldx + c));
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(X + r * ldx + c + 4));
+      __nv_bfloat162 p0 = __float22bfloat162_rn(make_float2(a.x, a.y));
+      __nv_bfloat162 p1 = __float22bfloat162_rn(make_float2(a.z, a.w));
+      __nv_bfloat162 p2 = __float22bfloat162_rn(make_float2(b.x, b.y));
+      __nv_bfloat162 p3 = __float22bfloat162_rn(make_float2(b.z, b.w));
+      uint4 o;
+      o.x = *reinterpret_cast<uint32_t*>(&p0);
+      o.y = *reinterpret_cast<uint32_t*>(&p1);
+      o.z = *reinterpret_cast<uint32_t*>(&p2);
+      o.w = *reinterpret_cast<uint32_t*>(&p3);
+      *reinterpret_cast<uint4*>(Xb + r * Kp + c) = o;
+    }
+  } else {
+    const int64_t total = (int64_t)rows * Kp;
+    for (int64_t i = tid; i < total; i += stride) {
+      const int64_t r = i / Kp;
+      const int c = (int)(i - r * Kp);
+      const float v = (c < K) ? X[r * ldx + c] : 0.0f;
+      Xb[i] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// src fp32 [batch][R][C] (row stride lds, batch stride sbs) -> dst bf16 [batch][C][Rp]
+// (row stride ldd, batch stride dbs), zeros for R <= r < Rp.  Rp must be even.
+__global__ void __launch_bounds__(256) k_transpose_cast(const float* __restrict__ src, int64_t lds, int64_t sbs, int R,
+                                                        int C, __nv_bfloat16* __restrict__ dst, int64_t ldd,
+                                                        int64_t dbs, int Rp) {
+  __shared__ float t[64][33];
+  const int c0 = blockIdx.x * 32;
+  const int r0 = blockIdx.y * 64;
+  const int b = blockIdx.z;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const float* s = src + (int64_t)b * sbs;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = ty + i * 8;
+    const int r = r0 + rr, c = c0 + tx;
+    t[rr][tx] = (r < R && c < C) ? __ldcs(s + (int64_t)r * lds + c) : 0.0f;
+  }
+  __syncthreads();
+  __nv_bfloat16* d = dst + (int64_t)b * dbs;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int idx = threadIdx.x + i * 256;
+    const int cc = idx >> 5, rp = idx & 31;
+    const int c = c0 + cc, r = r0 + 2 * rp;
+    if (c < C && r < Rp) {
+      __nv_bfloat162 p = __float22bfloat162_rn(make_float2(t[2 * rp][cc], t[2 * rp + 1][cc]));
+      *reinterpret_cast<__nv_bfloat162*>(d + (int64_t)c * ldd + r) = p;
+    }
+  }
+}
+
+// Explicit im2col for strided convolutions: NHWC bf16 [B][H][W][Cp] -> col bf16
+// [B][outH*outW][KH*KW*Cp] in (kh, kw, c) order, zeros outside the image.  8 channels/thread.
+__global__ void k_im2col_nhwc(const __nv_bfloat16* __restrict__ in, int B, int H, int W, int Cp, int KH, int KW,
+                              int stride, int pad, int outH, int outW, __nv_bfloat16* __restrict__ col) {
+  const int c8n = Cp / 8;
+  const int64_t total = (int64_t)B * outH * outW * KH * KW * c8n;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t t = i;
+    const int c8 = (int)(t % c8n); t /= c8n;
+    const int kw = (int)(t % KW); t /= KW;
+    const int kh = (int)(t % KH); t /= KH;
+    const int ow = (int)(t % outW); t /= outW;
+    const int oh = (int)(t % outH); t /= outH;
+    const int b = (int)t;
+    const int ih = oh * stride - pad + kh, iw = ow * stride - pad + kw;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+      v = *reinterpret_cast<const uint4*>(in + (((int64_t)b * H + ih) * W + iw) * Cp + c8 * 8);
+    const int64_t pix = ((int64_t)b * outH + oh) * outW + ow;
+    *reinterpret_cast<uint4*>(col + (pix * (KH * KW) + kh * KW + kw) * (int64_t)Cp + c8 * 8) = v;
+  }
+}
+
+// Self-test of the bounded wait: one CTA waits on a barrier nothing arrives at.
+__global__ void k_wait_selftest(int* status, uint64_t cap_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const WaitCtl wc{cap_ns, status, &abort_flag, 0};
+    wait_bounded(smem_u32(&bar), 0, wc, 99);
+  }
+}
+
+}  // namespace envg

@@ -1,0 +1,305 @@
+"""ctypes binding of libenvgemm.so (the C ABI in include/envgemm.h) plus a mirror of Envision's
+QNN operator names for this path.
+
+Two calling modes, picked from the argument types:
+
+* numpy arrays  -> host pointers (``ENVG_HOST_PTRS``): the library copies inputs to the GPU,
+  runs, copies the result back and synchronises -- what the Pascal host does;
+* torch CUDA tensors -> device pointers (``ENVG_DEVICE_PTRS``) on the current torch stream.
+
+There is no CPU fallback: if the shared library is missing or the GPU is absent, calls raise
+``EnvgError``.  The QNN-named mirror functions (``QNNLinear`` and friends) keep the reference's
+argument order and meaning (``src/quicknn_kernels.pas``) and raise ``AssertionError`` with an
+``ERROR ...`` message where the reference asserts.
+"""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libenvgemm.so")
+HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "envgemm.h")
+
+OK = 0
+ERR_ARG, ERR_OOM, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_STATE, ERR_UNSUPPORTED = -1, -2, -3, -4, -5, -6, -7
+LAYOUT_PLAIN, LAYOUT_GATE_UP = 0, 1
+EPI_NONE, EPI_BIAS, EPI_SILU_GATE, EPI_GATED_RESIDUAL, EPI_SILU = 0, 1, 2, 3, 4
+HOST_PTRS, DEVICE_PTRS, ASYNC = 0, 1, 2
+ROW_MAJOR, NO_TRANS, TRANS = 101, 111, 112
+
+
+class EnvgError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"envgemm error {code}: {msg}")
+        self.code = code
+
+
+class Stats(ctypes.Structure):
+    _fields_ = [("calls", ctypes.c_uint64), ("kernel_launches", ctypes.c_uint64), ("flops", ctypes.c_double),
+                ("h2d_bytes", ctypes.c_double), ("d2h_bytes", ctypes.c_double), ("weight_bytes", ctypes.c_uint64),
+                ("workspace_bytes", ctypes.c_uint64), ("device", ctypes.c_int32), ("last_status", ctypes.c_int32)]
+
+
+_lib = None
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_ci = ctypes.c_int
+
+
+def lib():
+    """Load libenvgemm.so (fails loudly when it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise EnvgError(ERR_STATE, f"{LIB_PATH} not built: run `python -c 'import __graft_entry__ as g; g.build()'`")
+        L = ctypes.CDLL(LIB_PATH)
+        L.envg_version.restype = ctypes.c_char_p
+        L.envg_last_error.restype = ctypes.c_char_p
+        L.envg_init.argtypes = [_ci, ctypes.POINTER(_ci)]
+        L.envg_weight_upload.argtypes = [_vp, _vp, _i64, _i64, _ci, ctypes.POINTER(_vp)]
+        L.envg_weight_upload_shard.argtypes = [_vp, _vp, _i64, _i64, _i64, _i64, _ci, ctypes.POINTER(_vp)]
+        L.envg_conv_weight_upload.argtypes = [_vp, _vp, _ci, _ci, _ci, _ci, ctypes.POINTER(_vp)]
+        L.envg_weight_free.argtypes = [_vp]
+        L.envg_linear.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
+        L.envg_conv2d.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 11
+        L.envg_sgemm.argtypes = [_ci, _ci, _ci, _i64, _i64, _i64, ctypes.c_float, _vp, _i64, _vp, _i64,
+                                 ctypes.c_float, _vp, _i64]
+        L.envg_set_stream.argtypes = [_vp]
+        L.envg_get_stats.argtypes = [ctypes.POINTER(Stats)]
+        L.envg_set_wait_cap_ns.argtypes = [ctypes.c_uint64]
+        L.envg_selftest_wait_timeout.argtypes = [ctypes.c_uint64]
+        _lib = L
+    return _lib
+
+
+def header_symbols():
+    """Names of every entry point declared in include/envgemm.h."""
+    with open(HEADER_PATH) as f:
+        txt = f.read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(envg_\w+)\s*\(", txt, re.M)))
+
+
+def last_error():
+    return lib().envg_last_error().decode()
+
+
+def version():
+    return lib().envg_version().decode()
+
+
+def _check(rc):
+    if rc != OK:
+        raise EnvgError(rc, last_error())
+    return rc
+
+
+def init(device=0):
+    ids = (_ci * 1)(device)
+    return _check(lib().envg_init(1, ids))
+
+
+def shutdown():
+    return _check(lib().envg_shutdown())
+
+
+def sync():
+    return _check(lib().envg_sync())
+
+
+def stats():
+    s = Stats()
+    _check(lib().envg_get_stats(ctypes.byref(s)))
+    return {f: getattr(s, f) for f, _ in Stats._fields_}
+
+
+def set_wait_cap_ns(ns):
+    return _check(lib().envg_set_wait_cap_ns(int(ns)))
+
+
+def selftest_wait_timeout(cap_ns):
+    """Return code of the bounded-wait self-test (ERR_TIMEOUT when the bound works)."""
+    return lib().envg_selftest_wait_timeout(int(cap_ns))
+
+
+def _is_torch(t):
+    return type(t).__module__.startswith("torch")
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    if _is_torch(a):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+def _host_f32(a, name):
+    if not (isinstance(a, np.ndarray) and a.dtype == np.float32 and a.flags.c_contiguous):
+        raise TypeError(f"{name}: expected a C-contiguous float32 numpy array")
+    return a
+
+
+def _mode(*arrays):
+    """HOST_PTRS for numpy operands, DEVICE_PTRS for torch CUDA tensors (never mixed)."""
+    kinds = {(_is_torch(a)) for a in arrays if a is not None}
+    if len(kinds) != 1:
+        raise TypeError("operands must be all numpy (host) or all torch CUDA tensors (device)")
+    if kinds.pop():
+        import torch
+
+        for a in arrays:
+            if a is None:
+                continue
+            if not (a.is_cuda and a.dtype == torch.float32 and a.is_contiguous()):
+                raise TypeError("device operands must be contiguous float32 CUDA tensors")
+        lib().envg_set_stream(_vp(torch.cuda.current_stream().cuda_stream))
+        return DEVICE_PTRS
+    for a in arrays:
+        if a is not None:
+            _host_f32(a, "operand")
+    return HOST_PTRS
+
+
+class Weight:
+    """A device-resident bf16 weight (envg_weight handle).
+
+    ``w`` is W[N, K] row-major as numpy uint16 (raw bf16 bits) or float32 (rounded to bf16 with
+    round-to-nearest-even at upload).  ``shard=(n0, n1)`` uploads only output rows [n0, n1)
+    (for GATE_UP: gate rows [n0, n1) and the same up rows).  ``conv=(out_ch, in_ch, kH, kW)``
+    uploads a convolution weight [out_ch, in_ch, kH, kW].
+    """
+
+    def __init__(self, w, layout=LAYOUT_PLAIN, shard=None, conv=None):
+        self.h = None
+        w = np.ascontiguousarray(w)
+        if w.dtype == np.uint16:
+            pb, pf = w.ctypes.data, None
+        elif w.dtype == np.float32:
+            pb, pf = None, w.ctypes.data
+        else:
+            raise TypeError("weight must be uint16 (bf16 bits) or float32")
+        h = _vp()
+        L = lib()
+        if conv is not None:
+            O, C, kH, kW = conv
+            assert w.size == O * C * kH * kW, "ERROR : conv weight size mismatch"
+            _check(L.envg_conv_weight_upload(pb, pf, O, C, kH, kW, ctypes.byref(h)))
+            self.N, self.K = O, C * kH * kW
+        else:
+            N, K = w.shape
+            if shard is None:
+                _check(L.envg_weight_upload(pb, pf, N, K, layout, ctypes.byref(h)))
+                self.N = N
+            else:
+                n0, n1 = shard
+                _check(L.envg_weight_upload_shard(pb, pf, N, K, n0, n1, layout, ctypes.byref(h)))
+                self.N = (n1 - n0) * (2 if layout == LAYOUT_GATE_UP else 1)
+            self.K = K
+        self.layout = layout
+        self.conv = conv
+        self.h = h
+
+    def free(self):
+        if self.h is not None and self.h.value:
+            _check(lib().envg_weight_free(self.h))
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def linear(dst, x, W, bias=None, epilogue=None, gate=None, sync=True):
+    """dst = epilogue(x . W^T): envg_linear.  x [M, K]; dst [M, N] (N/2 for SILU_GATE)."""
+    if epilogue is None:
+        epilogue = EPI_SILU_GATE if W.layout == LAYOUT_GATE_UP else (EPI_BIAS if bias is not None else EPI_NONE)
+    flags = _mode(dst, x, bias, gate)
+    if flags == DEVICE_PTRS and not sync:
+        flags |= ASYNC
+    M, K = x.shape
+    return _check(lib().envg_linear(_ptr(dst), _ptr(x), W.h, _ptr(bias), M, K, W.N, epilogue, _ptr(gate), flags))
+
+
+def conv2d(dst, src, W, bias, stride, pad, epilogue=None, sync=True):
+    """dst[B, O, outH, outW] = conv(src[B, C, H, W]) + bias (NCHW): envg_conv2d."""
+    if epilogue is None:
+        epilogue = EPI_BIAS if bias is not None else EPI_NONE
+    flags = _mode(dst, src, bias)
+    if flags == DEVICE_PTRS and not sync:
+        flags |= ASYNC
+    B, C, H, Wd = src.shape
+    O, C2, kH, kW = W.conv
+    return _check(lib().envg_conv2d(_ptr(dst), _ptr(src), W.h, _ptr(bias), C, O, H, Wd, kH, kW, stride, pad, B,
+                                    epilogue, flags))
+
+
+def sgemm(order, transA, transB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc):
+    """cblas_sgemm-compatible call on host numpy buffers (envg_sgemm)."""
+    for a in (A, B, C):
+        _host_f32(a, "sgemm operand")
+    return _check(lib().envg_sgemm(order, transA, transB, M, N, K, alpha, A.ctypes.data, lda, B.ctypes.data, ldb,
+                                   beta, C.ctypes.data, ldc))
+
+
+# ---------------------------------------------------------------------------------------------
+# Mirror of Envision's QNN operator surface for this path (src/quicknn_kernels.pas).  The
+# weight argument is a device-resident Weight in place of the fp32/bf16 TMemoryBlock.
+# ---------------------------------------------------------------------------------------------
+
+def _assert(cond, msg):
+    if not cond:
+        raise AssertionError(msg)
+
+
+def QNNLinear(dst, x, W, B, seqLen, inDIM, outDIM):
+    """quicknn_kernels.pas:897-911 -> quicknncpu.pas:1807-1820: dst = x.W^T (+ B per row)."""
+    _assert(W.N == outDIM and W.K == inDIM, "ERROR : QNNLinear weight shape mismatch")
+    _assert(x.shape[0] >= seqLen and dst.shape[0] >= seqLen, "ERROR : QNNLinear out of bound")
+    xs, ds = x[:seqLen], dst[:seqLen]
+    return linear(ds, xs, W, bias=B, epilogue=EPI_BIAS if B is not None else EPI_NONE)
+
+
+def QNNLinearNoBias(dst, x, W, seqLen, inDIM, outDIM):
+    """quicknn_kernels.pas:913-927 -> quicknncpu.pas:1822-1828."""
+    return QNNLinear(dst, x, W, None, seqLen, inDIM, outDIM)
+
+
+def QNNLINEAR_BF16_OR_F32(dst, src, weight, weight_bf16, seq, srcDim, dstDim):
+    """quicknn_kernels.pas:2093-2103 -> quicknncpu.pas:3062-3071: picks the bf16 weight if set."""
+    w = weight_bf16 if weight_bf16 is not None else weight
+    _assert(w is not None, "ERROR QNNLINEAR_BF16_OR_F32 : no weight or weight_16 assigned!")
+    return QNNLinearNoBias(dst, src, w, seq, srcDim, dstDim)
+
+
+def QNNMatMulNT(C, A, B, M, K, N):
+    """quicknn_kernels.pas:847-861 -> quicknncpu.pas:1773-1784 with B a device weight [N, K]."""
+    _assert(B.N == N and B.K == K, "ERROR : QNNMatMul out of bound [B]")
+    return linear(C[:M], A[:M], B, epilogue=EPI_NONE)
+
+
+def QNNLinearSiluMul(dst, x, W_gate_up, seqLen, inDIM, mlpDIM):
+    """Fused QNNLinearNoBias into [gate | up] then QNNSiluMul(gate, up) (quicknncpu.pas:2404-2419),
+    as the FLUX FFN does (quicknn_transformers.pas:1331-1341); dst is [seqLen, mlpDIM]."""
+    _assert(W_gate_up.layout == LAYOUT_GATE_UP and W_gate_up.N == 2 * mlpDIM, "ERROR : gate/up weight mismatch")
+    return linear(dst[:seqLen], x[:seqLen], W_gate_up, epilogue=EPI_SILU_GATE)
+
+
+def QNNLinearGatedAdd(h, x, W, gate, seqLen, inDIM, outDIM, B=None):
+    """Fused QNNLinear then QNNGatedAdd(h, gate, proj, seq, hidden) (quicknncpu.pas:853-859):
+    h += gate (.) (x.W^T + B)."""
+    _assert(W.N == outDIM and W.K == inDIM, "ERROR : QNNLinear weight shape mismatch")
+    return linear(h[:seqLen], x[:seqLen], W, bias=B, epilogue=EPI_GATED_RESIDUAL, gate=gate)
+
+
+def QNNConv2d(dst, src, weights, bias, in_ch, out_ch, H, W, kH, kW, stride, padding, batch):
+    """quicknn_kernels.pas:990-1010 -> quicknncpu.pas:1958-2132 (NCHW)."""
+    _assert(weights.conv == (out_ch, in_ch, kH, kW), "ERROR [Conv2D] : weight geometry mismatch")
+    outH = (H + 2 * padding - kH) // stride + 1
+    outW = (W + 2 * padding - kW) // stride + 1
+    _assert(dst.size >= batch * out_ch * outH * outW, "ERROR [Conv2D] : Incorrect destination size")
+    return conv2d(dst.reshape(batch, out_ch, outH, outW), src.reshape(batch, in_ch, H, W), weights, bias, stride,
+                  padding)

@@ -1,0 +1,228 @@
+"""ctypes front end of the CPU checkers -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg import this module.
+It wraps two shared libraries built by ``oracle/Makefile``:
+
+* ``liboracle.so`` -- the C++ restatement of the reference CPU path (``envg_oracle.cpp``;
+  each function there cites the Envision source line it restates);
+* ``_ref/libsgemm2.so`` -- the reference's own ``src/sgemm2.cpp`` compiled unmodified
+  (``cpp_sgemm``, sgemm2.cpp:530-547).  Optional: present only when it was built here.
+
+Arrays are numpy; every call checks dtype and contiguity before handing pointers to C.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PATH_AVX2 = 0
+PATH_SCALAR = 1
+ROW_MAJOR, NO_TRANS, TRANS = 101, 111, 112
+
+_lib = None
+_ref = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_i64 = ctypes.c_int64
+
+
+def _p(a, ct=_f32p):
+    return None if a is None else a.ctypes.data_as(ct)
+
+
+def _chk(a, dtype):
+    assert isinstance(a, np.ndarray) and a.dtype == dtype and a.flags.c_contiguous, (a.dtype, dtype)
+    return a
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            raise RuntimeError("oracle/liboracle.so missing: run `make -C oracle`")
+        L = ctypes.CDLL(path)
+        L.envo_set_threads.argtypes = [ctypes.c_int]
+        L.envo_set_threads.restype = ctypes.c_int
+        L.envo_get_threads.restype = ctypes.c_int
+        L.envo_bf16_to_f32.argtypes = [_i64, _u16p, _f32p]
+        L.envo_f32_to_bf16_trunc.argtypes = [_i64, _f32p, _u16p]
+        L.envo_sdot.argtypes = [ctypes.c_int, _i64, _f32p, _f32p]
+        L.envo_sdot.restype = ctypes.c_float
+        L.envo_qgemm.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i64, _i64, _i64,
+                                 ctypes.c_float, _f32p, _i64, _f32p, _i64, ctypes.c_float, _f32p, _i64]
+        L.envo_qgemm.restype = ctypes.c_int
+        L.envo_linear_f32.argtypes = [ctypes.c_int, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64]
+        L.envo_linear_bf16.argtypes = [ctypes.c_int, _f32p, _f32p, _u16p, _f32p, _i64, _i64, _i64]
+        L.envo_fast_exp.argtypes = [ctypes.c_float]
+        L.envo_fast_exp.restype = ctypes.c_float
+        L.envo_silu_mul.argtypes = [_f32p, _f32p, _i64]
+        L.envo_silu.argtypes = [_f32p, _i64]
+        L.envo_gated_add.argtypes = [_f32p, _f32p, _f32p, _i64, _i64]
+        L.envo_conv2d.argtypes = [ctypes.c_int, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 9
+        L.envo_conv2d.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def ref_lib():
+    """The reference's own sgemm2.cpp, or None when it was not built."""
+    global _ref
+    if _ref is None:
+        path = os.path.join(HERE, "_ref", "libsgemm2.so")
+        if not os.path.exists(path):
+            return None
+        L = ctypes.CDLL(path)
+        ci = ctypes.c_int
+        L.cpp_sgemm.argtypes = [ci, ci, ci, ci, ci, ctypes.c_float, _f32p, ci, _f32p, ci,
+                                ctypes.c_float, _f32p, ci, ci, ci]
+        L.cpp_sgemm.restype = None
+        _ref = L
+    return _ref
+
+
+def set_threads(n):
+    return lib().envo_set_threads(int(n))
+
+
+def bf16_to_f32(w_bits):
+    w_bits = _chk(np.ascontiguousarray(w_bits), np.uint16)
+    out = np.empty(w_bits.shape, np.float32)
+    lib().envo_bf16_to_f32(w_bits.size, _p(w_bits, _u16p), _p(out))
+    return out
+
+
+def f32_to_bf16_trunc(x):
+    x = _chk(np.ascontiguousarray(x), np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().envo_f32_to_bf16_trunc(x.size, _p(x), _p(out, _u16p))
+    return out
+
+
+def f32_to_bf16_rne(x):
+    """Round-to-nearest-even fp32 -> bf16 bits (the rounding the CUDA path applies to X)."""
+    x = np.ascontiguousarray(x, np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    r = ((u >> 16) & 1) + 0x7FFF
+    out = ((u + r) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return out
+
+
+def qgemm(transA, transB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, path=PATH_AVX2):
+    for a in (A, B, C):
+        _chk(a, np.float32)
+    rc = lib().envo_qgemm(path, ROW_MAJOR, transA, transB, M, N, K, alpha, _p(A), lda, _p(B), ldb,
+                          beta, _p(C), ldc)
+    assert rc == 0
+    return C
+
+
+def linear_bf16(x, w_bits, bias=None, path=PATH_AVX2):
+    """QNNLinearNoBias_BF16 (+ QNNLinear bias): Y[M,N] = X[M,K] . widen(W[N,K])^T (+ b)."""
+    x = _chk(np.ascontiguousarray(x), np.float32)
+    w_bits = _chk(np.ascontiguousarray(w_bits), np.uint16)
+    M, K = x.shape
+    N = w_bits.shape[0]
+    assert w_bits.shape == (N, K)
+    if bias is not None:
+        bias = _chk(np.ascontiguousarray(bias), np.float32)
+        assert bias.shape == (N,)
+    y = np.zeros((M, N), np.float32)
+    lib().envo_linear_bf16(path, _p(y), _p(x), _p(w_bits, _u16p), _p(bias), M, K, N)
+    return y
+
+
+def linear_f32(x, w, bias=None, path=PATH_AVX2):
+    x = _chk(np.ascontiguousarray(x), np.float32)
+    w = _chk(np.ascontiguousarray(w), np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    if bias is not None:
+        bias = _chk(np.ascontiguousarray(bias), np.float32)
+    y = np.zeros((M, N), np.float32)
+    lib().envo_linear_f32(path, _p(y), _p(x), _p(w), _p(bias), M, K, N)
+    return y
+
+
+def fast_exp(x):
+    return lib().envo_fast_exp(float(x))
+
+
+def silu_mul(gate, up):
+    """QNNSiluMul (scalar build): returns silu(gate) * up (inputs unchanged)."""
+    g = np.array(gate, np.float32, copy=True, order="C")
+    u = _chk(np.ascontiguousarray(up), np.float32)
+    lib().envo_silu_mul(_p(g), _p(u), g.size)
+    return g
+
+
+def silu(x):
+    g = np.array(x, np.float32, copy=True, order="C")
+    lib().envo_silu(_p(g), g.size)
+    return g
+
+
+def gated_add(dst, gate, proj):
+    """QNNGatedAdd: returns dst + gate (.) proj, row by row (inputs unchanged)."""
+    d = np.array(dst, np.float32, copy=True, order="C")
+    g = _chk(np.ascontiguousarray(gate), np.float32)
+    p = _chk(np.ascontiguousarray(proj), np.float32)
+    seq, hidden = d.shape
+    lib().envo_gated_add(_p(d), _p(g), _p(p), seq, hidden)
+    return d
+
+
+def conv2d(src, w, bias, stride, padding, path=PATH_AVX2):
+    """QNNConv2d: src fp32 [B,C,H,W], w fp32 [O,C,kH,kW] -> fp32 [B,O,outH,outW] (NCHW)."""
+    src = _chk(np.ascontiguousarray(src), np.float32)
+    w = _chk(np.ascontiguousarray(w), np.float32)
+    B, C, H, W = src.shape
+    O, C2, kH, kW = w.shape
+    assert C2 == C
+    if bias is not None:
+        bias = _chk(np.ascontiguousarray(bias), np.float32)
+    outH = (H + 2 * padding - kH) // stride + 1
+    outW = (W + 2 * padding - kW) // stride + 1
+    y = np.zeros((B, O, outH, outW), np.float32)
+    rc = lib().envo_conv2d(path, _p(y), _p(src), _p(w), _p(bias), C, O, H, W, kH, kW, stride, padding, B)
+    assert rc == 0
+    return y
+
+
+def sgemm2_nt(A, B, M, N, K, threads=0):
+    """The reference's cpp_sgemm(NoTrans, Trans) on pre-zeroed C (it ignores beta, sgemm2.cpp:312-324)."""
+    L = ref_lib()
+    if L is None:
+        raise RuntimeError("oracle/_ref/libsgemm2.so not built")
+    A = _chk(np.ascontiguousarray(A), np.float32)
+    B = _chk(np.ascontiguousarray(B), np.float32)
+    C = np.zeros((M, N), np.float32)
+    L.cpp_sgemm(NO_TRANS, TRANS, M, N, K, 1.0, _p(A), K, _p(B), K, 0.0, _p(C), N, 0, 0)
+    return C
+
+
+def sgemm2_nn(A, B, M, N, K):
+    L = ref_lib()
+    if L is None:
+        raise RuntimeError("oracle/_ref/libsgemm2.so not built")
+    A = _chk(np.ascontiguousarray(A), np.float32)
+    B = _chk(np.ascontiguousarray(B), np.float32)
+    C = np.zeros((M, N), np.float32)
+    L.cpp_sgemm(NO_TRANS, NO_TRANS, M, N, K, 1.0, _p(A), K, _p(B), N, 0.0, _p(C), N, 0, 0)
+    return C
+
+
+def parity_stats(y, ref):
+    """(max|d| / max|ref|, sum|d| / sum|ref|): the acceptance metrics of the hot path."""
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = np.abs(y - ref)
+    mref = np.abs(ref).max()
+    sref = np.abs(ref).sum()
+    return (float(d.max() / mref) if mref > 0 else float(d.max()),
+            float(d.sum() / sref) if sref > 0 else float(d.sum()))

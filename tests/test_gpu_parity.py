@@ -1,0 +1,199 @@
+"""GPU parity: libenvgemm (through its C ABI) against the CPU restatement of the reference.
+
+Every case runs the same seeded inputs through the CUDA path and through the oracle
+(oracle/envg_oracle.cpp, which restates src/quicknncpu.pas qgemm/gemm_nt/gemm_nn and the
+epilogue ops) and applies the acceptance bounds of tests/common.py.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.common import TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT, assert_parity, inputs
+
+pytestmark = pytest.mark.gpu
+
+# (M, K, N): model shapes scaled to oracle-friendly sizes, tile edges and ragged tails.
+LINEAR_SHAPES = [
+    (1024, 3072, 9216),   # FLUX2-Klein QKV
+    (256, 512, 768),
+    (200, 136, 300),      # ragged M and N, K not a multiple of 64
+    (129, 64, 257),       # one row / one column past a tile
+    (384, 1024, 512),
+    (65, 256, 128),       # smallest M on the large-M path
+]
+SKINNY_SHAPES = [
+    (1, 3072, 18432),     # adaLN modulation (config 2, M = 1)
+    (1, 2560, 1024),      # Qwen3 k/v at M = 1
+    (16, 2560, 4096),     # Qwen3 q at M = 16
+    (17, 512, 200),
+    (33, 256, 136),
+    (64, 1024, 512),
+    (48, 4096, 256),
+]
+
+
+@pytest.mark.parametrize("M,K,N", LINEAR_SHAPES + SKINNY_SHAPES)
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_linear_vs_oracle(gpu, M, K, N, with_bias):
+    x, w, b = inputs(M, K, N, seed=M * 7 + K + N, bias=with_bias)
+    W = gpu.Weight(w)
+    y = np.full((M, N), np.nan, np.float32)
+    gpu.linear(y, x, W, bias=b)
+    ref = O.linear_bf16(x, w, b, path=O.PATH_AVX2)
+    assert_parity(y, ref, what=f"linear {M}x{K}x{N} bias={with_bias}")
+
+
+@pytest.mark.parametrize("M,K,N", [(70, 131, 96), (5, 45, 33), (130, 1001, 260)])
+def test_linear_k_not_multiple_of_8(gpu, M, K, N):
+    """K % 8 != 0: the AVX2 build of the reference discards its main-loop sum here
+    (ops_avx2.inc:1442-1460), so parity is against the scalar build of the same GEMM."""
+    x, w, b = inputs(M, K, N, seed=3 + K)
+    W = gpu.Weight(w)
+    y = np.zeros((M, N), np.float32)
+    gpu.linear(y, x, W, bias=b)
+    ref = O.linear_bf16(x, w, b, path=O.PATH_SCALAR)
+    assert_parity(y, ref, what=f"K%8 {M}x{K}x{N}")
+
+
+def test_linear_f32_weight_upload_rounds_rne(gpu):
+    M, K, N = 96, 256, 192
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    wf = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
+    W = gpu.Weight(wf)
+    y = np.zeros((M, N), np.float32)
+    gpu.linear(y, x, W)
+    ref = O.linear_bf16(x, O.f32_to_bf16_rne(wf))
+    assert_parity(y, ref)
+
+
+@pytest.mark.parametrize("M,K,H", [(256, 512, 384), (4608 // 8, 3072, 1152), (1, 3072, 640), (16, 512, 200), (130, 256, 130)])
+def test_silu_gate_vs_oracle(gpu, M, K, H):
+    """Fused gate/up linear + QNNSiluMul: W = [gate (H rows) | up (H rows)], Y [M, H]."""
+    x, w, _ = inputs(M, K, 2 * H, seed=H + M)
+    W = gpu.Weight(w, layout=gpu.LAYOUT_GATE_UP)
+    y = np.zeros((M, H), np.float32)
+    gpu.linear(y, x, W)
+    gu = O.linear_bf16(x, w)
+    ref = O.silu_mul(np.ascontiguousarray(gu[:, :H]), np.ascontiguousarray(gu[:, H:]))
+    # the two GEMM halves through the plain path, at the GEMM bounds
+    Wp = gpu.Weight(w)
+    yg = np.zeros((M, 2 * H), np.float32)
+    gpu.linear(yg, x, Wp)
+    assert_parity(yg, gu, what=f"silu-gate halves {M}x{K}x{2 * H}")
+    # the fused epilogue applies exactly silu(g) * u to those GEMM values
+    np.testing.assert_allclose(y, O.silu_mul(np.ascontiguousarray(yg[:, :H]), np.ascontiguousarray(yg[:, H:])),
+                               rtol=2e-5, atol=2e-6)
+    assert_parity(y, ref, TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT, what=f"silu-gate {M}x{K}x{H}")
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 1024, 768), (8, 3072, 3072), (200, 256, 100)])
+def test_gated_residual_vs_oracle(gpu, M, K, N):
+    x, w, b = inputs(M, K, N, seed=N + 5)
+    rng = np.random.default_rng(N)
+    h0 = rng.standard_normal((M, N), dtype=np.float32)
+    gate = rng.standard_normal(N).astype(np.float32)
+    W = gpu.Weight(w)
+    h = h0.copy()
+    gpu.linear(h, x, W, bias=b, epilogue=gpu.EPI_GATED_RESIDUAL, gate=gate)
+    proj = O.linear_bf16(x, w, b)
+    ref = O.gated_add(h0, gate, proj)
+    # compare the update (h - h0) so the residual does not hide GEMM error
+    assert_parity(h - h0, ref - h0, what=f"gated residual {M}x{K}x{N}")
+
+
+CONV_CASES = [
+    # (B, C, H, W, O, k, stride, pad)
+    (1, 64, 32, 32, 128, 3, 1, 1),
+    (1, 128, 16, 48, 64, 3, 1, 1),
+    (2, 16, 20, 24, 32, 3, 1, 1),     # channels padded to 64, odd width
+    (1, 64, 8, 300, 64, 3, 1, 1),     # width above one 256-pixel tile
+    (1, 96, 16, 16, 200, 1, 1, 0),    # 1x1 (conv_shortcut shape)
+    (1, 32, 17, 19, 48, 3, 2, 1),     # strided: explicit im2col path
+]
+
+
+@pytest.mark.parametrize("B,C,H,Wd,O_,k,stride,pad", CONV_CASES)
+@pytest.mark.parametrize("silu", [False, True])
+def test_conv2d_vs_oracle(gpu, B, C, H, Wd, O_, k, stride, pad, silu):
+    rng = np.random.default_rng(B * 1000 + C + H + O_)
+    src = rng.standard_normal((B, C, H, Wd), dtype=np.float32)
+    wb = O.f32_to_bf16_rne((0.02 * rng.standard_normal((O_, C, k, k))).astype(np.float32))
+    bias = (0.01 * rng.standard_normal(O_)).astype(np.float32)
+    W = gpu.Weight(wb.reshape(O_, -1), conv=(O_, C, k, k))
+    outH = (H + 2 * pad - k) // stride + 1
+    outW = (Wd + 2 * pad - k) // stride + 1
+    y = np.full((B, O_, outH, outW), np.nan, np.float32)
+    gpu.conv2d(y, src, W, bias, stride, pad, epilogue=gpu.EPI_SILU if silu else gpu.EPI_BIAS)
+    ref = O.conv2d(src, O.bf16_to_f32(wb), bias, stride, pad)
+    if silu:
+        ref = O.silu(ref)
+    assert_parity(y, ref, what=f"conv {B}x{C}x{H}x{Wd}->{O_} k{k} s{stride} silu={silu}")
+
+
+@pytest.mark.parametrize("ta,tb", [(111, 112), (111, 111), (112, 111)])
+@pytest.mark.parametrize("M,N,K", [(96, 80, 72), (8, 300, 128), (257, 129, 64)])
+def test_sgemm_vs_oracle(gpu, ta, tb, M, N, K):
+    rng = np.random.default_rng(M + N + K + ta + tb)
+    A = rng.standard_normal((K, M) if ta == 112 else (M, K), dtype=np.float32)
+    B = rng.standard_normal((N, K) if tb == 112 else (K, N), dtype=np.float32)
+    C0 = rng.standard_normal((M, N), dtype=np.float32)
+    lda, ldb = A.shape[1], B.shape[1]
+    for alpha, beta in ((1.0, 0.0), (0.5, 2.0)):
+        C = C0.copy()
+        gpu.sgemm(101, ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, N)
+        ref = C0.copy()
+        Ab = O.bf16_to_f32(O.f32_to_bf16_rne(A))
+        Bb = O.bf16_to_f32(O.f32_to_bf16_rne(B))
+        O.qgemm(ta, tb, M, N, K, alpha, Ab, lda, Bb, ldb, beta, ref, N, path=O.PATH_SCALAR)
+        assert_parity(C, ref, what=f"sgemm {ta},{tb} a={alpha} b={beta}")
+
+
+def test_m_zero_is_noop(gpu):
+    x, w, _ = inputs(4, 64, 64, seed=1, bias=False)
+    W = gpu.Weight(w)
+    y = np.full((0, 64), 7.0, np.float32)
+    gpu.linear(y, np.zeros((0, 64), np.float32), W)
+
+
+def test_bounded_wait_times_out_cleanly(gpu):
+    """A wait nothing satisfies returns ENVG_ERR_TIMEOUT and the context stays usable."""
+    rc = gpu.selftest_wait_timeout(20_000_000)  # 20 ms bound
+    assert rc == gpu.ERR_TIMEOUT
+    assert "bound" in gpu.last_error()
+    x, w, b = inputs(128, 256, 256, seed=9)
+    W = gpu.Weight(w)
+    y = np.zeros((128, 256), np.float32)
+    gpu.linear(y, x, W, bias=b)
+    assert_parity(y, O.linear_bf16(x, w, b))
+
+
+def test_device_pointer_mode_and_canaries(gpu):
+    """torch CUDA tensors go through ENVG_DEVICE_PTRS; guard zones around Y stay untouched."""
+    import torch
+
+    M, K, N = 300, 512, 520
+    x, w, b = inputs(M, K, N, seed=21)
+    W = gpu.Weight(w)
+    guard = 4096
+    ybuf = torch.full((M * N + 2 * guard,), 12345.0, device="cuda")
+    y = ybuf[guard:guard + M * N].view(M, N)
+    gpu.linear(y, torch.from_numpy(x).cuda(), W, bias=torch.from_numpy(b).cuda())
+    torch.cuda.synchronize()
+    assert torch.all(ybuf[:guard] == 12345.0) and torch.all(ybuf[guard + M * N:] == 12345.0)
+    assert_parity(y.cpu().numpy(), O.linear_bf16(x, w, b))
+
+
+def test_errors_are_codes_not_crashes(gpu):
+    x, w, _ = inputs(8, 64, 32, seed=2, bias=False)
+    W = gpu.Weight(w)
+    y = np.zeros((8, 32), np.float32)
+    with pytest.raises(gpu.EnvgError) as e:
+        gpu.linear(y, np.zeros((8, 48), np.float32), W)  # K mismatch
+    assert e.value.code == gpu.ERR_ARG
+    with pytest.raises(gpu.EnvgError):
+        gpu.linear(y, x, W, epilogue=gpu.EPI_SILU_GATE)  # needs a GATE_UP weight
+    W.free()
+    with pytest.raises(gpu.EnvgError) as e:
+        gpu.linear(y, x, W)  # freed handle -> NULL
+    assert e.value.code == gpu.ERR_STATE
