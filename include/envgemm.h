@@ -136,7 +136,8 @@ int envg_sgemm(int order, int transA, int transB, int64_t M, int64_t N, int64_t 
                int64_t ldc);
 
 /* Make the library launch on a caller-owned stream (a cudaStream_t passed as void*), or back on
- * its own stream with NULL.  Lets a PyTorch or CUDA-graph caller order the kernels itself. */
+ * its own non-blocking stream with NULL.  The legacy default stream is cudaStreamLegacy
+ * ((void*)1), not NULL.  Lets a PyTorch or CUDA-graph caller order the kernels itself. */
 int envg_set_stream(void* stream);
 
 /* Wait for all work queued by this thread's calls. */

@@ -216,6 +216,45 @@ int tmap_nhwc(CUtensorMap* tm, const void* base, int Cp, int W, int H, int B, in
   return ENVG_OK;
 }
 
+// fp32 output maps for the TMA-store epilogue: 32 x 32 boxes, 128-byte swizzle.
+int tmap_out_2d(CUtensorMap* tm, const float* base, uint64_t cols, uint64_t rows, uint64_t ld) {
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ENVG_ERR_CUDA, "cuTensorMapEncodeTiled(out 2D) failed: %d", (int)r);
+  return ENVG_OK;
+}
+int tmap_out_3d(CUtensorMap* tm, const float* base, uint64_t plane, uint64_t ch, uint64_t nb) {
+  cuuint64_t dims[3] = {plane, ch, nb};
+  cuuint64_t strides[2] = {plane * 4, ch * plane * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ENVG_ERR_CUDA, "cuTensorMapEncodeTiled(out 3D) failed: %d", (int)r);
+  return ENVG_OK;
+}
+
+// Picks the k1_gemm store path for a row-major Y and builds its map.
+int choose_store(EpiArgs& e, CUtensorMap* tmY) {
+  e.store_mode = STORE_DIRECT;
+  const bool aligned = (reinterpret_cast<uintptr_t>(e.Y) & 15) == 0 && e.ldy % 4 == 0;
+  if (!aligned) return ENVG_OK;
+  int mode = STORE_TMA;
+  if (e.mode == EPI_GATED_RES) mode = STORE_TMA_ADD;
+  else if (e.mode == EPI_ALPHA_BETA) mode = e.beta == 0.0f ? STORE_TMA : (e.beta == 1.0f ? STORE_TMA_ADD : STORE_DIRECT);
+  if (mode == STORE_DIRECT) return ENVG_OK;
+  int rc = tmap_out_2d(tmY, e.Y, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy);
+  if (rc != ENVG_OK) return rc;
+  e.store_mode = mode;
+  return ENVG_OK;
+}
+
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t rup(int64_t a, int64_t b) { return cdiv(a, b) * b; }
 
@@ -297,7 +336,8 @@ int sync_and_check(Dev* d) {
 // ---- kernel launchers ----------------------------------------------------------------------
 
 template <bool CONV_B, bool SILU_GATE>
-int launch_k1(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, GemmArgs& a, double flops, double bytes) {
+int launch_k1(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tY, GemmArgs& a, double flops,
+              double bytes) {
   using L = K1Smem<K1_BN, K1_STAGES>;
   auto kern = k1_gemm<K1_BN, K1_STAGES, CONV_B, SILU_GATE>;
   static bool attr = false;
@@ -310,7 +350,7 @@ int launch_k1(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, GemmArgs& a,
   const int grid = (int)std::min<int64_t>(a.num_tiles, d->sms);
   if (grid <= 0) return ENVG_OK;
   ProfScope ps(stream_of(d), CONV_B ? KID_K1_CONV : (SILU_GATE ? KID_K1_SILU_GATE : KID_K1), flops, bytes);
-  kern<<<grid, K1_THREADS, L::TOTAL, stream_of(d)>>>(tA, tB, a);
+  kern<<<grid, K1_THREADS, L::TOTAL, stream_of(d)>>>(tA, tB, tY, a);
   ENVG_CUDA(cudaGetLastError());
   d->st.kernel_launches++;
   return ENVG_OK;
@@ -415,9 +455,12 @@ int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap&
   g.tiles_n = (int)cdiv(rows_b, K1_BN);
   g.num_tiles = g.tiles_m * g.tiles_n;
   g.group_m = 8;
+  CUtensorMap tY;
+  memset(&tY, 0, sizeof(tY));
+  ENVG_TRY(choose_store(e, &tY));
   g.epi = e;
-  if (silu_gate) return launch_k1<false, true>(d, tA, b256, g, flops, bytes);
-  return launch_k1<false, false>(d, tA, b256, g, flops, bytes);
+  if (silu_gate) return launch_k1<false, true>(d, tA, b256, tY, g, flops, bytes);
+  return launch_k1<false, false>(d, tA, b256, tY, g, flops, bytes);
 }
 
 int upload_common(Dev* d, WSrc src, int64_t N, int64_t K, int64_t n0, int64_t n1, int layout, envg_weight* out) {
@@ -834,11 +877,18 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
     e.ldy = plane;
     e.n_out = (int)plane;
     e.vec_ok = ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 4 == 0) ? 1 : 0;
+    CUtensorMap tY;
+    memset(&tY, 0, sizeof(tY));
+    e.store_mode = STORE_DIRECT;
+    if ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 32 == 0) {
+      ENVG_TRY(tmap_out_3d(&tY, dy, (uint64_t)plane, (uint64_t)out_ch, (uint64_t)batch));
+      e.store_mode = STORE_TMA;
+    }
     g.epi = e;
     const double cflops = 2.0 * out_ch * (double)plane * batch * (double)W->K;
     const double cbytes = 2.0 * (double)batch * H * W_ * Cp + 2.0 * out_ch * (double)W->Kp + 4.0 * (double)out_elems +
                           (dbias ? 4.0 * out_ch : 0.0);
-    ENVG_TRY(launch_k1<true, false>(d, W->tm128, tB, g, cflops, cbytes));
+    ENVG_TRY(launch_k1<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
   } else {
     // Strided convolution: explicit bf16 im2col, then one GEMM per image.
     const int64_t colK = W->Kp;
@@ -866,8 +916,11 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
       eb.ldy = plane;
       eb.n_out = (int)plane;
       eb.vec_ok = ((reinterpret_cast<uintptr_t>(eb.Y) & 15) == 0 && plane % 4 == 0) ? 1 : 0;
+      CUtensorMap tY;
+      memset(&tY, 0, sizeof(tY));
+      ENVG_TRY(choose_store(eb, &tY));
       g.epi = eb;
-      ENVG_TRY(launch_k1<false, false>(d, tA, tB, g, 2.0 * out_ch * (double)plane * (double)W->K,
+      ENVG_TRY(launch_k1<false, false>(d, tA, tB, tY, g, 2.0 * out_ch * (double)plane * (double)W->K,
                                        2.0 * (double)plane * colK + 2.0 * out_ch * (double)colK + 4.0 * out_ch * (double)plane));
     }
   }

@@ -45,7 +45,13 @@ struct EpiArgs {
   int m_valid;        // valid output rows
   int half_n;         // EPI_SILU_GATE: gate rows of the original W (up bias at half_n + col)
   int vec_ok;         // Y 16-byte aligned and ldy % 4 == 0
+  int store_mode;     // k1_gemm: STORE_DIRECT, STORE_TMA or STORE_TMA_ADD
 };
+
+// How k1_gemm writes Y: per-thread global stores, or 32x32 tiles staged in shared memory and
+// written by a TMA bulk store (coalesced; clipped at the tensor edges), or added into Y by a TMA
+// bulk reduce (Y += tile: the gated residual and alpha*AB + 1*C).
+enum StoreMode : int { STORE_DIRECT = 0, STORE_TMA = 1, STORE_TMA_ADD = 2 };
 
 struct ConvGeom {
   int tileW, tileH;   // pixel tile, tileW * tileH == BN
@@ -90,6 +96,26 @@ ENVG_DEV float epi_value(const EpiArgs& e, float acc, int row, int col, const fl
     v = (e.beta == 0.0f) ? __fmul_rn(e.alpha, v) : __fadd_rn(__fmul_rn(e.alpha, v), __fmul_rn(e.beta, *yp));
   }
   return v;
+}
+
+// Value handed to a TMA store / reduce: everything but the read of Y.
+ENVG_DEV float epi_pre(const EpiArgs& e, float acc, int row, int col) {
+  float v = acc;
+  const bool cok = col < e.n_out, rok = row < e.m_valid;
+  if (e.bias_mode == 1) v = __fadd_rn(v, cok ? __ldg(e.bias + col) : 0.0f);
+  else if (e.bias_mode == 2) v = __fadd_rn(v, rok ? __ldg(e.bias + row) : 0.0f);
+  if (e.act) v = silu_f(v);
+  if (e.mode == EPI_GATED_RES) v = __fmul_rn(cok ? __ldg(e.gate + col) : 0.0f, v);
+  else if (e.mode == EPI_ALPHA_BETA) v = __fmul_rn(e.alpha, v);
+  return v;
+}
+
+// Write row `lane` of a 32 x 32 fp32 tile into a 128-byte-swizzled staging buffer (16-byte chunk
+// j of row r lands at chunk j ^ (r % 8), the layout the TMA store reads).
+ENVG_DEV void stage_row32(uint8_t* buf, int lane, const float (&v)[32]) {
+  float4* rowp = reinterpret_cast<float4*>(buf + lane * 128);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) rowp[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 }
 
 // Store 32 consecutive output columns [col0, col0+32) of one row.
@@ -167,8 +193,9 @@ template <int BN, int STAGES>
 struct K1Smem {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = TILE_A_BYTES + B_BYTES;
+  static constexpr int STAGING_BYTES = 4 * 2 * 32 * 128;  // 4 epilogue warps x 2 buffers x 32x32 fp32
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
-  static constexpr int TOTAL = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int TOTAL = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
   static constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
 };
 
@@ -177,7 +204,8 @@ struct K1Smem {
 // ------------------------------------------------------------------------------------------
 template <int BN, int STAGES, bool CONV_B, bool SILU_GATE>
 __global__ void __launch_bounds__(K1_THREADS, 1)
-    k1_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+    k1_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmY, const GemmArgs args) {
   using L = K1Smem<BN, STAGES>;
   constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
@@ -187,7 +215,8 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * TILE_A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * L::B_BYTES);
+  uint8_t* sStage = sB + STAGES * L::B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + L::STAGING_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -215,6 +244,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (args.epi.store_mode != STORE_DIRECT) tma_prefetch_desc(&tmY);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), L::TMEM_COLS);
@@ -322,6 +352,9 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
   } else {
     // ---------------- epilogue: 4 warps, one TMEM lane quadrant each ----------------
     const int q = warp & 3;
+    const int smode = args.epi.store_mode;
+    uint8_t* stg = sStage + (warp - 2) * 8192;  // this warp's two 4 KB staging tiles
+    int sb = 0;
     int acc = 0;
     uint32_t aph = 0;
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
@@ -341,15 +374,18 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
       if (!wait_bounded_warp(tfull0 + 8 * acc, aph, wc, 4)) break;
       tc_fence_after();
       const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      const int row = m_blk * BM + q * 32 + lane;
-      if (SILU_GATE) {
+      const int row0 = m_blk * BM + q * 32;
+      const int row = row0 + lane;
+      constexpr int NCHUNK = SILU_GATE ? BN / 64 : BN / 32;
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+      for (int c = 0; c < NCHUNK; ++c) {
+        float v[32];
+        int col0;
+        if (SILU_GATE) {
           uint32_t g[32], u[32];
           tmem_ld32(trow + c * 32, g);
           tmem_ld32(trow + BN / 2 + c * 32, u);
-          float v[32];
-          const int col0 = n_blk * (BN / 2) + c * 32;
+          col0 = n_blk * (BN / 2) + c * 32;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float gv = __uint_as_float(g[j]);
@@ -361,24 +397,57 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
             }
             v[j] = __fmul_rn(silu_f(gv), uv);
           }
-          EpiArgs e2 = args.epi;
-          e2.bias_mode = 0;
-          e2.act = 0;
-          epi_store_row32(e2, row, col0, v);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        } else {
           uint32_t r[32];
           tmem_ld32(trow + c * 32, r);
-          float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if (CONV_B)
-            epi_store_conv32(args.epi, args.conv, b, row, h0, w0, c * 32, v);
-          else
-            epi_store_row32(args.epi, row, n_blk * BN + c * 32, v);
+          col0 = n_blk * BN + c * 32;
         }
+        if (smode == STORE_DIRECT) {
+          if (SILU_GATE) {
+            EpiArgs e2 = args.epi;
+            e2.bias_mode = 0;
+            e2.act = 0;
+            epi_store_row32(e2, row, col0, v);
+          } else if (CONV_B) {
+            epi_store_conv32(args.epi, args.conv, b, row, h0, w0, c * 32, v);
+          } else {
+            epi_store_row32(args.epi, row, col0, v);
+          }
+          continue;
+        }
+        // ---- TMA store path ----
+        int x = col0, y = row0;
+        if (CONV_B) {
+          const int jj = c * 32;
+          const int w = w0 + jj % args.conv.tileW;
+          const int h = h0 + jj / args.conv.tileW;
+          if (w >= args.conv.outW) continue;  // tile overhang past the image row (uniform per warp)
+          x = h * args.conv.outW + w;          // h >= outH lands past the plane and is clipped
+          const float bv = (args.epi.bias_mode == 2 && row < args.epi.m_valid) ? __ldg(args.epi.bias + row) : 0.0f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float t = __fadd_rn(v[j], bv);
+            v[j] = args.epi.act ? silu_f(t) : t;
+          }
+        } else if (!SILU_GATE) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = epi_pre(args.epi, v[j], row, col0 + j);
+        }
+        uint8_t* buf = stg + sb * 4096;
+        if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
+        __syncwarp();
+        stage_row32(buf, lane, v);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (CONV_B) tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+          else if (smode == STORE_TMA_ADD) tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
+          else tma_store_2d(&tmY, smem_u32(buf), x, y);
+          bulk_commit();
+        }
+        sb ^= 1;
       }
       tc_fence_before();
       __syncwarp();
@@ -386,6 +455,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
       acc ^= 1;
       if (acc == 0) aph ^= 1;
     }
+    if (lane == 0) bulk_wait_all();
   }
   __syncwarp();
   tc_fence_before();

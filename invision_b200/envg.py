@@ -28,12 +28,18 @@ LAYOUT_PLAIN, LAYOUT_GATE_UP = 0, 1
 EPI_NONE, EPI_BIAS, EPI_SILU_GATE, EPI_GATED_RESIDUAL, EPI_SILU = 0, 1, 2, 3, 4
 HOST_PTRS, DEVICE_PTRS, ASYNC = 0, 1, 2
 ROW_MAJOR, NO_TRANS, TRANS = 101, 111, 112
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
 
 
 class EnvgError(RuntimeError):
     def __init__(self, code, msg):
         super().__init__(f"envgemm error {code}: {msg}")
         self.code = code
+
+
+class KernelStat(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("launches", ctypes.c_uint64), ("ms", ctypes.c_double),
+                ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
 
 
 class Stats(ctypes.Structure):
@@ -70,6 +76,8 @@ def lib():
         L.envg_get_stats.argtypes = [ctypes.POINTER(Stats)]
         L.envg_set_wait_cap_ns.argtypes = [ctypes.c_uint64]
         L.envg_selftest_wait_timeout.argtypes = [ctypes.c_uint64]
+        L.envg_profile.argtypes = [_ci]
+        L.envg_profile_read.argtypes = [ctypes.POINTER(KernelStat), _ci, ctypes.POINTER(_ci)]
         _lib = L
     return _lib
 
@@ -114,6 +122,26 @@ def stats():
     return {f: getattr(s, f) for f, _ in Stats._fields_}
 
 
+def profile(enable):
+    """Start (resetting the counters) or stop per-launch CUDA-event timing inside the library."""
+    return _check(lib().envg_profile(1 if enable else 0))
+
+
+def profile_read():
+    """{kernel family: {launches, ms, flops, bytes}} accumulated since profile(True)."""
+    arr = (KernelStat * 16)()
+    n = _ci(0)
+    _check(lib().envg_profile_read(arr, 16, ctypes.byref(n)))
+    return {arr[i].name.decode(): {"launches": arr[i].launches, "ms": arr[i].ms, "flops": arr[i].flops,
+                                   "bytes": arr[i].bytes} for i in range(n.value)}
+
+
+def set_stream(stream_handle):
+    """Launch on a caller stream (an int cudaStream_t, e.g. torch.cuda.Stream().cuda_stream) or,
+    with None, on the library's own stream."""
+    return _check(lib().envg_set_stream(_vp(stream_handle) if stream_handle is not None else None))
+
+
 def set_wait_cap_ns(ns):
     return _check(lib().envg_set_wait_cap_ns(int(ns)))
 
@@ -141,6 +169,16 @@ def _host_f32(a, name):
     return a
 
 
+_follow_torch_stream = True
+
+
+def follow_torch_stream(on):
+    """Device-pointer calls launch on torch's current stream (default) or on whatever stream
+    set_stream() selected (on=False)."""
+    global _follow_torch_stream
+    _follow_torch_stream = bool(on)
+
+
 def _mode(*arrays):
     """HOST_PTRS for numpy operands, DEVICE_PTRS for torch CUDA tensors (never mixed)."""
     kinds = {(_is_torch(a)) for a in arrays if a is not None}
@@ -154,7 +192,11 @@ def _mode(*arrays):
                 continue
             if not (a.is_cuda and a.dtype == torch.float32 and a.is_contiguous()):
                 raise TypeError("device operands must be contiguous float32 CUDA tensors")
-        lib().envg_set_stream(_vp(torch.cuda.current_stream().cuda_stream))
+        if _follow_torch_stream:
+            h = torch.cuda.current_stream().cuda_stream
+            # torch's default stream has handle 0, which the C ABI reads as "the library's own
+            # stream"; name it as cudaStreamLegacy (0x1) so both order on the same stream.
+            lib().envg_set_stream(_vp(h if h else CUDA_STREAM_LEGACY))
         return DEVICE_PTRS
     for a in arrays:
         if a is not None:

@@ -87,7 +87,7 @@ def test_silu_gate_vs_oracle(gpu, M, K, H):
     assert_parity(y, ref, TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT, what=f"silu-gate {M}x{K}x{H}")
 
 
-@pytest.mark.parametrize("M,K,N", [(512, 1024, 768), (8, 3072, 3072), (200, 256, 100)])
+@pytest.mark.parametrize("M,K,N", [(512, 1024, 768), (8, 3072, 3072), (200, 256, 100), (150, 128, 101)])
 def test_gated_residual_vs_oracle(gpu, M, K, N):
     x, w, b = inputs(M, K, N, seed=N + 5)
     rng = np.random.default_rng(N)
@@ -110,6 +110,9 @@ CONV_CASES = [
     (1, 64, 8, 300, 64, 3, 1, 1),     # width above one 256-pixel tile
     (1, 96, 16, 16, 200, 1, 1, 0),    # 1x1 (conv_shortcut shape)
     (1, 32, 17, 19, 48, 3, 2, 1),     # strided: explicit im2col path
+    (1, 64, 12, 96, 128, 3, 1, 1),    # TMA-store epilogue with a skipped overhang chunk
+    (2, 64, 6, 64, 64, 3, 1, 1),      # two images, 4 rows per pixel tile
+    (1, 64, 3, 256, 160, 3, 1, 1),    # one row per pixel tile, out_ch past one 128 block
 ]
 
 
@@ -139,7 +142,7 @@ def test_sgemm_vs_oracle(gpu, ta, tb, M, N, K):
     B = rng.standard_normal((N, K) if tb == 112 else (K, N), dtype=np.float32)
     C0 = rng.standard_normal((M, N), dtype=np.float32)
     lda, ldb = A.shape[1], B.shape[1]
-    for alpha, beta in ((1.0, 0.0), (0.5, 2.0)):
+    for alpha, beta in ((1.0, 0.0), (0.5, 2.0), (1.5, 1.0)):
         C = C0.copy()
         gpu.sgemm(101, ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, N)
         ref = C0.copy()
