@@ -125,6 +125,29 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
                 int out_ch, int H, int W_, int kH, int kW, int stride, int pad, int batch,
                 int epilogue, int flags);
 
+/* Allocation-free linear for skinny M.  This entry point has no counterpart in the reference.
+ *
+ * envg_linear grows a device workspace on demand (cudaMalloc, and cudaFree of the smaller
+ * buffer, which waits for all work on the device).  Some callers cannot allow that: a host
+ * application whose own allocator has reserved the device memory and forbids other libraries to
+ * allocate, or a caller that shares the GPU with streams it must not stall mid-step.  This
+ * variant allocates nothing.  Its scratch (the bf16 copy of x, the split-K partial sums and
+ * their counters) is one file-scope __device__ array of ENVG_NOALLOC_SCRATCH_BYTES (4 MiB), which
+ * every GPU that loads the library holds until the process exits.
+ *
+ *  - Same arguments and epilogues as envg_linear, but x, dst, bias and gate must be device
+ *    pointers: flags must contain ENVG_DEVICE_PTRS (ENVG_ASYNC optional).
+ *  - Limits: 1 <= M <= 64 and M * Kp * 2 <= 2 MiB (Kp = K rounded up to 8), i.e. K <= 16384
+ *    at M = 64; larger requests return ENVG_ERR_ARG with the limit in envg_last_error().
+ *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *    with that device current; make that first call before any stream capture.
+ *  - Every call shares the one array, which keeps the last call's contents; the counters are
+ *    cleared on every call.  Calls whose kernels overlap on the GPU (different streams without
+ *    ordering) race on the array and must be serialised by the caller. */
+#define ENVG_NOALLOC_SCRATCH_BYTES (4u << 20)
+int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* bias, int64_t M,
+                        int64_t K, int64_t N, int epilogue, const float* gate, int flags);
+
 /* cblas_sgemm-compatible fp32 GEMM on host pointers: the signature of the function-pointer
  * slot TQNNSingleOPS.cblas_sgemm (quicknncpu.pas:102-109; enums quicknn_common.pas:54-58:
  * RowMajor = 101, NoTrans = 111, Trans = 112).  Re-pointing that slot to this entry moves

@@ -531,6 +531,28 @@ const char* epi_name(int e) {
 
 }  // namespace
 
+// ---- scratch of envg_linear_noalloc ----------------------------------------------------------
+// Layout: [0, 2 MiB) bf16 activations [M, Kp]; then split-K partial sums; the last 64 KiB hold
+// the per-tile split-K counters.  Host code must not take this symbol's address directly (it
+// names a host-side stand-in); noalloc_scratch() asks the runtime for the device address.
+constexpr size_t NOALLOC_XB_BYTES = 2u << 20;
+constexpr size_t NOALLOC_CNT_BYTES = 64u << 10;
+constexpr size_t NOALLOC_PART_BYTES = ENVG_NOALLOC_SCRATCH_BYTES - NOALLOC_XB_BYTES - NOALLOC_CNT_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ENVG_NOALLOC_SCRATCH_BYTES];
+void* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch array on the current device (looked up once per device).
+int noalloc_scratch(Dev* d, uint8_t** out) {
+  if (!g_noalloc_ptr[d->id]) {
+    void* p = nullptr;
+    ENVG_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    if (!p) return fail(ENVG_ERR_CUDA, "cudaGetSymbolAddress returned NULL for the no-alloc scratch");
+    g_noalloc_ptr[d->id] = p;
+  }
+  *out = reinterpret_cast<uint8_t*>(g_noalloc_ptr[d->id]);
+  return ENVG_OK;
+}
+
 // =============================================================================================
 // C ABI
 // =============================================================================================
@@ -791,6 +813,87 @@ int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, in
     d->st.d2h_bytes += (double)(M * n_out) * 4;
     return sync_and_check(d);
   }
+  if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
+  return ENVG_OK;
+}
+
+int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,
+                        int epilogue, const float* gate, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  ENVG_TRY(check_weight(d, W));
+  if (W->conv) return fail(ENVG_ERR_ARG, "envg_linear_noalloc: handle holds a convolution weight");
+  if (!(flags & ENVG_DEVICE_PTRS))
+    return fail(ENVG_ERR_ARG, "envg_linear_noalloc: needs device pointers (ENVG_DEVICE_PTRS); it stages nothing");
+  if (K != W->K || N != W->N)
+    return fail(ENVG_ERR_ARG, "envg_linear_noalloc: [K=%lld, N=%lld] does not match the weight [N=%lld, K=%lld]",
+                (long long)K, (long long)N, (long long)W->N, (long long)W->K);
+  const bool gu = W->layout == ENVG_LAYOUT_GATE_UP;
+  if ((epilogue == ENVG_EPI_SILU_GATE) != gu)
+    return fail(ENVG_ERR_ARG, "envg_linear_noalloc: SILU_GATE goes with (and only with) a GATE_UP weight");
+  if (epilogue != ENVG_EPI_NONE && epilogue != ENVG_EPI_BIAS && epilogue != ENVG_EPI_SILU_GATE &&
+      epilogue != ENVG_EPI_GATED_RESIDUAL)
+    return fail(ENVG_ERR_ARG, "envg_linear_noalloc: epilogue %d not valid for a linear", epilogue);
+  if (epilogue == ENVG_EPI_BIAS && !bias) return fail(ENVG_ERR_ARG, "envg_linear_noalloc: BIAS epilogue without bias");
+  if (epilogue == ENVG_EPI_GATED_RESIDUAL && !gate)
+    return fail(ENVG_ERR_ARG, "envg_linear_noalloc: GATED_RESIDUAL epilogue without gate");
+  if (M < 0 || M > SKINNY_MAX)
+    return fail(ENVG_ERR_ARG, "envg_linear_noalloc: M=%lld outside [0, %d] (the allocation-free path is skinny-M only)",
+                (long long)M, SKINNY_MAX);
+  if ((size_t)M * (size_t)W->Kp * 2 > NOALLOC_XB_BYTES)
+    return fail(ENVG_ERR_ARG, "envg_linear_noalloc: M*Kp*2 = %lld bytes exceeds the %zu-byte activation scratch",
+                (long long)(M * W->Kp * 2), NOALLOC_XB_BYTES);
+  const int R = gu ? 2 : 1;
+  const int64_t n_tiles = cdiv(W->rows, (int64_t)R * BM);
+  if ((size_t)n_tiles * sizeof(int) > NOALLOC_CNT_BYTES)
+    return fail(ENVG_ERR_ARG, "envg_linear_noalloc: %lld row tiles exceed the %zu-entry counter scratch",
+                (long long)n_tiles, NOALLOC_CNT_BYTES / sizeof(int));
+  if (M == 0) return ENVG_OK;
+  if (!dst || !x) return fail(ENVG_ERR_ARG, "envg_linear_noalloc: dst or x is NULL");
+  uint8_t* scratch = nullptr;
+  ENVG_TRY(noalloc_scratch(d, &scratch));
+  uint8_t* xb = scratch;
+  float* part = reinterpret_cast<float*>(scratch + NOALLOC_XB_BYTES);
+  int* cnt = reinterpret_cast<int*>(scratch + NOALLOC_XB_BYTES + NOALLOC_PART_BYTES);
+  cudaStream_t s = stream_of(d);
+  const int64_t n_out = gu ? N / 2 : N;
+
+  ENVG_TRY(launch_cast_rows(d, x, K, M, K, W->Kp, xb));
+  const int mpad = (int)rup(M, 16);
+  const int64_t num_kb = cdiv(W->Kp, BK);
+  SkinnyArgs a{};
+  a.n_tiles = (int)n_tiles;
+  a.num_kb = (int)num_kb;
+  int splits = std::max<int64_t>(1, (2 * d->sms) / n_tiles);
+  splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 2));
+  const size_t part_per_split = (size_t)n_tiles * R * BM * mpad * sizeof(float);
+  splits = (int)std::max<size_t>(1, std::min<size_t>((size_t)splits, NOALLOC_PART_BYTES / part_per_split));
+  a.kb_per_split = (int)cdiv(num_kb, splits);
+  a.splits = (int)cdiv(num_kb, a.kb_per_split);
+  if (a.splits > 1) {
+    ENVG_CUDA(cudaMemsetAsync(cnt, 0, (size_t)n_tiles * sizeof(int), s));  // counters start at zero
+    a.partial = part;
+    a.counters = cnt;
+  }
+  EpiArgs e{};
+  e.Y = dst;
+  e.ldy = n_out;
+  e.bias = bias;
+  e.bias_mode = bias ? 1 : 0;
+  e.mode = (epilogue == ENVG_EPI_GATED_RESIDUAL) ? EPI_GATED_RES : EPI_PLAIN;
+  e.gate = gate;
+  e.alpha = 1.0f;
+  e.n_out = (int)n_out;
+  e.m_valid = (int)M;
+  e.half_n = (int)(gu ? W->half : 0);
+  a.epi = e;
+  CUtensorMap tX;
+  ENVG_TRY(tmap_2d(&tX, xb, W->Kp, M, mpad));
+  ENVG_TRY(launch_k2(d, mpad, R, W->tm128, tX, a, 2.0 * (double)M * N * K,
+                     2.0 * (double)N * K + 2.0 * (double)M * W->Kp + 4.0 * (double)M * n_out));
+  d->st.calls++;
+  d->st.flops += 2.0 * (double)M * (double)N * (double)K;
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
 }

@@ -69,6 +69,7 @@ def lib():
         L.envg_conv_weight_upload.argtypes = [_vp, _vp, _ci, _ci, _ci, _ci, ctypes.POINTER(_vp)]
         L.envg_weight_free.argtypes = [_vp]
         L.envg_linear.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
+        L.envg_linear_noalloc.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_conv2d.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 11
         L.envg_sgemm.argtypes = [_ci, _ci, _ci, _i64, _i64, _i64, ctypes.c_float, _vp, _i64, _vp, _i64,
                                  ctypes.c_float, _vp, _i64]

@@ -1,0 +1,93 @@
+"""GPU: envg_linear_noalloc, the allocation-free skinny-M linear, against envg_linear.
+
+Some callers cannot let the library allocate device memory: a host whose own allocator has
+reserved the GPU's memory and forbids other libraries to allocate, or a caller sharing the GPU
+with streams that must not be stalled by the device-wide wait of cudaFree.  envg_linear_noalloc
+serves them from one fixed __device__ scratch array.  This file is collected last on purpose, so
+a run that stops at its first failure has already run every other test; it also passes alone in
+a fresh process.
+"""
+import numpy as np
+import pytest
+
+from tests.common import TOL_MAX, TOL_MEAN, assert_parity, inputs
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # (M, K, N, epilogue)
+    (1, 3072, 18432, "bias"),     # adaLN modulation shape
+    (16, 2560, 4096, "bias"),     # Qwen3 q at M = 16
+    (64, 4096, 1024, "none"),     # largest M, split-K
+    (7, 512, 2 * 384, "silu_gate"),
+]
+
+
+def _call_noalloc(envg, y, x, W, bias, epi):
+    L = envg.lib()
+    return L.envg_linear_noalloc(y.data_ptr(), x.data_ptr(), W.h, bias.data_ptr() if bias is not None else None,
+                                 x.shape[0], x.shape[1], W.N, epi, None, envg.DEVICE_PTRS)
+
+
+@pytest.mark.parametrize("M,K,N,kind", CASES)
+def test_noalloc_matches_envg_linear_twice(gpu, M, K, N, kind):
+    import torch
+
+    envg = gpu
+    x, w, b = inputs(M, K, N, seed=77 + M + K)
+    silu = kind == "silu_gate"
+    W = envg.Weight(w, layout=envg.LAYOUT_GATE_UP if silu else envg.LAYOUT_PLAIN)
+    epi = envg.EPI_SILU_GATE if silu else (envg.EPI_BIAS if kind == "bias" else envg.EPI_NONE)
+    bias = torch.from_numpy(b).cuda() if kind == "bias" else None
+    xt = torch.from_numpy(x).cuda()
+    n_out = N // 2 if silu else N
+    y_ref = torch.empty(M, n_out, device="cuda")
+    envg.linear(y_ref, xt, W, bias=bias, epilogue=epi)  # the existing entry point
+    torch.cuda.synchronize()
+    ref = y_ref.cpu().numpy()
+
+    ys = [torch.full((M, n_out), float("nan"), device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    ws_before = envg.stats()["workspace_bytes"]
+    free_before = torch.cuda.mem_get_info()[0]
+    outs = []
+    for y in ys:  # two calls in a row share (and reuse) the scratch array
+        rc = _call_noalloc(envg, y, xt, W, bias, epi)
+        assert rc == envg.OK, envg.last_error()
+        torch.cuda.synchronize()
+        outs.append(y.cpu().numpy())
+    assert envg.stats()["workspace_bytes"] == ws_before, "the library workspace grew"
+    assert torch.cuda.mem_get_info()[0] == free_before, "device memory was allocated"
+    for o in outs:
+        assert_parity(o, ref, TOL_MAX, TOL_MEAN, what=f"noalloc {M}x{K}x{N} {kind}")
+    W.free()
+
+
+def test_noalloc_rejects_what_it_cannot_hold(gpu):
+    import torch
+
+    envg = gpu
+    L = envg.lib()
+    x, w, _ = inputs(65, 256, 128, seed=5, bias=False)
+    W = envg.Weight(w)
+    xt = torch.from_numpy(x).cuda()
+    y = torch.empty(65, 128, device="cuda")
+    rc = L.envg_linear_noalloc(y.data_ptr(), xt.data_ptr(), W.h, None, 65, 256, 128, envg.EPI_NONE, None,
+                               envg.DEVICE_PTRS)
+    assert rc == envg.ERR_ARG and "M=65" in envg.last_error()
+    # host pointers are refused: the entry point stages nothing
+    xn = np.zeros((4, 256), np.float32)
+    yn = np.zeros((4, 128), np.float32)
+    rc = L.envg_linear_noalloc(yn.ctypes.data, xn.ctypes.data, W.h, None, 4, 256, 128, envg.EPI_NONE, None,
+                               envg.HOST_PTRS)
+    assert rc == envg.ERR_ARG and "device pointers" in envg.last_error()
+    # activation scratch limit: M * Kp * 2 bytes <= 2 MiB
+    x2, w2, _ = inputs(64, 16392, 128, seed=6, bias=False)
+    W2 = envg.Weight(w2)
+    xt2 = torch.from_numpy(x2).cuda()
+    y2 = torch.empty(64, 128, device="cuda")
+    rc = L.envg_linear_noalloc(y2.data_ptr(), xt2.data_ptr(), W2.h, None, 64, 16392, 128, envg.EPI_NONE, None,
+                               envg.DEVICE_PTRS)
+    assert rc == envg.ERR_ARG and "scratch" in envg.last_error()
+    W.free()
+    W2.free()
