@@ -1,8 +1,8 @@
 """Benchmark of the Envision dense-linear hot path on B200 (one JSON line on rank 0).
 
-Workload (the configuration the headline metric is quoted on): the linears of
-one FLUX2-Klein-4B-shaped double-stream block at 1024x1024, M = 4096 image + 512 text tokens =
-4608, hidden 3072:
+Default workload (the configuration the headline metric is quoted on): the
+linears of one FLUX2-Klein-4B-shaped double-stream block at 1024x1024, M = 4096 image + 512
+text tokens = 4608, hidden 3072:
 
     qkv      [4608, 3072] -> 9216   + bias
     out      [4608, 3072] -> 3072   + bias
@@ -13,11 +13,13 @@ one FLUX2-Klein-4B-shaped double-stream block at 1024x1024, M = 4096 image + 512
 X ~ N(0,1) fp32, W = bf16(0.02 N(0,1)), b = 0.01 N(0,1) fp32, all synthetic and seeded (no model
 weights exist in this environment).  One step = the five linears.  The working set (weights
 358 MB + activations) exceeds the 126 MB L2, so no flush is needed between steps.
+`--config c1|c3|c3_m16|c3_m1|c4|c5` runs the other BASELINE shapes (per-config figures; the
+headline stays config 2).
 
 Arms:
   (default)          libenvgemm through its C ABI.  `value` = device-resident throughput
                      (TFLOP/s, whole job); `e2e` = the same through host buffers (pinned), every
-                     step copying its inputs H2D and its outputs D2H.  With N > 1 GPUs the weights
+                     call copying its inputs H2D and its output D2H.  With N > 1 GPUs the weights
                      are N-split by output column and every output is all-gathered over NCCL
                      (strong scaling; the gather is part of the timed step).
   --impl reference   the reference's own CPU GEMM (src/sgemm2.cpp compiled from the reference
@@ -39,25 +41,68 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-M_TOK = 4096 + 512
-HID = 3072
-MLP = 9216
-LINEARS = [
-    # name, M, K, N (weight rows), kind
-    ("qkv", M_TOK, HID, 3 * HID, "bias"),
-    ("out", M_TOK, HID, HID, "bias"),
-    ("gate_up", M_TOK, HID, 2 * MLP, "silu_gate"),
-    ("down", M_TOK, MLP, HID, "bias"),
-    ("adaln", 1, HID, 6 * HID, "bias"),
-]
-FLOPS_PER_STEP = float(sum(2 * M * K * N for _, M, K, N, _ in LINEARS))
-WORKLOAD = ("BASELINE config 2: FLUX2-Klein-4B double-stream block linears, M=4608 (4096 img + 512 txt), "
-            "hidden 3072: qkv 3072->9216, out 3072->3072, gate_up 3072->18432 (SiLU-gate), down 9216->3072, "
-            "adaLN 3072->18432 at M=1; all with fp32 bias")
 METRIC = "block_linear_tflops"
 UNIT = "TFLOP/s"
-# DRAM bytes per k1_gemm launch of this workload, from one ncu capture (profiles/k1_gemm_config2.md);
-# None until a capture of the current kernel exists.
+
+
+def lin(name, M, K, N, epi="bias", x_from=None):
+    return dict(name=name, op="linear", M=M, K=K, N=N, epi=epi, x_from=x_from)
+
+
+def conv(name, B, C, H, W, O, k, stride, pad, epi="silu"):
+    return dict(name=name, op="conv", B=B, C=C, H=H, W=W, O=O, k=k, stride=stride, pad=pad, epi=epi)
+
+
+def qwen(M):
+    return [lin("q", M, 2560, 4096, "none"), lin("k", M, 2560, 1024, "none"), lin("v", M, 2560, 1024, "none"),
+            lin("o", M, 4096, 2560, "none"), lin("gate_up", M, 2560, 2 * 9728, "silu_gate_nobias"),
+            lin("down", M, 9728, 2560, "none", x_from="gate_up")]
+
+
+M_TOK = 4096 + 512
+WORKLOADS = {
+    "c2": ("BASELINE config 2: FLUX2-Klein-4B double-stream block linears, M=4608 (4096 img + 512 txt), hidden "
+           "3072: qkv 3072->9216, out 3072->3072, gate_up 3072->18432 (SiLU-gate), down 9216->3072, adaLN "
+           "3072->18432 at M=1; all with fp32 bias",
+           [lin("qkv", M_TOK, 3072, 9216), lin("out", M_TOK, 3072, 3072),
+            lin("gate_up", M_TOK, 3072, 18432, "silu_gate"), lin("down", M_TOK, 9216, 3072, x_from="gate_up"),
+            lin("adaln", 1, 3072, 18432)]),
+    "c1": ("BASELINE config 1: FLUX2-Klein-4B QKV linear Y[1024,9216] = X[1024,3072].W^T + b",
+           [lin("qkv", 1024, 3072, 9216)]),
+    "c3": ("BASELINE config 3: Qwen3-4B layer linears at M=512 (no bias)", qwen(512)),
+    "c3_m16": ("BASELINE config 3 at M=16 (skinny)", qwen(16)),
+    "c3_m1": ("BASELINE config 3 at M=1 (skinny)", qwen(1)),
+    "c4": ("BASELINE config 4: FLUX2-Klein-9B single-stream fused input linear M=18432, K=4096, N=36864, then "
+           "the output linear K=16384, N=4096 (no bias)",
+           [lin("fused_in", 18432, 4096, 36864, "none"), lin("out", 18432, 16384, 4096, "none")]),
+    "c5": ("BASELINE config 5: VAE-decoder 3x3 conv, [1,512,128,128] -> 512 ch, and [1,256,256,256] -> 256 ch, "
+           "fused bias + SiLU",
+           [conv("conv512", 1, 512, 128, 128, 512, 3, 1, 1), conv("conv256", 1, 256, 256, 256, 256, 3, 1, 1)]),
+}
+
+
+def item_flops(it):
+    if it["op"] == "linear":
+        return 2.0 * it["M"] * it["K"] * it["N"]
+    oh = (it["H"] + 2 * it["pad"] - it["k"]) // it["stride"] + 1
+    ow = (it["W"] + 2 * it["pad"] - it["k"]) // it["stride"] + 1
+    return 2.0 * it["O"] * oh * ow * it["B"] * it["C"] * it["k"] * it["k"]
+
+
+def is_gate(it):
+    return it["op"] == "linear" and it["epi"].startswith("silu_gate")
+
+
+def out_cols(it):
+    return it["N"] // 2 if is_gate(it) else it["N"]
+
+
+def has_bias(it):
+    return it["epi"] in ("bias", "silu_gate", "silu")
+
+
+# DRAM bytes per k1_gemm launch of the config-2 step, from one ncu capture (profiles/); None until a
+# capture of the current kernel exists.
 K1_TRAFFIC_BYTES_PER_LAUNCH = None
 
 
@@ -87,7 +132,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
@@ -139,6 +184,7 @@ def dist_setup():
         from datetime import timedelta
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -146,75 +192,110 @@ def dist_setup():
 # ---------------------------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------------------------
-def run_ours(args, world, rank, local):
+class Workload:
+    """Device-resident weights, inputs and outputs of one workload on this rank."""
+
+    def __init__(self, items, world, rank, dev):
+        import torch
+
+        from invision_b200 import envg
+        from invision_b200.nsplit import shard_bounds
+
+        self.items, self.world, self.rank, self.dev = items, world, rank, dev
+        self.envg = envg
+        gen = torch.Generator(device=dev)
+        self.W, self.b, self.x, self.y, self.shard, self.ys, self.gbuf = {}, {}, {}, {}, {}, {}, {}
+        names = [it["name"] for it in items]
+        for i, it in enumerate(items):
+            name = it["name"]
+            gen.manual_seed(1000 + i)
+            if it["op"] == "conv":
+                if world > 1:
+                    raise SystemExit("conv workloads run on one GPU")
+                O, C, k = it["O"], it["C"], it["k"]
+                w = (torch.randn(O, C * k * k, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+                self.W[name] = envg.Weight(w.view(torch.int16).cpu().numpy().view(np.uint16), conv=(O, C, k, k))
+                self.b[name] = torch.randn(O, generator=gen, device=dev) * 0.01
+                gen.manual_seed(2000 + i)
+                self.x[name] = torch.randn(it["B"], C, it["H"], it["W"], generator=gen, device=dev)
+                oh = (it["H"] + 2 * it["pad"] - k) // it["stride"] + 1
+                ow = (it["W"] + 2 * it["pad"] - k) // it["stride"] + 1
+                self.y[name] = torch.empty(it["B"], O, oh, ow, device=dev)
+                continue
+            M, K, N = it["M"], it["K"], it["N"]
+            w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+            b = torch.randn(N, generator=gen, device=dev) * 0.01 if has_bias(it) else None
+            w_host = w.view(torch.int16).cpu().numpy().view(np.uint16)
+            del w
+            gate = is_gate(it)
+            layout = envg.LAYOUT_GATE_UP if gate else envg.LAYOUT_PLAIN
+            if world == 1:
+                self.W[name] = envg.Weight(w_host, layout=layout)
+                self.b[name] = b
+            else:
+                half = N // 2 if gate else N
+                n0, n1, per = shard_bounds(half, world, rank, 128)
+                self.W[name] = envg.Weight(w_host, layout=layout, shard=(n0, n1))
+                if b is not None:
+                    self.b[name] = (torch.cat([b[n0:n1], b[half + n0:half + n1]]) if gate else b[n0:n1]).contiguous()
+                else:
+                    self.b[name] = None
+                self.shard[name] = (n0, n1, per)
+                self.ys[name] = torch.zeros(M, per, device=dev)
+                self.gbuf[name] = torch.empty(world, M, per, device=dev)
+            if it["x_from"] not in names:
+                gen.manual_seed(2000 + i)
+                self.x[name] = torch.randn(M, K, generator=gen, device=dev)
+            self.y[name] = torch.empty(M, out_cols(it), device=dev)
+
+    def input_of(self, it):
+        return self.x[it["name"]] if it["name"] in self.x else self.y[it["x_from"]]
+
+    def run_item(self, it, gather=True):
+        envg = self.envg
+        name = it["name"]
+        if it["op"] == "conv":
+            envg.conv2d(self.y[name], self.x[name], self.W[name], self.b[name], it["stride"], it["pad"],
+                        epilogue=envg.EPI_SILU if it["epi"] == "silu" else envg.EPI_BIAS, sync=False)
+            return
+        x = self.input_of(it)
+        if self.world == 1:
+            envg.linear(self.y[name], x, self.W[name], bias=self.b[name], sync=False)
+            return
+        import torch
+
+        from invision_b200.nsplit import gather_columns
+
+        n0, n1, per = self.shard[name]
+        if n1 - n0 == per:
+            envg.linear(self.ys[name], x, self.W[name], bias=self.b[name], sync=False)
+        elif n1 > n0:  # ragged last shard: compute into the first n1 - n0 columns
+            tmp = torch.empty(it["M"], n1 - n0, device=self.dev)
+            envg.linear(tmp, x, self.W[name], bias=self.b[name], sync=False)
+            self.ys[name][:, : n1 - n0].copy_(tmp)
+        if gather:
+            gather_columns(self.ys[name], self.y[name].shape[1], out=self.y[name], buf=self.gbuf[name])
+
+    def step(self, gather=True):
+        for it in self.items:
+            self.run_item(it, gather)
+
+    def free(self):
+        for w in self.W.values():
+            w.free()
+
+
+def run_ours(args, items, desc, world, rank, local):
     import torch
     import torch.distributed as dist
 
     from invision_b200 import envg
-    from invision_b200.nsplit import gather_columns, shard_bounds
 
     torch.cuda.set_device(local)
     envg.init(local)
     dev = torch.device("cuda", local)
-    gen = torch.Generator(device=dev)
-
-    weights, biases, shards = {}, {}, {}
-    for i, (name, M, K, N, kind) in enumerate(LINEARS):
-        if name not in ACTIVE:
-            continue
-        gen.manual_seed(1000 + i)
-        w = (torch.randn(N, K, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
-        b = torch.randn(N, generator=gen, device=dev) * 0.01
-        w_host = w.view(torch.int16).cpu().numpy().view(np.uint16)
-        layout = envg.LAYOUT_GATE_UP if kind == "silu_gate" else envg.LAYOUT_PLAIN
-        if world == 1:
-            weights[name] = envg.Weight(w_host, layout=layout)
-            biases[name] = b
-            shards[name] = (0, N if kind != "silu_gate" else N // 2, None)
-        else:
-            half = N // 2 if kind == "silu_gate" else N
-            n0, n1, per = shard_bounds(half, world, rank, 128)
-            weights[name] = envg.Weight(w_host, layout=layout, shard=(n0, n1))
-            if kind == "silu_gate":
-                biases[name] = torch.cat([b[n0:n1], b[half + n0:half + n1]]).contiguous()
-            else:
-                biases[name] = b[n0:n1].contiguous()
-            shards[name] = (n0, n1, per)
-        del w
-    xs = {}
-    for i, (name, M, K, N, kind) in enumerate(LINEARS):
-        if name == "down" and "gate_up" in ACTIVE:
-            continue
-        gen.manual_seed(2000 + i)
-        xs[name] = torch.randn(M, K, generator=gen, device=dev)
-
-    def out_cols(name, N, kind):
-        return N // 2 if kind == "silu_gate" else N
-
-    # outputs (full) and per-rank shard outputs for N-split
-    ys, ys_shard, gather_bufs = {}, {}, {}
-    for name, M, K, N, kind in RUN:
-        nout = out_cols(name, N, kind)
-        ys[name] = torch.empty(M, nout, device=dev)
-        if world > 1:
-            n0, n1, per = shards[name]
-            ys_shard[name] = torch.zeros(M, per, device=dev)
-            gather_bufs[name] = torch.empty(world, M, per, device=dev)
-
-    def step():
-        for name, M, K, N, kind in RUN:
-            x = ys["gate_up"] if name not in xs else xs[name]
-            if world == 1:
-                envg.linear(ys[name], x, weights[name], bias=biases[name], sync=False)
-                continue
-            n0, n1, per = shards[name]
-            if n1 - n0 == per:
-                envg.linear(ys_shard[name], x, weights[name], bias=biases[name], sync=False)
-            elif n1 > n0:  # ragged last shard: compute into the first n1 - n0 columns
-                tmp = torch.empty(M, n1 - n0, device=dev)
-                envg.linear(tmp, x, weights[name], bias=biases[name], sync=False)
-                ys_shard[name][:, : n1 - n0].copy_(tmp)
-            gather_columns(ys_shard[name], ys[name].shape[1], out=ys[name], buf=gather_bufs[name])
+    wl = Workload(items, world, rank, dev)
+    step_flops = float(sum(item_flops(it) for it in items))
 
     def timed(fn, steps):
         torch.cuda.synchronize()
@@ -236,13 +317,13 @@ def run_ours(args, world, rank, local):
         return ms
 
     for _ in range(args.warmup):
-        step()
+        wl.step()
     torch.cuda.synchronize()
 
     st0 = envg.stats()
     clk = ClockSampler(local)
     clk.start()
-    ms = timed(step, args.steps)
+    ms = timed(wl.step, args.steps)
     clocks = clk.stop()
     st1 = envg.stats()
     launches = int(st1["kernel_launches"] - st0["kernel_launches"])
@@ -250,108 +331,120 @@ def run_ours(args, world, rank, local):
         t = torch.tensor([launches], device=dev, dtype=torch.int64)
         dist.all_reduce(t)
         launches = int(t.item())
-    value = STEP_FLOPS / (ms * 1e-3) / 1e12
+    value = step_flops / (ms * 1e-3) / 1e12
 
     # GEMM-phase only (no gather) for N > 1: what the N-split itself scales like
     gemm_phase = None
     if world > 1:
-        def step_local():
-            for name, M, K, N, kind in RUN:
-                x = ys["gate_up"] if name not in xs else xs[name]
-                n0, n1, per = shards[name]
-                if n1 - n0 == per:
-                    envg.linear(ys_shard[name], x, weights[name], bias=biases[name], sync=False)
-        gms = timed(step_local, args.steps)
-        gemm_phase = {"value": STEP_FLOPS / (gms * 1e-3) / 1e12, "ms_per_step": gms}
+        gms = timed(lambda: wl.step(gather=False), args.steps)
+        gemm_phase = {"value": round(step_flops / (gms * 1e-3) / 1e12, 2), "ms_per_step": round(gms, 4),
+                      "note": "same step without the all-gather of Y"}
 
-    # per-kernel device time with CUDA events around each launch (roofline of the top kernel)
+    # per-kernel device time: CUDA events the library records around each launch
+    pk, hbm, src = peaks()
     envg.profile(True)
     prof_steps = max(3, min(args.steps, 10))
     for _ in range(prof_steps):
-        step()
+        wl.step(gather=False)
     torch.cuda.synchronize()
     prof = envg.profile_read()
     envg.profile(False)
-    pk, hbm, src = peaks()
     k1 = {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0}
-    for kname in ("k1_gemm", "k1_gemm_silu_gate"):
+    for kname in ("k1_gemm", "k1_gemm_silu_gate", "k1_gemm_conv"):
         for f in k1:
             k1[f] += prof.get(kname, {}).get(f, 0)
     roofline = None
     if k1["launches"]:
         ach = k1["flops"] / (k1["ms"] * 1e-3) / 1e12
-        traffic = K1_TRAFFIC_BYTES_PER_LAUNCH
         roofline = {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s",
-                    "frac": round(ach / pk, 4), "traffic": traffic, "kernel": "k1_gemm (+ silu_gate variant)",
-                    "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)" if src == "measured" else src,
+                    "frac": round(ach / pk, 4), "traffic": K1_TRAFFIC_BYTES_PER_LAUNCH,
+                    "kernel": "k1_gemm family (tcgen05 CTA-pair GEMM; plain, SiLU-gate and conv variants)",
+                    "peak_source": (f"{src}: MEASURED_PEAKS.json bf16_tflops (burst)" if src == "measured"
+                                    else "fallback 1.59 PFLOP/s"),
                     "algorithmic_flops_per_launch": k1["flops"] / k1["launches"],
-                    "avg_launch_ms": k1["ms"] / k1["launches"]}
-    kernels = {k: {"launches": v["launches"], "avg_us": round(1e3 * v["ms"] / v["launches"], 2),
-                   "share": None, "tflops": round(v["flops"] / (v["ms"] * 1e-3) / 1e12, 1) if v["flops"] else None,
-                   "gbs": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1)} for k, v in prof.items()}
+                    "avg_launch_ms": round(k1["ms"] / k1["launches"], 5)}
     tot = sum(v["ms"] for v in prof.values()) or 1.0
+    kernels = {}
     for k, v in prof.items():
-        kernels[k]["share"] = round(v["ms"] / tot, 4)
-    skinny = prof.get("k2_skinny")
-    if skinny:
-        kernels["k2_skinny"]["hbm_frac"] = round(skinny["bytes"] / (skinny["ms"] * 1e-3) / 1e9 / hbm, 4)
+        kernels[k] = {"launches": v["launches"], "avg_us": round(1e3 * v["ms"] / v["launches"], 2),
+                      "share": round(v["ms"] / tot, 4),
+                      "tflops": round(v["flops"] / (v["ms"] * 1e-3) / 1e12, 1) if v["flops"] else None,
+                      "gbs": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1),
+                      "hbm_frac": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9 / hbm, 4)}
 
-    # end to end through the public API with host (pinned) buffers
+    # per item (each linear / conv alone): main kernel time and rate
+    per_item = {}
+    for it in items:
+        envg.profile(True)
+        reps = 5
+        for _ in range(reps):
+            wl.run_item(it, gather=False)
+        torch.cuda.synchronize()
+        p = envg.profile_read()
+        envg.profile(False)
+        main = {k: v for k, v in p.items() if k.startswith("k1") or k.startswith("k2")}
+        mms = sum(v["ms"] for v in main.values()) / reps
+        mbytes = sum(v["bytes"] for v in main.values()) / reps
+        per_item[it["name"]] = {
+            "kernel": "+".join(sorted(main)), "gemm_us": round(1e3 * mms, 2),
+            "gemm_tflops": round(item_flops(it) / (mms * 1e-3) / 1e12, 1) if mms else None,
+            "gemm_gbs": round(mbytes / (mms * 1e-3) / 1e9, 1) if mms else None,
+            "total_us": round(1e3 * sum(v["ms"] for v in p.values()) / reps, 2)}
+
     e2e = None
-    if not args.no_e2e and world == 1 and len(RUN) == len(LINEARS):
-        e2e = run_e2e(args, envg, torch, dev, weights, biases, xs, ys)
+    if not args.no_e2e and world == 1 and all(it["op"] == "linear" for it in items):
+        e2e = run_e2e(args, envg, torch, dev, wl, step_flops)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and len(RUN) == len(LINEARS):
-        cpu = cpu_baseline(args, sample_seconds=args.cpu_seconds)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and all(it["op"] == "linear" for it in items):
+        cpu = cpu_baseline(items, sample_seconds=args.cpu_seconds)
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": WORKLOAD if len(RUN) == len(LINEARS) else
-                           f"one linear of the workload: {[r[0] for r in RUN]}", "M": M_TOK, "hidden": HID, "mlp": MLP,
-                           "flops_per_step": STEP_FLOPS,
+                "config": {"workload": desc, "config": args.config, "flops_per_step": step_flops,
                            "parallelism": "single GPU" if world == 1 else f"N-split x{world} + NCCL all-gather",
                            "arith": "fp32 activations rounded to bf16 (RNE), bf16 weights, fp32 accumulate",
-                           "l2": "working set ~0.6 GB > 126 MB L2; no flush"},
+                           "l2": "working set > 126 MB L2 (config 2: ~0.6 GB); no flush"},
                 "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "roofline": roofline,
-                "cpu_baseline": cpu, "kernels": kernels}
+                "cpu_baseline": cpu, "kernels": kernels, "per_item": per_item}
         if gemm_phase:
             line["gemm_phase"] = gemm_phase
         print(json.dumps(line), flush=True)
-
-    for w in weights.values():
-        w.free()
+    wl.free()
 
 
-def run_e2e(args, envg, torch, dev, weights, biases, xs, ys):
+def run_e2e(args, envg, torch, dev, wl, step_flops):
     """Same step through envg_linear with HOST pointers (pinned numpy views): each call copies its
     input and bias H2D, runs, and copies its output D2H, synchronously, as the Pascal host would."""
-    hx = {k: torch.empty(v.shape, dtype=torch.float32, pin_memory=True) for k, v in xs.items()}
-    for k in hx:
-        hx[k].copy_(xs[k])
-    hb = {k: torch.empty(v.shape, dtype=torch.float32, pin_memory=True) for k, v in biases.items()}
-    for k in hb:
-        hb[k].copy_(biases[k])
-    hy = {k: torch.empty(v.shape, dtype=torch.float32, pin_memory=True) for k, v in ys.items()}
+    def pinned(t):
+        h = torch.empty(t.shape, dtype=torch.float32, pin_memory=True)
+        h.copy_(t)
+        return h
+
+    hx = {k: pinned(v) for k, v in wl.x.items()}
+    hb = {k: pinned(v) for k, v in wl.b.items() if v is not None}
+    hy = {k: torch.empty(v.shape, dtype=torch.float32, pin_memory=True) for k, v in wl.y.items()}
     npx = {k: v.numpy() for k, v in hx.items()}
     npb = {k: v.numpy() for k, v in hb.items()}
     npy = {k: v.numpy() for k, v in hy.items()}
     h2d = d2h = 0
-    for name, M, K, N, kind in LINEARS:
-        x = npy["gate_up"] if name == "down" else npx[name]
-        h2d += x.nbytes + npb[name].nbytes
-        d2h += npy[name].nbytes
+    for it in wl.items:
+        n = it["name"]
+        x = npx[n] if n in npx else npy[it["x_from"]]
+        h2d += x.nbytes + (npb[n].nbytes if n in npb else 0)
+        d2h += npy[n].nbytes
 
     stream = torch.cuda.Stream(device=dev)
     envg.follow_torch_stream(False)
     envg.set_stream(stream.cuda_stream)
 
     def step():
-        for name, M, K, N, kind in LINEARS:
-            x = npy["gate_up"] if name == "down" else npx[name]
-            envg.linear(npy[name], x, weights[name], bias=npb[name])
+        for it in wl.items:
+            n = it["name"]
+            x = npx[n] if n in npx else npy[it["x_from"]]
+            envg.linear(npy[n], x, wl.W[n], bias=npb.get(n))
 
     steps = max(2, min(args.steps, 5))
     for _ in range(2):
@@ -366,7 +459,7 @@ def run_e2e(args, envg, torch, dev, weights, biases, xs, ys):
     ms = a.elapsed_time(b) / steps
     envg.set_stream(None)
     envg.follow_torch_stream(True)
-    return {"value": round(FLOPS_PER_STEP / (ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(ms, 3),
+    return {"value": round(step_flops / (ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(ms, 3),
             "steps": steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "path": "envg_linear(HOST_PTRS) from pinned host memory, synchronous per call"}
 
@@ -375,23 +468,26 @@ def run_e2e(args, envg, torch, dev, weights, biases, xs, ys):
 # CPU side: the reference's own GEMM on the host cores
 # ---------------------------------------------------------------------------------------------
 class CpuWorkload:
-    """Seeded host copies of the workload: fp32-widened bf16 weights (the reference widens at load,
-    src/safetensor.pas:584-647), fp32 biases and inputs.  A step runs an M-slice of `rows` rows."""
+    """Seeded host copies of a linear workload: fp32-widened bf16 weights (the reference widens at
+    load, src/safetensor.pas:584-647), fp32 biases and inputs.  A step runs an M-slice of `rows`
+    rows of every linear whose M exceeds it (M = 1 linears run in full)."""
 
-    def __init__(self):
+    def __init__(self, items):
         import torch
 
         from oracle import oracle as O
 
         self.O = O
+        self.items = items
         g = torch.Generator().manual_seed(7)
         self.w, self.b, self.x = {}, {}, {}
-        for name, M, K, N, kind in LINEARS:
-            wt = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).float()
-            self.w[name] = wt.numpy()
-            self.b[name] = (torch.randn(N, generator=g) * 0.01).numpy()
-            if name != "down":
-                self.x[name] = torch.randn(M, K, generator=g).numpy()
+        names = [it["name"] for it in items]
+        for it in items:
+            n, M, K, N = it["name"], it["M"], it["K"], it["N"]
+            self.w[n] = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+            self.b[n] = (torch.randn(N, generator=g) * 0.01).numpy() if has_bias(it) else None
+            if it["x_from"] not in names:
+                self.x[n] = torch.randn(M, K, generator=g).numpy()
         self.use_ref = O.ref_lib() is not None
 
     def gemm(self, x, w):
@@ -405,24 +501,27 @@ class CpuWorkload:
         O = self.O
         flops = 0.0
         y = {}
-        for name, M, K, N, kind in LINEARS:
-            x = y["gate_up"] if name == "down" else np.ascontiguousarray(self.x[name][: min(M, rows)])
-            out = self.gemm(x, self.w[name])
-            out += self.b[name]  # QNNAddInplace per row (quicknncpu.pas:1816-1819)
-            if kind == "silu_gate":
+        for it in self.items:
+            n, M, K, N = it["name"], it["M"], it["K"], it["N"]
+            x = np.ascontiguousarray(self.x[n][: min(M, rows)]) if n in self.x else y[it["x_from"]]
+            out = self.gemm(x, self.w[n])
+            if self.b[n] is not None:
+                out += self.b[n]  # QNNAddInplace per row (quicknncpu.pas:1816-1819)
+            if is_gate(it):
                 h = N // 2
                 out = O.silu_mul(np.ascontiguousarray(out[:, :h]), np.ascontiguousarray(out[:, h:]))
-            y[name] = out
+            y[n] = out
             flops += 2.0 * x.shape[0] * K * N
         return flops
 
     def pick_rows(self, target_s):
-        """Largest M-slice (multiple of 64, <= 4608) whose step takes about target_s seconds."""
+        """Largest M-slice (multiple of 64, <= the largest M) whose step takes about target_s seconds."""
+        mmax = max(it["M"] for it in self.items)
         t = time.perf_counter()
-        self.step(64)
+        self.step(min(64, mmax))
         dt = time.perf_counter() - t
         rows = int(64 * target_s / max(dt, 1e-3))
-        return max(64, min(M_TOK, (rows // 64) * 64))
+        return max(min(64, mmax), min(mmax, (rows // 64) * 64))
 
     def describe(self):
         return ("reference src/sgemm2.cpp cpp_sgemm (compiled from the reference tree, OpenMP)" if self.use_ref else
@@ -436,26 +535,30 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(args, sample_seconds=12.0):
+def cpu_baseline(items, sample_seconds=12.0):
     from oracle import oracle as O
 
     threads = cpu_threads()
     O.set_threads(threads)
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    wl = CpuWorkload()
+    wl = CpuWorkload(items)
     rows = wl.pick_rows(sample_seconds)
     t = time.perf_counter()
     flops = wl.step(rows)
     dt = time.perf_counter() - t
+    mmax = max(it["M"] for it in items)
     return {"value": round(flops / dt / 1e12, 5), "unit": UNIT, "cores": threads,
             "kind": "reference" if wl.use_ref else "port",
-            "sample": f"one step of the workload on an M-slice of {rows} of 4608 token rows (adaLN M=1 in full); "
+            "sample": f"one step of the workload on an M-slice of {rows} of {mmax} token rows (M=1 linears in full); "
                       f"{dt:.1f} s; {wl.describe()}"}
 
 
-def run_reference(args, world, rank):
+def run_reference(args, items, desc, world, rank):
     """--impl reference: the reference's CPU GEMM path on the host cores (rank 0 only)."""
     if rank != 0:
+        return
+    if not all(it["op"] == "linear" for it in items):
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU arm covers linear workloads only"}))
         return
     from oracle import oracle as O
 
@@ -463,7 +566,7 @@ def run_reference(args, world, rank):
     O.set_threads(threads)
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     per_step = max(0.5, min(15.0, 150.0 / max(1, args.steps + args.warmup)))
-    wl = CpuWorkload()
+    wl = CpuWorkload(items)
     rows = wl.pick_rows(per_step)
     for _ in range(args.warmup):
         wl.step(rows)
@@ -474,50 +577,47 @@ def run_reference(args, world, rank):
     dt = time.perf_counter() - t
     value = flops / dt / 1e12
     kind = "reference" if wl.use_ref else "port"
-    sample = (f"each step: the workload on an M-slice of {rows} of 4608 token rows (adaLN M=1 in full); "
+    mmax = max(it["M"] for it in items)
+    sample = (f"each step: the workload on an M-slice of {rows} of {mmax} token rows (M=1 linears in full); "
               f"{wl.describe()}")
     line = {"metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "M_slice": rows, "parallelism": f"{threads} host threads"},
+            "config": {"workload": desc, "config": args.config, "M_slice": rows,
+                       "parallelism": f"{threads} host threads"},
             "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-ACTIVE = {r[0] for r in LINEARS}
-RUN = list(LINEARS)
-STEP_FLOPS = FLOPS_PER_STEP
-
-
 def main():
-    global RUN, ACTIVE, STEP_FLOPS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--only", default=None, help="run one item of the workload (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--only", default=None, help="run one linear of the workload (profiling): " +
-                    ",".join(r[0] for r in LINEARS))
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    desc, items = WORKLOADS[args.config]
     if args.only:
-        RUN = [r for r in LINEARS if r[0] == args.only]
-        if not RUN:
-            ap.error(f"--only: unknown linear {args.only}")
-        ACTIVE = {args.only}
-        STEP_FLOPS = float(sum(2 * M * K * N for _, M, K, N, _ in RUN))
+        keep = [it for it in items if it["name"] == args.only]
+        if not keep:
+            ap.error(f"--only: no item {args.only} in {args.config}")
+        items = keep
+        desc = f"{args.config}: only {args.only}"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, world, rank)
+        run_reference(args, items, desc, world, rank)
         return
     world, rank, local = dist_setup()
     try:
-        run_ours(args, world, rank, local)
+        run_ours(args, items, desc, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

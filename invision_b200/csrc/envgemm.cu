@@ -32,6 +32,7 @@ namespace {
 constexpr uint32_t WEIGHT_MAGIC = 0xE17A9E11u;
 constexpr int K1_BN = 256;
 constexpr int K1_STAGES = 4;
+constexpr int KPAIR_STAGES = 6;
 constexpr int SKINNY_MAX = 64;
 constexpr uint64_t DEFAULT_WAIT_CAP_NS = 2000000000ull;  // 2 s
 
@@ -78,6 +79,9 @@ struct Dev {
   int* d_status = nullptr;
   uint64_t wait_cap_ns = DEFAULT_WAIT_CAP_NS;
   int skinny_max = SKINNY_MAX;
+  bool use_pair = true;  // 256x256 CTA-pair tiles for M > 128 (ENVG_K1=single selects k1_gemm)
+  int max_pairs = 0;     // co-resident CTA pairs of k1_gemm_pair
+  bool store_tma = true;  // TMA bulk-store epilogue; ENVG_STORE=coalesced selects warp-coalesced stores
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
@@ -240,8 +244,12 @@ int tmap_out_3d(CUtensorMap* tm, const float* base, uint64_t plane, uint64_t ch,
   return ENVG_OK;
 }
 
-// Picks the k1_gemm store path for a row-major Y and builds its map.
-int choose_store(EpiArgs& e, CUtensorMap* tmY) {
+// Picks the k1_gemm store path for a row-major Y (and builds its map for the TMA paths).
+int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY) {
+  if (!use_tma) {
+    e.store_mode = STORE_COALESCED;
+    return ENVG_OK;
+  }
   e.store_mode = STORE_DIRECT;
   const bool aligned = (reinterpret_cast<uintptr_t>(e.Y) & 15) == 0 && e.ldy % 4 == 0;
   if (!aligned) return ENVG_OK;
@@ -356,6 +364,45 @@ int launch_k1(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const CUtens
   return ENVG_OK;
 }
 
+template <bool CONV_B, bool SILU_GATE>
+int launch_k1_pair(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tY, GemmArgs& a,
+                   double flops, double bytes) {
+  using L = KPairSmem<KPAIR_STAGES>;
+  auto kern = k1_gemm_pair<KPAIR_STAGES, CONV_B, SILU_GATE>;
+  static bool attr = false;
+  static int max_pairs = 0;
+  if (!attr) {
+    ENVG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * d->sms, 1, 1);
+    cfg.blockDim = dim3(K1_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = d->sms / 2;
+    }
+    max_pairs = n;
+    attr = true;
+  }
+  a.status = d->d_status;
+  a.wait_cap_ns = d->wait_cap_ns;
+  const int pairs = (int)std::min<int64_t>(a.num_tiles, max_pairs);
+  if (pairs <= 0) return ENVG_OK;
+  ProfScope ps(stream_of(d), CONV_B ? KID_K1_CONV : (SILU_GATE ? KID_K1_SILU_GATE : KID_K1), flops, bytes);
+  kern<<<2 * pairs, K1_THREADS, L::TOTAL, stream_of(d)>>>(tA, tB, tY, a);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
 template <int MPAD, int R>
 int launch_k2_t(Dev* d, const CUtensorMap& tW, const CUtensorMap& tX, SkinnyArgs& a, double flops, double bytes) {
   constexpr int STAGE_BYTES = K2Smem<MPAD, R, 1>::STAGE_BYTES;
@@ -451,14 +498,21 @@ int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap&
   ENVG_TRY(tmap_2d(&tA, A, Kp, M, BM));
   GemmArgs g{};
   g.num_kb = (int)num_kb;
-  g.tiles_m = (int)cdiv(M, BM);
   g.tiles_n = (int)cdiv(rows_b, K1_BN);
-  g.num_tiles = g.tiles_m * g.tiles_n;
   g.group_m = 8;
   CUtensorMap tY;
   memset(&tY, 0, sizeof(tY));
-  ENVG_TRY(choose_store(e, &tY));
+  ENVG_TRY(choose_store(d->store_tma, e, &tY));
   g.epi = e;
+  if (d->use_pair && M > BM) {
+    g.tiles_m = (int)cdiv(M, 2 * BM);
+    g.num_tiles = g.tiles_m * g.tiles_n;
+    g.group_m = 4;
+    if (silu_gate) return launch_k1_pair<false, true>(d, tA, b128, tY, g, flops, bytes);
+    return launch_k1_pair<false, false>(d, tA, b128, tY, g, flops, bytes);
+  }
+  g.tiles_m = (int)cdiv(M, BM);
+  g.num_tiles = g.tiles_m * g.tiles_n;
   if (silu_gate) return launch_k1<false, true>(d, tA, b256, tY, g, flops, bytes);
   return launch_k1<false, false>(d, tA, b256, tY, g, flops, bytes);
 }
@@ -592,6 +646,8 @@ int envg_init(int ndev, const int* dev_ids) {
     long long ms = atoll(s);
     if (ms > 0) d->wait_cap_ns = (uint64_t)ms * 1000000ull;
   }
+  if (const char* s = getenv("ENVG_K1")) d->use_pair = strcmp(s, "single") != 0;
+  if (const char* s = getenv("ENVG_STORE")) d->store_tma = strcmp(s, "coalesced") != 0;
   if (const char* s = getenv("ENVG_SKINNY_M_MAX")) {
     int v = atoi(s);
     if (v >= 0 && v <= SKINNY_MAX) d->skinny_max = v;
@@ -958,11 +1014,15 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
     int tw = 1;
     while (tw < outW && tw < 256) tw <<= 1;
     const int th = 256 / tw;
+    const bool pair = d->use_pair && out_ch > BM;
     CUtensorMap tB;
-    ENVG_TRY(tmap_nhwc(&tB, d->act.p, Cp, W_, H, batch, tw, th));
+    if (pair)  // each CTA of the pair fetches half of the 256-pixel tile
+      ENVG_TRY(tmap_nhwc(&tB, d->act.p, Cp, W_, H, batch, th >= 2 ? tw : tw / 2, th >= 2 ? th / 2 : 1));
+    else
+      ENVG_TRY(tmap_nhwc(&tB, d->act.p, Cp, W_, H, batch, tw, th));
     GemmArgs g{};
     g.num_kb = (int)(W->Kp / BK);
-    g.tiles_m = (int)cdiv(out_ch, BM);
+    g.tiles_m = (int)cdiv(out_ch, pair ? 2 * BM : BM);
     g.conv.tileW = tw;
     g.conv.tileH = th;
     g.conv.outH = outH;
@@ -982,8 +1042,8 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
     e.vec_ok = ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 4 == 0) ? 1 : 0;
     CUtensorMap tY;
     memset(&tY, 0, sizeof(tY));
-    e.store_mode = STORE_DIRECT;
-    if ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 32 == 0) {
+    e.store_mode = (tw >= 32) ? STORE_COALESCED : STORE_DIRECT;  // a 32-pixel chunk stays in one row
+    if (d->store_tma && (reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 32 == 0) {
       ENVG_TRY(tmap_out_3d(&tY, dy, (uint64_t)plane, (uint64_t)out_ch, (uint64_t)batch));
       e.store_mode = STORE_TMA;
     }
@@ -991,7 +1051,8 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
     const double cflops = 2.0 * out_ch * (double)plane * batch * (double)W->K;
     const double cbytes = 2.0 * (double)batch * H * W_ * Cp + 2.0 * out_ch * (double)W->Kp + 4.0 * (double)out_elems +
                           (dbias ? 4.0 * out_ch : 0.0);
-    ENVG_TRY(launch_k1<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
+    if (pair) ENVG_TRY(launch_k1_pair<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
+    else ENVG_TRY(launch_k1<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
   } else {
     // Strided convolution: explicit bf16 im2col, then one GEMM per image.
     const int64_t colK = W->Kp;
@@ -1021,7 +1082,7 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
       eb.vec_ok = ((reinterpret_cast<uintptr_t>(eb.Y) & 15) == 0 && plane % 4 == 0) ? 1 : 0;
       CUtensorMap tY;
       memset(&tY, 0, sizeof(tY));
-      ENVG_TRY(choose_store(eb, &tY));
+      ENVG_TRY(choose_store(d->store_tma, eb, &tY));
       g.epi = eb;
       ENVG_TRY(launch_k1<false, false>(d, tA, tB, tY, g, 2.0 * out_ch * (double)plane * (double)W->K,
                                        2.0 * (double)plane * colK + 2.0 * out_ch * (double)colK + 4.0 * out_ch * (double)plane));

@@ -48,10 +48,12 @@ struct EpiArgs {
   int store_mode;     // k1_gemm: STORE_DIRECT, STORE_TMA or STORE_TMA_ADD
 };
 
-// How k1_gemm writes Y: per-thread global stores, or 32x32 tiles staged in shared memory and
-// written by a TMA bulk store (coalesced; clipped at the tensor edges), or added into Y by a TMA
-// bulk reduce (Y += tile: the gated residual and alpha*AB + 1*C).
-enum StoreMode : int { STORE_DIRECT = 0, STORE_TMA = 1, STORE_TMA_ADD = 2 };
+// How k1_gemm writes Y: per-thread global stores (one row per thread); 32x32 tiles staged in
+// shared memory and written by a TMA bulk store (clipped at the tensor edges) or added into Y by a
+// TMA bulk reduce (Y += tile); or (STORE_COALESCED, the default) the staged tile read back
+// transposed so that every warp store writes whole 128-byte rows, keeping the output off the
+// SM's TMA unit, which the operand loads keep busy.
+enum StoreMode : int { STORE_DIRECT = 0, STORE_TMA = 1, STORE_TMA_ADD = 2, STORE_COALESCED = 3 };
 
 struct ConvGeom {
   int tileW, tileH;   // pixel tile, tileW * tileH == BN
@@ -110,12 +112,137 @@ ENVG_DEV float epi_pre(const EpiArgs& e, float acc, int row, int col) {
   return v;
 }
 
+// Per-column vector (bias or gate) for the 32 columns [col0, col0+32): eight 16-byte loads when
+// the chunk is whole and aligned, guarded scalar loads at the ragged edge.
+ENVG_DEV void load_col32(const float* p, int col0, int n_out, float (&c)[32]) {
+  if (col0 + 32 <= n_out && (reinterpret_cast<uintptr_t>(p + col0) & 15) == 0) {
+    const float4* p4 = reinterpret_cast<const float4*>(p + col0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 t = __ldg(p4 + q);
+      c[4 * q] = t.x;
+      c[4 * q + 1] = t.y;
+      c[4 * q + 2] = t.z;
+      c[4 * q + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) c[j] = (col0 + j < n_out) ? __ldg(p + col0 + j) : 0.0f;
+  }
+}
+
+// epi_pre for a whole 32-column chunk of one row, with the mode tests taken once per chunk.
+// `e` is a register copy of the kernel's EpiArgs.
+ENVG_DEV void epi_pre_chunk(const EpiArgs& e, float (&v)[32], int row, int col0) {
+  if (e.bias_mode == 1) {
+    float b[32];
+    load_col32(e.bias, col0, e.n_out, b);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], b[j]);
+  } else if (e.bias_mode == 2) {
+    const float bv = row < e.m_valid ? __ldg(e.bias + row) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bv);
+  }
+  if (e.act) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+  }
+  if (e.mode == EPI_GATED_RES) {
+    float g[32];
+    load_col32(e.gate, col0, e.n_out, g);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(g[j], v[j]);
+  } else if (e.mode == EPI_ALPHA_BETA) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(e.alpha, v[j]);
+  }
+}
+
+// SiLU-gate of a 32-column chunk: v = silu(g + bias_g) * (u + bias_u).
+ENVG_DEV void silu_gate_chunk(const EpiArgs& e, const uint32_t (&g)[32], const uint32_t (&u)[32], int col0,
+                              float (&v)[32]) {
+  if (e.bias_mode == 1) {
+    float bg[32], bu[32];
+    load_col32(e.bias, col0, e.n_out, bg);
+    load_col32(e.bias + e.half_n, col0, e.n_out, bu);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      v[j] = __fmul_rn(silu_f(__fadd_rn(__uint_as_float(g[j]), bg[j])), __fadd_rn(__uint_as_float(u[j]), bu[j]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(silu_f(__uint_as_float(g[j])), __uint_as_float(u[j]));
+  }
+}
+
 // Write row `lane` of a 32 x 32 fp32 tile into a 128-byte-swizzled staging buffer (16-byte chunk
 // j of row r lands at chunk j ^ (r % 8), the layout the TMA store reads).
 ENVG_DEV void stage_row32(uint8_t* buf, int lane, const float (&v)[32]) {
   float4* rowp = reinterpret_cast<float4*>(buf + lane * 128);
 #pragma unroll
   for (int j = 0; j < 8; ++j) rowp[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// Write a staged 32 x 32 tile (rows row0.., columns col0..) of a row-major Y with coalesced
+// stores: lane l moves 16-byte chunk (l % 8) of rows (l / 8) + 4i, so each store instruction
+// covers four full 128-byte rows.  `v` already holds everything but the read of Y
+// (epi_pre); GATED_RES adds the old Y, ALPHA_BETA adds beta * old Y.
+ENVG_DEV void store_tile32_rows(const EpiArgs& e, const uint8_t* buf, int lane, int row0, int col0) {
+  const int ch = lane & 7;
+  const bool rmw = e.mode == EPI_GATED_RES || (e.mode == EPI_ALPHA_BETA && e.beta != 0.0f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = (lane >> 3) + 4 * i;
+    const int grow = row0 + r;
+    if (grow >= e.m_valid) continue;
+    const float4 t = *reinterpret_cast<const float4*>(buf + r * 128 + ((ch ^ (r & 7)) * 16));
+    const int gcol = col0 + ch * 4;
+    float* yp = e.Y + (int64_t)grow * e.ldy + gcol;
+    float tv[4] = {t.x, t.y, t.z, t.w};
+    if (e.vec_ok && gcol + 3 < e.n_out) {
+      if (rmw) {
+        const float4 o = *reinterpret_cast<const float4*>(yp);
+        const float ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tv[j] = (e.mode == EPI_GATED_RES) ? __fadd_rn(ov[j], tv[j]) : __fadd_rn(tv[j], __fmul_rn(e.beta, ov[j]));
+      }
+      *reinterpret_cast<float4*>(yp) = make_float4(tv[0], tv[1], tv[2], tv[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (gcol + j >= e.n_out) break;
+        float v = tv[j];
+        if (rmw) v = (e.mode == EPI_GATED_RES) ? __fadd_rn(yp[j], v) : __fadd_rn(v, __fmul_rn(e.beta, yp[j]));
+        yp[j] = v;
+      }
+    }
+  }
+}
+
+// Coalesced store of a staged 32 x 32 conv tile: rows are output channels row0.., the 32
+// columns are consecutive pixels starting at (h, w) of image b.
+ENVG_DEV void store_tile32_conv(const EpiArgs& e, const ConvGeom& g, const uint8_t* buf, int lane, int row0, int b,
+                                int h, int w) {
+  if (h >= g.outH) return;
+  const int ch = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = (lane >> 3) + 4 * i;
+    const int oc = row0 + r;
+    if (oc >= e.m_valid) continue;
+    const float4 t = *reinterpret_cast<const float4*>(buf + r * 128 + ((ch ^ (r & 7)) * 16));
+    const int wc = w + ch * 4;
+    float* yp = e.Y + (int64_t)b * g.img_stride + (int64_t)oc * g.plane + (int64_t)h * g.outW + wc;
+    if (e.vec_ok && wc + 3 < g.outW) {
+      *reinterpret_cast<float4*>(yp) = t;
+    } else {
+      const float tv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (wc + j < g.outW) yp[j] = tv[j];
+    }
+  }
 }
 
 // Store 32 consecutive output columns [col0, col0+32) of one row.
@@ -353,6 +480,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
     // ---------------- epilogue: 4 warps, one TMEM lane quadrant each ----------------
     const int q = warp & 3;
     const int smode = args.epi.store_mode;
+    const EpiArgs ep = args.epi;  // register copy: the chunk loops read it every iteration
     uint8_t* stg = sStage + (warp - 2) * 8192;  // this warp's two 4 KB staging tiles
     int sb = 0;
     int acc = 0;
@@ -386,17 +514,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
           tmem_ld32(trow + c * 32, g);
           tmem_ld32(trow + BN / 2 + c * 32, u);
           col0 = n_blk * (BN / 2) + c * 32;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float gv = __uint_as_float(g[j]);
-            float uv = __uint_as_float(u[j]);
-            const int col = col0 + j;
-            if (args.epi.bias_mode == 1 && col < args.epi.n_out) {
-              gv = __fadd_rn(gv, __ldg(args.epi.bias + col));
-              uv = __fadd_rn(uv, __ldg(args.epi.bias + args.epi.half_n + col));
-            }
-            v[j] = __fmul_rn(silu_f(gv), uv);
-          }
+          silu_gate_chunk(ep, g, u, col0, v);
         } else {
           uint32_t r[32];
           tmem_ld32(trow + c * 32, r);
@@ -406,14 +524,14 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
         }
         if (smode == STORE_DIRECT) {
           if (SILU_GATE) {
-            EpiArgs e2 = args.epi;
+            EpiArgs e2 = ep;
             e2.bias_mode = 0;
             e2.act = 0;
             epi_store_row32(e2, row, col0, v);
           } else if (CONV_B) {
-            epi_store_conv32(args.epi, args.conv, b, row, h0, w0, c * 32, v);
+            epi_store_conv32(ep, args.conv, b, row, h0, w0, c * 32, v);
           } else {
-            epi_store_row32(args.epi, row, col0, v);
+            epi_store_row32(ep, row, col0, v);
           }
           continue;
         }
@@ -425,17 +543,31 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
           const int h = h0 + jj / args.conv.tileW;
           if (w >= args.conv.outW) continue;  // tile overhang past the image row (uniform per warp)
           x = h * args.conv.outW + w;          // h >= outH lands past the plane and is clipped
-          const float bv = (args.epi.bias_mode == 2 && row < args.epi.m_valid) ? __ldg(args.epi.bias + row) : 0.0f;
+          const float bv = (ep.bias_mode == 2 && row < ep.m_valid) ? __ldg(ep.bias + row) : 0.0f;
+          if (ep.act) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float t = __fadd_rn(v[j], bv);
-            v[j] = args.epi.act ? silu_f(t) : t;
+            for (int j = 0; j < 32; ++j) v[j] = silu_f(__fadd_rn(v[j], bv));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bv);
           }
         } else if (!SILU_GATE) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = epi_pre(args.epi, v[j], row, col0 + j);
+          epi_pre_chunk(ep, v, row, col0);
         }
         uint8_t* buf = stg + sb * 4096;
+        if (smode == STORE_COALESCED) {
+          stage_row32(buf, lane, v);
+          __syncwarp();
+          if (CONV_B) {
+            const int jj = c * 32;
+            store_tile32_conv(ep, args.conv, buf, lane, row0, b, h0 + jj / args.conv.tileW,
+                              w0 + jj % args.conv.tileW);
+          } else {
+            store_tile32_rows(ep, buf, lane, row0, col0);
+          }
+          sb ^= 1;  // the other buffer is written next, so no wait before this one is reused
+          continue;
+        }
         if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
         __syncwarp();
         stage_row32(buf, lane, v);
@@ -463,6 +595,304 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// K1 pair: the same GEMM on 256 x 256 tiles computed by a CTA pair (cluster of 2) with
+// tcgen05.mma.cta_group::2.  Each CTA loads its own 128 rows of A and its own 128 rows of B
+// (no multicast loads); the even CTA issues the UMMAs, which read both CTAs' shared memory and
+// write each CTA's 128 accumulator rows into its own TMEM.  Per SM this halves the B bytes read
+// from L2 and from shared memory relative to k1_gemm.
+//   full[s]   (even CTA)  : its producer's expect_tx of both CTAs' bytes + both CTAs' TMA
+//   empty[s]  (both)      : UMMA commit multicast to the pair
+//   tfull[a]  (both)      : UMMA commit multicast after a tile's last k-block
+//   tempty[a] (even CTA)  : 4 epilogue warps x 2 CTAs arrive
+// ------------------------------------------------------------------------------------------
+template <int STAGES>
+struct KPairSmem {
+  static constexpr int HALF_B_BYTES = 128 * BK * 2;
+  static constexpr int STAGE_BYTES = TILE_A_BYTES + HALF_B_BYTES;  // this CTA's share of a stage
+  static constexpr int STAGING_BYTES = 4 * 2 * 32 * 128;
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
+  static constexpr uint32_t TMEM_COLS = 512;
+};
+
+template <int STAGES, bool CONV_B, bool SILU_GATE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
+    k1_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmY, const GemmArgs args) {
+  using L = KPairSmem<STAGES>;
+  constexpr int BN = 256;
+  constexpr uint32_t IDESC = idesc_bf16_f32(2 * BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * TILE_A_BYTES;
+  uint8_t* sStage = sB + STAGES * L::HALF_B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + L::STAGING_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * STAGES;
+  const uint32_t tfull0 = empty0 + 8 * STAGES;
+  const uint32_t tempty0 = tfull0 + 16;
+  const uint32_t drain = tempty0 + 16;
+  const uint32_t full0_leader = mapa_shared(full0, 0);
+  const uint32_t tempty0_leader = mapa_shared(tempty0, 0);
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 8);
+    }
+    mbar_init(drain, 1);
+    *abort_s = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (args.epi.store_mode != STORE_DIRECT) tma_prefetch_desc(&tmY);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), L::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtl wc{args.wait_cap_ns, args.status, abort_s, 0};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t pending = 0, issue_ph = 0;
+      for (int tile = pair; tile < args.num_tiles; tile += npairs) {
+        int m_blk, n_blk;
+        int b = 0, h0 = 0, w0 = 0;
+        if (CONV_B) {
+          m_blk = tile % args.tiles_m;
+          n_blk = tile / args.tiles_m;
+          const int per_img = args.conv.tiles_w * args.conv.tiles_h;
+          b = n_blk / per_img;
+          const int r = n_blk - b * per_img;
+          h0 = (r / args.conv.tiles_w) * args.conv.tileH;
+          w0 = (r % args.conv.tiles_w) * args.conv.tileW;
+          // this CTA's half of the pixel tile: half the rows, or half the row when one row
+          if (args.conv.tileH >= 2) h0 += (int)rank * (args.conv.tileH / 2);
+          else w0 += (int)rank * (args.conv.tileW / 2);
+        } else {
+          map_tile(tile, args, m_blk, n_blk);
+        }
+        const int m0 = m_blk * 2 * BM + (int)rank * BM;
+        const int n0 = n_blk * BN + (int)rank * 128;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!wait_bounded(empty0 + 8 * stage, ph ^ 1, wc, 21)) goto producer_done;
+          const uint32_t fb = full0_leader + 8 * stage;
+          if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, 2 * L::STAGE_BYTES);
+          tma_load_2d_pair(smem_u32(sA + stage * TILE_A_BYTES), &tmA, fb, kb * BK, m0);
+          if (CONV_B) {
+            const int kpos = kb / args.conv.cblocks;
+            const int cb = kb - kpos * args.conv.cblocks;
+            const int kh = kpos / args.conv.KW;
+            const int kw = kpos - kh * args.conv.KW;
+            tma_load_4d_pair(smem_u32(sB + stage * L::HALF_B_BYTES), &tmB, fb, cb * BK, w0 + kw - args.conv.pad,
+                             h0 + kh - args.conv.pad, b);
+          } else {
+            tma_load_2d_pair(smem_u32(sB + stage * L::HALF_B_BYTES), &tmB, fb, kb * BK, n0);
+          }
+          pending |= 1u << stage;
+          issue_ph = (issue_ph & ~(1u << stage)) | (ph << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    producer_done:
+      if (*abort_s && pending) {
+        if (leader) {
+          for (int s = 0; s < STAGES; ++s)
+            if (pending & (1u << s)) wait_drain(full0 + 8 * s, (issue_ph >> s) & 1u, args.wait_cap_ns);
+        } else {
+          // The odd CTA's copies signal the even CTA's barriers; give them time to land.
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      for (int tile = pair; tile < args.num_tiles; tile += npairs) {
+        if (!wait_bounded(tempty0 + 8 * acc, aph ^ 1, wc, 22)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!wait_bounded(full0 + 8 * stage, ph, wc, 23)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_kmajor_desc(smem_u32(sA + stage * TILE_A_BYTES));
+          const uint64_t bd = sw128_kmajor_desc(smem_u32(sB + stage * L::HALF_B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16_pair(d_tmem, ad + 2 * k, bd + 2 * k, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair_mc(empty0 + 8 * stage, 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(tfull0 + 8 * acc, 0x3);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
+      }
+      if (*abort_s) {
+        umma_commit_pair(drain);
+        wait_drain(drain, 0, args.wait_cap_ns);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int smode = args.epi.store_mode;
+    const EpiArgs ep = args.epi;  // register copy: the chunk loops read it every iteration
+    uint8_t* stg = sStage + (warp - 2) * 8192;
+    int sb = 0;
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int tile = pair; tile < args.num_tiles; tile += npairs) {
+      int m_blk, n_blk;
+      int b = 0, h0 = 0, w0 = 0;
+      if (CONV_B) {
+        m_blk = tile % args.tiles_m;
+        n_blk = tile / args.tiles_m;
+        const int per_img = args.conv.tiles_w * args.conv.tiles_h;
+        b = n_blk / per_img;
+        const int r = n_blk - b * per_img;
+        h0 = (r / args.conv.tiles_w) * args.conv.tileH;
+        w0 = (r % args.conv.tiles_w) * args.conv.tileW;
+      } else {
+        map_tile(tile, args, m_blk, n_blk);
+      }
+      if (!wait_bounded_warp(tfull0 + 8 * acc, aph, wc, 24)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const int row0 = m_blk * 2 * BM + (int)rank * BM + q * 32;
+      const int row = row0 + lane;
+      constexpr int NCHUNK = SILU_GATE ? BN / 64 : BN / 32;
+#pragma unroll 1
+      for (int c = 0; c < NCHUNK; ++c) {
+        float v[32];
+        int col0;
+        if (SILU_GATE) {
+          uint32_t g[32], u[32];
+          tmem_ld32(trow + c * 32, g);
+          tmem_ld32(trow + BN / 2 + c * 32, u);
+          col0 = n_blk * (BN / 2) + c * 32;
+          silu_gate_chunk(ep, g, u, col0, v);
+        } else {
+          uint32_t r[32];
+          tmem_ld32(trow + c * 32, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          col0 = n_blk * BN + c * 32;
+        }
+        if (smode == STORE_DIRECT) {
+          if (SILU_GATE) {
+            EpiArgs e2 = ep;
+            e2.bias_mode = 0;
+            e2.act = 0;
+            epi_store_row32(e2, row, col0, v);
+          } else if (CONV_B) {
+            epi_store_conv32(ep, args.conv, b, row, h0, w0, c * 32, v);
+          } else {
+            epi_store_row32(ep, row, col0, v);
+          }
+          continue;
+        }
+        int x = col0, y = row0;
+        if (CONV_B) {
+          const int jj = c * 32;
+          const int w = w0 + jj % args.conv.tileW;
+          const int h = h0 + jj / args.conv.tileW;
+          if (w >= args.conv.outW) continue;
+          x = h * args.conv.outW + w;
+          const float bv = (ep.bias_mode == 2 && row < ep.m_valid) ? __ldg(ep.bias + row) : 0.0f;
+          if (ep.act) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = silu_f(__fadd_rn(v[j], bv));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bv);
+          }
+        } else if (!SILU_GATE) {
+          epi_pre_chunk(ep, v, row, col0);
+        }
+        uint8_t* buf = stg + sb * 4096;
+        if (smode == STORE_COALESCED) {
+          stage_row32(buf, lane, v);
+          __syncwarp();
+          if (CONV_B) {
+            const int jj = c * 32;
+            store_tile32_conv(ep, args.conv, buf, lane, row0, b, h0 + jj / args.conv.tileW,
+                              w0 + jj % args.conv.tileW);
+          } else {
+            store_tile32_rows(ep, buf, lane, row0, col0);
+          }
+          sb ^= 1;  // the other buffer is written next, so no wait before this one is reused
+          continue;
+        }
+        if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
+        __syncwarp();
+        stage_row32(buf, lane, v);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (CONV_B) tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+          else if (smode == STORE_TMA_ADD) tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
+          else tma_store_2d(&tmY, smem_u32(buf), x, y);
+          bulk_commit();
+        }
+        sb ^= 1;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0_leader + 8 * acc);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, L::TMEM_COLS);
   }
 }
 
@@ -659,7 +1089,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
         }
       }
       if (finalize) {
-        const EpiArgs& e = args.epi;
+        const EpiArgs e = args.epi;
         const int col = tile * BM + rowin;  // output column
         if (col < e.n_out) {
 #pragma unroll

@@ -62,3 +62,14 @@ def test_calls_before_init_return_state_error():
 def test_mirror_asserts_like_the_reference():
     with pytest.raises(AssertionError, match="no weight"):
         envg.QNNLINEAR_BF16_OR_F32(None, None, None, None, 1, 1, 1)
+
+
+@pytest.mark.skipif(not _no_gpu(), reason="checks the no-GPU behaviour")
+def test_cpp_harness_links_and_fails_cleanly_without_gpu(tmp_path):
+    """A C++ host compiled against include/quicknn_cuda.hpp links the .so and gets status codes /
+    exceptions (not crashes) when no sm_100 GPU is present."""
+    from tests.abi.build_harness import build
+
+    exe = build(str(tmp_path))
+    r = subprocess.run([exe, "nogpu"], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr

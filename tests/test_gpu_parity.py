@@ -200,3 +200,45 @@ def test_errors_are_codes_not_crashes(gpu):
     with pytest.raises(gpu.EnvgError) as e:
         gpu.linear(y, x, W)  # freed handle -> NULL
     assert e.value.code == gpu.ERR_STATE
+
+
+@pytest.mark.parametrize("env", [{"ENVG_STORE": "coalesced"}, {"ENVG_STORE": "coalesced", "ENVG_K1": "single"},
+                                 {"ENVG_K1": "single"}])
+def test_alternate_kernel_paths_in_subprocess(env):
+    """The warp-coalesced store epilogue and the single-CTA k1_gemm (selected by environment at init) on a
+    few linear / SiLU-gate / gated-residual / conv cases, in a fresh process."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "import numpy as np\n"
+        "from invision_b200 import envg\n"
+        "from oracle import oracle as O\n"
+        "from tests.common import inputs, assert_parity, TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT\n"
+        "envg.init(0)\n"
+        "for (M, K, N) in [(300, 512, 520), (129, 64, 257), (1024, 3072, 9216)]:\n"
+        "    x, w, b = inputs(M, K, N, seed=M + N)\n"
+        "    W = envg.Weight(w); y = np.zeros((M, N), np.float32); envg.linear(y, x, W, bias=b)\n"
+        "    assert_parity(y, O.linear_bf16(x, w, b))\n"
+        "x, w, _ = inputs(256, 512, 768, seed=4)\n"
+        "W = envg.Weight(w, layout=envg.LAYOUT_GATE_UP); y = np.zeros((256, 384), np.float32); envg.linear(y, x, W)\n"
+        "g = O.linear_bf16(x, w)\n"
+        "assert_parity(y, O.silu_mul(np.ascontiguousarray(g[:, :384]), np.ascontiguousarray(g[:, 384:])), "
+        "TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT)\n"
+        "x, w, b = inputs(200, 256, 100, seed=8); rng = np.random.default_rng(1)\n"
+        "h0 = rng.standard_normal((200, 100), dtype=np.float32); gate = rng.standard_normal(100).astype(np.float32)\n"
+        "W = envg.Weight(w); h = h0.copy(); envg.linear(h, x, W, bias=b, epilogue=envg.EPI_GATED_RESIDUAL, gate=gate)\n"
+        "ref = O.gated_add(h0, gate, O.linear_bf16(x, w, b)); assert_parity(h - h0, ref - h0)\n"
+        "rng = np.random.default_rng(3); src = rng.standard_normal((1, 64, 12, 96), dtype=np.float32)\n"
+        "wb = O.f32_to_bf16_rne((0.02 * rng.standard_normal((256, 64, 3, 3))).astype(np.float32))\n"
+        "bias = (0.01 * rng.standard_normal(256)).astype(np.float32)\n"
+        "W = envg.Weight(wb.reshape(256, -1), conv=(256, 64, 3, 3)); y = np.zeros((1, 256, 12, 96), np.float32)\n"
+        "envg.conv2d(y, src, W, bias, 1, 1, epilogue=envg.EPI_SILU)\n"
+        "assert_parity(y, O.silu(O.conv2d(src, O.bf16_to_f32(wb), bias, 1, 1)))\n"
+        "print('ok')\n" % root)
+    r = subprocess.run([sys.executable, "-c", code], env={**os.environ, **env}, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
