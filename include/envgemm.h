@@ -118,6 +118,25 @@ int envg_weight_free(envg_weight w);
 int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, int64_t M,
                 int64_t K, int64_t N, int epilogue, const float* gate, int flags);
 
+/* One linear of a batch (arguments as envg_linear). */
+typedef struct envg_linear_desc {
+  float* dst;
+  const float* x;
+  envg_weight W;
+  const float* bias;
+  int64_t M, K, N;
+  int epilogue;
+  const float* gate;
+} envg_linear_desc;
+
+/* Several linears in one call, in order, on device pointers (flags must contain ENVG_DEVICE_PTRS;
+ * ENVG_ASYNC optional).  Equivalent to n envg_linear calls, but each distinct input x is rounded
+ * to bf16 once (the FLUX Q/K/V and Qwen3 q/k/v projections read the same normalised input,
+ * quicknn_transformers.pas:1402-1414, quicknn_qwen3.pas:712-714), and the rounding of the next
+ * input runs on a second stream while the current GEMM runs.  An input that is the output of an
+ * earlier linear of the batch waits for it. */
+int envg_linear_batch(const envg_linear_desc* descs, int n, int flags);
+
 /* dst[batch, out_ch, outH, outW] = conv(src[batch, in_ch, H, W], W) + bias, NCHW, as
  * QNNConv2d (quicknn_kernels.pas:984-1010 -> quicknncpu.pas:1958-2132); outH/outW follow
  * QNNConv2DShape (quicknn_kernels.pas:984-988).  epilogue: ENVG_EPI_NONE/BIAS or ENVG_EPI_SILU. */

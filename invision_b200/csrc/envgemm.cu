@@ -74,18 +74,21 @@ struct Dev {
   int sms = 0;
   cudaStream_t own = nullptr;
   cudaStream_t user = nullptr;
-  Buf x, y, xb, wb, part, cnt, bias, gate, act, col, b32;
+  Buf x, y, xb, wb, part, cnt, bias, gate, act, col, b32, xbatch;
+  cudaStream_t aux = nullptr;              // second stream of envg_linear_batch
+  std::vector<cudaEvent_t> batch_events;   // reused event pool of envg_linear_batch
   int* h_status = nullptr;  // mapped pinned: [0] status code, [1] wait site
   int* d_status = nullptr;
   uint64_t wait_cap_ns = DEFAULT_WAIT_CAP_NS;
   int skinny_max = SKINNY_MAX;
+  int gemv_max = 8;      // M <= gemv_max runs k_gemv (fp32 X on CUDA cores); ENVG_GEMV_M_MAX overrides
   bool use_pair = true;  // 256x256 CTA-pair tiles for M > 128 (ENVG_K1=single selects k1_gemm)
   int max_pairs = 0;     // co-resident CTA pairs of k1_gemm_pair
   bool store_tma = true;  // TMA bulk-store epilogue; ENVG_STORE=coalesced selects warp-coalesced stores
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
-           col.bytes + b32.bytes;
+           col.bytes + b32.bytes + xbatch.bytes;
   }
 };
 
@@ -94,9 +97,13 @@ Dev g_dev[64];
 int g_cur = -1;
 
 // ---- optional per-launch timing (envg_profile) ---------------------------------------------
-enum KernelId { KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_CAST, KID_TRANSPOSE, KID_IM2COL, KID_SELFTEST, KID_COUNT };
-const char* const kKernelNames[KID_COUNT] = {"k1_gemm", "k1_gemm_silu_gate", "k1_gemm_conv", "k2_skinny",
-                                             "k_cast_rows", "k_transpose_cast", "k_im2col_nhwc", "k_wait_selftest"};
+enum KernelId {
+  KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_TRANSPOSE, KID_IM2COL, KID_SELFTEST,
+  KID_COUNT
+};
+const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate", "k1_gemm_conv",
+                                             "k2_skinny",   "k_gemv",            "k_cast_rows",
+                                             "k_transpose_cast", "k_im2col_nhwc", "k_wait_selftest"};
 struct KAcc {
   uint64_t launches = 0;
   double ms = 0, flops = 0, bytes = 0;
@@ -443,6 +450,43 @@ int launch_k2(Dev* d, int mpad, int R, const CUtensorMap& tW, const CUtensorMap&
   return fail(ENVG_ERR_ARG, "skinny path: unsupported padded M %d", mpad);
 }
 
+// M <= 8 linear on CUDA cores straight from fp32 X (no cast).
+int launch_gemv(Dev* d, const float* X, int64_t M, int64_t K, envg_weight W, bool gu, const EpiArgs& e, double flops,
+                double bytes) {
+  GemvArgs a{};
+  a.X = X;
+  a.ldx = K;
+  a.M = (int)M;
+  a.K = (int)K;
+  a.W = W->d;
+  a.Kp = W->Kp;
+  a.rows = (int)W->rows;
+  a.gate_up = gu ? 1 : 0;
+  a.groups = (int)(gu ? cdiv(W->half, 32) : cdiv(W->rows, 64));
+  const int64_t kchunks = cdiv(K, 256);
+  // about two blocks per SM, but at least two 256-element chunks of K per split
+  int64_t splits = std::max<int64_t>(1, std::min<int64_t>(kchunks / 2, cdiv(2 * d->sms, a.groups)));
+  a.kchunk = (int)(cdiv(kchunks, splits) * 256);
+  a.splits = (int)cdiv(K, a.kchunk);
+  a.xvec = (K % 8 == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0) ? 1 : 0;
+  a.epi = e;
+  if (a.splits > 1) {
+    ENVG_TRY(ensure(d, d->part, (size_t)a.groups * a.splits * 8 * 64 * sizeof(float)));
+    ENVG_TRY(ensure(d, d->cnt, (size_t)a.groups * sizeof(int), true));
+    a.partial = reinterpret_cast<float*>(d->part.p);
+    a.counters = reinterpret_cast<int*>(d->cnt.p);
+  }
+  const int grid = a.groups * a.splits;
+  ProfScope ps(stream_of(d), KID_GEMV, flops, bytes);
+  if (M <= 1) k_gemv<1><<<grid, 256, 0, stream_of(d)>>>(a);
+  else if (M <= 2) k_gemv<2><<<grid, 256, 0, stream_of(d)>>>(a);
+  else if (M <= 4) k_gemv<4><<<grid, 256, 0, stream_of(d)>>>(a);
+  else k_gemv<8><<<grid, 256, 0, stream_of(d)>>>(a);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
 int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t K, int64_t Kp, void* xb) {
   if (rows == 0) return ENVG_OK;
   const int vec8 = (K == Kp && K % 8 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
@@ -481,8 +525,9 @@ int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap&
     SkinnyArgs s{};
     s.n_tiles = (int)cdiv(rows_b, (int64_t)R * BM);
     s.num_kb = (int)num_kb;
+    // about two CTAs per SM, but at least 4 k-blocks (32 KB of W per 128 rows) per split
     int splits = std::max(1, (2 * d->sms) / s.n_tiles);
-    splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 2));
+    splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 4));
     s.kb_per_split = (int)cdiv(num_kb, splits);
     s.splits = (int)cdiv(num_kb, s.kb_per_split);
     s.epi = e;
@@ -648,6 +693,10 @@ int envg_init(int ndev, const int* dev_ids) {
   }
   if (const char* s = getenv("ENVG_K1")) d->use_pair = strcmp(s, "single") != 0;
   if (const char* s = getenv("ENVG_STORE")) d->store_tma = strcmp(s, "coalesced") != 0;
+  if (const char* s = getenv("ENVG_GEMV_M_MAX")) {
+    int v = atoi(s);
+    if (v >= 0 && v <= 8) d->gemv_max = v;
+  }
   if (const char* s = getenv("ENVG_SKINNY_M_MAX")) {
     int v = atoi(s);
     if (v >= 0 && v <= SKINNY_MAX) d->skinny_max = v;
@@ -663,12 +712,17 @@ int envg_shutdown(void) {
   Dev* d = cur();
   if (!d) return ENVG_OK;
   cudaStreamSynchronize(stream_of(d));
-  Buf* bufs[] = {&d->x, &d->y, &d->xb, &d->wb, &d->part, &d->cnt, &d->bias, &d->gate, &d->act, &d->col, &d->b32};
+  Buf* bufs[] = {&d->x,    &d->y,   &d->xb,  &d->wb,  &d->part,  &d->cnt,
+                 &d->bias, &d->gate, &d->act, &d->col, &d->b32, &d->xbatch};
   for (Buf* b : bufs) {
     if (b->p) cudaFree(b->p);
     *b = Buf{};
   }
   if (d->own) cudaStreamDestroy(d->own);
+  if (d->aux) cudaStreamDestroy(d->aux);
+  for (cudaEvent_t e : d->batch_events) cudaEventDestroy(e);
+  d->batch_events.clear();
+  d->aux = nullptr;
   if (d->h_status) cudaFreeHost(d->h_status);
   d->own = nullptr;
   d->user = nullptr;
@@ -839,9 +893,6 @@ int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, in
       dgate = reinterpret_cast<float*>(d->gate.p);
     }
   }
-  ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
-  ENVG_TRY(launch_cast_rows(d, dx, K, M, K, W->Kp, d->xb.p));
-
   EpiArgs e{};
   e.Y = dy;
   e.ldy = n_out;
@@ -857,10 +908,17 @@ int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, in
   e.half_n = (int)(gu ? W->half : 0);
   e.vec_ok = ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && n_out % 4 == 0) ? 1 : 0;
   const double lin_flops = 2.0 * (double)M * (double)N * (double)K;
-  const double lin_bytes = 2.0 * (double)N * K + 2.0 * (double)M * W->Kp + 4.0 * (double)M * n_out +
-                           (dbias ? 4.0 * N : 0.0) +
+  const double out_bytes = 4.0 * (double)M * n_out + (dbias ? 4.0 * N : 0.0) +
                            (epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)M * n_out + 4.0 * N : 0.0);
-  ENVG_TRY(gemm_device(d, d->xb.p, M, W->Kp, W->tm256, W->tm128, W->rows, gu, e, lin_flops, lin_bytes));
+  if (M <= d->gemv_max) {
+    // fp32 X read directly: W once, X once per 64-row group (from L2)
+    ENVG_TRY(launch_gemv(d, dx, M, K, W, gu, e, lin_flops, 2.0 * (double)N * K + 4.0 * (double)M * K + out_bytes));
+  } else {
+    ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
+    ENVG_TRY(launch_cast_rows(d, dx, K, M, K, W->Kp, d->xb.p));
+    ENVG_TRY(gemm_device(d, d->xb.p, M, W->Kp, W->tm256, W->tm128, W->rows, gu, e, lin_flops,
+                         2.0 * (double)N * K + 2.0 * (double)M * W->Kp + out_bytes));
+  }
 
   d->st.calls++;
   d->st.flops += 2.0 * (double)M * (double)N * (double)K;
@@ -950,6 +1008,157 @@ int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* 
                      2.0 * (double)N * K + 2.0 * (double)M * W->Kp + 4.0 * (double)M * n_out));
   d->st.calls++;
   d->st.flops += 2.0 * (double)M * (double)N * (double)K;
+  if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
+  return ENVG_OK;
+}
+
+namespace {
+// Validation shared by envg_linear and envg_linear_batch (device pointers).
+int check_linear_args(Dev* d, const envg_linear_desc& q) {
+  ENVG_TRY(check_weight(d, q.W));
+  if (q.W->conv) return fail(ENVG_ERR_ARG, "linear: handle holds a convolution weight");
+  if (q.M < 0 || q.M > INT32_MAX / 2) return fail(ENVG_ERR_ARG, "linear: M=%lld out of range", (long long)q.M);
+  if (q.K != q.W->K || q.N != q.W->N)
+    return fail(ENVG_ERR_ARG, "linear: [K=%lld, N=%lld] does not match the weight [N=%lld, K=%lld]", (long long)q.K,
+                (long long)q.N, (long long)q.W->N, (long long)q.W->K);
+  const bool gu = q.W->layout == ENVG_LAYOUT_GATE_UP;
+  if ((q.epilogue == ENVG_EPI_SILU_GATE) != gu)
+    return fail(ENVG_ERR_ARG, "linear: SILU_GATE goes with (and only with) a GATE_UP weight");
+  if (q.epilogue != ENVG_EPI_NONE && q.epilogue != ENVG_EPI_BIAS && q.epilogue != ENVG_EPI_SILU_GATE &&
+      q.epilogue != ENVG_EPI_GATED_RESIDUAL)
+    return fail(ENVG_ERR_ARG, "linear: epilogue %d not valid for a linear", q.epilogue);
+  if (q.epilogue == ENVG_EPI_BIAS && !q.bias) return fail(ENVG_ERR_ARG, "linear: BIAS epilogue without bias");
+  if (q.epilogue == ENVG_EPI_GATED_RESIDUAL && !q.gate) return fail(ENVG_ERR_ARG, "linear: GATED_RESIDUAL without gate");
+  if (q.M > 0 && (!q.dst || !q.x)) return fail(ENVG_ERR_ARG, "linear: dst or x is NULL");
+  if (q.M > 0 && (const void*)q.dst == (const void*)q.x) return fail(ENVG_ERR_ARG, "linear: dst aliases x");
+  return ENVG_OK;
+}
+
+EpiArgs linear_epi(const envg_linear_desc& q) {
+  const bool gu = q.W->layout == ENVG_LAYOUT_GATE_UP;
+  const int64_t n_out = gu ? q.N / 2 : q.N;
+  EpiArgs e{};
+  e.Y = q.dst;
+  e.ldy = n_out;
+  e.bias = q.bias;
+  e.bias_mode = q.bias ? 1 : 0;
+  e.mode = (q.epilogue == ENVG_EPI_GATED_RESIDUAL) ? EPI_GATED_RES : EPI_PLAIN;
+  e.gate = q.gate;
+  e.alpha = 1.0f;
+  e.n_out = (int)n_out;
+  e.m_valid = (int)q.M;
+  e.half_n = (int)(gu ? q.W->half : 0);
+  e.vec_ok = ((reinterpret_cast<uintptr_t>(q.dst) & 15) == 0 && n_out % 4 == 0) ? 1 : 0;
+  return e;
+}
+
+cudaEvent_t batch_event(Dev* d, size_t i) {
+  while (d->batch_events.size() <= i) {
+    cudaEvent_t e = nullptr;
+    cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    d->batch_events.push_back(e);
+  }
+  return d->batch_events[i];
+}
+}  // namespace
+
+int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (n < 0 || (n > 0 && !descs)) return fail(ENVG_ERR_ARG, "envg_linear_batch: bad descriptor array");
+  if (!(flags & ENVG_DEVICE_PTRS)) return fail(ENVG_ERR_ARG, "envg_linear_batch: needs device pointers");
+  for (int i = 0; i < n; ++i) ENVG_TRY(check_linear_args(d, descs[i]));
+  if (!d->aux) ENVG_CUDA(cudaStreamCreateWithFlags(&d->aux, cudaStreamNonBlocking));
+  cudaStream_t s = stream_of(d);
+
+  // Distinct inputs that take the tcgen05 path (M > gemv_max) get one bf16 copy each, packed in
+  // one workspace; `src_of[i]` maps linear i to its copy.
+  std::vector<int> src_of(n, -1);
+  std::vector<int> first_use;  // linear index of each copy's first use
+  std::vector<size_t> offset;
+  size_t total = 0;
+  for (int i = 0; i < n; ++i) {
+    const envg_linear_desc& q = descs[i];
+    if (q.M == 0 || q.M <= d->gemv_max) continue;
+    for (size_t j = 0; j < first_use.size(); ++j) {
+      const envg_linear_desc& p = descs[first_use[j]];
+      if (p.x == q.x && p.M == q.M && p.W->Kp == q.W->Kp && p.K == q.K) {
+        src_of[i] = (int)j;
+        break;
+      }
+    }
+    if (src_of[i] < 0) {
+      src_of[i] = (int)first_use.size();
+      first_use.push_back(i);
+      offset.push_back(total);
+      total += ((size_t)(q.M * q.W->Kp) * 2 + 255) & ~size_t(255);
+    }
+  }
+  ENVG_TRY(ensure(d, d->xbatch, total));
+  uint8_t* base = reinterpret_cast<uint8_t*>(d->xbatch.p);
+
+  // Event plan: ev[0] = start of the batch on s; ev[1 + j] = copy j done on aux;
+  // ev[1 + ncopies + i] = linear i done on s.
+  const size_t ncopies = first_use.size();
+  ENVG_CUDA(cudaEventRecord(batch_event(d, 0), s));
+  ENVG_CUDA(cudaStreamWaitEvent(d->aux, batch_event(d, 0), 0));
+  cudaStream_t saved = d->user;
+  size_t next_copy = 0;
+  // Producers of copy j: earlier linears whose output overlaps copy j's input.
+  auto produces = [&](int p, size_t j) {
+    const envg_linear_desc& q = descs[first_use[j]];
+    const envg_linear_desc& pr = descs[p];
+    const bool gu = pr.W->layout == ENVG_LAYOUT_GATE_UP;
+    const char* y0 = reinterpret_cast<const char*>(pr.dst);
+    const char* y1 = y0 + (size_t)(pr.M * (gu ? pr.N / 2 : pr.N)) * 4;
+    const char* x0 = reinterpret_cast<const char*>(q.x);
+    const char* x1 = x0 + (size_t)(q.M * q.K) * 4;
+    return pr.M > 0 && x0 < y1 && y0 < x1;
+  };
+  // Cast j may be issued once every producer (index < issued) has been issued on s.
+  auto ready = [&](size_t j, int issued) {
+    for (int p = issued; p < first_use[j]; ++p)
+      if (produces(p, j)) return false;
+    return true;
+  };
+  auto issue_cast = [&](size_t j) -> int {
+    const envg_linear_desc& q = descs[first_use[j]];
+    for (int p = 0; p < first_use[j]; ++p)
+      if (produces(p, j)) ENVG_CUDA(cudaStreamWaitEvent(d->aux, batch_event(d, 1 + ncopies + p), 0));
+    d->user = d->aux;
+    int rc = launch_cast_rows(d, q.x, q.K, q.M, q.K, q.W->Kp, base + offset[j]);
+    d->user = saved;
+    if (rc != ENVG_OK) return rc;
+    ENVG_CUDA(cudaEventRecord(batch_event(d, 1 + j), d->aux));
+    return ENVG_OK;
+  };
+  for (int i = 0; i < n; ++i) {
+    const envg_linear_desc& q = descs[i];
+    // casts run one linear ahead of the GEMMs, in order, as soon as their inputs exist
+    while (next_copy < ncopies && first_use[next_copy] <= i + 1 && ready(next_copy, i)) {
+      ENVG_TRY(issue_cast(next_copy));
+      ++next_copy;
+    }
+    if (q.M == 0) continue;
+    const bool gu = q.W->layout == ENVG_LAYOUT_GATE_UP;
+    const EpiArgs e = linear_epi(q);
+    const int64_t n_out = gu ? q.N / 2 : q.N;
+    const double fl = 2.0 * (double)q.M * (double)q.N * (double)q.K;
+    const double ob = 4.0 * (double)q.M * n_out + (q.bias ? 4.0 * q.N : 0.0) +
+                      (q.epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)q.M * n_out + 4.0 * q.N : 0.0);
+    if (src_of[i] < 0) {
+      ENVG_TRY(launch_gemv(d, q.x, q.M, q.K, q.W, gu, e, fl, 2.0 * (double)q.N * q.K + 4.0 * (double)q.M * q.K + ob));
+    } else {
+      if ((size_t)src_of[i] >= next_copy) return fail(ENVG_ERR_STATE, "envg_linear_batch: internal schedule error");
+      ENVG_CUDA(cudaStreamWaitEvent(s, batch_event(d, 1 + src_of[i]), 0));
+      ENVG_TRY(gemm_device(d, base + offset[src_of[i]], q.M, q.W->Kp, q.W->tm256, q.W->tm128, q.W->rows, gu, e, fl,
+                           2.0 * (double)q.N * q.K + 2.0 * (double)q.M * q.W->Kp + ob));
+    }
+    ENVG_CUDA(cudaEventRecord(batch_event(d, 1 + ncopies + i), s));
+    d->st.calls++;
+    d->st.flops += fl;
+  }
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
 }

@@ -1073,6 +1073,9 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
           for (int r = 0; r < R; ++r) {
 #pragma unroll
             for (int m = 0; m < MPAD; ++m) acc[r][m] = 0.0f;
+            // unrolled so that the loads of several splits are in flight together; the adds
+            // still run in split order
+#pragma unroll 4
             for (int s = 0; s < args.splits; ++s) {
               const float* p = args.partial + ((((int64_t)tile * args.splits + s) * R + r) * BM + rowin) * MPAD;
 #pragma unroll
@@ -1119,6 +1122,157 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// k_gemv: linears with M <= 8 on CUDA cores.  X stays fp32 (products are exact fp32 x bf16, sums
+// in fp32, as in the reference), so no activation cast runs.  Each warp streams 8 rows of W with
+// 16-byte loads (one load instruction = 512 contiguous bytes of a row) and keeps the 8 x M dot
+// products in registers; a warp-wide xor reduction finishes them.  Blocks of 8 warps cover 64 W
+// rows (32 gate + 32 up output pairs for the GATE_UP layout); split-K across blocks reduces
+// deterministically: the last block of a row group sums the partials in split order.
+// ------------------------------------------------------------------------------------------
+struct GemvArgs {
+  const float* X;
+  int64_t ldx;
+  int M, K;
+  const uint16_t* W;
+  int64_t Kp;
+  int rows;       // W rows stored on the device
+  int gate_up;    // interleaved GATE_UP layout: 128 gate rows then their 128 up rows
+  int groups;     // row groups of 64 device rows
+  int splits, kchunk;  // split-K: K elements per split (multiple of 256)
+  int xvec;       // X rows 16-byte aligned and K % 8 == 0
+  EpiArgs epi;
+  float* partial;  // [groups][splits][8][64]
+  int* counters;   // [groups]
+};
+
+ENVG_DEV uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+template <int MT>
+__global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
+  __shared__ float s_sum[MT][64];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = blockIdx.x / a.splits;
+  const int split = blockIdx.x - group * a.splits;
+  // the 8 device rows of this warp
+  int drow[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (a.gate_up) {
+      const int c = group * 32 + warp * 4 + (j & 3);  // output column of the pair
+      drow[j] = 256 * (c >> 7) + (c & 127) + (j >= 4 ? 128 : 0);
+    } else {
+      drow[j] = group * 64 + warp * 8 + j;
+    }
+  }
+  float acc[MT][8];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[m][j] = 0.0f;
+  const int kb = split * a.kchunk;
+  const int ke = min(a.K, kb + a.kchunk);
+#pragma unroll 2
+  for (int k0 = kb + lane * 8; k0 < ke; k0 += 256) {
+    uint4 wv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      wv[j] = (drow[j] < a.rows) ? ld_nc_v4(a.W + (int64_t)drow[j] * a.Kp + k0) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m >= a.M) break;
+      float xv[8];
+      const float* xp = a.X + (int64_t)m * a.ldx + k0;
+      if (a.xvec && k0 + 8 <= a.K) {
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(xp));
+        const float4 x1 = __ldg(reinterpret_cast<const float4*>(xp + 4));
+        xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
+        xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[e] = (k0 + e < a.K) ? __ldg(xp + e) : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t w4[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+        float t = acc[m][j];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          t = fmaf(xv[2 * q], __uint_as_float(w4[q] << 16), t);
+          t = fmaf(xv[2 * q + 1], __uint_as_float(w4[q] & 0xFFFF0000u), t);
+        }
+        acc[m][j] = t;
+      }
+    }
+  }
+  // warp reduction; afterwards lane (m * 8 + j) % 32 owns sum (m, j)
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float v = acc[m][j];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      acc[m][j] = v;
+    }
+  if (lane == 0) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s_sum[m][warp * 8 + j] = acc[m][j];
+  }
+  __syncthreads();
+  if (a.splits > 1) {
+    float* part = a.partial + ((int64_t)group * a.splits + split) * (8 * 64);
+    for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) __stcg(part + t, s_sum[t / 64][t % 64]);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = (atomicAdd(a.counters + group, 1) == a.splits - 1) ? 1 : 0;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) {
+      float v = 0.0f;
+#pragma unroll 8
+      for (int sp = 0; sp < a.splits; ++sp) v += __ldcg(a.partial + ((int64_t)group * a.splits + sp) * (8 * 64) + t);
+      s_sum[t / 64][t % 64] = v;
+    }
+    if (threadIdx.x == 0) a.counters[group] = 0;  // re-arm for the next launch
+    __syncthreads();
+  }
+  const EpiArgs e = a.epi;
+  if (a.gate_up) {
+    for (int t = threadIdx.x; t < MT * 32; t += blockDim.x) {
+      const int m = t / 32, c = t % 32;
+      if (m >= a.M) continue;
+      const int col = group * 32 + c;
+      if (col >= e.n_out) continue;
+      float g = s_sum[m][(c >> 2) * 8 + (c & 3)], u = s_sum[m][(c >> 2) * 8 + 4 + (c & 3)];
+      if (e.bias_mode == 1) {
+        g = __fadd_rn(g, __ldg(e.bias + col));
+        u = __fadd_rn(u, __ldg(e.bias + e.half_n + col));
+      }
+      e.Y[(int64_t)m * e.ldy + col] = __fmul_rn(silu_f(g), u);
+    }
+  } else {
+    for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) {
+      const int m = t / 64, r = t % 64;
+      if (m >= a.M) continue;
+      const int col = group * 64 + r;
+      if (col >= e.n_out) continue;
+      float* yp = e.Y + (int64_t)m * e.ldy + col;
+      *yp = epi_value(e, s_sum[m][r], m, col, yp);
+    }
   }
 }
 

@@ -42,6 +42,12 @@ class KernelStat(ctypes.Structure):
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
 
 
+class LinearDesc(ctypes.Structure):
+    _fields_ = [("dst", ctypes.c_void_p), ("x", ctypes.c_void_p), ("W", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+                ("M", ctypes.c_int64), ("K", ctypes.c_int64), ("N", ctypes.c_int64), ("epilogue", ctypes.c_int),
+                ("gate", ctypes.c_void_p)]
+
+
 class Stats(ctypes.Structure):
     _fields_ = [("calls", ctypes.c_uint64), ("kernel_launches", ctypes.c_uint64), ("flops", ctypes.c_double),
                 ("h2d_bytes", ctypes.c_double), ("d2h_bytes", ctypes.c_double), ("weight_bytes", ctypes.c_uint64),
@@ -70,6 +76,7 @@ def lib():
         L.envg_weight_free.argtypes = [_vp]
         L.envg_linear.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_noalloc.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
+        L.envg_linear_batch.argtypes = [ctypes.POINTER(LinearDesc), _ci, _ci]
         L.envg_conv2d.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 11
         L.envg_sgemm.argtypes = [_ci, _ci, _ci, _i64, _i64, _i64, ctypes.c_float, _vp, _i64, _vp, _i64,
                                  ctypes.c_float, _vp, _i64]
@@ -265,6 +272,26 @@ def linear(dst, x, W, bias=None, epilogue=None, gate=None, sync=True):
         flags |= ASYNC
     M, K = x.shape
     return _check(lib().envg_linear(_ptr(dst), _ptr(x), W.h, _ptr(bias), M, K, W.N, epilogue, _ptr(gate), flags))
+
+
+def linear_batch(calls, sync=True):
+    """Several linears in one envg_linear_batch call (torch CUDA tensors only).  `calls` is a list
+    of dicts with keys dst, x, W and optionally bias, epilogue, gate; each distinct x is cast once
+    and the casts overlap the previous GEMM on a second stream."""
+    arr = (LinearDesc * len(calls))()
+    keep = []
+    for i, c in enumerate(calls):
+        W = c["W"]
+        bias, gate = c.get("bias"), c.get("gate")
+        epi = c.get("epilogue")
+        if epi is None:
+            epi = EPI_SILU_GATE if W.layout == LAYOUT_GATE_UP else (EPI_BIAS if bias is not None else EPI_NONE)
+        _mode(c["dst"], c["x"], bias, gate)
+        M, K = c["x"].shape
+        arr[i] = LinearDesc(_ptr(c["dst"]), _ptr(c["x"]), W.h, _ptr(bias), M, K, W.N, epi, _ptr(gate))
+        keep.append(c)
+    flags = DEVICE_PTRS | (0 if sync else ASYNC)
+    return _check(lib().envg_linear_batch(arr, len(calls), flags))
 
 
 def conv2d(dst, src, W, bias, stride, pad, epilogue=None, sync=True):

@@ -242,3 +242,71 @@ def test_alternate_kernel_paths_in_subprocess(env):
     r = subprocess.run([sys.executable, "-c", code], env={**os.environ, **env}, capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 3072, 18432), (8, 2560, 1024), (3, 131, 257), (5, 4096, 2560), (2, 64, 70)])
+def test_gemv_path_is_fp32_exact(gpu, M, K, N):
+    """M <= 8 runs k_gemv: fp32 X times bf16 W in fp32 (no bf16 rounding of X), so it matches the
+    reference's fp32 GEMM (scalar build) to fp32 round-off, far inside the GEMM bound."""
+    x, w, b = inputs(M, K, N, seed=600 + M + K)
+    W = gpu.Weight(w)
+    y = np.zeros((M, N), np.float32)
+    gpu.linear(y, x, W, bias=b)
+    assert_parity(y, O.linear_bf16(x, w, b, path=O.PATH_SCALAR), 1e-5, 5e-6, what=f"gemv {M}x{K}x{N}")
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_gemv_silu_gate_and_gated_residual(gpu, M):
+    K, H = 768, 300
+    x, w, _ = inputs(M, K, 2 * H, seed=M + 31)
+    W = gpu.Weight(w, layout=gpu.LAYOUT_GATE_UP)
+    y = np.zeros((M, H), np.float32)
+    gpu.linear(y, x, W)
+    g = O.linear_bf16(x, w, path=O.PATH_SCALAR)
+    assert_parity(y, O.silu_mul(np.ascontiguousarray(g[:, :H]), np.ascontiguousarray(g[:, H:])), 1e-5, 5e-6,
+                  what=f"gemv silu-gate M={M}")
+    x2, w2, b2 = inputs(M, K, H, seed=M + 77)
+    rng = np.random.default_rng(M)
+    h0 = rng.standard_normal((M, H), dtype=np.float32)
+    gate = rng.standard_normal(H).astype(np.float32)
+    W2 = gpu.Weight(w2)
+    h = h0.copy()
+    gpu.linear(h, x2, W2, bias=b2, epilogue=gpu.EPI_GATED_RESIDUAL, gate=gate)
+    ref = O.gated_add(h0, gate, O.linear_bf16(x2, w2, b2, path=O.PATH_SCALAR))
+    assert_parity(h - h0, ref - h0, 1e-5, 1e-5, what=f"gemv gated residual M={M}")
+
+
+def test_linear_batch_equals_separate_calls(gpu):
+    """envg_linear_batch (one cast per distinct input, casts overlapped on a second stream, a
+    chained input waiting for its producer) gives bit-identical results to envg_linear calls."""
+    import torch
+
+    dev = "cuda"
+    M, H, F = 300, 256, 384
+    rng = np.random.default_rng(5)
+    x = torch.from_numpy(rng.standard_normal((M, H), dtype=np.float32)).to(dev)
+    x2 = torch.from_numpy(rng.standard_normal((M, H), dtype=np.float32)).to(dev)
+    xs = torch.from_numpy(rng.standard_normal((4, H), dtype=np.float32)).to(dev)
+
+    def wt(n, k, seed):
+        return O.f32_to_bf16_rne((0.02 * np.random.default_rng(seed).standard_normal((n, k))).astype(np.float32))
+
+    Wq, Wk, Wv = gpu.Weight(wt(H, H, 1)), gpu.Weight(wt(H, H, 2)), gpu.Weight(wt(H, H, 3))
+    Wgu = gpu.Weight(wt(2 * F, H, 4), layout=gpu.LAYOUT_GATE_UP)
+    Wd = gpu.Weight(wt(H, F, 5))
+    Ws = gpu.Weight(wt(520, H, 6))
+    b = torch.from_numpy((0.01 * rng.standard_normal(H)).astype(np.float32)).to(dev)
+    outs = {k: torch.empty(M, H, device=dev) for k in ("q", "k", "v", "d")}
+    outs["gu"] = torch.empty(M, F, device=dev)
+    outs["s"] = torch.empty(4, 520, device=dev)
+    calls = [dict(dst=outs["q"], x=x, W=Wq, bias=b), dict(dst=outs["k"], x=x, W=Wk),
+             dict(dst=outs["v"], x=x, W=Wv, bias=b), dict(dst=outs["gu"], x=x2, W=Wgu),
+             dict(dst=outs["d"], x=outs["gu"], W=Wd, bias=b), dict(dst=outs["s"], x=xs, W=Ws)]
+    gpu.linear_batch(calls)
+    torch.cuda.synchronize()
+    got = {k: v.cpu().numpy() for k, v in outs.items()}
+    for c in calls:  # the same linears one by one
+        gpu.linear(c["dst"], c["x"], c["W"], bias=c.get("bias"))
+    torch.cuda.synchronize()
+    for k, v in outs.items():
+        np.testing.assert_array_equal(got[k], v.cpu().numpy(), err_msg=k)

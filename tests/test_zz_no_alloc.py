@@ -10,7 +10,7 @@ a fresh process.
 import numpy as np
 import pytest
 
-from tests.common import TOL_MAX, TOL_MEAN, assert_parity, inputs
+from tests.common import TOL_MAX, TOL_MAX_PRODUCT, TOL_MEAN, TOL_MEAN_PRODUCT, assert_parity, inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -58,8 +58,12 @@ def test_noalloc_matches_envg_linear_twice(gpu, M, K, N, kind):
         outs.append(y.cpu().numpy())
     assert envg.stats()["workspace_bytes"] == ws_before, "the library workspace grew"
     assert torch.cuda.mem_get_info()[0] == free_before, "device memory was allocated"
+    # silu(g) * u multiplies two GEMM outputs, so it carries the product bound (tests/common.py);
+    # for M <= 8 envg_linear multiplies fp32 X exactly while this entry rounds X to bf16.
+    tmax, tmean = (TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT) if silu else (TOL_MAX, TOL_MEAN)
     for o in outs:
-        assert_parity(o, ref, TOL_MAX, TOL_MEAN, what=f"noalloc {M}x{K}x{N} {kind}")
+        assert_parity(o, ref, tmax, tmean, what=f"noalloc {M}x{K}x{N} {kind}")
+    np.testing.assert_array_equal(outs[0], outs[1])  # the second call reuses the scratch exactly
     W.free()
 
 
