@@ -228,7 +228,7 @@ def dist_setup():
 class Workload:
     """Device-resident weights, inputs and outputs of one workload on this rank."""
 
-    def __init__(self, items, world, rank, dev):
+    def __init__(self, items, world, rank, dev, gather="peer", force_p2p=False):
         import torch
 
         from invision_b200 import envg
@@ -237,6 +237,9 @@ class Workload:
         self.items, self.world, self.rank, self.dev = items, world, rank, dev
         self.envg = envg
         self.batch = True
+        self.gather = gather
+        self.force_p2p = force_p2p
+        self.sym = {}
         gen = torch.Generator(device=dev)
         self.W, self.b, self.x, self.y, self.shard, self.ys, self.gbuf = {}, {}, {}, {}, {}, {}, {}
         names = [it["name"] for it in items]
@@ -277,13 +280,26 @@ class Workload:
                 self.shard[name] = (n0, n1, per)
                 self.ys[name] = torch.zeros(M, per, device=dev)
                 self.gbuf[name] = torch.empty(world, M, per, device=dev)
+                if self.gather == "peer":
+                    import torch.distributed as dist
+                    import torch.distributed._symmetric_memory as symm_mem
+
+                    ysym = symm_mem.empty(M, out_cols(it), device=dev)
+                    h = symm_mem.rendezvous(ysym, dist.group.WORLD)
+                    mc = h.multicast_ptr if (h.has_multicast_support and not self.force_p2p) else 0
+                    self.sym[name] = (ysym, h, list(h.buffer_ptrs), mc)
             if it["x_from"] not in names:
                 gen.manual_seed(2000 + i)
                 self.x[name] = torch.randn(M, K, generator=gen, device=dev)
             self.y[name] = torch.empty(M, out_cols(it), device=dev)
 
     def input_of(self, it):
-        return self.x[it["name"]] if it["name"] in self.x else self.y[it["x_from"]]
+        if it["name"] in self.x:
+            return self.x[it["name"]]
+        return self.sym[it["x_from"]][0] if it["x_from"] in self.sym else self.y[it["x_from"]]
+
+    def out_of(self, name):
+        return self.sym[name][0] if name in self.sym else self.y[name]
 
     def run_item(self, it, gather=True):
         envg = self.envg
@@ -301,6 +317,14 @@ class Workload:
         from invision_b200.nsplit import gather_columns
 
         n0, n1, per = self.shard[name]
+        if gather and name in self.sym:
+            # all-gather fused into the epilogue: this rank's columns go to every rank's copy of Y
+            ysym, h, peers, mc = self.sym[name]
+            if n1 > n0:
+                envg.linear_nsplit(ysym, x, self.W[name], n0, peers=None if mc else peers, multicast=mc,
+                                   bias=self.b[name], sync=False)
+            h.barrier()
+            return
         if n1 - n0 == per:
             envg.linear(self.ys[name], x, self.W[name], bias=self.b[name], sync=False)
         elif n1 > n0:  # ragged last shard: compute into the first n1 - n0 columns
@@ -322,6 +346,7 @@ class Workload:
     def free(self):
         for w in self.W.values():
             w.free()
+        self.sym.clear()  # symmetric buffers go before the process group
 
 
 def capture(torch, fn):
@@ -344,7 +369,7 @@ def run_ours(args, items, desc, world, rank, local):
     torch.cuda.set_device(local)
     envg.init(local)
     dev = torch.device("cuda", local)
-    wl = Workload(items, world, rank, dev)
+    wl = Workload(items, world, rank, dev, gather=args.gather, force_p2p=args.p2p)
     wl.batch = not args.no_batch
     step_flops = float(sum(item_flops(it) for it in items))
 
@@ -459,8 +484,9 @@ def run_ours(args, items, desc, world, rank, local):
         main = {k: v for k, v in p.items() if k.startswith("k1") or k.startswith("k2") or k == "k_gemv"}
         mms = sum(v["ms"] for v in main.values()) / reps
         mbytes = sum(v["bytes"] for v in main.values()) / reps
+        rank_flops = item_flops(it) / (world if it["op"] == "linear" else 1)  # this rank's shard
         rec = {"kernel": "+".join(sorted(main)), "gemm_us": round(1e3 * mms, 2),
-               "gemm_tflops": round(item_flops(it) / (mms * 1e-3) / 1e12, 1) if mms else None,
+               "gemm_tflops": round(rank_flops / (mms * 1e-3) / 1e12, 1) if mms else None,
                "gemm_gbs": round(mbytes / (mms * 1e-3) / 1e9, 1) if mms else None}
         if world == 1 and not args.no_graph:
             g = capture(torch, lambda: [wl.run_item(it, gather=False) for _ in range(20)])
@@ -488,7 +514,10 @@ def run_ours(args, items, desc, world, rank, local):
                                       else "steps launched from the host"),
                            "api": "envg_linear_batch (one call per step)" if wl.batch and world == 1 else
                                   "envg_linear per linear",
-                           "parallelism": "single GPU" if world == 1 else f"N-split x{world} + NCCL all-gather",
+                           "parallelism": "single GPU" if world == 1 else (
+                               f"N-split x{world}, all-gather fused into the GEMM epilogue ("
+                               + ("NVLS multimem stores" if any(v[3] for v in wl.sym.values()) else "P2P stores")
+                               + ")" if args.gather == "peer" else f"N-split x{world} + NCCL all-gather"),
                            "arith": "fp32 activations rounded to bf16 (RNE), bf16 weights, fp32 accumulate",
                            "l2": "working set > 126 MB L2 (config 2: ~0.6 GB); no flush"},
                 "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "roofline": roofline,
@@ -619,12 +648,22 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(items, sample_seconds=12.0):
-    from oracle import oracle as O
+def use_all_host_threads():
+    """The CPU legs run on every host thread (torchrun exports OMP_NUM_THREADS=1, and the
+    reference's sgemm2 parallelises with OpenMP, which shares torch's runtime)."""
+    import torch
 
     threads = cpu_threads()
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    torch.set_num_threads(threads)
+    from oracle import oracle as O
+
     O.set_threads(threads)
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    return threads
+
+
+def cpu_baseline(items, sample_seconds=12.0):
+    threads = use_all_host_threads()
     wl = CpuWorkload(items)
     rows = wl.pick_rows(sample_seconds)
     t = time.perf_counter()
@@ -644,11 +683,7 @@ def run_reference(args, items, desc, world, rank):
     if not all(it["op"] == "linear" for it in items):
         print(json.dumps({"impl": "reference", "unavailable": "the CPU arm covers linear workloads only"}))
         return
-    from oracle import oracle as O
-
-    threads = cpu_threads()
-    O.set_threads(threads)
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    threads = use_all_host_threads()
     per_step = max(0.5, min(15.0, 150.0 / max(1, args.steps + args.warmup)))
     wl = CpuWorkload(items)
     rows = wl.pick_rows(per_step)
@@ -685,6 +720,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
     ap.add_argument("--no-batch", action="store_true", help="one envg_linear call per linear")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N>1: all-gather fused into the GEMM epilogue (peer/multicast stores) or NCCL")
+    ap.add_argument("--p2p", action="store_true", help="N>1 peer gather: P2P stores even where NVLS exists")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()

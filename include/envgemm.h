@@ -137,6 +137,21 @@ typedef struct envg_linear_desc {
  * earlier linear of the batch waits for it. */
 int envg_linear_batch(const envg_linear_desc* descs, int n, int flags);
 
+/* One rank's part of an N-split linear, with the all-gather fused into the GEMM epilogue.  The
+ * weight handle holds this rank's output-column shard (envg_weight_upload_shard); its outputs go
+ * to columns [col0, col0 + shard width) of Y (row stride ldy) on EVERY rank:
+ *   y_multicast != NULL: one multimem store per value to an NVLink multicast address (NVSwitch
+ *                        NVLS) bound to all ranks' copies of Y;
+ *   otherwise:           peer stores to each of y_peers[0 .. npeers) (every rank's copy of Y
+ *                        mapped into this process, this rank's included; npeers <= 8).
+ * y_local is this rank's copy (read for ENVG_EPI_GATED_RESIDUAL).  The transfer overlaps the
+ * remaining tiles, replacing the separate all-gather + reorder of the N-split.  Device pointers
+ * only; the caller synchronises the ranks (e.g. a symmetric-memory barrier) before Y is read.
+ * New with this library (the reference runs on one CPU). */
+int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float* y_multicast, int64_t ldy,
+                       int64_t col0, const float* x, envg_weight W, const float* bias, int64_t M,
+                       int64_t K, int64_t N, int epilogue, const float* gate, int flags);
+
 /* dst[batch, out_ch, outH, outW] = conv(src[batch, in_ch, H, W], W) + bias, NCHW, as
  * QNNConv2d (quicknn_kernels.pas:984-1010 -> quicknncpu.pas:1958-2132); outH/outW follow
  * QNNConv2DShape (quicknn_kernels.pas:984-988).  epilogue: ENVG_EPI_NONE/BIAS or ENVG_EPI_SILU. */

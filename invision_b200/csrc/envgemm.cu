@@ -253,7 +253,7 @@ int tmap_out_3d(CUtensorMap* tm, const float* base, uint64_t plane, uint64_t ch,
 
 // Picks the k1_gemm store path for a row-major Y (and builds its map for the TMA paths).
 int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY) {
-  if (!use_tma) {
+  if (!use_tma || e.nremote != 0) {  // N-split outputs leave through peer / multicast stores
     e.store_mode = STORE_COALESCED;
     return ENVG_OK;
   }
@@ -1159,6 +1159,55 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
     d->st.calls++;
     d->st.flops += fl;
   }
+  if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
+  return ENVG_OK;
+}
+
+int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float* y_multicast, int64_t ldy,
+                       int64_t col0, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K,
+                       int64_t N, int epilogue, const float* gate, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (!(flags & ENVG_DEVICE_PTRS)) return fail(ENVG_ERR_ARG, "envg_linear_nsplit: needs device pointers");
+  envg_linear_desc q{y_local, x, W, bias, M, K, N, epilogue, gate};
+  ENVG_TRY(check_linear_args(d, q));
+  const bool gu = W->layout == ENVG_LAYOUT_GATE_UP;
+  const int64_t n_out = gu ? N / 2 : N;
+  if (col0 < 0 || col0 + n_out > ldy) return fail(ENVG_ERR_ARG, "envg_linear_nsplit: columns [%lld, %lld) outside ldy %lld",
+                                                  (long long)col0, (long long)(col0 + n_out), (long long)ldy);
+  if (!y_multicast && (npeers < 1 || npeers > 8 || !y_peers))
+    return fail(ENVG_ERR_ARG, "envg_linear_nsplit: give a multicast address or 1..8 peer copies of Y");
+  if (M == 0) return ENVG_OK;
+  EpiArgs e = linear_epi(q);
+  e.ldy = ldy;
+  e.col_off = (int)col0;
+  bool aligned = (reinterpret_cast<uintptr_t>(y_local) & 15) == 0 && ldy % 4 == 0 && col0 % 4 == 0;
+  if (y_multicast) {
+    e.nremote = -1;
+    e.remote[0] = y_multicast;
+    aligned = aligned && (reinterpret_cast<uintptr_t>(y_multicast) & 15) == 0;
+  } else {
+    e.nremote = npeers;
+    for (int r = 0; r < npeers; ++r) {
+      if (!y_peers[r]) return fail(ENVG_ERR_ARG, "envg_linear_nsplit: peer copy %d is NULL", r);
+      e.remote[r] = y_peers[r];
+      aligned = aligned && (reinterpret_cast<uintptr_t>(y_peers[r]) & 15) == 0;
+    }
+  }
+  e.vec_ok = (aligned && n_out % 4 == 0) ? 1 : 0;
+  const double fl = 2.0 * (double)M * (double)N * (double)K;
+  const double ob = 4.0 * (double)M * n_out + (bias ? 4.0 * N : 0.0);
+  if (M <= d->gemv_max) {
+    ENVG_TRY(launch_gemv(d, x, M, K, W, gu, e, fl, 2.0 * (double)N * K + 4.0 * (double)M * K + ob));
+  } else {
+    ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
+    ENVG_TRY(launch_cast_rows(d, x, K, M, K, W->Kp, d->xb.p));
+    ENVG_TRY(gemm_device(d, d->xb.p, M, W->Kp, W->tm256, W->tm128, W->rows, gu, e, fl,
+                         2.0 * (double)N * K + 2.0 * (double)M * W->Kp + ob));
+  }
+  d->st.calls++;
+  d->st.flops += fl;
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
 }

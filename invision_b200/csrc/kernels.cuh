@@ -46,7 +46,35 @@ struct EpiArgs {
   int half_n;         // EPI_SILU_GATE: gate rows of the original W (up bias at half_n + col)
   int vec_ok;         // Y 16-byte aligned and ldy % 4 == 0
   int store_mode;     // k1_gemm: STORE_DIRECT, STORE_TMA or STORE_TMA_ADD
+  // N-split output (envg_linear_nsplit): every value goes to the same offset of each rank's copy
+  // of Y.  nremote = 0: Y only; > 0: P2P stores to remote[0 .. nremote); -1: one multimem store
+  // through the multicast address remote[0].  Column indices are shard-relative; col_off places
+  // them in the full Y (row stride ldy).  Reads of Y (residual) use the local copy Y.
+  float* remote[8];
+  int nremote;
+  int col_off;
 };
+
+// Write one value / four consecutive values (16-byte aligned) at element offset idx of Y, on
+// every copy the epilogue targets.
+ENVG_DEV void out_store1(const EpiArgs& e, int64_t idx, float v) {
+  if (e.nremote == 0) {
+    e.Y[idx] = v;
+  } else if (e.nremote < 0) {
+    multimem_st_f32(e.remote[0] + idx, v);
+  } else {
+    for (int r = 0; r < e.nremote; ++r) e.remote[r][idx] = v;
+  }
+}
+ENVG_DEV void out_store4(const EpiArgs& e, int64_t idx, float4 v) {
+  if (e.nremote == 0) {
+    *reinterpret_cast<float4*>(e.Y + idx) = v;
+  } else if (e.nremote < 0) {
+    multimem_st_v4(e.remote[0] + idx, v);
+  } else {
+    for (int r = 0; r < e.nremote; ++r) *reinterpret_cast<float4*>(e.remote[r] + idx) = v;
+  }
+}
 
 // How k1_gemm writes Y: per-thread global stores (one row per thread); 32x32 tiles staged in
 // shared memory and written by a TMA bulk store (clipped at the tensor edges) or added into Y by a
@@ -197,7 +225,8 @@ ENVG_DEV void store_tile32_rows(const EpiArgs& e, const uint8_t* buf, int lane, 
     if (grow >= e.m_valid) continue;
     const float4 t = *reinterpret_cast<const float4*>(buf + r * 128 + ((ch ^ (r & 7)) * 16));
     const int gcol = col0 + ch * 4;
-    float* yp = e.Y + (int64_t)grow * e.ldy + gcol;
+    const int64_t idx = (int64_t)grow * e.ldy + e.col_off + gcol;
+    const float* yp = e.Y + idx;
     float tv[4] = {t.x, t.y, t.z, t.w};
     if (e.vec_ok && gcol + 3 < e.n_out) {
       if (rmw) {
@@ -207,14 +236,14 @@ ENVG_DEV void store_tile32_rows(const EpiArgs& e, const uint8_t* buf, int lane, 
         for (int j = 0; j < 4; ++j)
           tv[j] = (e.mode == EPI_GATED_RES) ? __fadd_rn(ov[j], tv[j]) : __fadd_rn(tv[j], __fmul_rn(e.beta, ov[j]));
       }
-      *reinterpret_cast<float4*>(yp) = make_float4(tv[0], tv[1], tv[2], tv[3]);
+      out_store4(e, idx, make_float4(tv[0], tv[1], tv[2], tv[3]));
     } else {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (gcol + j >= e.n_out) break;
         float v = tv[j];
         if (rmw) v = (e.mode == EPI_GATED_RES) ? __fadd_rn(yp[j], v) : __fadd_rn(v, __fmul_rn(e.beta, yp[j]));
-        yp[j] = v;
+        out_store1(e, idx + j, v);
       }
     }
   }
@@ -588,6 +617,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
       if (acc == 0) aph ^= 1;
     }
     if (lane == 0) bulk_wait_all();
+    if (ep.nremote != 0) __threadfence_system();
   }
   __syncwarp();
   tc_fence_before();
@@ -886,6 +916,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       if (acc == 0) aph ^= 1;
     }
     if (lane == 0) bulk_wait_all();
+    if (ep.nremote != 0) __threadfence_system();  // peer / multicast stores ordered before the caller's barrier
   }
   __syncwarp();
   tc_fence_before();
@@ -1093,12 +1124,13 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
       }
       if (finalize) {
         const EpiArgs e = args.epi;
-        const int col = tile * BM + rowin;  // output column
+        const int col = tile * BM + rowin;  // output column (shard-relative)
         if (col < e.n_out) {
 #pragma unroll
           for (int m = 0; m < MPAD; ++m) {
             if (m >= e.m_valid) break;
-            float* yp = e.Y + (int64_t)m * e.ldy + col;
+            const int64_t idx = (int64_t)m * e.ldy + e.col_off + col;
+            float* yp = e.Y + idx;
             float v;
             if (R == 2) {
               float gv = acc[0][m], uv = acc[R - 1][m];
@@ -1110,9 +1142,10 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
             } else {
               v = epi_value(e, acc[0][m], m, col, yp);
             }
-            *yp = v;
+            out_store1(e, idx, v);
           }
         }
+        if (e.nremote != 0) __threadfence_system();
       }
     }
     tc_fence_before();
@@ -1262,7 +1295,7 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
         g = __fadd_rn(g, __ldg(e.bias + col));
         u = __fadd_rn(u, __ldg(e.bias + e.half_n + col));
       }
-      e.Y[(int64_t)m * e.ldy + col] = __fmul_rn(silu_f(g), u);
+      out_store1(e, (int64_t)m * e.ldy + e.col_off + col, __fmul_rn(silu_f(g), u));
     }
   } else {
     for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) {
@@ -1270,10 +1303,11 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
       if (m >= a.M) continue;
       const int col = group * 64 + r;
       if (col >= e.n_out) continue;
-      float* yp = e.Y + (int64_t)m * e.ldy + col;
-      *yp = epi_value(e, s_sum[m][r], m, col, yp);
+      const int64_t idx = (int64_t)m * e.ldy + e.col_off + col;
+      out_store1(e, idx, epi_value(e, s_sum[m][r], m, col, e.Y + idx));
     }
   }
+  if (e.nremote != 0) __threadfence_system();
 }
 
 // ------------------------------------------------------------------------------------------

@@ -277,6 +277,18 @@ ENVG_DEV void umma_commit_pair(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+// ---- NVLink multicast (NVLS) -------------------------------------------------------------
+// A store to a multicast address is replicated by the NVSwitch into the same offset of every
+// GPU's buffer bound to that multicast object.
+ENVG_DEV void multimem_st_v4(float* mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+ENVG_DEV void multimem_st_f32(float* mc, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
+}
+
 // Named barrier among `n` threads (ids 1..15; 0 is __syncthreads).
 ENVG_DEV void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 

@@ -77,6 +77,8 @@ def lib():
         L.envg_linear.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_noalloc.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_batch.argtypes = [ctypes.POINTER(LinearDesc), _ci, _ci]
+        L.envg_linear_nsplit.argtypes = [_vp, ctypes.POINTER(_vp), _ci, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64,
+                                         _i64, _ci, _vp, _ci]
         L.envg_conv2d.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 11
         L.envg_sgemm.argtypes = [_ci, _ci, _ci, _i64, _i64, _i64, ctypes.c_float, _vp, _i64, _vp, _i64,
                                  ctypes.c_float, _vp, _i64]
@@ -292,6 +294,22 @@ def linear_batch(calls, sync=True):
         keep.append(c)
     flags = DEVICE_PTRS | (0 if sync else ASYNC)
     return _check(lib().envg_linear_batch(arr, len(calls), flags))
+
+
+def linear_nsplit(y_local, x, W, col0, peers=None, multicast=0, bias=None, epilogue=None, gate=None, sync=True):
+    """This rank's shard of an N-split linear, writing its columns [col0, col0 + width) into every
+    rank's copy of Y (torch CUDA tensors; `peers` = list of int device pointers of all ranks' Y,
+    `multicast` = NVLS multicast address or 0).  Synchronise the ranks before reading Y."""
+    if epilogue is None:
+        epilogue = EPI_SILU_GATE if W.layout == LAYOUT_GATE_UP else (EPI_BIAS if bias is not None else EPI_NONE)
+    _mode(y_local, x, bias, gate)
+    M, K = x.shape
+    ldy = y_local.shape[1]
+    plist = list(peers or [])
+    arr = (_vp * max(1, len(plist)))(*[_vp(p) for p in plist]) if plist else None
+    flags = DEVICE_PTRS | (0 if sync else ASYNC)
+    return _check(lib().envg_linear_nsplit(_ptr(y_local), arr, len(plist), _vp(multicast) if multicast else None, ldy,
+                                           col0, _ptr(x), W.h, _ptr(bias), M, K, W.N, epilogue, _ptr(gate), flags))
 
 
 def conv2d(dst, src, W, bias, stride, pad, epilogue=None, sync=True):

@@ -1,0 +1,105 @@
+"""GPU, 2 ranks (skipped with fewer GPUs): the N-split with the all-gather fused into the GEMM
+epilogue (envg_linear_nsplit).  Each rank holds one output-column shard of W and writes its
+columns into both ranks' copies of Y -- by peer stores and, where the NVSwitch offers it, by one
+NVLS multimem store -- and every rank then holds the full Y, bit-identical to the unsplit
+linear computed on one GPU."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import sys
+    from datetime import timedelta
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+
+    from invision_b200 import envg
+    from invision_b200.nsplit import shard_bounds
+    from tests.common import inputs
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    results = []
+    try:
+        envg.init(rank)
+        dev = torch.device("cuda", rank)
+        for (M, K, N, gate_up) in [(300, 512, 1040, False), (257, 256, 2 * 392, True), (40, 1024, 768, False),
+                                   (5, 768, 520, False)]:
+            x, w, b = inputs(M, K, N, seed=M + K + N)
+            half = N // 2 if gate_up else N
+            n0, n1, per = shard_bounds(half, world, rank, 128)
+            layout = envg.LAYOUT_GATE_UP if gate_up else envg.LAYOUT_PLAIN
+            Ws = envg.Weight(w, layout=layout, shard=(n0, n1))
+            bs = np.concatenate([b[n0:n1], b[half + n0:half + n1]]) if gate_up else b[n0:n1]
+            xt = torch.from_numpy(x).to(dev)
+            bt = torch.from_numpy(np.ascontiguousarray(bs)).to(dev)
+            Y = symm_mem.empty(M, half, device=dev)
+            hdl = symm_mem.rendezvous(Y, dist.group.WORLD)
+            modes = [("p2p", list(hdl.buffer_ptrs), 0)]
+            if hdl.has_multicast_support and hdl.multicast_ptr:
+                modes.append(("multicast", None, hdl.multicast_ptr))
+            Wf = envg.Weight(w, layout=layout)
+            ref = torch.empty(M, half, device=dev)
+            envg.linear(ref, xt, Wf, bias=torch.from_numpy(b).to(dev))
+            torch.cuda.synchronize()
+            for name, peers, mc in modes:
+                Y.fill_(float("nan"))
+                torch.cuda.synchronize()
+                hdl.barrier()
+                envg.linear_nsplit(Y, xt, Ws, n0, peers=peers, multicast=mc, bias=bt)
+                torch.cuda.synchronize()
+                hdl.barrier()
+                ok = bool(torch.equal(Y, ref))
+                results.append((f"{name} {M}x{K}x{N} gate_up={gate_up}", ok))
+            Ws.free()
+            Wf.free()
+            del Y, hdl
+        if rank == 0:
+            q.put(results)
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def test_nsplit_fused_gather_two_ranks():
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    res = q.get(timeout=5)
+    bad = [name for name, ok in res if not ok]
+    assert not bad and len(res) >= 4, res
