@@ -369,7 +369,7 @@ def run_ours(args, items, desc, world, rank, local):
     torch.cuda.set_device(local)
     envg.init(local)
     dev = torch.device("cuda", local)
-    wl = Workload(items, world, rank, dev, gather=args.gather, force_p2p=args.p2p)
+    wl = Workload(items, world, rank, dev, gather=args.gather, force_p2p=not args.multicast)
     wl.batch = not args.no_batch
     step_flops = float(sum(item_flops(it) for it in items))
 
@@ -722,7 +722,9 @@ def main():
     ap.add_argument("--no-batch", action="store_true", help="one envg_linear call per linear")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="N>1: all-gather fused into the GEMM epilogue (peer/multicast stores) or NCCL")
-    ap.add_argument("--p2p", action="store_true", help="N>1 peer gather: P2P stores even where NVLS exists")
+    ap.add_argument("--multicast", action="store_true",
+                    help="N>1 peer gather through an NVLS multicast address (default: P2P stores, which load each "
+                         "GPU's NVLink ingress less: multicast also returns the local copy through the switch)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()

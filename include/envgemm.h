@@ -109,6 +109,43 @@ int envg_conv_weight_upload(const uint16_t* w_bf16, const float* w_f32, int out_
 
 int envg_weight_free(envg_weight w);
 
+/* ---- weights straight from a .safetensors file ---------------------------------------------
+ * Replace TSafeTensorFile.open (safetensor.pas:466-513) + getTensorDataMemBlock /
+ * getTensorDataMemBlockBF16 (safetensor.pas:584-683), which map the file and then widen each
+ * BF16/F16 weight to fp32 on the host for every linear.  Here the tensor's bytes are read from
+ * the mapped file and go to HBM once, as bf16. */
+#define ENVG_DTYPE_OTHER 0 /* any safetensors dtype other than the three below                   */
+#define ENVG_DTYPE_BF16 1
+#define ENVG_DTYPE_F16 2
+#define ENVG_DTYPE_F32 3
+
+typedef struct envg_tensor_info {
+  int dtype;          /* ENVG_DTYPE_*                                                          */
+  int ndim;           /* number of dimensions (<= 8)                                           */
+  int64_t shape[8];   /* row-major shape; unused entries 0                                      */
+  int64_t offset;     /* absolute byte offset of the tensor's data in the file                 */
+  int64_t nbytes;     /* data_offsets[1] - data_offsets[0]                                      */
+  char dtype_name[16];/* the dtype string as written in the header ("BF16", "F8_E4M3", ...)    */
+} envg_tensor_info;
+
+/* Header query; reads only the file's header and needs no GPU or envg_init.  Mirrors
+ * TSafeTensorFile.find (safetensor.pas:525-531): ENVG_ERR_ARG when the tensor is absent or the
+ * header is malformed (message in envg_last_error). */
+int envg_safetensors_tensor_info(const char* path, const char* name, envg_tensor_info* out);
+
+/* Reads tensor `name` widened to fp32 into host memory dst[count] (count = the element count).
+ * BF16 -> fp32 is `bits << 16` (BF16ToSingle, quicknn_common.pas:1991-2008); F16 -> fp32 is the
+ * exact IEEE widening (FP16ToSingle); F32 is copied.  For biases, norms and modulation vectors,
+ * which stay on the host side of the boundary.  Needs no GPU. */
+int envg_safetensors_read_f32(const char* path, const char* name, float* dst, int64_t count);
+
+/* Uploads tensor `name` as a device weight.  2-D tensors [N, K] become a linear weight with
+ * `layout_flags` (shard rows [n0, n1) as envg_weight_upload_shard; n0 = n1 = 0 means all rows);
+ * 4-D tensors [out_ch, in_ch, kH, kW] become a convolution weight (n0 = n1 = 0 required).
+ * BF16 bits are kept; F16 and F32 are rounded to bf16 (RNE), as envg_weight_upload does. */
+int envg_weight_upload_safetensors(const char* path, const char* name, int layout_flags, int64_t n0,
+                                   int64_t n1, envg_weight* out);
+
 /* Y = epilogue(X . W^T).  Mirrors QNNLinear(dst, x, W, B, seqLen, inDIM, outDIM)
  * (quicknn_kernels.pas:897-911 -> quicknncpu.pas:1807-1820) with M = seqLen, K = inDIM,
  * N = outDIM, and QNNLINEAR_BF16_OR_F32 / QNNLinearNoBias (quicknn_kernels.pas:2093-2103,
@@ -158,6 +195,18 @@ int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float*
 int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, int in_ch,
                 int out_ch, int H, int W_, int kH, int kW, int stride, int pad, int batch,
                 int epilogue, int flags);
+
+/* The modulated linear of the FLUX blocks: QNNAdaLN (quicknn_kernels.pas:315 ->
+ * quicknncpu.pas:3042-3060; call sites quicknn_transformers.pas:1400,1410,1440,1449,1500) followed
+ * by QNNLinear, with the normalisation fused into the activation cast:
+ *   xn[r][k] = (1 + scale[k]) * (x[r][k] - mean_r) / sqrt(var_r + 1e-6) + shift[k]
+ *   dst = epilogue(xn . W^T)
+ * mean_r / var_r are the row mean and population variance (QNNMean :679, QNNVariance :687); 1e-6
+ * is EPSILON (quicknn_common.pas:51), which QNNAdaLN's body uses.  shift, scale: fp32 [K]; other
+ * arguments and flags as envg_linear. */
+int envg_linear_adaln(float* dst, const float* x, const float* shift, const float* scale, envg_weight W,
+                      const float* bias, int64_t M, int64_t K, int64_t N, int epilogue, const float* gate,
+                      int flags);
 
 /* Allocation-free linear for skinny M.  This entry point has no counterpart in the reference.
  *

@@ -55,6 +55,27 @@ class QNNWeight {
     w.kW_ = kW;
     return w;
   }
+  // Tensor `name` of a .safetensors file (TSafeTensorFiles.getTensorDataMemBlockBF16,
+  // safetensor.pas:650-683, then upload): 2-D [N, K] -> linear weight, 4-D -> conv weight.
+  static QNNWeight from_safetensors(const char* path, const char* name, int layout = ENVG_LAYOUT_PLAIN) {
+    envg_tensor_info info;
+    check(envg_safetensors_tensor_info(path, name, &info), "QNNWeight safetensors");
+    QNNWeight w;
+    check(envg_weight_upload_safetensors(path, name, layout, 0, 0, &w.h_), "QNNWeight safetensors upload");
+    w.N_ = info.shape[0];
+    w.layout_ = layout;
+    if (info.ndim == 4) {
+      w.conv_ = true;
+      w.out_ch_ = (int)info.shape[0];
+      w.in_ch_ = (int)info.shape[1];
+      w.kH_ = (int)info.shape[2];
+      w.kW_ = (int)info.shape[3];
+      w.K_ = info.shape[1] * info.shape[2] * info.shape[3];
+    } else {
+      w.K_ = info.shape[1];
+    }
+    return w;
+  }
   QNNWeight(const QNNWeight&) = delete;
   QNNWeight& operator=(const QNNWeight&) = delete;
   QNNWeight(QNNWeight&& o) noexcept { *this = static_cast<QNNWeight&&>(o); }

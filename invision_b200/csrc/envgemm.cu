@@ -12,10 +12,14 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <fcntl.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <mutex>
@@ -24,6 +28,7 @@
 
 #include "../../include/envgemm.h"
 #include "kernels.cuh"
+#include "safetensors.hpp"
 
 using namespace envg;
 
@@ -74,7 +79,7 @@ struct Dev {
   int sms = 0;
   cudaStream_t own = nullptr;
   cudaStream_t user = nullptr;
-  Buf x, y, xb, wb, part, cnt, bias, gate, act, col, b32, xbatch;
+  Buf x, y, xb, wb, part, cnt, bias, gate, act, col, b32, xbatch, ada, xn;
   cudaStream_t aux = nullptr;              // second stream of envg_linear_batch
   std::vector<cudaEvent_t> batch_events;   // reused event pool of envg_linear_batch
   int* h_status = nullptr;  // mapped pinned: [0] status code, [1] wait site
@@ -88,7 +93,7 @@ struct Dev {
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
-           col.bytes + b32.bytes + xbatch.bytes;
+           col.bytes + b32.bytes + xbatch.bytes + ada.bytes + xn.bytes;
   }
 };
 
@@ -98,12 +103,13 @@ int g_cur = -1;
 
 // ---- optional per-launch timing (envg_profile) ---------------------------------------------
 enum KernelId {
-  KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_TRANSPOSE, KID_IM2COL, KID_SELFTEST,
-  KID_COUNT
+  KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_ADALN, KID_TRANSPOSE, KID_IM2COL,
+  KID_SELFTEST, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate", "k1_gemm_conv",
                                              "k2_skinny",   "k_gemv",            "k_cast_rows",
-                                             "k_transpose_cast", "k_im2col_nhwc", "k_wait_selftest"};
+                                             "k_adaln",     "k_transpose_cast",  "k_im2col_nhwc",
+                                             "k_wait_selftest"};
 struct KAcc {
   uint64_t launches = 0;
   double ms = 0, flops = 0, bytes = 0;
@@ -281,12 +287,42 @@ uint16_t f32_to_bf16_rne(float f) {
   return (uint16_t)(u >> 16);
 }
 
-// Reads element (r, k) of the caller's weight as bf16 bits.
+// IEEE binary16 -> binary32 (exact; subnormals normalised, Inf/NaN kept).
+float f16_to_f32(uint16_t h) {
+  const uint32_t s = (uint32_t)(h & 0x8000u) << 16;
+  int e = (h >> 10) & 0x1f;
+  uint32_t m = h & 0x3ffu, u;
+  if (e == 31) {
+    u = s | 0x7f800000u | (m << 13);
+  } else if (e != 0) {
+    u = s | ((uint32_t)(e + 112) << 23) | (m << 13);
+  } else if (m == 0) {
+    u = s;
+  } else {
+    e = 1;
+    while (!(m & 0x400u)) {
+      m <<= 1;
+      --e;
+    }
+    u = s | ((uint32_t)(e + 112) << 23) | ((m & 0x3ffu) << 13);
+  }
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+// Reads element (r, k) of the caller's weight as bf16 bits: b = bf16 bits, f = fp32,
+// h = IEEE half bits (exactly one is set).
 struct WSrc {
   const uint16_t* b;
   const float* f;
   int64_t ld;
-  uint16_t at(int64_t r, int64_t k) const { return b ? b[r * ld + k] : f32_to_bf16_rne(f[r * ld + k]); }
+  const uint16_t* h = nullptr;
+  uint16_t at(int64_t r, int64_t k) const {
+    if (b) return b[r * ld + k];
+    if (h) return f32_to_bf16_rne(f16_to_f32(h[r * ld + k]));
+    return f32_to_bf16_rne(f[r * ld + k]);
+  }
 };
 
 }  // namespace
@@ -487,6 +523,17 @@ int launch_gemv(Dev* d, const float* X, int64_t M, int64_t K, envg_weight W, boo
   return ENVG_OK;
 }
 
+// QNNAdaLN (EPSILON = 1e-6, quicknn_common.pas:51) fused with the bf16 cast, or into fp32.
+int launch_adaln(Dev* d, const float* x, int64_t rows, int64_t K, int64_t Kp, const float* shift, const float* scale,
+                 void* out, bool bf16) {
+  if (rows == 0) return ENVG_OK;
+  ProfScope ps(stream_of(d), KID_ADALN, 0.0, (double)rows * K * 4 + (double)rows * Kp * (bf16 ? 2 : 4) + 8.0 * K);
+  k_adaln<<<(unsigned)rows, 256, 0, stream_of(d)>>>(x, K, (int)K, (int)Kp, shift, scale, 1e-6f, out, bf16 ? 1 : 0);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
 int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t K, int64_t Kp, void* xb) {
   if (rows == 0) return ENVG_OK;
   const int vec8 = (K == Kp && K % 8 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
@@ -617,6 +664,119 @@ int upload_common(Dev* d, WSrc src, int64_t N, int64_t K, int64_t n0, int64_t n1
   return ENVG_OK;
 }
 
+int conv_upload_common(Dev* d, WSrc src, int out_ch, int in_ch, int kH, int kW, envg_weight* out) {
+  if (!out) return fail(ENVG_ERR_ARG, "out handle pointer is NULL");
+  *out = nullptr;
+  if (out_ch <= 0 || in_ch <= 0 || kH <= 0 || kW <= 0)
+    return fail(ENVG_ERR_ARG, "conv weight shape [%d, %d, %d, %d] invalid", out_ch, in_ch, kH, kW);
+  // Device layout W'[out_ch][kH][kW][Cp] (Cp = in_ch rounded up to 64, zero filled): the
+  // reduction index becomes (kh, kw, c), matching the NHWC activation tiles.
+  auto* w = new envg_weight_s();
+  w->magic = WEIGHT_MAGIC;
+  w->dev = d->id;
+  w->conv = true;
+  w->out_ch = out_ch;
+  w->in_ch = in_ch;
+  w->kH = kH;
+  w->kW = kW;
+  w->Cp = (int)rup(in_ch, BK);
+  w->K = (int64_t)in_ch * kH * kW;
+  w->Kp = (int64_t)kH * kW * w->Cp;
+  w->N = out_ch;
+  w->rows = out_ch;
+  w->layout = ENVG_LAYOUT_PLAIN;
+  std::vector<uint16_t> host((size_t)(w->rows * w->Kp), 0);
+  for (int o = 0; o < out_ch; ++o)
+    for (int c = 0; c < in_ch; ++c)
+      for (int kh = 0; kh < kH; ++kh)
+        for (int kw = 0; kw < kW; ++kw)
+          host[(size_t)(o * w->Kp + ((int64_t)kh * kW + kw) * w->Cp + c)] = src.at(o, ((int64_t)c * kH + kh) * kW + kw);
+  int rc = finish_weight(d, w, host);
+  if (rc != ENVG_OK) {
+    if (w->d) cudaFree(w->d);
+    w->magic = 0;
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return ENVG_OK;
+}
+
+
+// A read-only mapping of a whole file (the reference maps its safetensors files the same way,
+// safetensor.pas:275-326).
+struct MappedFile {
+  void* p = MAP_FAILED;
+  size_t size = 0;
+  ~MappedFile() {
+    if (p != MAP_FAILED) munmap(p, size);
+  }
+  int open(const char* path) {
+    const int fd = ::open(path, O_RDONLY);
+    if (fd < 0) return fail(ENVG_ERR_ARG, "cannot open %s", path);
+    struct stat st;
+    if (fstat(fd, &st) != 0 || st.st_size <= 0) {
+      ::close(fd);
+      return fail(ENVG_ERR_ARG, "cannot stat %s", path);
+    }
+    size = (size_t)st.st_size;
+    p = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+    ::close(fd);
+    if (p == MAP_FAILED) return fail(ENVG_ERR_OOM, "mmap of %s (%zu bytes) failed", path, size);
+    return ENVG_OK;
+  }
+};
+
+int st_dtype(const std::string& dt) {
+  if (dt == "BF16") return ENVG_DTYPE_BF16;
+  if (dt == "F16") return ENVG_DTYPE_F16;
+  if (dt == "F32") return ENVG_DTYPE_F32;
+  return ENVG_DTYPE_OTHER;
+}
+
+// Finds `name` and checks that its byte count matches dtype x shape.  *count = element count.
+int st_lookup(const char* path, const char* name, envg_st::TensorInfo* ti, int64_t* count) {
+  if (!path || !name) return fail(ENVG_ERR_ARG, "path and tensor name must be set");
+  const std::string why = envg_st::find_tensor(path, name, ti);
+  if (!why.empty()) return fail(ENVG_ERR_ARG, "safetensors %s: %s", path, why.c_str());
+  if (ti->shape.size() > 8) return fail(ENVG_ERR_UNSUPPORTED, "tensor %s has %zu dims (> 8)", name, ti->shape.size());
+  int64_t n = 1;
+  for (int64_t v : ti->shape) {
+    if (v < 0) return fail(ENVG_ERR_ARG, "tensor %s has a negative dimension", name);
+    n *= v;
+  }
+  *count = n;
+  const int64_t eb = envg_st::dtype_bytes(ti->dtype);
+  if (eb && n * eb != ti->end - ti->begin)
+    return fail(ENVG_ERR_ARG, "tensor %s: %lld bytes of data for %lld elements of %s", name,
+                (long long)(ti->end - ti->begin), (long long)n, ti->dtype.c_str());
+  return ENVG_OK;
+}
+
+// Maps the file and points `src` at the tensor's data.  Data that is not aligned to its element
+// size (the format does not promise it) is copied into `copy` first.
+int st_source(const char* path, const envg_st::TensorInfo& ti, int64_t ld, MappedFile* mf,
+              std::vector<uint32_t>* copy, WSrc* src) {
+  ENVG_TRY(mf->open(path));
+  const int dt = st_dtype(ti.dtype);
+  if (dt == ENVG_DTYPE_OTHER)
+    return fail(ENVG_ERR_UNSUPPORTED, "tensor dtype %s cannot be uploaded (BF16, F16 or F32 only)", ti.dtype.c_str());
+  const size_t nbytes = (size_t)(ti.end - ti.begin);
+  const unsigned char* base = static_cast<const unsigned char*>(mf->p) + ti.data_start + ti.begin;
+  const void* data = base;
+  const size_t align = dt == ENVG_DTYPE_F32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(base) % align) {
+    copy->assign((nbytes + 3) / 4, 0);
+    memcpy(copy->data(), base, nbytes);
+    data = copy->data();
+  }
+  *src = WSrc{nullptr, nullptr, ld};
+  if (dt == ENVG_DTYPE_BF16) src->b = static_cast<const uint16_t*>(data);
+  if (dt == ENVG_DTYPE_F16) src->h = static_cast<const uint16_t*>(data);
+  if (dt == ENVG_DTYPE_F32) src->f = static_cast<const float*>(data);
+  return ENVG_OK;
+}
+
 const char* epi_name(int e) {
   switch (e) {
     case ENVG_EPI_NONE: return "NONE";
@@ -713,7 +873,7 @@ int envg_shutdown(void) {
   if (!d) return ENVG_OK;
   cudaStreamSynchronize(stream_of(d));
   Buf* bufs[] = {&d->x,    &d->y,   &d->xb,  &d->wb,  &d->part,  &d->cnt,
-                 &d->bias, &d->gate, &d->act, &d->col, &d->b32, &d->xbatch};
+                 &d->bias, &d->gate, &d->act, &d->col, &d->b32, &d->xbatch, &d->ada, &d->xn};
   for (Buf* b : bufs) {
     if (b->p) cudaFree(b->p);
     *b = Buf{};
@@ -792,40 +952,7 @@ int envg_conv_weight_upload(const uint16_t* w_bf16, const float* w_f32, int out_
   if (!out) return fail(ENVG_ERR_ARG, "out handle pointer is NULL");
   *out = nullptr;
   if ((w_bf16 == nullptr) == (w_f32 == nullptr)) return fail(ENVG_ERR_ARG, "exactly one of w_bf16 / w_f32 must be set");
-  if (out_ch <= 0 || in_ch <= 0 || kH <= 0 || kW <= 0)
-    return fail(ENVG_ERR_ARG, "conv weight shape [%d, %d, %d, %d] invalid", out_ch, in_ch, kH, kW);
-  // Device layout W'[out_ch][kH][kW][Cp] (Cp = in_ch rounded up to 64, zero filled): the
-  // reduction index becomes (kh, kw, c), matching the NHWC activation tiles.
-  auto* w = new envg_weight_s();
-  w->magic = WEIGHT_MAGIC;
-  w->dev = d->id;
-  w->conv = true;
-  w->out_ch = out_ch;
-  w->in_ch = in_ch;
-  w->kH = kH;
-  w->kW = kW;
-  w->Cp = (int)rup(in_ch, BK);
-  w->K = (int64_t)in_ch * kH * kW;
-  w->Kp = (int64_t)kH * kW * w->Cp;
-  w->N = out_ch;
-  w->rows = out_ch;
-  w->layout = ENVG_LAYOUT_PLAIN;
-  std::vector<uint16_t> host((size_t)(w->rows * w->Kp), 0);
-  WSrc src{w_bf16, w_f32, w->K};
-  for (int o = 0; o < out_ch; ++o)
-    for (int c = 0; c < in_ch; ++c)
-      for (int kh = 0; kh < kH; ++kh)
-        for (int kw = 0; kw < kW; ++kw)
-          host[(size_t)(o * w->Kp + ((int64_t)kh * kW + kw) * w->Cp + c)] = src.at(o, ((int64_t)c * kH + kh) * kW + kw);
-  int rc = finish_weight(d, w, host);
-  if (rc != ENVG_OK) {
-    if (w->d) cudaFree(w->d);
-    w->magic = 0;
-    delete w;
-    return rc;
-  }
-  *out = w;
-  return ENVG_OK;
+  return conv_upload_common(d, WSrc{w_bf16, w_f32, (int64_t)in_ch * kH * kW}, out_ch, in_ch, kH, kW, out);
 }
 
 int envg_weight_free(envg_weight w) {
@@ -840,11 +967,81 @@ int envg_weight_free(envg_weight w) {
   return ENVG_OK;
 }
 
-int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,
-                int epilogue, const float* gate, int flags) {
+int envg_safetensors_tensor_info(const char* path, const char* name, envg_tensor_info* out) {
+  if (!out) return fail(ENVG_ERR_ARG, "info pointer is NULL");
+  memset(out, 0, sizeof(*out));
+  envg_st::TensorInfo ti;
+  int64_t count = 0;
+  ENVG_TRY(st_lookup(path, name, &ti, &count));
+  out->dtype = st_dtype(ti.dtype);
+  out->ndim = (int)ti.shape.size();
+  for (size_t i = 0; i < ti.shape.size(); ++i) out->shape[i] = ti.shape[i];
+  out->offset = ti.data_start + ti.begin;
+  out->nbytes = ti.end - ti.begin;
+  snprintf(out->dtype_name, sizeof(out->dtype_name), "%s", ti.dtype.c_str());
+  return ENVG_OK;
+}
+
+int envg_safetensors_read_f32(const char* path, const char* name, float* dst, int64_t count) {
+  if (!dst && count) return fail(ENVG_ERR_ARG, "dst is NULL");
+  envg_st::TensorInfo ti;
+  int64_t n = 0;
+  ENVG_TRY(st_lookup(path, name, &ti, &n));
+  if (n != count)
+    return fail(ENVG_ERR_ARG, "tensor %s has %lld elements, dst holds %lld", name, (long long)n, (long long)count);
+  MappedFile mf;
+  std::vector<uint32_t> copy;
+  WSrc src{};
+  ENVG_TRY(st_source(path, ti, 0, &mf, &copy, &src));
+  for (int64_t i = 0; i < n; ++i) {
+    if (src.b) {
+      const uint32_t u = (uint32_t)src.b[i] << 16;
+      memcpy(&dst[i], &u, 4);
+    } else if (src.h) {
+      dst[i] = f16_to_f32(src.h[i]);
+    } else {
+      dst[i] = src.f[i];
+    }
+  }
+  return ENVG_OK;
+}
+
+int envg_weight_upload_safetensors(const char* path, const char* name, int layout_flags, int64_t n0, int64_t n1,
+                                   envg_weight* out) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!out) return fail(ENVG_ERR_ARG, "out handle pointer is NULL");
+  *out = nullptr;
   Dev* d = cur();
   if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  envg_st::TensorInfo ti;
+  int64_t n = 0;
+  ENVG_TRY(st_lookup(path, name, &ti, &n));
+  const size_t nd = ti.shape.size();
+  if (nd != 2 && nd != 4)
+    return fail(ENVG_ERR_ARG, "tensor %s has %zu dims; a weight is 2-D [N, K] or 4-D [O, C, kH, kW]", name, nd);
+  const int64_t N = ti.shape[0], K = n / std::max<int64_t>(1, N);
+  MappedFile mf;
+  std::vector<uint32_t> copy;
+  WSrc src{};
+  ENVG_TRY(st_source(path, ti, K, &mf, &copy, &src));
+  if (nd == 4) {
+    if (n0 != 0 || n1 != 0) return fail(ENVG_ERR_ARG, "convolution weights are uploaded whole (n0 = n1 = 0)");
+    if (layout_flags != ENVG_LAYOUT_PLAIN) return fail(ENVG_ERR_ARG, "convolution weights take ENVG_LAYOUT_PLAIN");
+    for (int i = 0; i < 4; ++i)
+      if (ti.shape[i] <= 0 || ti.shape[i] > INT32_MAX) return fail(ENVG_ERR_ARG, "conv weight %s: bad shape", name);
+    return conv_upload_common(d, src, (int)ti.shape[0], (int)ti.shape[1], (int)ti.shape[2], (int)ti.shape[3], out);
+  }
+  if (n0 == 0 && n1 == 0) n1 = layout_flags == ENVG_LAYOUT_GATE_UP ? N / 2 : N;
+  return upload_common(d, src, N, K, n0, n1, layout_flags, out);
+}
+
+}  // extern "C"
+
+namespace {
+// envg_linear and envg_linear_adaln.  With ad_shift / ad_scale set, X is first normalised per row
+// and modulated (QNNAdaLN) inside the activation-cast kernel.
+int linear_core(Dev* d, float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,
+                int epilogue, const float* gate, int flags, const float* ad_shift, const float* ad_scale) {
   ENVG_TRY(check_weight(d, W));
   if (W->conv) return fail(ENVG_ERR_ARG, "envg_linear: handle holds a convolution weight");
   if (M < 0) return fail(ENVG_ERR_ARG, "envg_linear: M=%lld < 0", (long long)M);
@@ -870,9 +1067,18 @@ int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, in
   const int64_t n_out = gu ? N / 2 : N;
   cudaStream_t s = stream_of(d);
 
-  const float *dx = x, *dbias = bias, *dgate = gate;
+  const float *dx = x, *dbias = bias, *dgate = gate, *dshift = ad_shift, *dscale = ad_scale;
   float* dy = dst;
   if (!devp) {
+    if (ad_shift) {
+      ENVG_TRY(ensure(d, d->ada, (size_t)(2 * K) * 4));
+      float* a = reinterpret_cast<float*>(d->ada.p);
+      ENVG_CUDA(cudaMemcpyAsync(a, ad_shift, (size_t)K * 4, cudaMemcpyHostToDevice, s));
+      ENVG_CUDA(cudaMemcpyAsync(a + K, ad_scale, (size_t)K * 4, cudaMemcpyHostToDevice, s));
+      d->st.h2d_bytes += (double)(2 * K) * 4;
+      dshift = a;
+      dscale = a + K;
+    }
     ENVG_TRY(ensure(d, d->x, (size_t)(M * K) * 4));
     ENVG_TRY(ensure(d, d->y, (size_t)(M * n_out) * 4));
     ENVG_CUDA(cudaMemcpyAsync(d->x.p, x, (size_t)(M * K) * 4, cudaMemcpyHostToDevice, s));
@@ -911,11 +1117,17 @@ int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, in
   const double out_bytes = 4.0 * (double)M * n_out + (dbias ? 4.0 * N : 0.0) +
                            (epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)M * n_out + 4.0 * N : 0.0);
   if (M <= d->gemv_max) {
+    if (dshift) {  // normalised X kept in fp32 for the CUDA-core path
+      ENVG_TRY(ensure(d, d->xn, (size_t)(M * K) * 4));
+      ENVG_TRY(launch_adaln(d, dx, M, K, K, dshift, dscale, d->xn.p, false));
+      dx = reinterpret_cast<const float*>(d->xn.p);
+    }
     // fp32 X read directly: W once, X once per 64-row group (from L2)
     ENVG_TRY(launch_gemv(d, dx, M, K, W, gu, e, lin_flops, 2.0 * (double)N * K + 4.0 * (double)M * K + out_bytes));
   } else {
     ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
-    ENVG_TRY(launch_cast_rows(d, dx, K, M, K, W->Kp, d->xb.p));
+    if (dshift) ENVG_TRY(launch_adaln(d, dx, M, K, W->Kp, dshift, dscale, d->xb.p, true));
+    else ENVG_TRY(launch_cast_rows(d, dx, K, M, K, W->Kp, d->xb.p));
     ENVG_TRY(gemm_device(d, d->xb.p, M, W->Kp, W->tm256, W->tm128, W->rows, gu, e, lin_flops,
                          2.0 * (double)N * K + 2.0 * (double)M * W->Kp + out_bytes));
   }
@@ -929,6 +1141,26 @@ int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, in
   }
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,
+                int epilogue, const float* gate, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  return linear_core(d, dst, x, W, bias, M, K, N, epilogue, gate, flags, nullptr, nullptr);
+}
+
+int envg_linear_adaln(float* dst, const float* x, const float* shift, const float* scale, envg_weight W,
+                      const float* bias, int64_t M, int64_t K, int64_t N, int epilogue, const float* gate, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (!shift || !scale) return fail(ENVG_ERR_ARG, "envg_linear_adaln: shift and scale are required");
+  return linear_core(d, dst, x, W, bias, M, K, N, epilogue, gate, flags, shift, scale);
 }
 
 int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,

@@ -1404,6 +1404,63 @@ __global__ void k_im2col_nhwc(const __nv_bfloat16* __restrict__ in, int B, int H
   }
 }
 
+// Adaptive layer norm fused with the activation cast (QNNAdaLN, quicknncpu.pas:3042-3060, then
+// the linear's bf16 rounding): per row r, mean and population variance in fp32, then
+//   out[r][k] = (1 + scale[k]) * ((x[r][k] - mean) * rsqrt-free 1/sqrt(var + eps)) + shift[k]
+// written as bf16 (RNE) into [rows][Kp] with zero padding for the tensor-core paths, or as fp32
+// into [rows][K] for k_gemv.  One block per row; the row is re-read from L1 by the later passes.
+ENVG_DEV float block_sum256(float v, float* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (threadIdx.x < 8) ? red[threadIdx.x] : 0.0f;
+  if (w == 0) {
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+    if (l == 0) red[8] = t;
+  }
+  __syncthreads();
+  return red[8];
+}
+
+__global__ void __launch_bounds__(256) k_adaln(const float* __restrict__ X, int64_t ldx, int K, int Kp,
+                                               const float* __restrict__ shift, const float* __restrict__ scale,
+                                               float eps, void* out, int out_bf16) {
+  __shared__ float red[9];
+  const int64_t r = blockIdx.x;
+  const float* xr = X + r * ldx;
+  float s = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) s += xr[k];
+  const float mean = block_sum256(s, red) / (float)K;
+  float q = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    const float dlt = xr[k] - mean;
+    q = fmaf(dlt, dlt, q);
+  }
+  const float var = block_sum256(q, red) / (float)K;
+  const float inv = 1.0f / sqrtf(var + eps);
+  if (out_bf16) {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + r * Kp;
+    for (int k = threadIdx.x; k < Kp; k += 256) {
+      float v = 0.0f;
+      if (k < K) {
+        const float norm = __fmul_rn(__fsub_rn(xr[k], mean), inv);
+        v = __fadd_rn(__fmul_rn(__fadd_rn(1.0f, __ldg(scale + k)), norm), __ldg(shift + k));
+      }
+      o[k] = __float2bfloat16_rn(v);
+    }
+  } else {
+    float* o = reinterpret_cast<float*>(out) + r * K;
+    for (int k = threadIdx.x; k < K; k += 256) {
+      const float norm = __fmul_rn(__fsub_rn(xr[k], mean), inv);
+      o[k] = __fadd_rn(__fmul_rn(__fadd_rn(1.0f, __ldg(scale + k)), norm), __ldg(shift + k));
+    }
+  }
+}
+
 // Self-test of the bounded wait: one CTA waits on a barrier nothing arrives at.
 __global__ void k_wait_selftest(int* status, uint64_t cap_ns) {
   __shared__ __align__(8) uint64_t bar;

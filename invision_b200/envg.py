@@ -28,6 +28,7 @@ LAYOUT_PLAIN, LAYOUT_GATE_UP = 0, 1
 EPI_NONE, EPI_BIAS, EPI_SILU_GATE, EPI_GATED_RESIDUAL, EPI_SILU = 0, 1, 2, 3, 4
 HOST_PTRS, DEVICE_PTRS, ASYNC = 0, 1, 2
 ROW_MAJOR, NO_TRANS, TRANS = 101, 111, 112
+DTYPE_OTHER, DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2, 3
 CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
 
 
@@ -46,6 +47,11 @@ class LinearDesc(ctypes.Structure):
     _fields_ = [("dst", ctypes.c_void_p), ("x", ctypes.c_void_p), ("W", ctypes.c_void_p), ("bias", ctypes.c_void_p),
                 ("M", ctypes.c_int64), ("K", ctypes.c_int64), ("N", ctypes.c_int64), ("epilogue", ctypes.c_int),
                 ("gate", ctypes.c_void_p)]
+
+
+class TensorInfo(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int), ("ndim", ctypes.c_int), ("shape", ctypes.c_int64 * 8),
+                ("offset", ctypes.c_int64), ("nbytes", ctypes.c_int64), ("dtype_name", ctypes.c_char * 16)]
 
 
 class Stats(ctypes.Structure):
@@ -74,9 +80,14 @@ def lib():
         L.envg_weight_upload_shard.argtypes = [_vp, _vp, _i64, _i64, _i64, _i64, _ci, ctypes.POINTER(_vp)]
         L.envg_conv_weight_upload.argtypes = [_vp, _vp, _ci, _ci, _ci, _ci, ctypes.POINTER(_vp)]
         L.envg_weight_free.argtypes = [_vp]
+        L.envg_safetensors_tensor_info.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(TensorInfo)]
+        L.envg_safetensors_read_f32.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _vp, _i64]
+        L.envg_weight_upload_safetensors.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _ci, _i64, _i64,
+                                                     ctypes.POINTER(_vp)]
         L.envg_linear.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_noalloc.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_batch.argtypes = [ctypes.POINTER(LinearDesc), _ci, _ci]
+        L.envg_linear_adaln.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_nsplit.argtypes = [_vp, ctypes.POINTER(_vp), _ci, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64,
                                          _i64, _ci, _vp, _ci]
         L.envg_conv2d.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 11
@@ -225,6 +236,8 @@ class Weight:
 
     def __init__(self, w, layout=LAYOUT_PLAIN, shard=None, conv=None):
         self.h = None
+        if w is None:  # filled in by from_safetensors
+            return
         w = np.ascontiguousarray(w)
         if w.dtype == np.uint16:
             pb, pf = w.ctypes.data, None
@@ -253,6 +266,30 @@ class Weight:
         self.conv = conv
         self.h = h
 
+    @classmethod
+    def from_safetensors(cls, path, name, layout=LAYOUT_PLAIN, shard=None):
+        """Upload tensor ``name`` of a ``.safetensors`` file (envg_weight_upload_safetensors).
+
+        A 2-D tensor [N, K] becomes a linear weight (``layout``, ``shard`` as in the constructor);
+        a 4-D tensor [out_ch, in_ch, kH, kW] a convolution weight."""
+        info = safetensors_tensor_info(path, name)
+        n0, n1 = shard if shard is not None else (0, 0)
+        h = _vp()
+        _check(lib().envg_weight_upload_safetensors(os.fsencode(path), name.encode(), layout, n0, n1,
+                                                    ctypes.byref(h)))
+        self = cls(None)
+        shape = info["shape"]
+        if len(shape) == 4:
+            self.conv = tuple(shape)
+            self.N, self.K = shape[0], shape[1] * shape[2] * shape[3]
+        else:
+            self.conv = None
+            rows = shape[0] if shard is None else (n1 - n0) * (2 if layout == LAYOUT_GATE_UP else 1)
+            self.N, self.K = rows, shape[1]
+        self.layout = layout
+        self.h = h
+        return self
+
     def free(self):
         if self.h is not None and self.h.value:
             _check(lib().envg_weight_free(self.h))
@@ -265,6 +302,22 @@ class Weight:
             pass
 
 
+def safetensors_tensor_info(path, name):
+    """Header entry of tensor ``name`` (envg_safetensors_tensor_info; needs no GPU)."""
+    info = TensorInfo()
+    _check(lib().envg_safetensors_tensor_info(os.fsencode(path), name.encode(), ctypes.byref(info)))
+    return {"dtype": info.dtype, "dtype_name": info.dtype_name.decode(), "shape": [info.shape[i] for i in range(info.ndim)],
+            "offset": info.offset, "nbytes": info.nbytes}
+
+
+def safetensors_read_f32(path, name):
+    """Tensor ``name`` widened to fp32 on the host (envg_safetensors_read_f32; needs no GPU)."""
+    shape = safetensors_tensor_info(path, name)["shape"]
+    out = np.empty(shape, dtype=np.float32)
+    _check(lib().envg_safetensors_read_f32(os.fsencode(path), name.encode(), out.ctypes.data, out.size))
+    return out
+
+
 def linear(dst, x, W, bias=None, epilogue=None, gate=None, sync=True):
     """dst = epilogue(x . W^T): envg_linear.  x [M, K]; dst [M, N] (N/2 for SILU_GATE)."""
     if epilogue is None:
@@ -274,6 +327,18 @@ def linear(dst, x, W, bias=None, epilogue=None, gate=None, sync=True):
         flags |= ASYNC
     M, K = x.shape
     return _check(lib().envg_linear(_ptr(dst), _ptr(x), W.h, _ptr(bias), M, K, W.N, epilogue, _ptr(gate), flags))
+
+
+def linear_adaln(dst, x, shift, scale, W, bias=None, epilogue=None, gate=None, sync=True):
+    """dst = epilogue(AdaLN(x; shift, scale) . W^T): envg_linear_adaln (QNNAdaLN fused into the cast)."""
+    if epilogue is None:
+        epilogue = EPI_SILU_GATE if W.layout == LAYOUT_GATE_UP else (EPI_BIAS if bias is not None else EPI_NONE)
+    flags = _mode(dst, x, shift, scale, bias, gate)
+    if flags == DEVICE_PTRS and not sync:
+        flags |= ASYNC
+    M, K = x.shape
+    return _check(lib().envg_linear_adaln(_ptr(dst), _ptr(x), _ptr(shift), _ptr(scale), W.h, _ptr(bias), M, K, W.N,
+                                          epilogue, _ptr(gate), flags))
 
 
 def linear_batch(calls, sync=True):
@@ -381,6 +446,15 @@ def QNNLinearGatedAdd(h, x, W, gate, seqLen, inDIM, outDIM, B=None):
     h += gate (.) (x.W^T + B)."""
     _assert(W.N == outDIM and W.K == inDIM, "ERROR : QNNLinear weight shape mismatch")
     return linear(h[:seqLen], x[:seqLen], W, bias=B, epilogue=EPI_GATED_RESIDUAL, gate=gate)
+
+
+def QNNAdaLNLinear(dst, src, shift, scale, W, B, seqLen, inDIM, outDIM):
+    """QNNAdaLN(norm, src, shift, scale, seq, hidden) (quicknncpu.pas:3042-3060) followed by
+    QNNLinear(dst, norm, W, B, seq, hidden, outDIM), fused: the normalised input never leaves the
+    GPU as fp32."""
+    _assert(W.N == outDIM and W.K == inDIM, "ERROR : QNNLinear weight shape mismatch")
+    return linear_adaln(dst[:seqLen], src[:seqLen], shift, scale, W, bias=B,
+                        epilogue=EPI_BIAS if B is not None else EPI_NONE)
 
 
 def QNNConv2d(dst, src, weights, bias, in_ch, out_ch, H, W, kH, kW, stride, padding, batch):

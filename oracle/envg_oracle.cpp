@@ -24,6 +24,8 @@
 //   * QNNGatedAdd           src/quicknncpu.pas:853-859, 1752-1758
 //   * QNNConv2d             src/quicknncpu.pas:1958-2132      (row-tiled im2col, NN GEMM,
 //                                                              per-channel bias)
+//   * QNNAdaLN              src/quicknncpu.pas:3042-3060      (QNNMean :679-685, QNNVariance
+//                                                              :687-695, EPSILON quicknn_common.pas:51)
 //
 // Two builds of the reference are restated, selected by `path`:
 //   ENVO_PATH_AVX2   (0) -- the shipped configuration (USE_AVX2 defined in
@@ -369,6 +371,32 @@ void envo_gated_add(float* dst, const float* gate, const float* proj, int64_t se
     for (int64_t i = 0; i < hidden; ++i) {
       float t = gate[i] * p[i];
       d[i] = d[i] + t;
+    }
+  }
+}
+
+// QNNAdaLN (quicknncpu.pas:3042-3060), scalar build: per row, mean = sequential fp32 sum / n,
+// population variance = sequential sum of squared differences / n, stdInv = 1/sqrt(var +
+// EPSILON) with EPSILON = 1e-6 (quicknn_common.pas:51; the eps argument of QNNAdaLN is not used
+// by its body), out = (1 + scale[j]) * ((x - mean) * stdInv) + bias[j].
+void envo_adaln(float* dst, const float* src, const float* bias, const float* scale, int64_t seq, int64_t hidden) {
+  const float EPS = 1e-6f;
+  for (int64_t i = 0; i < seq; ++i) {
+    const float* in = src + i * hidden;
+    float* out = dst + i * hidden;
+    float sum = 0.0f;
+    for (int64_t j = 0; j < hidden; ++j) sum = sum + in[j];
+    const float mean = hidden ? sum / (float)hidden : 0.0f;
+    float ssd = 0.0f;
+    for (int64_t j = 0; j < hidden; ++j) {
+      const float d = in[j] - mean;
+      ssd = ssd + d * d;
+    }
+    const float var = hidden ? ssd / (float)hidden : 0.0f;
+    const float stdInv = 1.0f / sqrtf(var + EPS);
+    for (int64_t j = 0; j < hidden; ++j) {
+      const float norm = (in[j] - mean) * stdInv;
+      out[j] = (1.0f + scale[j]) * norm + bias[j];
     }
   }
 }

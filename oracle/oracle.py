@@ -62,6 +62,7 @@ def lib():
         L.envo_silu.argtypes = [_f32p, _i64]
         L.envo_gated_add.argtypes = [_f32p, _f32p, _f32p, _i64, _i64]
         L.envo_conv2d.argtypes = [ctypes.c_int, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 9
+        L.envo_adaln.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64]
         L.envo_conv2d.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -175,6 +176,17 @@ def gated_add(dst, gate, proj):
     seq, hidden = d.shape
     lib().envo_gated_add(_p(d), _p(g), _p(p), seq, hidden)
     return d
+
+
+def adaln(src, shift, scale):
+    """QNNAdaLN: per row (1 + scale) * (x - mean) / sqrt(var + 1e-6) + shift (returns a new array)."""
+    src = _chk(np.ascontiguousarray(src), np.float32)
+    shift = _chk(np.ascontiguousarray(shift), np.float32)
+    scale = _chk(np.ascontiguousarray(scale), np.float32)
+    seq, hidden = src.shape
+    out = np.empty_like(src)
+    lib().envo_adaln(_p(out), _p(src), _p(shift), _p(scale), seq, hidden)
+    return out
 
 
 def conv2d(src, w, bias, stride, padding, path=PATH_AVX2):

@@ -1,6 +1,7 @@
 """Seeded synthetic inputs and the acceptance check shared by the parity tests."""
 import json
 import os
+import struct
 
 import numpy as np
 
@@ -42,3 +43,24 @@ def assert_parity(y, ref, tol_max=TOL_MAX, tol_mean=TOL_MEAN, what=""):
     _log(what, mx, mean)
     assert mx <= tol_max and mean <= tol_mean, f"{what}: max-rel {mx:.3e} (<= {tol_max}), mean-rel {mean:.3e} (<= {tol_mean})"
     return mx, mean
+
+
+def write_safetensors(path, tensors, pad_to=8, metadata=None, extra_header_bytes=0):
+    """tensors: {name: (dtype_str, shape, raw_bytes)} in file order."""
+    header, blobs, off = {}, [], 0
+    if metadata is not None:
+        header["__metadata__"] = metadata
+    for name, (dt, shape, raw) in tensors.items():
+        header[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    hj = json.dumps(header).encode()
+    if pad_to:
+        hj += b" " * ((-(8 + len(hj))) % pad_to)
+    hj += b" " * extra_header_bytes
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hj)))
+        f.write(hj)
+        for b in blobs:
+            f.write(b)
+    return path

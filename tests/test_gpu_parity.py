@@ -310,3 +310,70 @@ def test_linear_batch_equals_separate_calls(gpu):
     torch.cuda.synchronize()
     for k, v in outs.items():
         np.testing.assert_array_equal(got[k], v.cpu().numpy(), err_msg=k)
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 3072, 1024), (4, 3072, 768), (130, 200, 264)])
+def test_adaln_linear_vs_oracle(gpu, M, K, N):
+    """QNNAdaLN + QNNLinear fused (envg_linear_adaln) against the oracle's QNNAdaLN then linear."""
+    rng = np.random.default_rng(M + K)
+    x = (1.5 + 2 * rng.standard_normal((M, K))).astype(np.float32)
+    shift = (0.1 * rng.standard_normal(K)).astype(np.float32)
+    scale = (0.1 * rng.standard_normal(K)).astype(np.float32)
+    _, w, b = inputs(M, K, N, seed=K + N)
+    W = gpu.Weight(w)
+    y = np.zeros((M, N), np.float32)
+    gpu.QNNAdaLNLinear(y, x, shift, scale, W, b, M, K, N)
+    xn = O.adaln(x, shift, scale)
+    ref = O.linear_bf16(xn, w, b, path=O.PATH_SCALAR if K % 8 else O.PATH_AVX2)
+    if M <= 8:  # fp32 path: far inside the GEMM bound
+        assert_parity(y, ref, 1e-4, 2e-5, what=f"adaln gemv {M}x{K}x{N}")
+    else:
+        assert_parity(y, ref, what=f"adaln {M}x{K}x{N}")
+
+
+def test_safetensors_upload_matches_array_upload(gpu, tmp_path):
+    """Weights uploaded straight from a .safetensors file (BF16, F16, F32; plain, GATE_UP, a shard
+    and a 4-D conv weight) give the same outputs, bit for bit, as the same values uploaded from
+    arrays, and pass parity against the oracle."""
+    from tests.common import write_safetensors
+
+    rng = np.random.default_rng(77)
+    M, K, N = 96, 320, 272
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w_bf = O.f32_to_bf16_rne((0.02 * rng.standard_normal((N, K))).astype(np.float32))
+    w_h = (0.02 * rng.standard_normal((N, K))).astype(np.float16)
+    w_f = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
+    conv = O.f32_to_bf16_rne((0.02 * rng.standard_normal((24, 16, 3, 3))).astype(np.float32))
+    p = write_safetensors(str(tmp_path / "w.safetensors"), {
+        "bf": ("BF16", [N, K], w_bf.tobytes()), "h": ("F16", [N, K], w_h.tobytes()),
+        "f": ("F32", [N, K], w_f.tobytes()), "conv": ("BF16", list(conv.shape), conv.tobytes())},
+        pad_to=0, extra_header_bytes=1)   # odd data offset: the unaligned path
+    for name, arr in (("bf", w_bf), ("h", w_h.astype(np.float32)), ("f", w_f)):
+        y_file = np.full((M, N), np.nan, np.float32)
+        y_arr = np.full((M, N), np.nan, np.float32)
+        gpu.linear(y_file, x, gpu.Weight.from_safetensors(p, name))
+        gpu.linear(y_arr, x, gpu.Weight(arr))
+        np.testing.assert_array_equal(y_file, y_arr, err_msg=name)
+        wb = arr if arr.dtype == np.uint16 else O.f32_to_bf16_rne(arr)
+        assert_parity(y_file, O.linear_bf16(x, wb, None, path=O.PATH_AVX2), what=f"safetensors {name}")
+    # GATE_UP from file, and a shard of it
+    y_file = np.zeros((M, N // 2), np.float32)
+    y_arr = np.zeros((M, N // 2), np.float32)
+    gpu.linear(y_file, x, gpu.Weight.from_safetensors(p, "bf", layout=gpu.LAYOUT_GATE_UP))
+    gpu.linear(y_arr, x, gpu.Weight(w_bf, layout=gpu.LAYOUT_GATE_UP))
+    np.testing.assert_array_equal(y_file, y_arr)
+    ys_file = np.zeros((M, 40), np.float32)
+    ys_arr = np.zeros((M, 40), np.float32)
+    gpu.linear(ys_file, x, gpu.Weight.from_safetensors(p, "bf", layout=gpu.LAYOUT_GATE_UP, shard=(16, 56)))
+    gpu.linear(ys_arr, x, gpu.Weight(w_bf, layout=gpu.LAYOUT_GATE_UP, shard=(16, 56)))
+    np.testing.assert_array_equal(ys_file, ys_arr)
+    # 4-D conv weight
+    src = rng.standard_normal((1, 16, 20, 20), dtype=np.float32)
+    bias = (0.01 * rng.standard_normal(24)).astype(np.float32)
+    yc_file = np.zeros((1, 24, 20, 20), np.float32)
+    yc_arr = np.zeros((1, 24, 20, 20), np.float32)
+    gpu.conv2d(yc_file, src, gpu.Weight.from_safetensors(p, "conv"), bias, 1, 1)
+    gpu.conv2d(yc_arr, src, gpu.Weight(conv.reshape(24, -1), conv=(24, 16, 3, 3)), bias, 1, 1)
+    np.testing.assert_array_equal(yc_file, yc_arr)
+    with pytest.raises(gpu.EnvgError):
+        gpu.Weight.from_safetensors(p, "conv", shard=(0, 8))

@@ -149,3 +149,16 @@ def test_conv2d_stride1_valid_padding_quirk():
     # same padding is exact
     y1 = O.conv2d(src, w, None, 1, 1)
     np.testing.assert_allclose(y1, conv_f64(src, w, None, 1, 1), rtol=1e-4, atol=1e-4)
+
+
+def test_adaln_vs_fp64():
+    rng = np.random.default_rng(9)
+    x = (3 + 2 * rng.standard_normal((7, 3072))).astype(np.float32)
+    shift = (0.1 * rng.standard_normal(3072)).astype(np.float32)
+    scale = (0.1 * rng.standard_normal(3072)).astype(np.float32)
+    y = O.adaln(x, shift, scale)
+    xd = x.astype(np.float64)
+    mu = xd.mean(1, keepdims=True)
+    var = ((xd - mu) ** 2).mean(1, keepdims=True)
+    ref = (1 + scale) * (xd - mu) / np.sqrt(var + 1e-6) + shift
+    np.testing.assert_allclose(y, ref, rtol=2e-4, atol=2e-4)
