@@ -196,6 +196,36 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
                 int out_ch, int H, int W_, int kH, int kW, int stride, int pad, int batch,
                 int epilogue, int flags);
 
+/* dst = GroupNorm(src) (then SiLU when act_silu != 0), NCHW fp32 [batch, channels, H, W]; as
+ * QNNGroupNorm (quicknncpu.pas:2259-2313: population variance, eps 1e-6, per-channel gamma /
+ * beta) followed by QNNSiluInplace (:2372-2386).  gamma/beta may be NULL (1 / 0).  channels %
+ * num_groups == 0.  dst may equal src.  gamma/beta follow the flags' pointer kind. */
+int envg_group_norm(float* dst, const float* src, const float* gamma, const float* beta, int batch,
+                    int channels, int H, int W, int num_groups, int act_silu, int flags);
+
+/* One VAE ResBlock (TVAEResBlock.forward, quicknn_vae.pas:164-187):
+ *   dst = skip(src) + conv2(SiLU(GN2(conv1(SiLU(GN1(src)))))),
+ * skip = identity when skip == NULL (in_ch == out_ch), else the 1x1 conv `skip` + skip_bias.
+ * Each GroupNorm + SiLU is folded into the NCHW -> NHWC bf16 cast that feeds the next 3x3 conv,
+ * and the final add is the second conv's store (a TMA reduce-add into dst).  Vectors are host
+ * pointers with ENVG_HOST_PTRS and device pointers with ENVG_DEVICE_PTRS, like src and dst. */
+typedef struct envg_resblock {
+  int in_ch, out_ch;
+  const float* norm1_gamma;  /* [in_ch]  */
+  const float* norm1_beta;   /* [in_ch]  */
+  envg_weight conv1;         /* 3x3, in_ch -> out_ch, padding 1 */
+  const float* conv1_bias;   /* [out_ch] */
+  const float* norm2_gamma;  /* [out_ch] */
+  const float* norm2_beta;   /* [out_ch] */
+  envg_weight conv2;         /* 3x3, out_ch -> out_ch, padding 1 */
+  const float* conv2_bias;   /* [out_ch] */
+  envg_weight skip;          /* 1x1, in_ch -> out_ch, or NULL when in_ch == out_ch */
+  const float* skip_bias;    /* [out_ch] or NULL */
+} envg_resblock;
+
+int envg_vae_resblock(float* dst, const float* src, const envg_resblock* rb, int batch, int H,
+                      int W, int num_groups, int flags);
+
 /* The modulated linear of the FLUX blocks: QNNAdaLN (quicknn_kernels.pas:315 ->
  * quicknncpu.pas:3042-3060; call sites quicknn_transformers.pas:1400,1410,1440,1449,1500) followed
  * by QNNLinear, with the normalisation fused into the activation cast:

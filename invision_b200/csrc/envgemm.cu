@@ -80,6 +80,7 @@ struct Dev {
   cudaStream_t own = nullptr;
   cudaStream_t user = nullptr;
   Buf x, y, xb, wb, part, cnt, bias, gate, act, col, b32, xbatch, ada, xn;
+  Buf gn, c1, vec;  // GroupNorm statistics + affine, ResBlock conv1 output, small parameter vectors
   cudaStream_t aux = nullptr;              // second stream of envg_linear_batch
   std::vector<cudaEvent_t> batch_events;   // reused event pool of envg_linear_batch
   int* h_status = nullptr;  // mapped pinned: [0] status code, [1] wait site
@@ -93,7 +94,7 @@ struct Dev {
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
-           col.bytes + b32.bytes + xbatch.bytes + ada.bytes + xn.bytes;
+           col.bytes + b32.bytes + xbatch.bytes + ada.bytes + xn.bytes + gn.bytes + c1.bytes + vec.bytes;
   }
 };
 
@@ -104,12 +105,13 @@ int g_cur = -1;
 // ---- optional per-launch timing (envg_profile) ---------------------------------------------
 enum KernelId {
   KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_ADALN, KID_TRANSPOSE, KID_IM2COL,
-  KID_SELFTEST, KID_COUNT
+  KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate", "k1_gemm_conv",
                                              "k2_skinny",   "k_gemv",            "k_cast_rows",
                                              "k_adaln",     "k_transpose_cast",  "k_im2col_nhwc",
-                                             "k_wait_selftest"};
+                                             "k_wait_selftest", "k_group_stats",     "k_group_affine",
+                                             "k_group_apply"};
 struct KAcc {
   uint64_t launches = 0;
   double ms = 0, flops = 0, bytes = 0;
@@ -265,7 +267,10 @@ int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY) {
   }
   e.store_mode = STORE_DIRECT;
   const bool aligned = (reinterpret_cast<uintptr_t>(e.Y) & 15) == 0 && e.ldy % 4 == 0;
-  if (!aligned) return ENVG_OK;
+  if (!aligned) {
+    if (e.yb) e.store_mode = STORE_COALESCED;  // the bf16 side output is written on the staged paths
+    return ENVG_OK;
+  }
   int mode = STORE_TMA;
   if (e.mode == EPI_GATED_RES) mode = STORE_TMA_ADD;
   else if (e.mode == EPI_ALPHA_BETA) mode = e.beta == 0.0f ? STORE_TMA : (e.beta == 1.0f ? STORE_TMA_ADD : STORE_DIRECT);
@@ -536,7 +541,8 @@ int launch_adaln(Dev* d, const float* x, int64_t rows, int64_t K, int64_t Kp, co
 
 int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t K, int64_t Kp, void* xb) {
   if (rows == 0) return ENVG_OK;
-  const int vec8 = (K == Kp && K % 8 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
+  int vec8 = (K == Kp && K % 8 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
+  if (vec8 && ldx == K && (reinterpret_cast<uintptr_t>(xb) & 15) == 0) vec8 = 2;
   const int64_t work = vec8 ? rows * K / 8 : rows * Kp;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)d->sms * 8));
   ProfScope ps(stream_of(d), KID_CAST, 0.0, (double)rows * K * 4 + (double)rows * Kp * 2);
@@ -549,11 +555,11 @@ int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t 
 
 // fp32 [batch][R][C] -> bf16 [batch][C][Rp]
 int launch_transpose_cast(Dev* d, const float* src, int64_t lds, int64_t sbs, int R, int C, void* dst, int64_t ldd,
-                          int64_t dbs, int Rp, int batch) {
+                          int64_t dbs, int Rp, int batch, const float2* aff = nullptr, int act = 0) {
   dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(Rp, 64), (unsigned)batch);
   ProfScope ps(stream_of(d), KID_TRANSPOSE, 0.0, (double)batch * ((double)R * C * 4 + (double)C * Rp * 2));
   k_transpose_cast<<<grid, 256, 0, stream_of(d)>>>(src, lds, sbs, R, C, reinterpret_cast<__nv_bfloat16*>(dst), ldd,
-                                                   dbs, Rp);
+                                                   dbs, Rp, aff, act);
   ENVG_CUDA(cudaGetLastError());
   d->st.kernel_launches++;
   return ENVG_OK;
@@ -873,7 +879,8 @@ int envg_shutdown(void) {
   if (!d) return ENVG_OK;
   cudaStreamSynchronize(stream_of(d));
   Buf* bufs[] = {&d->x,    &d->y,   &d->xb,  &d->wb,  &d->part,  &d->cnt,
-                 &d->bias, &d->gate, &d->act, &d->col, &d->b32, &d->xbatch, &d->ada, &d->xn};
+                 &d->bias, &d->gate, &d->act, &d->col, &d->b32, &d->xbatch, &d->ada, &d->xn,
+                 &d->gn,   &d->c1,   &d->vec};
   for (Buf* b : bufs) {
     if (b->p) cudaFree(b->p);
     *b = Buf{};
@@ -1284,6 +1291,171 @@ EpiArgs linear_epi(const envg_linear_desc& q) {
   return e;
 }
 
+// Convolution of an NHWC bf16 activation `act` ([batch][H][W][Cp], Cp = W->Cp) into NCHW fp32 dy.
+// residual: dy += conv + bias (stride 1 only; the residual add of QNNAddInplace,
+// src/quicknncpu.pas:704-709, fused into the store).
+int conv_core(Dev* d, envg_weight W, const void* act, float* dy, const float* dbias, int H, int W_, int stride, int pad,
+              int batch, int act_silu, bool residual) {
+  cudaStream_t s = stream_of(d);
+  const int out_ch = W->out_ch, kH = W->kH, kW = W->kW, Cp = W->Cp;
+  const int outH = (H + 2 * pad - kH) / stride + 1;
+  const int outW = (W_ + 2 * pad - kW) / stride + 1;
+  if (residual && stride != 1) return fail(ENVG_ERR_UNSUPPORTED, "conv residual add needs stride 1");
+  const int64_t plane = (int64_t)outH * outW;
+  const int64_t out_elems = (int64_t)batch * out_ch * plane;
+  EpiArgs e{};
+  e.Y = dy;
+  e.bias = dbias;
+  e.bias_mode = dbias ? 2 : 0;
+  e.act = act_silu;
+  e.mode = residual ? EPI_GATED_RES : EPI_PLAIN;
+  e.alpha = 1.0f;
+  e.m_valid = out_ch;
+  if (stride == 1) {
+    // Implicit im2col: each B tile is one 4D TMA box of the NHWC activation.
+    int tw = 1;
+    while (tw < outW && tw < 256) tw <<= 1;
+    const int th = 256 / tw;
+    const bool pair = d->use_pair && out_ch > BM;
+    CUtensorMap tB;
+    if (pair)  // each CTA of the pair fetches half of the 256-pixel tile
+      ENVG_TRY(tmap_nhwc(&tB, act, Cp, W_, H, batch, th >= 2 ? tw : tw / 2, th >= 2 ? th / 2 : 1));
+    else
+      ENVG_TRY(tmap_nhwc(&tB, act, Cp, W_, H, batch, tw, th));
+    GemmArgs g{};
+    g.num_kb = (int)(W->Kp / BK);
+    g.tiles_m = (int)cdiv(out_ch, pair ? 2 * BM : BM);
+    g.conv.tileW = tw;
+    g.conv.tileH = th;
+    g.conv.outH = outH;
+    g.conv.outW = outW;
+    g.conv.tiles_w = (int)cdiv(outW, tw);
+    g.conv.tiles_h = (int)cdiv(outH, th);
+    g.conv.KW = kW;
+    g.conv.pad = pad;
+    g.conv.cblocks = Cp / BK;
+    g.conv.img_stride = (int64_t)out_ch * plane;
+    g.conv.plane = plane;
+    g.tiles_n = batch * g.conv.tiles_w * g.conv.tiles_h;
+    g.num_tiles = g.tiles_m * g.tiles_n;
+    g.group_m = 1;
+    e.ldy = plane;
+    e.n_out = (int)plane;
+    e.vec_ok = ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 4 == 0) ? 1 : 0;
+    CUtensorMap tY;
+    memset(&tY, 0, sizeof(tY));
+    e.store_mode = (tw >= 32) ? STORE_COALESCED : STORE_DIRECT;  // a 32-pixel chunk stays in one row
+    if (d->store_tma && (reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 32 == 0) {
+      ENVG_TRY(tmap_out_3d(&tY, dy, (uint64_t)plane, (uint64_t)out_ch, (uint64_t)batch));
+      e.store_mode = residual ? STORE_TMA_ADD : STORE_TMA;
+    }
+    g.epi = e;
+    const double cflops = 2.0 * out_ch * (double)plane * batch * (double)W->K;
+    const double cbytes = 2.0 * (double)batch * H * W_ * Cp + 2.0 * out_ch * (double)W->Kp + 4.0 * (double)out_elems +
+                          (dbias ? 4.0 * out_ch : 0.0);
+    if (pair) ENVG_TRY(launch_k1_pair<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
+    else ENVG_TRY(launch_k1<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
+  } else {
+    // Strided convolution: explicit bf16 im2col, then one GEMM per image.
+    const int64_t colK = W->Kp;
+    ENVG_TRY(ensure(d, d->col, (size_t)batch * plane * colK * 2));
+    const int64_t total = (int64_t)batch * plane * kH * kW * (Cp / 8);
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(total, 256), (int64_t)d->sms * 16));
+    ProfScope ps_im(s, KID_IM2COL, 0.0, 2.0 * (double)batch * H * W_ * Cp + 2.0 * (double)batch * plane * colK);
+    k_im2col_nhwc<<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(act), batch, H, W_, Cp, kH, kW,
+                                         stride, pad, outH, outW, reinterpret_cast<__nv_bfloat16*>(d->col.p));
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches++;
+    for (int b = 0; b < batch; ++b) {
+      const void* colb = reinterpret_cast<const uint8_t*>(d->col.p) + (size_t)b * plane * colK * 2;
+      CUtensorMap tB;
+      ENVG_TRY(tmap_2d(&tB, colb, colK, plane, 256));
+      CUtensorMap tA = W->tm128;
+      GemmArgs g{};
+      g.num_kb = (int)(colK / BK);
+      g.tiles_m = (int)cdiv(out_ch, BM);
+      g.tiles_n = (int)cdiv(plane, K1_BN);
+      g.num_tiles = g.tiles_m * g.tiles_n;
+      g.group_m = 8;
+      EpiArgs eb = e;
+      eb.Y = dy + (int64_t)b * out_ch * plane;
+      eb.ldy = plane;
+      eb.n_out = (int)plane;
+      eb.vec_ok = ((reinterpret_cast<uintptr_t>(eb.Y) & 15) == 0 && plane % 4 == 0) ? 1 : 0;
+      CUtensorMap tY;
+      memset(&tY, 0, sizeof(tY));
+      ENVG_TRY(choose_store(d->store_tma, eb, &tY));
+      g.epi = eb;
+      ENVG_TRY(launch_k1<false, false>(d, tA, tB, tY, g, 2.0 * out_ch * (double)plane * (double)W->K,
+                                       2.0 * (double)plane * colK + 2.0 * out_ch * (double)colK + 4.0 * out_ch * (double)plane));
+    }
+  }
+  return ENVG_OK;
+}
+
+constexpr float GN_EPS = 1e-6f;  // EPSILON of QNNGroupNorm (src/quicknn_common.pas:51)
+
+int gn_chunks(int C, int64_t HW, int groups) { return (int)cdiv((int64_t)(C / groups) * HW, GN_CHUNK); }
+
+// Bytes of GroupNorm scratch for one tensor: chunk partials (3 doubles each) + float2 affine.
+size_t gn_bytes(int batch, int C, int64_t HW, int groups) {
+  return (size_t)rup((int64_t)batch * groups * gn_chunks(C, HW, groups) * 24, 256) + (size_t)batch * C * 8;
+}
+
+// Per-(b, c) GroupNorm affine {gamma*std_inv, beta - mean*gamma*std_inv} of a device NCHW tensor,
+// written after the partials in d->gn (which must hold gn_bytes()).
+int launch_group_affine(Dev* d, const float* src, int batch, int C, int64_t HW, int groups, const float* gamma,
+                        const float* beta, float2** aff_out) {
+  cudaStream_t s = stream_of(d);
+  const int cpg = C / groups, chunks = gn_chunks(C, HW, groups);
+  double* part = reinterpret_cast<double*>(d->gn.p);
+  float2* aff = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(d->gn.p) +
+                                          rup((int64_t)batch * groups * chunks * 24, 256));
+  {
+    ProfScope ps(s, KID_GN_STATS, 0.0, 4.0 * batch * (double)C * HW + 24.0 * batch * groups * chunks);
+    k_group_stats<<<dim3((unsigned)chunks, (unsigned)(batch * groups)), GN_THREADS, 0, s>>>(src, C, HW, cpg, groups,
+                                                                                           part, chunks);
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches++;
+  }
+  {
+    ProfScope ps(s, KID_GN_AFFINE, 0.0, 24.0 * batch * groups * chunks + 8.0 * C + 8.0 * batch * C);
+    k_group_affine<<<(unsigned)cdiv((int64_t)batch * C, 256), 256, 0, s>>>(part, chunks, batch, C, cpg, groups, gamma,
+                                                                           beta, GN_EPS, aff);
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches++;
+  }
+  *aff_out = aff;
+  return ENVG_OK;
+}
+
+int check_gn_geometry(int batch, int C, int H, int W, int groups) {
+  if (batch < 0 || C <= 0 || H <= 0 || W <= 0 || groups <= 0 || C % groups)
+    return fail(ENVG_ERR_ARG, "group norm: batch %d, channels %d, %dx%d, %d groups invalid", batch, C, H, W, groups);
+  if ((int64_t)batch * groups > 65535)
+    return fail(ENVG_ERR_UNSUPPORTED, "group norm: batch x groups = %lld > 65535", (long long)batch * groups);
+  return ENVG_OK;
+}
+
+// Copies host vectors into d->vec (sized beforehand by the caller) and returns device pointers.
+struct VecStage {
+  Dev* d;
+  bool devp;
+  size_t off = 0;
+  int put(const float* v, int64_t n, const float** out) {
+    if (!v || devp) {
+      *out = v;
+      return ENVG_OK;
+    }
+    float* dv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d->vec.p) + off);
+    ENVG_CUDA(cudaMemcpyAsync(dv, v, (size_t)n * 4, cudaMemcpyHostToDevice, stream_of(d)));
+    d->st.h2d_bytes += (double)n * 4;
+    off += (size_t)rup(n * 4, 256);
+    *out = dv;
+    return ENVG_OK;
+  }
+};
+
 cudaEvent_t batch_event(Dev* d, size_t i) {
   while (d->batch_events.size() <= i) {
     cudaEvent_t e = nullptr;
@@ -1348,6 +1520,28 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
     const char* x1 = x0 + (size_t)(q.M * q.K) * 4;
     return pr.M > 0 && x0 < y1 && y0 < x1;
   };
+  // A copy whose input is exactly the output of one earlier linear on the tcgen05 path (same
+  // [M, K] shape, K % 8 == 0, overwrite epilogue) is written by that linear's epilogue as a bf16
+  // side output instead of by a cast: fused_from[j] = the producer, yb_copy[p] = the copy.
+  std::vector<int> fused_from(ncopies, -1), yb_copy(n, -1);
+  for (size_t j = 0; j < ncopies; ++j) {
+    const envg_linear_desc& q = descs[first_use[j]];
+    if (q.W->Kp != q.K) continue;
+    int prod = -1, count = 0;
+    for (int p = 0; p < first_use[j]; ++p)
+      if (produces(p, j)) {
+        ++count;
+        prod = p;
+      }
+    if (count != 1) continue;
+    const envg_linear_desc& pr = descs[prod];
+    const int64_t pn = pr.W->layout == ENVG_LAYOUT_GATE_UP ? pr.N / 2 : pr.N;
+    if ((const void*)pr.dst != (const void*)q.x || pr.M != q.M || pn != q.K) continue;
+    if (pr.epilogue == ENVG_EPI_GATED_RESIDUAL || pr.M <= d->skinny_max || src_of[prod] < 0) continue;
+    if (yb_copy[prod] >= 0) continue;
+    fused_from[j] = prod;
+    yb_copy[prod] = (int)j;
+  }
   // Cast j may be issued once every producer (index < issued) has been issued on s.
   auto ready = [&](size_t j, int issued) {
     for (int p = issued; p < first_use[j]; ++p)
@@ -1369,12 +1563,16 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
     const envg_linear_desc& q = descs[i];
     // casts run one linear ahead of the GEMMs, in order, as soon as their inputs exist
     while (next_copy < ncopies && first_use[next_copy] <= i + 1 && ready(next_copy, i)) {
-      ENVG_TRY(issue_cast(next_copy));
+      if (fused_from[next_copy] < 0) ENVG_TRY(issue_cast(next_copy));  // else written by its producer on s
       ++next_copy;
     }
     if (q.M == 0) continue;
     const bool gu = q.W->layout == ENVG_LAYOUT_GATE_UP;
-    const EpiArgs e = linear_epi(q);
+    EpiArgs e = linear_epi(q);
+    if (yb_copy[i] >= 0) {
+      e.yb = reinterpret_cast<__nv_bfloat16*>(base + offset[yb_copy[i]]);
+      e.ldyb = descs[first_use[yb_copy[i]]].W->Kp;
+    }
     const int64_t n_out = gu ? q.N / 2 : q.N;
     const double fl = 2.0 * (double)q.M * (double)q.N * (double)q.K;
     const double ob = 4.0 * (double)q.M * n_out + (q.bias ? 4.0 * q.N : 0.0) +
@@ -1383,7 +1581,7 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
       ENVG_TRY(launch_gemv(d, q.x, q.M, q.K, q.W, gu, e, fl, 2.0 * (double)q.N * q.K + 4.0 * (double)q.M * q.K + ob));
     } else {
       if ((size_t)src_of[i] >= next_copy) return fail(ENVG_ERR_STATE, "envg_linear_batch: internal schedule error");
-      ENVG_CUDA(cudaStreamWaitEvent(s, batch_event(d, 1 + src_of[i]), 0));
+      if (fused_from[src_of[i]] < 0) ENVG_CUDA(cudaStreamWaitEvent(s, batch_event(d, 1 + src_of[i]), 0));
       ENVG_TRY(gemm_device(d, base + offset[src_of[i]], q.M, q.W->Kp, q.W->tm256, q.W->tm128, q.W->rows, gu, e, fl,
                            2.0 * (double)q.N * q.K + 2.0 * (double)q.M * q.W->Kp + ob));
     }
@@ -1491,95 +1689,138 @@ int envg_conv2d(float* dst, const float* src, envg_weight W, const float* bias, 
   ENVG_TRY(ensure(d, d->act, (size_t)batch * H * W_ * Cp * 2));
   ENVG_TRY(launch_transpose_cast(d, dsrc, (int64_t)H * W_, (int64_t)in_ch * H * W_, in_ch, H * W_, d->act.p, Cp,
                                  (int64_t)H * W_ * Cp, Cp, batch));
-  EpiArgs e{};
-  e.Y = dy;
-  e.bias = dbias;
-  e.bias_mode = dbias ? 2 : 0;
-  e.act = (epilogue == ENVG_EPI_SILU) ? 1 : 0;
-  e.mode = EPI_PLAIN;
-  e.alpha = 1.0f;
-  e.m_valid = out_ch;
-  if (stride == 1) {
-    // Implicit im2col: each B tile is one 4D TMA box of the NHWC activation.
-    int tw = 1;
-    while (tw < outW && tw < 256) tw <<= 1;
-    const int th = 256 / tw;
-    const bool pair = d->use_pair && out_ch > BM;
-    CUtensorMap tB;
-    if (pair)  // each CTA of the pair fetches half of the 256-pixel tile
-      ENVG_TRY(tmap_nhwc(&tB, d->act.p, Cp, W_, H, batch, th >= 2 ? tw : tw / 2, th >= 2 ? th / 2 : 1));
-    else
-      ENVG_TRY(tmap_nhwc(&tB, d->act.p, Cp, W_, H, batch, tw, th));
-    GemmArgs g{};
-    g.num_kb = (int)(W->Kp / BK);
-    g.tiles_m = (int)cdiv(out_ch, pair ? 2 * BM : BM);
-    g.conv.tileW = tw;
-    g.conv.tileH = th;
-    g.conv.outH = outH;
-    g.conv.outW = outW;
-    g.conv.tiles_w = (int)cdiv(outW, tw);
-    g.conv.tiles_h = (int)cdiv(outH, th);
-    g.conv.KW = kW;
-    g.conv.pad = pad;
-    g.conv.cblocks = Cp / BK;
-    g.conv.img_stride = (int64_t)out_ch * plane;
-    g.conv.plane = plane;
-    g.tiles_n = batch * g.conv.tiles_w * g.conv.tiles_h;
-    g.num_tiles = g.tiles_m * g.tiles_n;
-    g.group_m = 1;
-    e.ldy = plane;
-    e.n_out = (int)plane;
-    e.vec_ok = ((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 4 == 0) ? 1 : 0;
-    CUtensorMap tY;
-    memset(&tY, 0, sizeof(tY));
-    e.store_mode = (tw >= 32) ? STORE_COALESCED : STORE_DIRECT;  // a 32-pixel chunk stays in one row
-    if (d->store_tma && (reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 32 == 0) {
-      ENVG_TRY(tmap_out_3d(&tY, dy, (uint64_t)plane, (uint64_t)out_ch, (uint64_t)batch));
-      e.store_mode = STORE_TMA;
-    }
-    g.epi = e;
-    const double cflops = 2.0 * out_ch * (double)plane * batch * (double)W->K;
-    const double cbytes = 2.0 * (double)batch * H * W_ * Cp + 2.0 * out_ch * (double)W->Kp + 4.0 * (double)out_elems +
-                          (dbias ? 4.0 * out_ch : 0.0);
-    if (pair) ENVG_TRY(launch_k1_pair<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
-    else ENVG_TRY(launch_k1<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
-  } else {
-    // Strided convolution: explicit bf16 im2col, then one GEMM per image.
-    const int64_t colK = W->Kp;
-    ENVG_TRY(ensure(d, d->col, (size_t)batch * plane * colK * 2));
-    const int64_t total = (int64_t)batch * plane * kH * kW * (Cp / 8);
-    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(total, 256), (int64_t)d->sms * 16));
-    ProfScope ps_im(s, KID_IM2COL, 0.0, 2.0 * (double)batch * H * W_ * Cp + 2.0 * (double)batch * plane * colK);
-    k_im2col_nhwc<<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(d->act.p), batch, H, W_, Cp, kH, kW,
-                                         stride, pad, outH, outW, reinterpret_cast<__nv_bfloat16*>(d->col.p));
-    ENVG_CUDA(cudaGetLastError());
-    d->st.kernel_launches++;
-    for (int b = 0; b < batch; ++b) {
-      const void* colb = reinterpret_cast<const uint8_t*>(d->col.p) + (size_t)b * plane * colK * 2;
-      CUtensorMap tB;
-      ENVG_TRY(tmap_2d(&tB, colb, colK, plane, 256));
-      CUtensorMap tA = W->tm128;
-      GemmArgs g{};
-      g.num_kb = (int)(colK / BK);
-      g.tiles_m = (int)cdiv(out_ch, BM);
-      g.tiles_n = (int)cdiv(plane, K1_BN);
-      g.num_tiles = g.tiles_m * g.tiles_n;
-      g.group_m = 8;
-      EpiArgs eb = e;
-      eb.Y = dy + (int64_t)b * out_ch * plane;
-      eb.ldy = plane;
-      eb.n_out = (int)plane;
-      eb.vec_ok = ((reinterpret_cast<uintptr_t>(eb.Y) & 15) == 0 && plane % 4 == 0) ? 1 : 0;
-      CUtensorMap tY;
-      memset(&tY, 0, sizeof(tY));
-      ENVG_TRY(choose_store(d->store_tma, eb, &tY));
-      g.epi = eb;
-      ENVG_TRY(launch_k1<false, false>(d, tA, tB, tY, g, 2.0 * out_ch * (double)plane * (double)W->K,
-                                       2.0 * (double)plane * colK + 2.0 * out_ch * (double)colK + 4.0 * out_ch * (double)plane));
-    }
-  }
+  ENVG_TRY(conv_core(d, W, d->act.p, dy, dbias, H, W_, stride, pad, batch, epilogue == ENVG_EPI_SILU ? 1 : 0, false));
   d->st.calls++;
   d->st.flops += 2.0 * (double)out_ch * (double)plane * (double)batch * (double)W->K;
+  if (!devp) {
+    ENVG_CUDA(cudaMemcpyAsync(dst, dy, (size_t)out_elems * 4, cudaMemcpyDeviceToHost, s));
+    d->st.d2h_bytes += (double)out_elems * 4;
+    return sync_and_check(d);
+  }
+  if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
+  return ENVG_OK;
+}
+
+int envg_group_norm(float* dst, const float* src, const float* gamma, const float* beta, int batch, int channels, int H,
+                    int W_, int num_groups, int act_silu, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  ENVG_TRY(check_gn_geometry(batch, channels, H, W_, num_groups));
+  if (batch == 0) return ENVG_OK;
+  if (!dst || !src) return fail(ENVG_ERR_ARG, "group norm: dst or src is NULL");
+  const bool devp = (flags & ENVG_DEVICE_PTRS) != 0;
+  cudaStream_t s = stream_of(d);
+  const int64_t HW = (int64_t)H * W_, elems = (int64_t)batch * channels * HW;
+  const float* dsrc = src;
+  float* dy = dst;
+  ENVG_TRY(ensure(d, d->gn, gn_bytes(batch, channels, HW, num_groups)));
+  if (!devp) {
+    ENVG_TRY(ensure(d, d->x, (size_t)elems * 4));
+    ENVG_TRY(ensure(d, d->vec, (size_t)2 * rup((int64_t)channels * 4, 256)));
+    ENVG_CUDA(cudaMemcpyAsync(d->x.p, src, (size_t)elems * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)elems * 4;
+    dsrc = reinterpret_cast<float*>(d->x.p);
+    dy = reinterpret_cast<float*>(d->x.p);  // applied in place on the device copy
+  }
+  VecStage vs{d, devp};
+  const float *g = nullptr, *b = nullptr;
+  ENVG_TRY(vs.put(gamma, channels, &g));
+  ENVG_TRY(vs.put(beta, channels, &b));
+  float2* aff = nullptr;
+  ENVG_TRY(launch_group_affine(d, dsrc, batch, channels, HW, num_groups, g, b, &aff));
+  {
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(elems, 256), (int64_t)d->sms * 8));
+    ProfScope ps(s, KID_GN_APPLY, 0.0, 8.0 * (double)elems);
+    k_group_apply<<<blocks, 256, 0, s>>>(dsrc, dy, HW, batch * channels, aff, act_silu);
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches++;
+  }
+  d->st.calls++;
+  if (!devp) {
+    ENVG_CUDA(cudaMemcpyAsync(dst, dy, (size_t)elems * 4, cudaMemcpyDeviceToHost, s));
+    d->st.d2h_bytes += (double)elems * 4;
+    return sync_and_check(d);
+  }
+  if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
+  return ENVG_OK;
+}
+
+int envg_vae_resblock(float* dst, const float* src, const envg_resblock* rb, int batch, int H, int W_, int num_groups,
+                      int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (!rb) return fail(ENVG_ERR_ARG, "resblock: descriptor is NULL");
+  const int Ci = rb->in_ch, Co = rb->out_ch;
+  ENVG_TRY(check_weight(d, rb->conv1));
+  ENVG_TRY(check_weight(d, rb->conv2));
+  auto conv_is = [](envg_weight w, int o, int c, int k) {
+    return w->conv && w->out_ch == o && w->in_ch == c && w->kH == k && w->kW == k;
+  };
+  if (!conv_is(rb->conv1, Co, Ci, 3)) return fail(ENVG_ERR_ARG, "resblock: conv1 is not a 3x3 %d -> %d conv", Ci, Co);
+  if (!conv_is(rb->conv2, Co, Co, 3)) return fail(ENVG_ERR_ARG, "resblock: conv2 is not a 3x3 %d -> %d conv", Co, Co);
+  if (rb->skip) {
+    ENVG_TRY(check_weight(d, rb->skip));
+    if (!conv_is(rb->skip, Co, Ci, 1)) return fail(ENVG_ERR_ARG, "resblock: skip is not a 1x1 %d -> %d conv", Ci, Co);
+  } else if (Ci != Co) {
+    return fail(ENVG_ERR_ARG, "resblock: in_ch %d != out_ch %d needs a skip conv", Ci, Co);
+  }
+  ENVG_TRY(check_gn_geometry(batch, Ci, H, W_, num_groups));
+  ENVG_TRY(check_gn_geometry(batch, Co, H, W_, num_groups));
+  if (batch == 0) return ENVG_OK;
+  if (!dst || !src) return fail(ENVG_ERR_ARG, "resblock: dst or src is NULL");
+  if ((const void*)dst == (const void*)src) return fail(ENVG_ERR_ARG, "resblock: dst aliases src");
+  const bool devp = (flags & ENVG_DEVICE_PTRS) != 0;
+  cudaStream_t s = stream_of(d);
+  const int64_t HW = (int64_t)H * W_;
+  const int64_t in_elems = (int64_t)batch * Ci * HW, out_elems = (int64_t)batch * Co * HW;
+  const int Cp = (int)std::max(rb->conv1->Cp, rb->conv2->Cp);
+  ENVG_TRY(ensure(d, d->gn, std::max(gn_bytes(batch, Ci, HW, num_groups), gn_bytes(batch, Co, HW, num_groups))));
+  ENVG_TRY(ensure(d, d->act, (size_t)batch * HW * Cp * 2));
+  ENVG_TRY(ensure(d, d->c1, (size_t)out_elems * 4));
+  const float* dsrc = src;
+  float* dy = dst;
+  if (!devp) {
+    ENVG_TRY(ensure(d, d->x, (size_t)in_elems * 4));
+    ENVG_TRY(ensure(d, d->y, (size_t)out_elems * 4));
+    ENVG_TRY(ensure(d, d->vec, (size_t)2 * rup((int64_t)Ci * 4, 256) + 5 * rup((int64_t)Co * 4, 256)));
+    ENVG_CUDA(cudaMemcpyAsync(d->x.p, src, (size_t)in_elems * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)in_elems * 4;
+    dsrc = reinterpret_cast<float*>(d->x.p);
+    dy = reinterpret_cast<float*>(d->y.p);
+  }
+  VecStage vs{d, devp};
+  const float *g1, *b1, *cb1, *g2, *b2, *cb2, *sb;
+  ENVG_TRY(vs.put(rb->norm1_gamma, Ci, &g1));
+  ENVG_TRY(vs.put(rb->norm1_beta, Ci, &b1));
+  ENVG_TRY(vs.put(rb->conv1_bias, Co, &cb1));
+  ENVG_TRY(vs.put(rb->norm2_gamma, Co, &g2));
+  ENVG_TRY(vs.put(rb->norm2_beta, Co, &b2));
+  ENVG_TRY(vs.put(rb->conv2_bias, Co, &cb2));
+  ENVG_TRY(vs.put(rb->skip_bias, Co, &sb));
+  float* c1 = reinterpret_cast<float*>(d->c1.p);
+  // skip path into dst
+  if (rb->skip) {
+    const int Cs = rb->skip->Cp;
+    ENVG_TRY(launch_transpose_cast(d, dsrc, HW, (int64_t)Ci * HW, Ci, (int)HW, d->act.p, Cs, HW * Cs, Cs, batch));
+    ENVG_TRY(conv_core(d, rb->skip, d->act.p, dy, sb, H, W_, 1, 0, batch, 0, false));
+  } else {
+    ENVG_CUDA(cudaMemcpyAsync(dy, dsrc, (size_t)in_elems * 4, cudaMemcpyDeviceToDevice, s));
+  }
+  // conv1(SiLU(GN1(src)))
+  float2* aff = nullptr;
+  ENVG_TRY(launch_group_affine(d, dsrc, batch, Ci, HW, num_groups, g1, b1, &aff));
+  const int C1p = rb->conv1->Cp, C2p = rb->conv2->Cp;
+  ENVG_TRY(launch_transpose_cast(d, dsrc, HW, (int64_t)Ci * HW, Ci, (int)HW, d->act.p, C1p, HW * C1p, C1p, batch, aff, 1));
+  ENVG_TRY(conv_core(d, rb->conv1, d->act.p, c1, cb1, H, W_, 1, 1, batch, 0, false));
+  // dst += conv2(SiLU(GN2(c1)))
+  ENVG_TRY(launch_group_affine(d, c1, batch, Co, HW, num_groups, g2, b2, &aff));
+  ENVG_TRY(launch_transpose_cast(d, c1, HW, (int64_t)Co * HW, Co, (int)HW, d->act.p, C2p, HW * C2p, C2p, batch, aff, 1));
+  ENVG_TRY(conv_core(d, rb->conv2, d->act.p, dy, cb2, H, W_, 1, 1, batch, 0, true));
+  d->st.calls++;
+  d->st.flops += 2.0 * (double)batch * HW * ((double)Co * rb->conv1->K + (double)Co * rb->conv2->K +
+                                             (rb->skip ? (double)Co * Ci : 0.0));
   if (!devp) {
     ENVG_CUDA(cudaMemcpyAsync(dst, dy, (size_t)out_elems * 4, cudaMemcpyDeviceToHost, s));
     d->st.d2h_bytes += (double)out_elems * 4;

@@ -39,7 +39,7 @@ struct EpiArgs {
   int bias_mode;      // 0 none, 1 per output column, 2 per output row
   int act;            // 1: SiLU after the bias
   int mode;           // EpiMode
-  const float* gate;  // EPI_GATED_RES: per-column gate
+  const float* gate;  // EPI_GATED_RES: per-column gate (convolutions: no gate, Y += conv + bias)
   float alpha, beta;  // EPI_ALPHA_BETA: Y = alpha*acc + beta*Y
   int n_out;          // valid output columns
   int m_valid;        // valid output rows
@@ -53,6 +53,11 @@ struct EpiArgs {
   float* remote[8];
   int nremote;
   int col_off;
+  // Optional bf16 copy of the finished output (row stride ldyb elements, ldyb % 8 == 0): the
+  // activation operand of a following linear that reads this Y, written here instead of by a
+  // separate cast (row-major linears on the TMA / coalesced store paths only).
+  __nv_bfloat16* yb;
+  int64_t ldyb;
 };
 
 // Write one value / four consecutive values (16-byte aligned) at element offset idx of Y, on
@@ -264,13 +269,43 @@ ENVG_DEV void store_tile32_conv(const EpiArgs& e, const ConvGeom& g, const uint8
     const int wc = w + ch * 4;
     float* yp = e.Y + (int64_t)b * g.img_stride + (int64_t)oc * g.plane + (int64_t)h * g.outW + wc;
     if (e.vec_ok && wc + 3 < g.outW) {
-      *reinterpret_cast<float4*>(yp) = t;
+      float4 o = t;
+      if (e.mode == EPI_GATED_RES) {
+        const float4 old = *reinterpret_cast<const float4*>(yp);
+        o = make_float4(__fadd_rn(old.x, t.x), __fadd_rn(old.y, t.y), __fadd_rn(old.z, t.z), __fadd_rn(old.w, t.w));
+      }
+      *reinterpret_cast<float4*>(yp) = o;
     } else {
       const float tv[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        if (wc + j < g.outW) yp[j] = tv[j];
+        if (wc + j < g.outW) yp[j] = (e.mode == EPI_GATED_RES) ? __fadd_rn(yp[j], tv[j]) : tv[j];
     }
+  }
+}
+
+// bf16 (RNE) copy of the finished 32-column chunk [col0, col0+32) of row `row` into e.yb.
+ENVG_DEV void store_bf16_row32(const EpiArgs& e, int row, int col0, const float (&v)[32]) {
+  if (row >= e.m_valid) return;
+  __nv_bfloat16* p = e.yb + (int64_t)row * e.ldyb + col0;
+  if (col0 + 32 <= e.n_out) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 o;
+      __nv_bfloat162 h0 = __float22bfloat162_rn(make_float2(v[j + 0], v[j + 1]));
+      __nv_bfloat162 h1 = __float22bfloat162_rn(make_float2(v[j + 2], v[j + 3]));
+      __nv_bfloat162 h2 = __float22bfloat162_rn(make_float2(v[j + 4], v[j + 5]));
+      __nv_bfloat162 h3 = __float22bfloat162_rn(make_float2(v[j + 6], v[j + 7]));
+      o.x = *reinterpret_cast<uint32_t*>(&h0);
+      o.y = *reinterpret_cast<uint32_t*>(&h1);
+      o.z = *reinterpret_cast<uint32_t*>(&h2);
+      o.w = *reinterpret_cast<uint32_t*>(&h3);
+      *reinterpret_cast<uint4*>(p + j) = o;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < e.n_out) p[j] = __float2bfloat16_rn(v[j]);
   }
 }
 
@@ -321,13 +356,23 @@ ENVG_DEV void epi_store_conv32(const EpiArgs& e, const ConvGeom& g, int b, int o
     }
     float* yp = yplane + (int64_t)h * g.outW + w;
     if (e.vec_ok && (g.tileW % 4) == 0 && w + 3 < g.outW) {
+      if (e.mode == EPI_GATED_RES) {
+        const float4 old = *reinterpret_cast<const float4*>(yp);
+        o[0] = __fadd_rn(old.x, o[0]);
+        o[1] = __fadd_rn(old.y, o[1]);
+        o[2] = __fadd_rn(old.z, o[2]);
+        o[3] = __fadd_rn(old.w, o[3]);
+      }
       *reinterpret_cast<float4*>(yp) = make_float4(o[0], o[1], o[2], o[3]);
     } else {
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         const int jt = jj + t;
         const int ht = h0 + jt / g.tileW, wt = w0 + jt % g.tileW;
-        if (ht < g.outH && wt < g.outW) yplane[(int64_t)ht * g.outW + wt] = o[t];
+        if (ht < g.outH && wt < g.outW) {
+          float* q = yplane + (int64_t)ht * g.outW + wt;
+          *q = (e.mode == EPI_GATED_RES) ? __fadd_rn(*q, o[t]) : o[t];
+        }
       }
     }
   }
@@ -583,6 +628,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
         } else if (!SILU_GATE) {
           epi_pre_chunk(ep, v, row, col0);
         }
+        if (!CONV_B && ep.yb) store_bf16_row32(ep, row, col0, v);
         uint8_t* buf = stg + sb * 4096;
         if (smode == STORE_COALESCED) {
           stage_row32(buf, lane, v);
@@ -603,7 +649,10 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (CONV_B) tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+          if (CONV_B) {
+            if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&tmY, smem_u32(buf), x, y, b);
+            else tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+          }
           else if (smode == STORE_TMA_ADD) tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
           else tma_store_2d(&tmY, smem_u32(buf), x, y);
           bulk_commit();
@@ -882,6 +931,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
         } else if (!SILU_GATE) {
           epi_pre_chunk(ep, v, row, col0);
         }
+        if (!CONV_B && ep.yb) store_bf16_row32(ep, row, col0, v);
         uint8_t* buf = stg + sb * 4096;
         if (smode == STORE_COALESCED) {
           stage_row32(buf, lane, v);
@@ -902,7 +952,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (CONV_B) tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+          if (CONV_B) {
+            if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&tmY, smem_u32(buf), x, y, b);
+            else tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+          }
           else if (smode == STORE_TMA_ADD) tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
           else tma_store_2d(&tmY, smem_u32(buf), x, y);
           bulk_commit();
@@ -1319,7 +1372,40 @@ __global__ void k_cast_rows(const float* __restrict__ X, int64_t ldx, int rows, 
                             __nv_bfloat16* __restrict__ Xb, int vec8) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  if (vec8) {
+  if (vec8 == 2) {
+    // Contiguous rows (ldx == K == Kp, K % 8 == 0, 16-byte aligned): one flat run of 8-float
+    // groups, four groups in flight per thread (all loads issued before the first store).
+    const int64_t total = (int64_t)rows * (K / 8);
+    const float4* src = reinterpret_cast<const float4*>(X);
+    uint4* dst = reinterpret_cast<uint4*>(Xb);
+    for (int64_t i0 = tid; i0 < total; i0 += 4 * stride) {
+      float4 a[4], b[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = i0 + u * stride;
+        if (i < total) {
+          a[u] = __ldcs(src + 2 * i);
+          b[u] = __ldcs(src + 2 * i + 1);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = i0 + u * stride;
+        if (i < total) {
+          __nv_bfloat162 p0 = __float22bfloat162_rn(make_float2(a[u].x, a[u].y));
+          __nv_bfloat162 p1 = __float22bfloat162_rn(make_float2(a[u].z, a[u].w));
+          __nv_bfloat162 p2 = __float22bfloat162_rn(make_float2(b[u].x, b[u].y));
+          __nv_bfloat162 p3 = __float22bfloat162_rn(make_float2(b[u].z, b[u].w));
+          uint4 o;
+          o.x = *reinterpret_cast<uint32_t*>(&p0);
+          o.y = *reinterpret_cast<uint32_t*>(&p1);
+          o.z = *reinterpret_cast<uint32_t*>(&p2);
+          o.w = *reinterpret_cast<uint32_t*>(&p3);
+          dst[i] = o;
+        }
+      }
+    }
+  } else if (vec8) {
     // K == Kp, K % 8 == 0, ldx % 4 == 0, 16-byte aligned rows.
     const int kv = K / 8;
     const int64_t total = (int64_t)rows * kv;
@@ -1352,9 +1438,12 @@ __global__ void k_cast_rows(const float* __restrict__ X, int64_t ldx, int rows, 
 
 // src fp32 [batch][R][C] (row stride lds, batch stride sbs) -> dst bf16 [batch][C][Rp]
 // (row stride ldd, batch stride dbs), zeros for R <= r < Rp.  Rp must be even.
+// With aff set, each value first becomes x * aff[b*R + r].x + aff[b*R + r].y (the per-channel
+// form of a GroupNorm), then SiLU when act != 0: the GroupNorm + SiLU prologue of a conv.
 __global__ void __launch_bounds__(256) k_transpose_cast(const float* __restrict__ src, int64_t lds, int64_t sbs, int R,
                                                         int C, __nv_bfloat16* __restrict__ dst, int64_t ldd,
-                                                        int64_t dbs, int Rp) {
+                                                        int64_t dbs, int Rp, const float2* __restrict__ aff,
+                                                        int act) {
   __shared__ float t[64][33];
   const int c0 = blockIdx.x * 32;
   const int r0 = blockIdx.y * 64;
@@ -1365,7 +1454,16 @@ __global__ void __launch_bounds__(256) k_transpose_cast(const float* __restrict_
   for (int i = 0; i < 8; ++i) {
     const int rr = ty + i * 8;
     const int r = r0 + rr, c = c0 + tx;
-    t[rr][tx] = (r < R && c < C) ? __ldcs(s + (int64_t)r * lds + c) : 0.0f;
+    float v = 0.0f;
+    if (r < R && c < C) {
+      v = __ldcs(s + (int64_t)r * lds + c);
+      if (aff) {
+        const float2 a = __ldg(aff + (int64_t)b * R + r);
+        v = __fmaf_rn(v, a.x, a.y);
+      }
+      if (act) v = silu_f(v);
+    }
+    t[rr][tx] = v;
   }
   __syncthreads();
   __nv_bfloat16* d = dst + (int64_t)b * dbs;
@@ -1458,6 +1556,109 @@ __global__ void __launch_bounds__(256) k_adaln(const float* __restrict__ X, int6
       const float norm = __fmul_rn(__fsub_rn(xr[k], mean), inv);
       o[k] = __fadd_rn(__fmul_rn(__fadd_rn(1.0f, __ldg(scale + k)), norm), __ldg(shift + k));
     }
+  }
+}
+
+// ---- GroupNorm (QNNGroupNorm, src/quicknncpu.pas:2259-2313) --------------------------------
+// Group (b, g) of an NCHW tensor is the contiguous run of cpg * HW floats starting at
+// (b*C + g*cpg) * HW.  Statistics are taken in two launches:
+//   k_group_stats   grid (chunks, B*G): each CTA takes GN_CHUNK consecutive floats of one group
+//                   and writes {count, mean, M2} of its chunk (two passes over registers);
+//   k_group_affine  one thread per (b, c): merges its group's chunks in order (Chan et al.'s
+//                   pairwise update, fp64), then var = M2 / n (population, as QNNVariance),
+//                   std_inv = 1 / sqrt(var + eps) and the per-channel affine
+//                   a = gamma_c * std_inv, s = beta_c - mean * gamma_c * std_inv (QNNFusedScaleBias).
+constexpr int GN_THREADS = 256;
+constexpr int GN_PER_THREAD = 32;
+constexpr int GN_CHUNK = GN_THREADS * GN_PER_THREAD;  // 8192 floats
+
+ENVG_DEV double block_sum256_d(double v, double* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < GN_THREADS / 32; ++i) t += red[i];
+    red[8] = t;
+  }
+  __syncthreads();
+  return red[8];
+}
+
+__global__ void __launch_bounds__(GN_THREADS) k_group_stats(const float* __restrict__ X, int C, int64_t HW, int cpg,
+                                                            int groups, double* __restrict__ part, int chunks) {
+  __shared__ double red[9];
+  const int bg = blockIdx.y;
+  const int b = bg / groups, g = bg - b * groups;
+  const int64_t n = (int64_t)cpg * HW;
+  const int64_t c0 = (int64_t)blockIdx.x * GN_CHUNK;
+  const int64_t cn = min((int64_t)GN_CHUNK, n - c0);
+  const float* src = X + ((int64_t)b * C + (int64_t)g * cpg) * HW + c0;
+  float v[GN_PER_THREAD];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < GN_PER_THREAD; ++i) {
+    const int64_t k = threadIdx.x + (int64_t)i * GN_THREADS;
+    v[i] = k < cn ? __ldg(src + k) : 0.0f;
+    s += v[i];
+  }
+  const double mean = block_sum256_d((double)s, red) / (double)cn;
+  const float mf = (float)mean;
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < GN_PER_THREAD; ++i) {
+    const int64_t k = threadIdx.x + (int64_t)i * GN_THREADS;
+    const float dl = v[i] - mf;
+    if (k < cn) q = __fmaf_rn(dl, dl, q);
+  }
+  // M2 about the chunk mean in double: shift the fp32 deviations' sum back from mf to mean.
+  double dq = (double)q;
+  const double m2 = block_sum256_d(dq, red);
+  if (threadIdx.x == 0) {
+    const double dm = mean - (double)mf;  // |dm| is one fp32 ulp of the mean at most
+    double* o = part + ((int64_t)bg * chunks + blockIdx.x) * 3;
+    o[0] = (double)cn;
+    o[1] = mean;
+    o[2] = m2 - (double)cn * dm * dm;
+  }
+}
+
+__global__ void k_group_affine(const double* __restrict__ part, int chunks, int batch, int C, int cpg, int groups,
+                               const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+                               float2* __restrict__ aff) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= batch * C) return;
+  const int b = i / C, c = i - b * C, g = c / cpg;
+  const double* p = part + (int64_t)(b * groups + g) * chunks * 3;
+  double n = p[0], mean = p[1], m2 = p[2];
+  for (int k = 1; k < chunks; ++k) {
+    const double nb = p[3 * k], mb = p[3 * k + 1], qb = p[3 * k + 2];
+    const double nn = n + nb, dl = mb - mean;
+    mean += dl * (nb / nn);
+    m2 += qb + dl * dl * (n * nb / nn);
+    n = nn;
+  }
+  const float var = (float)(m2 / n);
+  const float std_inv = 1.0f / sqrtf(var + eps);
+  const float ga = gamma ? __ldg(gamma + c) : 1.0f;
+  const float be = beta ? __ldg(beta + c) : 0.0f;
+  const float a = __fmul_rn(ga, std_inv);
+  aff[i] = make_float2(a, __fsub_rn(be, __fmul_rn(__fmul_rn((float)mean, ga), std_inv)));
+}
+
+// dst[b][c][i] = act(src[b][c][i] * aff[b*C + c].x + aff[b*C + c].y), fp32 NCHW (in place allowed).
+__global__ void __launch_bounds__(256) k_group_apply(const float* src, float* dst, int64_t HW, int BC,
+                                                     const float2* __restrict__ aff, int act) {
+  const int64_t total = (int64_t)BC * HW;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const float2 a = __ldg(aff + i / HW);
+    float v = __fmaf_rn(src[i], a.x, a.y);
+    if (act) v = silu_f(v);
+    dst[i] = v;
   }
 }
 

@@ -133,6 +133,12 @@ ENVG_DEV void tma_reduce_add_2d(const void* desc, uint32_t src, int c0, int c1) 
                "r"(src), "r"(c0), "r"(c1)
                : "memory");
 }
+ENVG_DEV void tma_reduce_add_3d(const void* desc, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 ENVG_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N committed bulk groups still read their shared-memory source.
 template <int N>

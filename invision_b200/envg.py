@@ -54,6 +54,15 @@ class TensorInfo(ctypes.Structure):
                 ("offset", ctypes.c_int64), ("nbytes", ctypes.c_int64), ("dtype_name", ctypes.c_char * 16)]
 
 
+class ResBlockDesc(ctypes.Structure):
+    _fields_ = [("in_ch", ctypes.c_int), ("out_ch", ctypes.c_int),
+                ("norm1_gamma", ctypes.c_void_p), ("norm1_beta", ctypes.c_void_p),
+                ("conv1", ctypes.c_void_p), ("conv1_bias", ctypes.c_void_p),
+                ("norm2_gamma", ctypes.c_void_p), ("norm2_beta", ctypes.c_void_p),
+                ("conv2", ctypes.c_void_p), ("conv2_bias", ctypes.c_void_p),
+                ("skip", ctypes.c_void_p), ("skip_bias", ctypes.c_void_p)]
+
+
 class Stats(ctypes.Structure):
     _fields_ = [("calls", ctypes.c_uint64), ("kernel_launches", ctypes.c_uint64), ("flops", ctypes.c_double),
                 ("h2d_bytes", ctypes.c_double), ("d2h_bytes", ctypes.c_double), ("weight_bytes", ctypes.c_uint64),
@@ -91,6 +100,8 @@ def lib():
         L.envg_linear_nsplit.argtypes = [_vp, ctypes.POINTER(_vp), _ci, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64,
                                          _i64, _ci, _vp, _ci]
         L.envg_conv2d.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 11
+        L.envg_group_norm.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 7
+        L.envg_vae_resblock.argtypes = [_vp, _vp, ctypes.POINTER(ResBlockDesc), _ci, _ci, _ci, _ci, _ci]
         L.envg_sgemm.argtypes = [_ci, _ci, _ci, _i64, _i64, _i64, ctypes.c_float, _vp, _i64, _vp, _i64,
                                  ctypes.c_float, _vp, _i64]
         L.envg_set_stream.argtypes = [_vp]
@@ -390,6 +401,59 @@ def conv2d(dst, src, W, bias, stride, pad, epilogue=None, sync=True):
                                     epilogue, flags))
 
 
+def group_norm(dst, src, gamma, beta, num_groups, silu=False, sync=True):
+    """dst = GroupNorm(src) (+ SiLU), NCHW [B, C, H, W]: envg_group_norm (dst may be src)."""
+    flags = _mode(dst, src, gamma, beta)
+    if flags == DEVICE_PTRS and not sync:
+        flags |= ASYNC
+    B, C, H, Wd = src.shape
+    return _check(lib().envg_group_norm(_ptr(dst), _ptr(src), _ptr(gamma), _ptr(beta), B, C, H, Wd, num_groups,
+                                        1 if silu else 0, flags))
+
+
+class ResBlock:
+    """One VAE ResBlock (TVAEResBlock, quicknn_vae.pas:164-187) with device-resident conv weights.
+
+    ``p`` holds norm1_gamma/beta [in_ch], conv1_w [out, in, 3, 3], conv1_b, norm2_gamma/beta
+    [out_ch], conv2_w [out, out, 3, 3], conv2_b and, when in_ch != out_ch, skip_w [out, in, 1, 1]
+    and skip_b.  Conv weights are numpy uint16 (bf16 bits) or float32 (rounded RNE at upload);
+    the vectors are float32 numpy arrays (host calls) or CUDA tensors (device calls)."""
+
+    def __init__(self, p):
+        self.p = p
+        w1 = p["conv1_w"]
+        self.out_ch, self.in_ch = w1.shape[0], w1.shape[1]
+        self.conv1 = Weight(w1.reshape(self.out_ch, -1), conv=tuple(w1.shape))
+        w2 = p["conv2_w"]
+        self.conv2 = Weight(w2.reshape(w2.shape[0], -1), conv=tuple(w2.shape))
+        ws = p.get("skip_w")
+        self.skip = Weight(ws.reshape(ws.shape[0], -1), conv=tuple(ws.shape)) if ws is not None else None
+
+    def desc(self, vecs=None):
+        v = vecs or self.p
+        d = ResBlockDesc()
+        d.in_ch, d.out_ch = self.in_ch, self.out_ch
+        d.norm1_gamma, d.norm1_beta = _ptr(v.get("norm1_gamma")), _ptr(v.get("norm1_beta"))
+        d.conv1, d.conv1_bias = self.conv1.h, _ptr(v.get("conv1_b"))
+        d.norm2_gamma, d.norm2_beta = _ptr(v.get("norm2_gamma")), _ptr(v.get("norm2_beta"))
+        d.conv2, d.conv2_bias = self.conv2.h, _ptr(v.get("conv2_b"))
+        d.skip = self.skip.h if self.skip is not None else None
+        d.skip_bias = _ptr(v.get("skip_b"))
+        return d
+
+    def forward(self, dst, src, num_groups, vecs=None, sync=True):
+        """dst = skip(src) + conv2(SiLU(GN2(conv1(SiLU(GN1(src)))))): envg_vae_resblock.
+        ``vecs`` overrides the vectors of ``p`` (e.g. CUDA tensors for a device call)."""
+        v = vecs or self.p
+        flags = _mode(dst, src, *[v.get(k) for k in ("norm1_gamma", "norm1_beta", "conv1_b", "norm2_gamma",
+                                                      "norm2_beta", "conv2_b", "skip_b")])
+        if flags == DEVICE_PTRS and not sync:
+            flags |= ASYNC
+        B, C, H, Wd = src.shape
+        d = self.desc(v)
+        return _check(lib().envg_vae_resblock(_ptr(dst), _ptr(src), ctypes.byref(d), B, H, Wd, num_groups, flags))
+
+
 def sgemm(order, transA, transB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc):
     """cblas_sgemm-compatible call on host numpy buffers (envg_sgemm)."""
     for a in (A, B, C):
@@ -455,6 +519,13 @@ def QNNAdaLNLinear(dst, src, shift, scale, W, B, seqLen, inDIM, outDIM):
     _assert(W.N == outDIM and W.K == inDIM, "ERROR : QNNLinear weight shape mismatch")
     return linear_adaln(dst[:seqLen], src[:seqLen], shift, scale, W, bias=B,
                         epilogue=EPI_BIAS if B is not None else EPI_NONE)
+
+
+def QNNGroupNorm(dst, src, gamma, beta, batch, channels, H, W, num_groups):
+    """quicknncpu.pas:2259-2313 (NCHW)."""
+    _assert(channels % num_groups == 0, "ERROR [GroupNorm] : channels not divisible by groups")
+    return group_norm(dst.reshape(batch, channels, H, W), src.reshape(batch, channels, H, W), gamma, beta,
+                      num_groups)
 
 
 def QNNConv2d(dst, src, weights, bias, in_ch, out_ch, H, W, kH, kW, stride, padding, batch):

@@ -401,6 +401,45 @@ void envo_adaln(float* dst, const float* src, const float* bias, const float* sc
   }
 }
 
+// QNNGroupNorm (quicknncpu.pas:2259-2313), scalar build: per (batch, group) over the contiguous
+// run of channels_per_group * H * W floats, mean = QNNMean (sequential fp32 sum / n, :536-547 and
+// :679-685), variance = QNNVariance population form (sequential sum of squared differences / n,
+// :566-581 and :687-695), std_inv = 1 / sqrt(variance + EPSILON) (EPSILON = 1e-6,
+// quicknn_common.pas:51), then per channel QNNFusedScaleBias with scale = gamma*std_inv and
+// bias = beta - mean*gamma*std_inv (:769-780).  act != 0 applies QNNSiluInplace (:2372-2386,
+// scalar form) afterwards.  dst may equal src.
+void envo_group_norm(float* dst, const float* src, const float* gamma, const float* beta, int batch, int channels,
+                     int H, int W, int num_groups, int act) {
+  const float EPS = 1e-6f;
+  const int cpg = channels / num_groups;
+  const int64_t spatial = (int64_t)H * W;
+  const int64_t n = (int64_t)cpg * spatial;
+  for (int b = 0; b < batch; ++b)
+    for (int g = 0; g < num_groups; ++g) {
+      const int c_start = g * cpg;
+      const float* s1 = src + ((int64_t)b * channels + c_start) * spatial;
+      float* d1 = dst + ((int64_t)b * channels + c_start) * spatial;
+      float sum = 0.0f;
+      for (int64_t i = 0; i < n; ++i) sum = sum + s1[i];
+      const float mean = sum / (float)n;
+      float ssd = 0.0f;
+      for (int64_t i = 0; i < n; ++i) {
+        const float dl = s1[i] - mean;
+        ssd = ssd + dl * dl;
+      }
+      const float variance = ssd / (float)n;
+      const float std_inv = 1.0f / sqrtf(variance + EPS);
+      for (int c = 0; c < cpg; ++c) {
+        const float ga = gamma ? gamma[c + c_start] : 1.0f;
+        const float be = beta ? beta[c + c_start] : 0.0f;
+        const float scale = ga * std_inv;
+        const float bias = be - mean * ga * std_inv;
+        for (int64_t i = 0; i < spatial; ++i) d1[c * spatial + i] = s1[c * spatial + i] * scale + bias;
+      }
+    }
+  if (act) envo_silu(dst, (int64_t)batch * channels * spatial);
+}
+
 // QNNConv2d, im2col build (quicknncpu.pas:1958-2132).  fp32 weights [out_ch, in_ch, kH, kW].
 // Restated including its stride-1 copy, which is exact only for "same" padding
 // (outW == W); batches processed one after another, the col buffer row-tiled at

@@ -63,6 +63,7 @@ def lib():
         L.envo_gated_add.argtypes = [_f32p, _f32p, _f32p, _i64, _i64]
         L.envo_conv2d.argtypes = [ctypes.c_int, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 9
         L.envo_adaln.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64]
+        L.envo_group_norm.argtypes = [_f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 6
         L.envo_conv2d.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -187,6 +188,37 @@ def adaln(src, shift, scale):
     out = np.empty_like(src)
     lib().envo_adaln(_p(out), _p(src), _p(shift), _p(scale), seq, hidden)
     return out
+
+
+def group_norm(src, gamma, beta, num_groups, act=False):
+    """QNNGroupNorm (+ QNNSiluInplace when act): src fp32 [B, C, H, W] -> new array."""
+    src = _chk(np.ascontiguousarray(src), np.float32)
+    B, C, H, W = src.shape
+    g = None if gamma is None else _chk(np.ascontiguousarray(gamma), np.float32)
+    b = None if beta is None else _chk(np.ascontiguousarray(beta), np.float32)
+    out = np.empty_like(src)
+    lib().envo_group_norm(_p(out), _p(src), _p(g) if g is not None else None, _p(b) if b is not None else None,
+                          B, C, H, W, num_groups, 1 if act else 0)
+    return out
+
+
+def vae_resblock(src, p, num_groups, path=PATH_AVX2):
+    """TVAEResBlock.forward (quicknn_vae.pas:164-187) on fp32 weights.
+
+    p: dict with norm1_gamma, norm1_beta, conv1_w [O, C, 3, 3], conv1_b, norm2_gamma, norm2_beta,
+    conv2_w [O, O, 3, 3], conv2_b and, when in_ch != out_ch, skip_w [O, C, 1, 1], skip_b.
+    dst := skip(src); work := SiLU(GN1(src)); c1 := conv1(work); work := SiLU(GN2(c1));
+    c1 := conv2(work); dst += c1 (QNNAddInplace, quicknncpu.pas:704-709)."""
+    src = _chk(np.ascontiguousarray(src), np.float32)
+    if p.get("skip_w") is not None:
+        dst = conv2d(src, p["skip_w"], p.get("skip_b"), 1, 0, path=path)
+    else:
+        dst = src.copy()
+    work = group_norm(src, p["norm1_gamma"], p["norm1_beta"], num_groups, act=True)
+    c1 = conv2d(work, p["conv1_w"], p["conv1_b"], 1, 1, path=path)
+    work = group_norm(c1, p["norm2_gamma"], p["norm2_beta"], num_groups, act=True)
+    c2 = conv2d(work, p["conv2_w"], p["conv2_b"], 1, 1, path=path)
+    return (dst + c2).astype(np.float32)
 
 
 def conv2d(src, w, bias, stride, padding, path=PATH_AVX2):

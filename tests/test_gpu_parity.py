@@ -295,13 +295,20 @@ def test_linear_batch_equals_separate_calls(gpu):
     Wgu = gpu.Weight(wt(2 * F, H, 4), layout=gpu.LAYOUT_GATE_UP)
     Wd = gpu.Weight(wt(H, F, 5))
     Ws = gpu.Weight(wt(520, H, 6))
+    Wr, Wr2 = gpu.Weight(wt(201, H, 7)), gpu.Weight(wt(96, 201, 8))
     b = torch.from_numpy((0.01 * rng.standard_normal(H)).astype(np.float32)).to(dev)
-    outs = {k: torch.empty(M, H, device=dev) for k in ("q", "k", "v", "d")}
+    outs = {k: torch.empty(M, H, device=dev) for k in ("q", "k", "v", "d", "q2")}
     outs["gu"] = torch.empty(M, F, device=dev)
     outs["s"] = torch.empty(4, 520, device=dev)
+    outs["r"] = torch.empty(M, 201, device=dev)
+    outs["r2"] = torch.empty(M, 96, device=dev)
+    # chains: gu -> d (SiLU-gate producer) and q -> q2 (bias producer) hand their bf16 copy over in
+    # the producer's epilogue; r -> r2 (K = 201, not a multiple of 8) goes through a cast.
     calls = [dict(dst=outs["q"], x=x, W=Wq, bias=b), dict(dst=outs["k"], x=x, W=Wk),
              dict(dst=outs["v"], x=x, W=Wv, bias=b), dict(dst=outs["gu"], x=x2, W=Wgu),
-             dict(dst=outs["d"], x=outs["gu"], W=Wd, bias=b), dict(dst=outs["s"], x=xs, W=Ws)]
+             dict(dst=outs["d"], x=outs["gu"], W=Wd, bias=b), dict(dst=outs["s"], x=xs, W=Ws),
+             dict(dst=outs["q2"], x=outs["q"], W=Wk), dict(dst=outs["r"], x=x2, W=Wr),
+             dict(dst=outs["r2"], x=outs["r"], W=Wr2)]
     gpu.linear_batch(calls)
     torch.cuda.synchronize()
     got = {k: v.cpu().numpy() for k, v in outs.items()}
@@ -377,3 +384,89 @@ def test_safetensors_upload_matches_array_upload(gpu, tmp_path):
     np.testing.assert_array_equal(yc_file, yc_arr)
     with pytest.raises(gpu.EnvgError):
         gpu.Weight.from_safetensors(p, "conv", shard=(0, 8))
+
+
+def _resblock_params(rng, Ci, Co, skip):
+    def bfw(shape, s):
+        return O.f32_to_bf16_rne((s * rng.standard_normal(shape)).astype(np.float32))
+
+    p = {"norm1_gamma": (1 + 0.1 * rng.standard_normal(Ci)).astype(np.float32),
+         "norm1_beta": (0.1 * rng.standard_normal(Ci)).astype(np.float32),
+         "conv1_w": bfw((Co, Ci, 3, 3), 0.03), "conv1_b": (0.01 * rng.standard_normal(Co)).astype(np.float32),
+         "norm2_gamma": (1 + 0.1 * rng.standard_normal(Co)).astype(np.float32),
+         "norm2_beta": (0.1 * rng.standard_normal(Co)).astype(np.float32),
+         "conv2_w": bfw((Co, Co, 3, 3), 0.03), "conv2_b": (0.01 * rng.standard_normal(Co)).astype(np.float32)}
+    if skip:
+        p["skip_w"] = bfw((Co, Ci, 1, 1), 0.1)
+        p["skip_b"] = (0.01 * rng.standard_normal(Co)).astype(np.float32)
+    return p
+
+
+def _oracle_params(p):
+    q = dict(p)
+    for k in ("conv1_w", "conv2_w", "skip_w"):
+        if k in q:
+            q[k] = O.bf16_to_f32(q[k])
+    return q
+
+
+@pytest.mark.parametrize("B,C,H,W,G,silu", [(1, 128, 32, 32, 32, True), (2, 64, 24, 40, 8, False),
+                                             (1, 96, 7, 9, 32, True), (1, 32, 256, 256, 32, True)])
+def test_group_norm_vs_oracle(gpu, B, C, H, W, G, silu):
+    rng = np.random.default_rng(B + C + H + W)
+    x = (0.5 + 2 * rng.standard_normal((B, C, H, W))).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    beta = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    y = np.full_like(x, np.nan)
+    gpu.group_norm(y, x, gamma, beta, G, silu=silu)
+    ref = O.group_norm(x, gamma, beta, G, act=silu)
+    # fp32 elementwise op: statistics in fp64 partials vs the reference's sequential fp32 sums
+    assert_parity(y, ref, tol_max=1e-4, tol_mean=1e-5, what=f"group_norm {B}x{C}x{H}x{W} G{G} silu={silu}")
+
+
+@pytest.mark.parametrize("B,Ci,Co,H,W,G", [(1, 128, 256, 32, 32, 32),   # skip conv, TMA reduce-add store
+                                           (1, 128, 128, 24, 40, 32),   # identity skip, non-TMA residual store
+                                           (2, 64, 64, 16, 16, 16),
+                                           (1, 64, 128, 9, 13, 32)])    # ragged image
+def test_vae_resblock_vs_oracle(gpu, B, Ci, Co, H, W, G):
+    rng = np.random.default_rng(Ci * 7 + Co + H)
+    x = rng.standard_normal((B, Ci, H, W)).astype(np.float32)
+    p = _resblock_params(rng, Ci, Co, Ci != Co)
+    rb = gpu.ResBlock(p)
+    y = np.full((B, Co, H, W), np.nan, np.float32)
+    rb.forward(y, x, G)
+    ref = O.vae_resblock(x, _oracle_params(p), G)
+    assert_parity(y, ref, what=f"resblock {B}x{Ci}->{Co} {H}x{W} G{G}")
+
+
+def test_vae_resblock_device_pointers_match_host(gpu):
+    import torch
+
+    rng = np.random.default_rng(5)
+    B, Ci, Co, H, W, G = 1, 64, 128, 64, 64, 32
+    x = rng.standard_normal((B, Ci, H, W)).astype(np.float32)
+    p = _resblock_params(rng, Ci, Co, True)
+    rb = gpu.ResBlock(p)
+    y_host = np.zeros((B, Co, H, W), np.float32)
+    rb.forward(y_host, x, G)
+    vecs = {k: torch.from_numpy(v).cuda() for k, v in p.items() if not k.endswith("_w")}
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.full((B, Co, H, W), float("nan"), device="cuda")
+    rb.forward(yd, xd, G, vecs=vecs)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(yd.cpu().numpy(), y_host)
+
+
+def test_resblock_argument_errors(gpu):
+    rng = np.random.default_rng(6)
+    p = _resblock_params(rng, 64, 128, False)   # in != out without a skip conv
+    rb = gpu.ResBlock(p)
+    x = np.zeros((1, 64, 8, 8), np.float32)
+    y = np.zeros((1, 128, 8, 8), np.float32)
+    with pytest.raises(gpu.EnvgError) as e:
+        rb.forward(y, x, 32)
+    assert "skip" in str(e.value)
+    p2 = _resblock_params(rng, 64, 64, False)
+    rb2 = gpu.ResBlock(p2)
+    with pytest.raises(gpu.EnvgError):
+        rb2.forward(np.zeros((1, 64, 8, 8), np.float32), x, 48)   # 64 % 48 != 0

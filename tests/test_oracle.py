@@ -162,3 +162,60 @@ def test_adaln_vs_fp64():
     var = ((xd - mu) ** 2).mean(1, keepdims=True)
     ref = (1 + scale) * (xd - mu) / np.sqrt(var + 1e-6) + shift
     np.testing.assert_allclose(y, ref, rtol=2e-4, atol=2e-4)
+
+
+def _gn_fp64(x, gamma, beta, G, eps=1e-6):
+    B, C, H, W = x.shape
+    xd = x.astype(np.float64).reshape(B, G, -1)
+    mu = xd.mean(2, keepdims=True)
+    var = ((xd - mu) ** 2).mean(2, keepdims=True)
+    y = ((xd - mu) / np.sqrt(var + eps)).reshape(B, C, H, W)
+    return y * gamma.reshape(1, C, 1, 1) + beta.reshape(1, C, 1, 1)
+
+
+def test_group_norm_vs_fp64():
+    rng = np.random.default_rng(21)
+    x = (1.5 + 2 * rng.standard_normal((2, 64, 12, 10))).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(64)).astype(np.float32)
+    beta = (0.1 * rng.standard_normal(64)).astype(np.float32)
+    y = O.group_norm(x, gamma, beta, 32)
+    np.testing.assert_allclose(y, _gn_fp64(x, gamma, beta, 32), rtol=2e-4, atol=2e-4)
+    ys = O.group_norm(x, gamma, beta, 8, act=True)
+    r = _gn_fp64(x, gamma, beta, 8)
+    np.testing.assert_allclose(ys, r / (1 + np.exp(-r)), rtol=2e-3, atol=2e-3)   # fast_exp SiLU
+
+
+def test_vae_resblock_composition():
+    """The ResBlock oracle is skip + conv2(SiLU(GN2(conv1(SiLU(GN1(x)))))), checked against fp64."""
+    rng = np.random.default_rng(22)
+    B, Ci, Co, H, W, G = 1, 32, 64, 8, 8, 8
+    x = rng.standard_normal((B, Ci, H, W)).astype(np.float32)
+    p = {"norm1_gamma": (1 + 0.1 * rng.standard_normal(Ci)).astype(np.float32),
+         "norm1_beta": (0.1 * rng.standard_normal(Ci)).astype(np.float32),
+         "conv1_w": (0.05 * rng.standard_normal((Co, Ci, 3, 3))).astype(np.float32),
+         "conv1_b": (0.01 * rng.standard_normal(Co)).astype(np.float32),
+         "norm2_gamma": (1 + 0.1 * rng.standard_normal(Co)).astype(np.float32),
+         "norm2_beta": (0.1 * rng.standard_normal(Co)).astype(np.float32),
+         "conv2_w": (0.05 * rng.standard_normal((Co, Co, 3, 3))).astype(np.float32),
+         "conv2_b": (0.01 * rng.standard_normal(Co)).astype(np.float32),
+         "skip_w": (0.1 * rng.standard_normal((Co, Ci, 1, 1))).astype(np.float32),
+         "skip_b": (0.01 * rng.standard_normal(Co)).astype(np.float32)}
+    y = O.vae_resblock(x, p, G, path=O.PATH_SCALAR)
+
+    def conv(a, w, b, pad):
+        a = a.astype(np.float64)
+        O_, C, kh, kw = w.shape
+        ap = np.pad(a, ((0, 0), (0, 0), (pad, pad), (pad, pad)))
+        out = np.zeros((a.shape[0], O_, H, W))
+        for i in range(kh):
+            for j in range(kw):
+                out += np.einsum("oc,bchw->bohw", w[:, :, i, j], ap[:, :, i:i + H, j:j + W])
+        return out + b.reshape(1, -1, 1, 1)
+
+    def silu(v):
+        return v / (1 + np.exp(-v))
+
+    h = conv(silu(_gn_fp64(x, p["norm1_gamma"], p["norm1_beta"], G)), p["conv1_w"], p["conv1_b"], 1)
+    h = conv(silu(_gn_fp64(h, p["norm2_gamma"], p["norm2_beta"], G)), p["conv2_w"], p["conv2_b"], 1)
+    ref = conv(x, p["skip_w"], p["skip_b"], 0) + h
+    np.testing.assert_allclose(y, ref, rtol=5e-3, atol=5e-3)
