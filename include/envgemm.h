@@ -226,6 +226,21 @@ typedef struct envg_resblock {
 int envg_vae_resblock(float* dst, const float* src, const envg_resblock* rb, int batch, int H,
                       int W, int num_groups, int flags);
 
+/* Multi-head attention, per head h (kv head h / (heads / kv_heads)):
+ *   dst[:, h*hd : (h+1)*hd] = softmax(scale * Q_h K_kv^T + mask) V_kv
+ * Q [seq_q, ldq], K and V [seq_k, ldk / ldv], dst [seq_q, ldo] fp32 row-major, head h at column
+ * h * head_dim (the reference's [seq, hidden] layout).  Replaces the per-head cblas_gemm +
+ * QNNSoftmaxRows + cblas_gemm of TTransformerFlux.multiHeadForward / jointAttentionForward
+ * (quicknn_transformers.pas:1150-1270) and of the Qwen3 attention (quicknn_qwen3.pas:726-768,
+ * GQA), and QNNFlashAttention(dst, Q, K, V, heads, seq_q, seq_k, head_dim, scale)
+ * (quicknncpu.pas:2763-2860).  causal != 0 hides key c from query r when c > r + (seq_k -
+ * seq_q) (QNNMatTriangularFill for seq_q == seq_k); key_mask (int32 [seq_k], may be NULL) hides
+ * keys whose entry is 0.  Q, K and V are rounded to bf16 (RNE); both matrix products accumulate
+ * in fp32; softmax is fp32.  head_dim must be 128 in this build. */
+int envg_attention(float* dst, const float* Q, const float* K, const float* V, int seq_q, int seq_k,
+                   int heads, int kv_heads, int head_dim, int64_t ldq, int64_t ldk, int64_t ldv,
+                   int64_t ldo, float scale, int causal, const int32_t* key_mask, int flags);
+
 /* The modulated linear of the FLUX blocks: QNNAdaLN (quicknn_kernels.pas:315 ->
  * quicknncpu.pas:3042-3060; call sites quicknn_transformers.pas:1400,1410,1440,1449,1500) followed
  * by QNNLinear, with the normalisation fused into the activation cast:

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "../../include/envgemm.h"
+#include "attention.cuh"
 #include "kernels.cuh"
 #include "safetensors.hpp"
 
@@ -81,6 +82,7 @@ struct Dev {
   cudaStream_t user = nullptr;
   Buf x, y, xb, wb, part, cnt, bias, gate, act, col, b32, xbatch, ada, xn;
   Buf gn, c1, vec;  // GroupNorm statistics + affine, ResBlock conv1 output, small parameter vectors
+  Buf fa, fain;     // attention operands (bf16 Q / K / V^T + key bits), host-call staging
   cudaStream_t aux = nullptr;              // second stream of envg_linear_batch
   std::vector<cudaEvent_t> batch_events;   // reused event pool of envg_linear_batch
   int* h_status = nullptr;  // mapped pinned: [0] status code, [1] wait site
@@ -94,7 +96,8 @@ struct Dev {
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
-           col.bytes + b32.bytes + xbatch.bytes + ada.bytes + xn.bytes + gn.bytes + c1.bytes + vec.bytes;
+           col.bytes + b32.bytes + xbatch.bytes + ada.bytes + xn.bytes + gn.bytes + c1.bytes + vec.bytes +
+           fa.bytes + fain.bytes;
   }
 };
 
@@ -105,13 +108,14 @@ int g_cur = -1;
 // ---- optional per-launch timing (envg_profile) ---------------------------------------------
 enum KernelId {
   KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_ADALN, KID_TRANSPOSE, KID_IM2COL,
-  KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_COUNT
+  KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_ATTN, KID_CAST_HEADS, KID_KEY_BITS, KID_ABSMAX, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate", "k1_gemm_conv",
                                              "k2_skinny",   "k_gemv",            "k_cast_rows",
                                              "k_adaln",     "k_transpose_cast",  "k_im2col_nhwc",
                                              "k_wait_selftest", "k_group_stats",     "k_group_affine",
-                                             "k_group_apply"};
+                                             "k_group_apply",   "k_attention",       "k_cast_heads",
+                                             "k_key_bits",      "k_absmax_heads"};
 struct KAcc {
   uint64_t launches = 0;
   double ms = 0, flops = 0, bytes = 0;
@@ -880,7 +884,7 @@ int envg_shutdown(void) {
   cudaStreamSynchronize(stream_of(d));
   Buf* bufs[] = {&d->x,    &d->y,   &d->xb,  &d->wb,  &d->part,  &d->cnt,
                  &d->bias, &d->gate, &d->act, &d->col, &d->b32, &d->xbatch, &d->ada, &d->xn,
-                 &d->gn,   &d->c1,   &d->vec};
+                 &d->gn,   &d->c1,   &d->vec,  &d->fa,  &d->fain};
   for (Buf* b : bufs) {
     if (b->p) cudaFree(b->p);
     *b = Buf{};
@@ -1824,6 +1828,142 @@ int envg_vae_resblock(float* dst, const float* src, const envg_resblock* rb, int
   if (!devp) {
     ENVG_CUDA(cudaMemcpyAsync(dst, dy, (size_t)out_elems * 4, cudaMemcpyDeviceToHost, s));
     d->st.d2h_bytes += (double)out_elems * 4;
+    return sync_and_check(d);
+  }
+  if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
+  return ENVG_OK;
+}
+
+int envg_attention(float* dst, const float* Q, const float* K, const float* V, int seq_q, int seq_k, int heads,
+                   int kv_heads, int head_dim, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, float scale,
+                   int causal, const int32_t* key_mask, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (head_dim != FA_D) return fail(ENVG_ERR_UNSUPPORTED, "attention: head_dim %d (this build: 128)", head_dim);
+  if (seq_q < 0 || seq_k <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads)
+    return fail(ENVG_ERR_ARG, "attention: seq_q %d, seq_k %d, heads %d, kv_heads %d invalid", seq_q, seq_k, heads,
+                kv_heads);
+  if (heads > 65535) return fail(ENVG_ERR_UNSUPPORTED, "attention: more than 65535 heads");
+  if (causal && seq_k < seq_q) return fail(ENVG_ERR_ARG, "attention: causal needs seq_k >= seq_q");
+  if (ldq < (int64_t)heads * FA_D || ldk < (int64_t)kv_heads * FA_D || ldv < (int64_t)kv_heads * FA_D ||
+      ldo < (int64_t)heads * FA_D)
+    return fail(ENVG_ERR_ARG, "attention: a row stride is shorter than its heads x head_dim");
+  if (!(scale > 0.0f)) return fail(ENVG_ERR_ARG, "attention: scale must be positive");
+  if (seq_q == 0) return ENVG_OK;
+  if (!dst || !Q || !K || !V) return fail(ENVG_ERR_ARG, "attention: NULL operand");
+  const bool devp = (flags & ENVG_DEVICE_PTRS) != 0;
+  cudaStream_t s = stream_of(d);
+  const int sq_pad = (int)rup(seq_q, FA_BQ), sk_pad = (int)rup(seq_k, FA_BKV);
+  const int64_t wq = (int64_t)heads * FA_D, wk = (int64_t)kv_heads * FA_D;
+  // device operands: Qh | Kh | Vt (fp16) | key bits | per-head max |x|
+  const size_t qb = (size_t)heads * sq_pad * FA_D * 2, kb = (size_t)kv_heads * sk_pad * FA_D * 2;
+  const size_t words = (size_t)sk_pad / 32;
+  const size_t nmax = (size_t)heads + 2 * (size_t)kv_heads;
+  ENVG_TRY(ensure(d, d->fa, qb + 2 * kb + words * 4 + nmax * 4));
+  uint8_t* fa = reinterpret_cast<uint8_t*>(d->fa.p);
+  __half* Qh = reinterpret_cast<__half*>(fa);
+  __half* Kh = reinterpret_cast<__half*>(fa + qb);
+  __half* Vt = reinterpret_cast<__half*>(fa + qb + kb);
+  uint32_t* bits = reinterpret_cast<uint32_t*>(fa + qb + 2 * kb);
+  float* amax = reinterpret_cast<float*>(fa + qb + 2 * kb + words * 4);
+  const float *dq = Q, *dk = K, *dv = V;
+  const int32_t* dm = key_mask;
+  float* dout = dst;
+  int64_t lq = ldq, lkk = ldk, lv = ldv, lo = ldo;
+  if (!devp) {
+    // host rows are packed to the heads' width on the device
+    const size_t bq = (size_t)seq_q * wq * 4, bk = (size_t)seq_k * wk * 4, bo = bq;
+    const size_t bm = key_mask ? (size_t)rup(seq_k * 4, 256) : 0;
+    ENVG_TRY(ensure(d, d->fain, bq + 2 * bk + bm + bo));
+    uint8_t* st = reinterpret_cast<uint8_t*>(d->fain.p);
+    float* q_d = reinterpret_cast<float*>(st);
+    float* k_d = reinterpret_cast<float*>(st + bq);
+    float* v_d = reinterpret_cast<float*>(st + bq + bk);
+    int32_t* m_d = reinterpret_cast<int32_t*>(st + bq + 2 * bk);
+    float* o_d = reinterpret_cast<float*>(st + bq + 2 * bk + bm);
+    ENVG_CUDA(cudaMemcpy2DAsync(q_d, wq * 4, Q, ldq * 4, wq * 4, seq_q, cudaMemcpyHostToDevice, s));
+    ENVG_CUDA(cudaMemcpy2DAsync(k_d, wk * 4, K, ldk * 4, wk * 4, seq_k, cudaMemcpyHostToDevice, s));
+    ENVG_CUDA(cudaMemcpy2DAsync(v_d, wk * 4, V, ldv * 4, wk * 4, seq_k, cudaMemcpyHostToDevice, s));
+    if (key_mask) ENVG_CUDA(cudaMemcpyAsync(m_d, key_mask, (size_t)seq_k * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)(bq + 2 * bk) + (key_mask ? seq_k * 4.0 : 0.0);
+    dq = q_d, dk = k_d, dv = v_d, dm = key_mask ? m_d : nullptr, dout = o_d;
+    lq = wq, lkk = wk, lv = wk, lo = wq;
+  }
+  // operand preparation: per-head max |x|, then scaled fp16 copies (V transposed) and key bits
+  {
+    ENVG_CUDA(cudaMemsetAsync(amax, 0, nmax * 4, s));
+    ProfScope ps(s, KID_ABSMAX, 0.0, 4.0 * ((double)seq_q * wq + 2.0 * seq_k * wk));
+    k_absmax_heads<<<dim3((unsigned)cdiv(seq_q, 64), (unsigned)heads), 256, 0, s>>>(dq, lq, seq_q, amax);
+    ENVG_CUDA(cudaGetLastError());
+    k_absmax_heads<<<dim3((unsigned)cdiv(seq_k, 64), (unsigned)kv_heads), 256, 0, s>>>(dk, lkk, seq_k, amax + heads);
+    ENVG_CUDA(cudaGetLastError());
+    k_absmax_heads<<<dim3((unsigned)cdiv(seq_k, 64), (unsigned)kv_heads), 256, 0, s>>>(dv, lv, seq_k,
+                                                                                       amax + heads + kv_heads);
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches += 3;
+  }
+  {
+    const bool vq = (lq % 4 == 0) && ((reinterpret_cast<uintptr_t>(dq) & 15) == 0);
+    const bool vk = (lkk % 4 == 0) && ((reinterpret_cast<uintptr_t>(dk) & 15) == 0);
+    ProfScope ps(s, KID_CAST_HEADS, 0.0, 4.0 * ((double)seq_q * wq + 2.0 * seq_k * wk) + (double)qb + 2.0 * kb);
+    k_cast_heads<<<dim3((unsigned)cdiv((int64_t)sq_pad * 16, 256), (unsigned)heads), 256, 0, s>>>(
+        dq, lq, seq_q, sq_pad, amax, Qh, vq);
+    ENVG_CUDA(cudaGetLastError());
+    k_cast_heads<<<dim3((unsigned)cdiv((int64_t)sk_pad * 16, 256), (unsigned)kv_heads), 256, 0, s>>>(
+        dk, lkk, seq_k, sk_pad, amax + heads, Kh, vk);
+    ENVG_CUDA(cudaGetLastError());
+    k_v_transpose<<<dim3((unsigned)(sk_pad / 64), FA_D / 32, (unsigned)kv_heads), 256, 0, s>>>(
+        dv, lv, seq_k, sk_pad, amax + heads + kv_heads, Vt);
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches += 3;
+  }
+  {
+    ProfScope ps(s, KID_KEY_BITS, 0.0, (dm ? 4.0 * seq_k : 0.0) + 4.0 * words);
+    k_key_bits<<<(unsigned)cdiv((int64_t)words, 128), 128, 0, s>>>(dm, seq_k, (int)words, bits);
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches++;
+  }
+  CUtensorMap tQ, tK, tV;
+  // 16-bit element maps (TMA copies the fp16 bits unchanged)
+  ENVG_TRY(tmap_2d(&tQ, Qh, FA_D, (uint64_t)heads * sq_pad, FA_BQ));
+  ENVG_TRY(tmap_2d(&tK, Kh, FA_D, (uint64_t)kv_heads * sk_pad, FA_BKV));
+  ENVG_TRY(tmap_2d(&tV, Vt, (uint64_t)sk_pad, (uint64_t)kv_heads * FA_D, FA_D));
+  FaArgs a{};
+  a.seq_q = seq_q;
+  a.seq_k = seq_k;
+  a.heads = heads;
+  a.kv_heads = kv_heads;
+  a.sq_pad = sq_pad;
+  a.sk_pad = sk_pad;
+  a.causal = causal ? 1 : 0;
+  a.sl2 = scale * 1.4426950408889634f;
+  a.kbits = bits;
+  a.amax = amax;
+  a.out = dout;
+  a.ldo = lo;
+  a.status = d->d_status;
+  a.wait_cap_ns = d->wait_cap_ns;
+  static bool attr_set[64] = {};
+  if (!attr_set[d->id]) {
+    ENVG_CUDA(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, FaSmem::TOTAL));
+    attr_set[d->id] = true;
+  }
+  {
+    // visible (q, k) pairs: all of them, or the causal triangle
+    double pairs = (double)seq_q * seq_k;
+    if (causal) pairs = (double)seq_q * seq_k - 0.5 * (double)seq_q * (seq_q - 1);
+    const double fl = 4.0 * FA_D * pairs * heads;
+    ProfScope ps(s, KID_ATTN, fl, (double)qb + 2.0 * kb * (double)(sq_pad / FA_BQ) + 4.0 * seq_q * wq);
+    k_attention<<<dim3((unsigned)(sq_pad / FA_BQ), (unsigned)heads), FA_THREADS, FaSmem::TOTAL, s>>>(tQ, tK, tV, a);
+    ENVG_CUDA(cudaGetLastError());
+    d->st.kernel_launches++;
+    d->st.flops += fl;
+  }
+  d->st.calls++;
+  if (!devp) {
+    ENVG_CUDA(cudaMemcpy2DAsync(dst, ldo * 4, dout, wq * 4, wq * 4, seq_q, cudaMemcpyDeviceToHost, s));
+    d->st.d2h_bytes += (double)seq_q * wq * 4;
     return sync_and_check(d);
   }
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);

@@ -101,6 +101,7 @@ def lib():
                                          _i64, _ci, _vp, _ci]
         L.envg_conv2d.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 11
         L.envg_group_norm.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 7
+        L.envg_attention.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 5 + [_i64] * 4 + [ctypes.c_float, _ci, _vp, _ci]
         L.envg_vae_resblock.argtypes = [_vp, _vp, ctypes.POINTER(ResBlockDesc), _ci, _ci, _ci, _ci, _ci]
         L.envg_sgemm.argtypes = [_ci, _ci, _ci, _i64, _i64, _i64, ctypes.c_float, _vp, _i64, _vp, _i64,
                                  ctypes.c_float, _vp, _i64]
@@ -411,6 +412,33 @@ def group_norm(dst, src, gamma, beta, num_groups, silu=False, sync=True):
                                         1 if silu else 0, flags))
 
 
+def attention(dst, q, k, v, heads, kv_heads, head_dim=128, scale=None, causal=False, key_mask=None, sync=True):
+    """dst[seq_q, heads*hd] = per-head softmax(scale Q K^T (+ masks)) V: envg_attention.
+
+    q [seq_q, >= heads*hd], k / v [seq_k, >= kv_heads*hd] fp32 (row strides = their widths);
+    key_mask: int32 [seq_k] (numpy for host calls, CUDA tensor for device calls) or None."""
+    if scale is None:
+        scale = 1.0 / float(np.sqrt(head_dim))
+    flags = _mode(dst, q, k, v)
+    if flags == DEVICE_PTRS and not sync:
+        flags |= ASYNC
+    mp = None
+    if key_mask is not None:
+        if _is_torch(key_mask):
+            import torch
+
+            if not (key_mask.is_cuda and key_mask.dtype == torch.int32 and key_mask.is_contiguous()):
+                raise TypeError("key_mask must be a contiguous int32 CUDA tensor")
+            mp = key_mask.data_ptr()
+        else:
+            key_mask = np.ascontiguousarray(key_mask, dtype=np.int32)
+            mp = key_mask.ctypes.data
+    seq_q, seq_k = q.shape[0], k.shape[0]
+    return _check(lib().envg_attention(_ptr(dst), _ptr(q), _ptr(k), _ptr(v), seq_q, seq_k, heads, kv_heads, head_dim,
+                                       q.shape[1], k.shape[1], v.shape[1], dst.shape[1], float(scale),
+                                       1 if causal else 0, mp, flags))
+
+
 class ResBlock:
     """One VAE ResBlock (TVAEResBlock, quicknn_vae.pas:164-187) with device-resident conv weights.
 
@@ -526,6 +554,14 @@ def QNNGroupNorm(dst, src, gamma, beta, batch, channels, H, W, num_groups):
     _assert(channels % num_groups == 0, "ERROR [GroupNorm] : channels not divisible by groups")
     return group_norm(dst.reshape(batch, channels, H, W), src.reshape(batch, channels, H, W), gamma, beta,
                       num_groups)
+
+
+def QNNFlashAttention(dst, Q, K, V, heads, seq_q, seq_k, head_dim, scale):
+    """quicknncpu.pas:2763-2860: Q/K/V/dst [seq, heads*head_dim] (head h at column h*head_dim)."""
+    _assert(head_dim == 128, "ERROR [FlashAttention] : head_dim must be 128 on this device")
+    return attention(dst.reshape(seq_q, heads * head_dim), Q.reshape(seq_q, heads * head_dim),
+                     K.reshape(seq_k, heads * head_dim), V.reshape(seq_k, heads * head_dim), heads, heads,
+                     head_dim, scale)
 
 
 def QNNConv2d(dst, src, weights, bias, in_ch, out_ch, H, W, kH, kW, stride, padding, batch):

@@ -440,6 +440,47 @@ void envo_group_norm(float* dst, const float* src, const float* gamma, const flo
   if (act) envo_silu(dst, (int64_t)batch * channels * spatial);
 }
 
+// Multi-head attention as the reference's BLAS path runs it, per head h (kv head h / (heads /
+// kv_heads)): scores = scale * Q_h K_h^T with cblas_gemm (NoTrans, Trans; restated qgemm),
+// masked entries set to -inf (QNNMatTriangularFill, quicknncpu.pas:3017-3029: column c > row r,
+// or key_mask[c] == 0), QNNSoftmaxRows (QNNSoftmax scalar build :2421-2444: max, fast_exp(x -
+// max), sum, scale by 1/sum), then O_h = P V_h with cblas_gemm (NoTrans, NoTrans).  Sources:
+// TTransformerFlux.multiHeadForward (quicknn_transformers.pas:1150-1200) and the Qwen3 attention
+// (quicknn_qwen3.pas:726-768).  Q/K/V/dst rows are strided (ldq, ldk, ldv, ldo); head h sits at
+// column h * head_dim.  causal keeps column c <= r + (seq_k - seq_q) (the square case of the
+// reference when seq_q == seq_k).
+int envo_attention(int path, float* dst, const float* Q, const float* K, const float* V, int seq_q, int seq_k,
+                   int heads, int kv_heads, int head_dim, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo,
+                   float scale, int causal, const int32_t* key_mask) {
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads) return -1;
+  std::vector<float> sc((size_t)seq_q * seq_k);
+  const int per_kv = heads / kv_heads;
+  const int64_t off = (int64_t)seq_k - seq_q;
+  for (int h = 0; h < heads; ++h) {
+    const int kvh = h / per_kv;
+    gemm_nt(path, seq_q, seq_k, head_dim, scale, Q + (int64_t)h * head_dim, ldq, K + (int64_t)kvh * head_dim, ldk,
+            0.0f, sc.data(), seq_k);
+    for (int r = 0; r < seq_q; ++r) {
+      float* row = sc.data() + (int64_t)r * seq_k;
+      for (int c = 0; c < seq_k; ++c)
+        if ((causal && c > r + off) || (key_mask && key_mask[c] == 0)) row[c] = -INFINITY;
+      float mx = row[0];
+      for (int c = 1; c < seq_k; ++c)
+        if (row[c] > mx) mx = row[c];
+      float sum = 0.0f;
+      for (int c = 0; c < seq_k; ++c) {
+        row[c] = fast_exp(row[c] - mx);
+        sum = sum + row[c];
+      }
+      const float inv = 1.0f / sum;
+      for (int c = 0; c < seq_k; ++c) row[c] = row[c] * inv;
+    }
+    gemm_nn(path, seq_q, head_dim, seq_k, 1.0f, sc.data(), seq_k, V + (int64_t)kvh * head_dim, ldv, 0.0f,
+            dst + (int64_t)h * head_dim, ldo);
+  }
+  return 0;
+}
+
 // QNNConv2d, im2col build (quicknncpu.pas:1958-2132).  fp32 weights [out_ch, in_ch, kH, kW].
 // Restated including its stride-1 copy, which is exact only for "same" padding
 // (outW == W); batches processed one after another, the col buffer row-tiled at

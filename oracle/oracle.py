@@ -64,6 +64,9 @@ def lib():
         L.envo_conv2d.argtypes = [ctypes.c_int, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 9
         L.envo_adaln.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64]
         L.envo_group_norm.argtypes = [_f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 6
+        L.envo_attention.argtypes = [ctypes.c_int, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 5 + \
+            [_i64] * 4 + [ctypes.c_float, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)]
+        L.envo_attention.restype = ctypes.c_int
         L.envo_conv2d.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -219,6 +222,28 @@ def vae_resblock(src, p, num_groups, path=PATH_AVX2):
     work = group_norm(c1, p["norm2_gamma"], p["norm2_beta"], num_groups, act=True)
     c2 = conv2d(work, p["conv2_w"], p["conv2_b"], 1, 1, path=path)
     return (dst + c2).astype(np.float32)
+
+
+def attention(q, k, v, heads, kv_heads, head_dim, scale=None, causal=False, key_mask=None, path=PATH_AVX2):
+    """Per-head cblas_gemm + QNNSoftmaxRows + cblas_gemm (the reference's BLAS attention).
+
+    q [seq_q, >= heads*head_dim], k/v [seq_k, >= kv_heads*head_dim] fp32 (row strides = their
+    widths); returns [seq_q, heads*head_dim]."""
+    q = _chk(np.ascontiguousarray(q), np.float32)
+    k = _chk(np.ascontiguousarray(k), np.float32)
+    v = _chk(np.ascontiguousarray(v), np.float32)
+    seq_q, seq_k = q.shape[0], k.shape[0]
+    if scale is None:
+        scale = 1.0 / np.sqrt(head_dim)
+    out = np.zeros((seq_q, heads * head_dim), np.float32)
+    m = None
+    if key_mask is not None:
+        m = np.ascontiguousarray(key_mask, dtype=np.int32)
+    rc = lib().envo_attention(path, _p(out), _p(q), _p(k), _p(v), seq_q, seq_k, heads, kv_heads, head_dim,
+                              q.shape[1], k.shape[1], v.shape[1], out.shape[1], float(scale), 1 if causal else 0,
+                              m.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)) if m is not None else None)
+    assert rc == 0
+    return out
 
 
 def conv2d(src, w, bias, stride, padding, path=PATH_AVX2):

@@ -470,3 +470,63 @@ def test_resblock_argument_errors(gpu):
     rb2 = gpu.ResBlock(p2)
     with pytest.raises(gpu.EnvgError):
         rb2.forward(np.zeros((1, 64, 8, 8), np.float32), x, 48)   # 64 % 48 != 0
+
+
+ATTN_CASES = [
+    # seq_q, seq_k, heads, kv_heads, causal, masked
+    (256, 256, 2, 2, False, False),
+    (200, 333, 3, 3, False, False),     # ragged q and k tiles
+    (130, 130, 4, 2, True, False),      # GQA + causal
+    (512, 512, 2, 1, True, True),       # causal + key mask
+    (64, 300, 2, 2, False, True),
+    (1, 200, 2, 2, True, False),        # one query row, causal with offset (sees all keys)
+]
+
+
+@pytest.mark.parametrize("Sq,Sk,H,KVH,causal,masked", ATTN_CASES)
+def test_attention_vs_oracle(gpu, Sq, Sk, H, KVH, causal, masked):
+    rng = np.random.default_rng(Sq * 3 + Sk + H)
+    D = 128
+    q = rng.standard_normal((Sq, H * D)).astype(np.float32)
+    k = rng.standard_normal((Sk, KVH * D)).astype(np.float32)
+    v = rng.standard_normal((Sk, KVH * D)).astype(np.float32)
+    mask = None
+    if masked:
+        mask = (rng.random(Sk) > 0.25).astype(np.int32)
+        mask[0] = 1
+    y = np.full((Sq, H * D), np.nan, np.float32)
+    gpu.attention(y, q, k, v, H, KVH, causal=causal, key_mask=mask)
+    ref = O.attention(q, k, v, H, KVH, D, causal=causal, key_mask=mask)
+    assert_parity(y, ref, what=f"attention {Sq}x{Sk} H{H}/{KVH} causal={causal} masked={masked}")
+
+
+def test_attention_large_scores_and_strides(gpu):
+    """Scores spread over a wide range (the running max moves several times) and strided rows
+    (the reference's [seq, hidden] buffers with the heads at an offset)."""
+    import torch
+
+    rng = np.random.default_rng(3)
+    Sq, Sk, H, D = 384, 640, 2, 128
+    q = (3.0 * rng.standard_normal((Sq, H * D + 64))).astype(np.float32)
+    k = (3.0 * rng.standard_normal((Sk, H * D + 32))).astype(np.float32)
+    k[:, :H * D] += np.linspace(0, 4, Sk, dtype=np.float32)[:, None]   # later keys score higher
+    v = rng.standard_normal((Sk, H * D)).astype(np.float32)
+    ref = O.attention(q[:, :H * D].copy(), k[:, :H * D].copy(), v, H, H, D)
+    yd = torch.full((Sq, H * D + 16), float("nan"), device="cuda")
+    gpu.attention(yd, torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), H, H)
+    torch.cuda.synchronize()
+    y = yd.cpu().numpy()
+    assert np.isnan(y[:, H * D:]).all()          # columns past the heads untouched
+    assert_parity(np.ascontiguousarray(y[:, :H * D]), ref, what="attention wide scores, strided")
+
+
+def test_attention_argument_errors(gpu):
+    q = np.zeros((4, 128), np.float32)
+    with pytest.raises(gpu.EnvgError) as e:
+        gpu.attention(np.zeros((4, 64), np.float32), q[:, :64].copy(), q[:, :64].copy(), q[:, :64].copy(), 1, 1,
+                      head_dim=64)
+    assert e.value.code == gpu.ERR_UNSUPPORTED
+    with pytest.raises(gpu.EnvgError):
+        gpu.attention(np.zeros((8, 128), np.float32), np.zeros((8, 128), np.float32), q, q, 1, 1, causal=True)
+    with pytest.raises(gpu.EnvgError):
+        gpu.attention(np.zeros((4, 384), np.float32), np.zeros((4, 384), np.float32), q, q, 3, 2)

@@ -219,3 +219,34 @@ def test_vae_resblock_composition():
     h = conv(silu(_gn_fp64(h, p["norm2_gamma"], p["norm2_beta"], G)), p["conv2_w"], p["conv2_b"], 1)
     ref = conv(x, p["skip_w"], p["skip_b"], 0) + h
     np.testing.assert_allclose(y, ref, rtol=5e-3, atol=5e-3)
+
+
+def _attn_fp64(q, k, v, H, KVH, D, causal=False, mask=None):
+    Sq, Sk = q.shape[0], k.shape[0]
+    out = np.zeros((Sq, H * D))
+    for h in range(H):
+        g = h // (H // KVH)
+        s = q[:, h * D:(h + 1) * D].astype(np.float64) @ k[:, g * D:(g + 1) * D].astype(np.float64).T / np.sqrt(D)
+        if causal:
+            s = np.where(np.arange(Sk)[None, :] > np.arange(Sq)[:, None] + (Sk - Sq), -np.inf, s)
+        if mask is not None:
+            s = np.where(np.asarray(mask)[None, :] == 0, -np.inf, s)
+        s = np.exp(s - s.max(1, keepdims=True))
+        s /= s.sum(1, keepdims=True)
+        out[:, h * D:(h + 1) * D] = s @ v[:, g * D:(g + 1) * D].astype(np.float64)
+    return out
+
+
+@pytest.mark.parametrize("Sq,Sk,H,KVH,causal", [(37, 37, 2, 2, False), (64, 80, 4, 2, False), (50, 50, 4, 1, True),
+                                               (20, 45, 2, 2, True)])
+def test_attention_vs_fp64(Sq, Sk, H, KVH, causal):
+    rng = np.random.default_rng(Sq + Sk + H)
+    D = 32
+    q = rng.standard_normal((Sq, H * D)).astype(np.float32)
+    k = rng.standard_normal((Sk, KVH * D)).astype(np.float32)
+    v = rng.standard_normal((Sk, KVH * D)).astype(np.float32)
+    mask = (rng.random(Sk) > 0.2).astype(np.int32)
+    mask[0] = 1
+    for m in (None, mask):
+        y = O.attention(q, k, v, H, KVH, D, causal=causal, key_mask=m, path=O.PATH_SCALAR)
+        np.testing.assert_allclose(y, _attn_fp64(q, k, v, H, KVH, D, causal, m), rtol=1e-4, atol=1e-4)
