@@ -53,6 +53,14 @@ def conv(name, B, C, H, W, O, k, stride, pad, epi="silu"):
     return dict(name=name, op="conv", B=B, C=C, H=H, W=W, O=O, k=k, stride=stride, pad=pad, epi=epi)
 
 
+def attn(name, Sq, Sk, H, KVH, causal=False):
+    return dict(name=name, op="attn", Sq=Sq, Sk=Sk, H=H, KVH=KVH, causal=causal, epi="none")
+
+
+def resblock(name, B, Ci, Co, H, W, G=32):
+    return dict(name=name, op="resblock", B=B, Ci=Ci, Co=Co, H=H, W=W, G=G, epi="none")
+
+
 def qwen(M):
     return [lin("q", M, 2560, 4096, "none"), lin("k", M, 2560, 1024, "none"), lin("v", M, 2560, 1024, "none"),
             lin("o", M, 4096, 2560, "none"), lin("gate_up", M, 2560, 2 * 9728, "silu_gate_nobias"),
@@ -78,12 +86,26 @@ WORKLOADS = {
     "c5": ("BASELINE config 5: VAE-decoder 3x3 conv, [1,512,128,128] -> 512 ch, and [1,256,256,256] -> 256 ch, "
            "fused bias + SiLU",
            [conv("conv512", 1, 512, 128, 128, 512, 3, 1, 1), conv("conv256", 1, 256, 256, 256, 256, 3, 1, 1)]),
+    "f3": ("VAE-decoder ResBlocks (GroupNorm 32 + SiLU + 3x3 conv, twice, + residual): 512 ch at 128x128 and "
+           "256 ch at 256x256",
+           [resblock("rb512", 1, 512, 512, 128, 128), resblock("rb256", 1, 256, 256, 256, 256)]),
+    "f4": ("attention: FLUX2-Klein-4B joint attention (4608 tokens, 24 heads x 128, non-causal) and Qwen3-4B "
+           "prefill (512 tokens, 32 query / 8 kv heads x 128, causal)",
+           [attn("flux", M_TOK, M_TOK, 24, 24), attn("qwen3", 512, 512, 32, 8, causal=True)]),
 }
 
 
 def item_flops(it):
     if it["op"] == "linear":
         return 2.0 * it["M"] * it["K"] * it["N"]
+    if it["op"] == "attn":
+        pairs = it["Sq"] * it["Sk"]
+        if it["causal"]:
+            pairs -= it["Sq"] * (it["Sq"] - 1) / 2
+        return 4.0 * 128 * pairs * it["H"]
+    if it["op"] == "resblock":
+        skip = it["Ci"] * it["Co"] if it["Ci"] != it["Co"] else 0
+        return 2.0 * it["B"] * it["H"] * it["W"] * (9 * it["Co"] * it["Ci"] + 9 * it["Co"] * it["Co"] + skip)
     oh = (it["H"] + 2 * it["pad"] - it["k"]) // it["stride"] + 1
     ow = (it["W"] + 2 * it["pad"] - it["k"]) // it["stride"] + 1
     return 2.0 * it["O"] * oh * ow * it["B"] * it["C"] * it["k"] * it["k"]
@@ -246,6 +268,38 @@ class Workload:
         for i, it in enumerate(items):
             name = it["name"]
             gen.manual_seed(1000 + i)
+            if it["op"] in ("attn", "resblock") and world > 1:
+                raise SystemExit(f"{it['op']} workloads run on one GPU")
+            if it["op"] == "attn":
+                D = 128
+                self.x[name] = tuple(torch.randn(n, h * D, generator=gen, device=dev)
+                                     for n, h in ((it["Sq"], it["H"]), (it["Sk"], it["KVH"]), (it["Sk"], it["KVH"])))
+                self.y[name] = torch.empty(it["Sq"], it["H"] * D, device=dev)
+                self.b[name] = None
+                continue
+            if it["op"] == "resblock":
+                Ci, Co = it["Ci"], it["Co"]
+
+                def bfw(shape, sc):
+                    w = (torch.randn(*shape, generator=gen, device=dev) * sc).to(torch.bfloat16)
+                    return w.view(torch.int16).cpu().numpy().view(np.uint16)
+
+                p = {"conv1_w": bfw((Co, Ci, 3, 3), 0.03), "conv2_w": bfw((Co, Co, 3, 3), 0.03)}
+                if Ci != Co:
+                    p["skip_w"] = bfw((Co, Ci, 1, 1), 0.1)
+                vec = {"norm1_gamma": 1 + 0.1 * torch.randn(Ci, generator=gen, device=dev),
+                       "norm1_beta": 0.1 * torch.randn(Ci, generator=gen, device=dev),
+                       "conv1_b": 0.01 * torch.randn(Co, generator=gen, device=dev),
+                       "norm2_gamma": 1 + 0.1 * torch.randn(Co, generator=gen, device=dev),
+                       "norm2_beta": 0.1 * torch.randn(Co, generator=gen, device=dev),
+                       "conv2_b": 0.01 * torch.randn(Co, generator=gen, device=dev)}
+                if Ci != Co:
+                    vec["skip_b"] = 0.01 * torch.randn(Co, generator=gen, device=dev)
+                self.W[name] = envg.ResBlock(p)
+                self.b[name] = vec
+                self.x[name] = torch.randn(it["B"], Ci, it["H"], it["W"], generator=gen, device=dev)
+                self.y[name] = torch.empty(it["B"], Co, it["H"], it["W"], device=dev)
+                continue
             if it["op"] == "conv":
                 if world > 1:
                     raise SystemExit("conv workloads run on one GPU")
@@ -308,6 +362,13 @@ class Workload:
             envg.conv2d(self.y[name], self.x[name], self.W[name], self.b[name], it["stride"], it["pad"],
                         epilogue=envg.EPI_SILU if it["epi"] == "silu" else envg.EPI_BIAS, sync=False)
             return
+        if it["op"] == "attn":
+            q, k, v = self.x[name]
+            envg.attention(self.y[name], q, k, v, it["H"], it["KVH"], causal=it["causal"], sync=False)
+            return
+        if it["op"] == "resblock":
+            self.W[name].forward(self.y[name], self.x[name], it["G"], vecs=self.b[name], sync=False)
+            return
         x = self.input_of(it)
         if self.world == 1:
             envg.linear(self.y[name], x, self.W[name], bias=self.b[name], sync=False)
@@ -345,7 +406,12 @@ class Workload:
 
     def free(self):
         for w in self.W.values():
-            w.free()
+            if isinstance(w, self.envg.ResBlock):
+                for c in (w.conv1, w.conv2, w.skip):
+                    if c is not None:
+                        c.free()
+            else:
+                w.free()
         self.sym.clear()  # symmetric buffers go before the process group
 
 
@@ -449,6 +515,16 @@ def run_ours(args, items, desc, world, rank, local):
         for f in k1:
             k1[f] += prof.get(kname, {}).get(f, 0)
     roofline = None
+    if not k1["launches"] and prof.get("k_attention", {}).get("launches"):
+        fa = prof["k_attention"]
+        ach = fa["flops"] / (fa["ms"] * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s",
+                    "frac": round(ach / pk, 4), "traffic": None,
+                    "kernel": "k_attention (tcgen05 flash-attention forward, fp16 operands)",
+                    "peak_source": ("measured: MEASURED_PEAKS.json bf16_tflops_sustained (fp16 runs at the bf16 "
+                                    "rate)" if src == "measured" else "fallback: 1.4 PFLOP/s sustained"),
+                    "algorithmic_flops_per_launch": fa["flops"] / fa["launches"],
+                    "avg_launch_ms": round(fa["ms"] / fa["launches"], 5)}
     if k1["launches"]:
         ach = k1["flops"] / (k1["ms"] * 1e-3) / 1e12
         roofline = {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s",
@@ -481,7 +557,8 @@ def run_ours(args, items, desc, world, rank, local):
         torch.cuda.synchronize()
         p = envg.profile_read()
         envg.profile(False)
-        main = {k: v for k, v in p.items() if k.startswith("k1") or k.startswith("k2") or k == "k_gemv"}
+        main = {k: v for k, v in p.items()
+                if k.startswith("k1") or k.startswith("k2") or k in ("k_gemv", "k_attention")}
         mms = sum(v["ms"] for v in main.values()) / reps
         mbytes = sum(v["bytes"] for v in main.values()) / reps
         rank_flops = item_flops(it) / (world if it["op"] == "linear" else 1)  # this rank's shard

@@ -83,6 +83,28 @@ ENVG_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 ENVG_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 64 consecutive 32-bit columns -> 64 registers per thread, without the wait: the
+// caller issues tmem_ld_wait() before any use of r.
+ENVG_DEV void tmem_ld64_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
+ENVG_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // Instruction descriptor, kind::f16 with fp16 A and B (type fields 0), fp32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -285,20 +307,31 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       tc_fence_after();
       const uint32_t sb = tl + (uint32_t)((j & 1) * 128);
       const int kc0 = j * FA_BKV;
-      // pass 1: row maximum of the visible scores
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(sb + c * 32, r);
-        const uint32_t bits = __ldg(a.kbits + (kc0 >> 5) + c);
-        const int cbase = kc0 + c * 32;
+      // the whole score row of this block in registers (one TMEM round trip)
+      uint32_t r[128];
+      tmem_ld64_nowait(sb, r);
+      tmem_ld64_nowait(sb + 64, r + 64);
+      tmem_ld_wait();
+      // masks only where the block is not fully visible to every row of the warp
+      const uint32_t w0 = __ldg(a.kbits + (kc0 >> 5)), w1 = __ldg(a.kbits + (kc0 >> 5) + 1);
+      const uint32_t w2 = __ldg(a.kbits + (kc0 >> 5) + 2), w3 = __ldg(a.kbits + (kc0 >> 5) + 3);
+      const bool full = (w0 & w1 & w2 & w3) == 0xffffffffu && (int64_t)kc0 + FA_BKV - 1 <= climit;
+      if (!__all_sync(0xffffffffu, full)) {
+        const uint32_t wd[4] = {w0, w1, w2, w3};
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const bool vis = ((bits >> t) & 1u) && (int64_t)(cbase + t) <= climit;
-          mx = fmaxf(mx, vis ? __uint_as_float(r[t]) : -INFINITY);
+        for (int t = 0; t < 128; ++t) {
+          const bool vis = ((wd[t >> 5] >> (t & 31)) & 1u) && (int64_t)(kc0 + t) <= climit;
+          if (!vis) r[t] = 0xff800000u;  // -inf
         }
       }
+      // row maximum, eight independent chains
+      float mx8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mx8[u] = __uint_as_float(r[u]);
+#pragma unroll
+      for (int t = 8; t < 128; ++t) mx8[t & 7] = fmaxf(mx8[t & 7], __uint_as_float(r[t]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_cand = mx * sl2;
       float factor = 1.0f;
       bool rescale = false;
@@ -312,6 +345,18 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           m_use = m_new;
           lsum *= factor;
         }
+      }
+      // p = 2^(s * sl2 - m) in place, eight partial sums
+      const float msub = (m_use == -INFINITY) ? 0.0f : m_use;
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int t = 0; t < 128; ++t) {
+        const float pv = ex2_approx(__fmaf_rn(__uint_as_float(r[t]), sl2, -msub));
+        ps8[t & 7] += pv;
+        r[t] = __float_as_uint(pv);
+      }
+      lsum += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+      if (j > 0) {
         // P and O are free once PV_{j-1} is complete
         if (!wait_bounded_warp(o_done, (uint32_t)(j - 1) & 1u, wc, 26)) {
           ok = false;
@@ -321,36 +366,21 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         if (rescale) {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tl + 256 + c * 32, r);
+            uint32_t o[32];
+            tmem_ld32(tl + 256 + c * 32, o);
 #pragma unroll
-            for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * factor);
-            tmem_st32(tl + 256 + c * 32, r);
+            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * factor);
+            tmem_st32(tl + 256 + c * 32, o);
           }
           tmem_st_wait();
         }
       }
-      // pass 2: p = 2^(s * sl2 - m), the row sum, and P (fp16) into shared memory
-      const float msub = (m_use == -INFINITY) ? 0.0f : m_use;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(sb + c * 32, r);
-        const uint32_t bits = __ldg(a.kbits + (kc0 >> 5) + c);
-        const int cbase = kc0 + c * 32;
-        float p[32];
+      // P (fp16) into shared memory, 128-byte swizzled K-major rows
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const bool vis = ((bits >> t) & 1u) && (int64_t)(cbase + t) <= climit;
-          p[t] = vis ? ex2_approx(__fmaf_rn(__uint_as_float(r[t]), sl2, -msub)) : 0.0f;
-          lsum += p[t];
-        }
-        uint8_t* rowp = sP + (c >> 1) * FA_SUB + prow * 128;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int chunk = (c & 1) * 4 + u;
-          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (prow & 7)) << 4)) = pack_half8(p + 8 * u);
-        }
+      for (int ch = 0; ch < 16; ++ch) {
+        uint8_t* rowp = sP + (ch >> 3) * FA_SUB + prow * 128;
+        *reinterpret_cast<uint4*>(rowp + (((ch & 7) ^ (prow & 7)) << 4)) =
+            pack_half8(reinterpret_cast<const float*>(r) + 8 * ch);
       }
       fence_proxy_async_smem();
       tc_fence_before();

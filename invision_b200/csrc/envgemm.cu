@@ -1424,8 +1424,8 @@ int launch_group_affine(Dev* d, const float* src, int batch, int C, int64_t HW, 
   }
   {
     ProfScope ps(s, KID_GN_AFFINE, 0.0, 24.0 * batch * groups * chunks + 8.0 * C + 8.0 * batch * C);
-    k_group_affine<<<(unsigned)cdiv((int64_t)batch * C, 256), 256, 0, s>>>(part, chunks, batch, C, cpg, groups, gamma,
-                                                                           beta, GN_EPS, aff);
+    k_group_affine<<<(unsigned)cdiv((int64_t)batch * groups * 32, 256), 256, 0, s>>>(part, chunks, batch, C, cpg,
+                                                                                     groups, gamma, beta, GN_EPS, aff);
     ENVG_CUDA(cudaGetLastError());
     d->st.kernel_launches++;
   }

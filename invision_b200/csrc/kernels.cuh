@@ -1564,8 +1564,8 @@ __global__ void __launch_bounds__(256) k_adaln(const float* __restrict__ X, int6
 // (b*C + g*cpg) * HW.  Statistics are taken in two launches:
 //   k_group_stats   grid (chunks, B*G): each CTA takes GN_CHUNK consecutive floats of one group
 //                   and writes {count, mean, M2} of its chunk (two passes over registers);
-//   k_group_affine  one thread per (b, c): merges its group's chunks in order (Chan et al.'s
-//                   pairwise update, fp64), then var = M2 / n (population, as QNNVariance),
+//   k_group_affine  one warp per (b, g): merges its group's chunks (Chan et al.'s pairwise
+//                   update, fp64, fixed order), then var = M2 / n (population, as QNNVariance),
 //                   std_inv = 1 / sqrt(var + eps) and the per-channel affine
 //                   a = gamma_c * std_inv, s = beta_c - mean * gamma_c * std_inv (QNNFusedScaleBias).
 constexpr int GN_THREADS = 256;
@@ -1599,26 +1599,40 @@ __global__ void __launch_bounds__(GN_THREADS) k_group_stats(const float* __restr
   const float* src = X + ((int64_t)b * C + (int64_t)g * cpg) * HW + c0;
   float v[GN_PER_THREAD];
   float s = 0.0f;
+  if ((HW & 3) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0) {
+    // 16-byte loads: thread t takes float4 t, t + 256, ... (cn is a multiple of 4 here)
 #pragma unroll
-  for (int i = 0; i < GN_PER_THREAD; ++i) {
-    const int64_t k = threadIdx.x + (int64_t)i * GN_THREADS;
-    v[i] = k < cn ? __ldg(src + k) : 0.0f;
-    s += v[i];
+    for (int i = 0; i < GN_PER_THREAD / 4; ++i) {
+      const int64_t k = 4 * ((int64_t)threadIdx.x + (int64_t)i * GN_THREADS);
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < cn) x = __ldg(reinterpret_cast<const float4*>(src + k));
+      v[4 * i] = x.x, v[4 * i + 1] = x.y, v[4 * i + 2] = x.z, v[4 * i + 3] = x.w;
+      s += (x.x + x.y) + (x.z + x.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < GN_PER_THREAD; ++i) {
+      const int64_t k = threadIdx.x + (int64_t)i * GN_THREADS;
+      v[i] = k < cn ? __ldg(src + k) : 0.0f;
+      s += v[i];
+    }
   }
   const double mean = block_sum256_d((double)s, red) / (double)cn;
   const float mf = (float)mean;
+  // padding slots hold 0 and must not count: they sit beyond cn in both layouts
   float q = 0.0f;
+  const bool vec = (HW & 3) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
 #pragma unroll
   for (int i = 0; i < GN_PER_THREAD; ++i) {
-    const int64_t k = threadIdx.x + (int64_t)i * GN_THREADS;
+    const int64_t k = vec ? 4 * ((int64_t)threadIdx.x + (int64_t)(i >> 2) * GN_THREADS) + (i & 3)
+                          : threadIdx.x + (int64_t)i * GN_THREADS;
     const float dl = v[i] - mf;
     if (k < cn) q = __fmaf_rn(dl, dl, q);
   }
-  // M2 about the chunk mean in double: shift the fp32 deviations' sum back from mf to mean.
-  double dq = (double)q;
-  const double m2 = block_sum256_d(dq, red);
+  const double m2 = block_sum256_d((double)q, red);
   if (threadIdx.x == 0) {
-    const double dm = mean - (double)mf;  // |dm| is one fp32 ulp of the mean at most
+    // M2 about the chunk mean: shift the fp32 deviations' sum back from mf to mean
+    const double dm = mean - (double)mf;
     double* o = part + ((int64_t)bg * chunks + blockIdx.x) * 3;
     o[0] = (double)cn;
     o[1] = mean;
@@ -1626,27 +1640,51 @@ __global__ void __launch_bounds__(GN_THREADS) k_group_stats(const float* __restr
   }
 }
 
-__global__ void k_group_affine(const double* __restrict__ part, int chunks, int batch, int C, int cpg, int groups,
-                               const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
-                               float2* __restrict__ aff) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= batch * C) return;
-  const int b = i / C, c = i - b * C, g = c / cpg;
-  const double* p = part + (int64_t)(b * groups + g) * chunks * 3;
-  double n = p[0], mean = p[1], m2 = p[2];
-  for (int k = 1; k < chunks; ++k) {
-    const double nb = p[3 * k], mb = p[3 * k + 1], qb = p[3 * k + 2];
-    const double nn = n + nb, dl = mb - mean;
-    mean += dl * (nb / nn);
-    m2 += qb + dl * dl * (n * nb / nn);
-    n = nn;
+// Chan et al.'s pairwise update: (n, mean, m2) <- (n, mean, m2) merged with (nb, mb, qb).
+ENVG_DEV void chan_merge(double& n, double& mean, double& m2, double nb, double mb, double qb) {
+  if (nb == 0.0) return;
+  if (n == 0.0) {
+    n = nb, mean = mb, m2 = qb;
+    return;
   }
+  const double nn = n + nb, dl = mb - mean;
+  mean += dl * (nb / nn);
+  m2 += qb + dl * dl * (n * nb / nn);
+  n = nn;
+}
+
+// One warp per (b, g): lane l merges chunks l, l + 32, ... in order, then a fixed shuffle tree
+// merges the lanes (deterministic); the warp writes the group's per-channel affine.
+__global__ void __launch_bounds__(256) k_group_affine(const double* __restrict__ part, int chunks, int batch, int C,
+                                                      int cpg, int groups, const float* __restrict__ gamma,
+                                                      const float* __restrict__ beta, float eps,
+                                                      float2* __restrict__ aff) {
+  const int wid = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wid >= batch * groups) return;
+  const int b = wid / groups, g = wid - b * groups;
+  const double* p = part + (int64_t)wid * chunks * 3;
+  double n = 0.0, mean = 0.0, m2 = 0.0;
+  for (int k = lane; k < chunks; k += 32) chan_merge(n, mean, m2, p[3 * k], p[3 * k + 1], p[3 * k + 2]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double nb = __shfl_down_sync(0xffffffffu, n, o);
+    const double mb = __shfl_down_sync(0xffffffffu, mean, o);
+    const double qb = __shfl_down_sync(0xffffffffu, m2, o);
+    if (lane < o) chan_merge(n, mean, m2, nb, mb, qb);
+  }
+  n = __shfl_sync(0xffffffffu, n, 0);
+  mean = __shfl_sync(0xffffffffu, mean, 0);
+  m2 = __shfl_sync(0xffffffffu, m2, 0);
   const float var = (float)(m2 / n);
   const float std_inv = 1.0f / sqrtf(var + eps);
-  const float ga = gamma ? __ldg(gamma + c) : 1.0f;
-  const float be = beta ? __ldg(beta + c) : 0.0f;
-  const float a = __fmul_rn(ga, std_inv);
-  aff[i] = make_float2(a, __fsub_rn(be, __fmul_rn(__fmul_rn((float)mean, ga), std_inv)));
+  const float mf = (float)mean;
+  for (int c = g * cpg + lane; c < (g + 1) * cpg; c += 32) {
+    const float ga = gamma ? __ldg(gamma + c) : 1.0f;
+    const float be = beta ? __ldg(beta + c) : 0.0f;
+    const float a = __fmul_rn(ga, std_inv);
+    aff[(int64_t)b * C + c] = make_float2(a, __fsub_rn(be, __fmul_rn(__fmul_rn(mf, ga), std_inv)));
+  }
 }
 
 // dst[b][c][i] = act(src[b][c][i] * aff[b*C + c].x + aff[b*C + c].y), fp32 NCHW (in place allowed).
