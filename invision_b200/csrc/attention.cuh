@@ -415,6 +415,317 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   }
 }
 
+// ---- two query tiles per CTA ------------------------------------------------------------------
+// k_attention2: 256 query rows (tiles 0 and 1) of one head per CTA, 320 threads: warp 0 TMA,
+// warp 1 UMMA issuer, warps 2-5 softmax of tile 0, warps 6-9 softmax of tile 1 (two softmax warps
+// per SM sub-partition).  K and V blocks are loaded once for both tiles.  TMEM: S_t at columns
+// [128t, 128t+128), O_t at [256 + 128t, ...).  The softmax writes P_t (fp16, packed two per
+// column) over the first 64 columns of S_t, and the PV product reads it from there as its A
+// operand (tcgen05.mma with A in tensor memory).  The UMMA thread issues S_t(j+1) only after the
+// commit of PV_t(j) has arrived, so the overwrite of P_t is ordered after its last read; O_t is
+// quiescent while softmax t works (PV_t(j-1) completed before S_t(j) was issued), which is when
+// the softmax may rescale it.
+constexpr int FA2_THREADS = 320;
+
+struct Fa2Smem {
+  static constexpr int Q = 0;                                  // tile t: Q at t * FA_TILE
+  static constexpr int KV = 2 * FA_TILE;                       // stage s: K, then V
+  static constexpr int BARS = KV + FA_STAGES * 2 * FA_TILE;
+  static constexpr int NBARS = 1 + 2 * FA_STAGES + 2 + 2 + 2 + 1;  // q, kv full/empty, s, p, pv, drain
+  static constexpr int END = BARS + NBARS * 8 + 16;
+  static constexpr int TOTAL = END + 1024;
+};
+
+// D[tmem] += A[tmem] . B[smem]^T (A: 128 lanes x 16 fp16 packed in 8 columns), one thread.
+ENVG_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 64 registers per thread -> 32 lanes x 64 consecutive columns; completion by tmem_st_wait.
+ENVG_DEV void tmem_st64(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,"
+      "%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,"
+      "%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32]),
+      "r"(r[33]), "r"(r[34]), "r"(r[35]), "r"(r[36]), "r"(r[37]), "r"(r[38]), "r"(r[39]), "r"(r[40]),
+      "r"(r[41]), "r"(r[42]), "r"(r[43]), "r"(r[44]), "r"(r[45]), "r"(r[46]), "r"(r[47]), "r"(r[48]),
+      "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]), "r"(r[55]), "r"(r[56]),
+      "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63])
+      : "memory");
+}
+
+// 320 threads x 200 registers = 64000 of the SM's 65536.
+__global__ void __maxnreg__(200)
+    k_attention2(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                 const __grid_constant__ CUtensorMap tmV, const FaArgs a) {
+  constexpr uint32_t IDESC = idesc_f16_f32(FA_BQ, 128);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = sm + Fa2Smem::Q;
+  uint8_t* sKV = sm + Fa2Smem::KV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Fa2Smem::BARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Fa2Smem::NBARS);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t q_full = smem_u32(bars);
+  const uint32_t kv_full0 = q_full + 8;
+  const uint32_t kv_empty0 = kv_full0 + 8 * FA_STAGES;
+  const uint32_t s_full0 = kv_empty0 + 8 * FA_STAGES;  // [t]
+  const uint32_t p_full0 = s_full0 + 16;               // [t]
+  const uint32_t pv_done0 = p_full0 + 16;              // [t]
+  const uint32_t drain = pv_done0 + 16;
+
+  const int h = blockIdx.y;
+  const int kvh = h / (a.heads / a.kv_heads);
+  const int q0 = blockIdx.x * 2 * FA_BQ;
+  const int64_t coff = (int64_t)a.seq_k - a.seq_q;
+  int nb = (a.seq_k + FA_BKV - 1) / FA_BKV;
+  if (a.causal) {
+    const int64_t last = (int64_t)q0 + 2 * FA_BQ - 1 + coff;
+    nb = (int)min((int64_t)nb, last / FA_BKV + 1);
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < FA_STAGES; ++s) {
+      mbar_init(kv_full0 + 8 * s, 1);
+      mbar_init(kv_empty0 + 8 * s, 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full0 + 8 * t, 1);
+      mbar_init(p_full0 + 8 * t, 4);
+      mbar_init(pv_done0 + 8 * t, 1);
+    }
+    mbar_init(drain, 1);
+    *abort_s = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), FA_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtl wc{a.wait_cap_ns, a.status, abort_s, 0};
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t pending = 0, issue_ph = 0;
+      mbar_arrive_expect_tx(q_full, 2 * FA_TILE);
+      for (int t = 0; t < 2; ++t) {
+        tma_load_2d(smem_u32(sQ + t * FA_TILE), &tmQ, q_full, 0, h * a.sq_pad + q0 + t * FA_BQ);
+        tma_load_2d(smem_u32(sQ + t * FA_TILE + FA_SUB), &tmQ, q_full, 64, h * a.sq_pad + q0 + t * FA_BQ);
+      }
+      for (int j = 0; j < nb; ++j) {
+        const int stage = j & 1;
+        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+        if (!wait_bounded(kv_empty0 + 8 * stage, ph ^ 1u, wc, 31)) break;
+        const uint32_t fb = kv_full0 + 8 * stage;
+        uint8_t* sK = sKV + stage * 2 * FA_TILE;
+        uint8_t* sV = sK + FA_TILE;
+        mbar_arrive_expect_tx(fb, 2 * FA_TILE);
+        tma_load_2d(smem_u32(sK), &tmK, fb, 0, kvh * a.sk_pad + j * FA_BKV);
+        tma_load_2d(smem_u32(sK + FA_SUB), &tmK, fb, 64, kvh * a.sk_pad + j * FA_BKV);
+        tma_load_2d(smem_u32(sV), &tmV, fb, j * FA_BKV, kvh * FA_D);
+        tma_load_2d(smem_u32(sV + FA_SUB), &tmV, fb, j * FA_BKV + 64, kvh * FA_D);
+        pending |= 1u << stage;
+        issue_ph = (issue_ph & ~(1u << stage)) | (ph << stage);
+      }
+      if (*abort_s) {
+        wait_drain(q_full, 0, a.wait_cap_ns);
+        for (int s = 0; s < FA_STAGES; ++s)
+          if (pending & (1u << s)) wait_drain(kv_full0 + 8 * s, (issue_ph >> s) & 1u, a.wait_cap_ns);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      bool ok = wait_bounded(q_full, 0, wc, 32) && wait_bounded(kv_full0, 0, wc, 33);
+      tc_fence_after();
+      uint64_t qd[2][2];
+      for (int t = 0; t < 2; ++t) {
+        qd[t][0] = sw128_kmajor_desc(smem_u32(sQ + t * FA_TILE));
+        qd[t][1] = sw128_kmajor_desc(smem_u32(sQ + t * FA_TILE + FA_SUB));
+      }
+      auto issue_s = [&](int t, int j) {
+        const uint8_t* sK = sKV + (j & 1) * 2 * FA_TILE;
+        const uint64_t kd0 = sw128_kmajor_desc(smem_u32(sK));
+        const uint64_t kd1 = sw128_kmajor_desc(smem_u32(sK + FA_SUB));
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16(tmem_base + (uint32_t)(t * 128), qd[t][k >> 2] + 2 * (k & 3), (k < 4 ? kd0 : kd1) + 2 * (k & 3),
+                    IDESC, k > 0 ? 1u : 0u);
+        umma_commit(s_full0 + 8 * t);
+      };
+      if (ok) {
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; ok && j < nb; ++j) {
+        const int stage = j & 1;
+        const uint8_t* sV = sKV + stage * 2 * FA_TILE + FA_TILE;
+        const uint64_t vd0 = sw128_kmajor_desc(smem_u32(sV));
+        const uint64_t vd1 = sw128_kmajor_desc(smem_u32(sV + FA_SUB));
+        for (int t = 0; t < 2; ++t) {
+          if (!wait_bounded(p_full0 + 8 * t, (uint32_t)j & 1u, wc, 34)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            umma_f16_ts(tmem_base + 256 + (uint32_t)(t * 128), tmem_base + (uint32_t)(t * 128 + 8 * k),
+                        (k < 4 ? vd0 : vd1) + 2 * (k & 3), IDESC, (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit(pv_done0 + 8 * t);
+          if (t == 1) umma_commit(kv_empty0 + 8 * stage);
+        }
+        if (!ok || j + 1 >= nb) break;
+        if (!wait_bounded(kv_full0 + 8 * ((j + 1) & 1), (uint32_t)((j + 1) >> 1) & 1u, wc, 35)) break;
+        for (int t = 0; t < 2; ++t) {
+          // P_t(j) (in S_t's columns) must be consumed before S_t(j+1) overwrites them
+          if (!wait_bounded(pv_done0 + 8 * t, (uint32_t)j & 1u, wc, 36)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(t, j + 1);
+        }
+      }
+      if (*abort_s) {
+        umma_commit(drain);
+        wait_drain(drain, 0, a.wait_cap_ns);
+      }
+    }
+  } else {
+    // ---------------- softmax: warpgroup t = tile t, one query row per thread ----------------
+    const int t = (warp - 2) >> 2;
+    const int qd = warp & 3;
+    const int prow = qd * 32 + lane;
+    const int row = q0 + t * FA_BQ + prow;
+    const uint32_t tl = tmem_base + ((uint32_t)(qd * 32) << 16);
+    const uint32_t s_addr = tl + (uint32_t)(t * 128);
+    const uint32_t o_addr = tl + 256 + (uint32_t)(t * 128);
+    const int64_t climit = a.causal ? (int64_t)row + coff : INT64_MAX;
+    const float sq = fa_pow2_scale(__ldg(a.amax + h));
+    const float sk = fa_pow2_scale(__ldg(a.amax + a.heads + kvh));
+    const float sv = fa_pow2_scale(__ldg(a.amax + a.heads + a.kv_heads + kvh));
+    const float sl2 = a.sl2 / (sq * sk);
+    float m_use = -INFINITY, lsum = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nb; ++j) {
+      if (!wait_bounded_warp(s_full0 + 8 * t, (uint32_t)j & 1u, wc, 37)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kc0 = j * FA_BKV;
+      uint32_t r[128];
+      tmem_ld64_nowait(s_addr, r);
+      tmem_ld64_nowait(s_addr + 64, r + 64);
+      tmem_ld_wait();
+      const uint32_t w0 = __ldg(a.kbits + (kc0 >> 5)), w1 = __ldg(a.kbits + (kc0 >> 5) + 1);
+      const uint32_t w2 = __ldg(a.kbits + (kc0 >> 5) + 2), w3 = __ldg(a.kbits + (kc0 >> 5) + 3);
+      const bool full = (w0 & w1 & w2 & w3) == 0xffffffffu && (int64_t)kc0 + FA_BKV - 1 <= climit;
+      if (!__all_sync(0xffffffffu, full)) {
+        const uint32_t wd[4] = {w0, w1, w2, w3};
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const bool vis = ((wd[c >> 5] >> (c & 31)) & 1u) && (int64_t)(kc0 + c) <= climit;
+          if (!vis) r[c] = 0xff800000u;
+        }
+      }
+      float mx8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mx8[u] = __uint_as_float(r[u]);
+#pragma unroll
+      for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(r[c]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_cand = mx * sl2;
+      if (j == 0) {
+        m_use = m_cand;
+      } else if (__any_sync(0xffffffffu, m_cand > m_use + FA_RESCALE_LOG2)) {
+        // O_t is quiescent here: PV_t(j-1) completed before S_t(j) was issued
+        const float m_new = fmaxf(m_use, m_cand);
+        const float factor = (m_new == -INFINITY) ? 1.0f : ex2_approx(m_use - m_new);
+        m_use = m_new;
+        lsum *= factor;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+#pragma unroll
+          for (int u = 0; u < 32; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * factor);
+          tmem_st32(o_addr + c * 32, o);
+        }
+      }
+      const float msub = (m_use == -INFINITY) ? 0.0f : m_use;
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t ph[64];
+#pragma unroll
+      for (int c = 0; c < 128; c += 2) {
+        const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[c]), sl2, -msub));
+        const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[c + 1]), sl2, -msub));
+        ps8[c & 7] += p0;
+        ps8[(c + 1) & 7] += p1;
+        __half2 hp = __floats2half2_rn(p0, p1);
+        ph[c >> 1] = *reinterpret_cast<uint32_t*>(&hp);
+      }
+      lsum += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+      tmem_st64(s_addr, ph);  // P_t over the first 64 columns of S_t
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full0 + 8 * t);
+    }
+    if (ok && nb > 0 && wait_bounded_warp(pv_done0 + 8 * t, (uint32_t)(nb - 1) & 1u, wc, 38)) {
+      tc_fence_after();
+      const float inv = lsum > 0.0f ? 1.0f / (lsum * sv) : 0.0f;
+      float* orow = a.out + (int64_t)row * a.ldo + (int64_t)h * FA_D;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c * 32, o);
+        if (row < a.seq_q) {
+#pragma unroll
+          for (int u = 0; u < 32; u += 4)
+            *reinterpret_cast<float4*>(orow + c * 32 + u) =
+                make_float4(__uint_as_float(o[u]) * inv, __uint_as_float(o[u + 1]) * inv,
+                            __uint_as_float(o[u + 2]) * inv, __uint_as_float(o[u + 3]) * inv);
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, FA_TMEM_COLS);
+  }
+}
+
 // Max |x| per head of an fp32 [seq][ld] tensor (head h at column h * 128) into amax[h]
 // (atomicMax on the float bits; amax zeroed beforehand).  Grid (row blocks of 64, heads).
 __global__ void __launch_bounds__(256) k_absmax_heads(const float* __restrict__ X, int64_t ld, int seq,

@@ -93,6 +93,7 @@ struct Dev {
   bool use_pair = true;  // 256x256 CTA-pair tiles for M > 128 (ENVG_K1=single selects k1_gemm)
   int max_pairs = 0;     // co-resident CTA pairs of k1_gemm_pair
   bool store_tma = true;  // TMA bulk-store epilogue; ENVG_STORE=coalesced selects warp-coalesced stores
+  int attn_tiles = 0;     // query tiles per attention CTA: 0 = by grid size, ENVG_ATTN_TILES=1|2 forces
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
@@ -863,6 +864,10 @@ int envg_init(int ndev, const int* dev_ids) {
   }
   if (const char* s = getenv("ENVG_K1")) d->use_pair = strcmp(s, "single") != 0;
   if (const char* s = getenv("ENVG_STORE")) d->store_tma = strcmp(s, "coalesced") != 0;
+  if (const char* s = getenv("ENVG_ATTN_TILES")) {
+    const int v = atoi(s);
+    if (v == 1 || v == 2) d->attn_tiles = v;
+  }
   if (const char* s = getenv("ENVG_GEMV_M_MAX")) {
     int v = atoi(s);
     if (v >= 0 && v <= 8) d->gemv_max = v;
@@ -1854,7 +1859,9 @@ int envg_attention(float* dst, const float* Q, const float* K, const float* V, i
   if (!dst || !Q || !K || !V) return fail(ENVG_ERR_ARG, "attention: NULL operand");
   const bool devp = (flags & ENVG_DEVICE_PTRS) != 0;
   cudaStream_t s = stream_of(d);
-  const int sq_pad = (int)rup(seq_q, FA_BQ), sk_pad = (int)rup(seq_k, FA_BKV);
+  // two query tiles per CTA when that still fills the GPU (one wave or more)
+  const bool two = d->attn_tiles == 2 || (d->attn_tiles == 0 && cdiv(seq_q, 2 * FA_BQ) * heads >= d->sms);
+  const int sq_pad = (int)rup(seq_q, two ? 2 * FA_BQ : FA_BQ), sk_pad = (int)rup(seq_k, FA_BKV);
   const int64_t wq = (int64_t)heads * FA_D, wk = (int64_t)kv_heads * FA_D;
   // device operands: Qh | Kh | Vt (fp16) | key bits | per-head max |x|
   const size_t qb = (size_t)heads * sq_pad * FA_D * 2, kb = (size_t)kv_heads * sk_pad * FA_D * 2;
@@ -1947,6 +1954,7 @@ int envg_attention(float* dst, const float* Q, const float* K, const float* V, i
   static bool attr_set[64] = {};
   if (!attr_set[d->id]) {
     ENVG_CUDA(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, FaSmem::TOTAL));
+    ENVG_CUDA(cudaFuncSetAttribute(k_attention2, cudaFuncAttributeMaxDynamicSharedMemorySize, Fa2Smem::TOTAL));
     attr_set[d->id] = true;
   }
   {
@@ -1955,7 +1963,11 @@ int envg_attention(float* dst, const float* Q, const float* K, const float* V, i
     if (causal) pairs = (double)seq_q * seq_k - 0.5 * (double)seq_q * (seq_q - 1);
     const double fl = 4.0 * FA_D * pairs * heads;
     ProfScope ps(s, KID_ATTN, fl, (double)qb + 2.0 * kb * (double)(sq_pad / FA_BQ) + 4.0 * seq_q * wq);
-    k_attention<<<dim3((unsigned)(sq_pad / FA_BQ), (unsigned)heads), FA_THREADS, FaSmem::TOTAL, s>>>(tQ, tK, tV, a);
+    if (two)
+      k_attention2<<<dim3((unsigned)(sq_pad / (2 * FA_BQ)), (unsigned)heads), FA2_THREADS, Fa2Smem::TOTAL, s>>>(tQ, tK,
+                                                                                                        tV, a);
+    else
+      k_attention<<<dim3((unsigned)(sq_pad / FA_BQ), (unsigned)heads), FA_THREADS, FaSmem::TOTAL, s>>>(tQ, tK, tV, a);
     ENVG_CUDA(cudaGetLastError());
     d->st.kernel_launches++;
     d->st.flops += fl;

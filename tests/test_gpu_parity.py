@@ -530,3 +530,39 @@ def test_attention_argument_errors(gpu):
         gpu.attention(np.zeros((8, 128), np.float32), np.zeros((8, 128), np.float32), q, q, 1, 1, causal=True)
     with pytest.raises(gpu.EnvgError):
         gpu.attention(np.zeros((4, 384), np.float32), np.zeros((4, 384), np.float32), q, q, 3, 2)
+
+
+def test_attention_two_tile_kernel_in_subprocess():
+    """k_attention2 (two query tiles per CTA, P in tensor memory), forced with ENVG_ATTN_TILES=2 so
+    that small, oracle-sized cases reach it: ragged, GQA, causal and masked."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "import numpy as np\n"
+        "from invision_b200 import envg\n"
+        "from oracle import oracle as O\n"
+        "from tests.common import assert_parity\n"
+        "envg.init(0)\n"
+        "for (Sq, Sk, H, KVH, causal, masked) in [(256, 256, 2, 2, False, False), (300, 333, 3, 3, False, False),\n"
+        "        (130, 130, 4, 2, True, False), (512, 512, 2, 1, True, True), (64, 300, 2, 2, False, True),\n"
+        "        (700, 900, 2, 2, True, False)]:\n"
+        "    rng = np.random.default_rng(Sq + Sk + H)\n"
+        "    q = rng.standard_normal((Sq, H * 128)).astype(np.float32)\n"
+        "    k = rng.standard_normal((Sk, KVH * 128)).astype(np.float32)\n"
+        "    v = rng.standard_normal((Sk, KVH * 128)).astype(np.float32)\n"
+        "    k[:, :] += np.linspace(0, 3, Sk, dtype=np.float32)[:, None]\n"
+        "    mask = None\n"
+        "    if masked:\n"
+        "        mask = (rng.random(Sk) > 0.25).astype(np.int32); mask[0] = 1\n"
+        "    y = np.full((Sq, H * 128), np.nan, np.float32)\n"
+        "    envg.attention(y, q, k, v, H, KVH, causal=causal, key_mask=mask)\n"
+        "    assert_parity(y, O.attention(q, k, v, H, KVH, 128, causal=causal, key_mask=mask),\n"
+        "                  what=f'attention2 {Sq}x{Sk} H{H}/{KVH} causal={causal} masked={masked}')\n"
+        "print('ok')\n" % root)
+    r = subprocess.run([sys.executable, "-c", code], env={**os.environ, "ENVG_ATTN_TILES": "2"}, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
