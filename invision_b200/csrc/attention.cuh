@@ -465,8 +465,8 @@ ENVG_DEV void tmem_st64(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
-// 320 threads x 200 registers = 64000 of the SM's 65536.
-__global__ void __maxnreg__(200)
+// 320 threads x 192 registers = 61440 of the SM's 65536.
+__global__ void __maxnreg__(192)
     k_attention2(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const FaArgs a) {
   constexpr uint32_t IDESC = idesc_f16_f32(FA_BQ, 128);
@@ -578,16 +578,24 @@ __global__ void __maxnreg__(200)
                     IDESC, k > 0 ? 1u : 0u);
         umma_commit(s_full0 + 8 * t);
       };
-      if (ok) {
-        issue_s(0, 0);
-        issue_s(1, 0);
-      }
+      // Tile 1 starts one softmax behind tile 0 (its first S is issued with tile 0's first PV),
+      // so the two softmax warpgroups alternate instead of running in lock-step.
+      if (ok) issue_s(0, 0);
+      bool s1_started = false;
+      // Per block j and tile t: PV_t(j) as soon as P_t(j) is ready, then S_t(j+1) once PV_t(j) has
+      // read P_t; tile 0 never waits for tile 1's softmax, so the two softmax warpgroups drift
+      // apart and each runs while the tensor pipe works for the other.
       for (int j = 0; ok && j < nb; ++j) {
         const int stage = j & 1;
         const uint8_t* sV = sKV + stage * 2 * FA_TILE + FA_TILE;
         const uint64_t vd0 = sw128_kmajor_desc(smem_u32(sV));
         const uint64_t vd1 = sw128_kmajor_desc(smem_u32(sV + FA_SUB));
+        const bool more = j + 1 < nb;
         for (int t = 0; t < 2; ++t) {
+          if (t == 1 && !s1_started) {
+            issue_s(1, 0);
+            s1_started = true;
+          }
           if (!wait_bounded(p_full0 + 8 * t, (uint32_t)j & 1u, wc, 34)) {
             ok = false;
             break;
@@ -599,10 +607,11 @@ __global__ void __maxnreg__(200)
                         (k < 4 ? vd0 : vd1) + 2 * (k & 3), IDESC, (j > 0 || k > 0) ? 1u : 0u);
           umma_commit(pv_done0 + 8 * t);
           if (t == 1) umma_commit(kv_empty0 + 8 * stage);
-        }
-        if (!ok || j + 1 >= nb) break;
-        if (!wait_bounded(kv_full0 + 8 * ((j + 1) & 1), (uint32_t)((j + 1) >> 1) & 1u, wc, 35)) break;
-        for (int t = 0; t < 2; ++t) {
+          if (!more) continue;
+          if (t == 0 && !wait_bounded(kv_full0 + 8 * ((j + 1) & 1), (uint32_t)((j + 1) >> 1) & 1u, wc, 35)) {
+            ok = false;
+            break;
+          }
           // P_t(j) (in S_t's columns) must be consumed before S_t(j+1) overwrites them
           if (!wait_bounded(pv_done0 + 8 * t, (uint32_t)j & 1u, wc, 36)) {
             ok = false;
