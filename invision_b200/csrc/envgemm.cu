@@ -264,8 +264,20 @@ int tmap_out_3d(CUtensorMap* tm, const float* base, uint64_t plane, uint64_t ch,
   return ENVG_OK;
 }
 
-// Picks the k1_gemm store path for a row-major Y (and builds its map for the TMA paths).
-int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY) {
+// Picks the k1_gemm store path for a row-major Y (and builds its map for the TMA paths).  With
+// peer copies of Y (N-split) and `pm` given, the chunks go out as TMA bulk stores, one per copy.
+int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = nullptr) {
+  if (use_tma && pm && e.nremote > 0 && e.mode != EPI_ALPHA_BETA) {
+    bool ok = e.ldy % 4 == 0 && e.col_off % 4 == 0;
+    for (int r = 0; r < e.nremote; ++r) ok = ok && (reinterpret_cast<uintptr_t>(e.remote[r] + e.col_off) & 15) == 0;
+    if (ok) {
+      for (int r = 0; r < e.nremote; ++r)
+        ENVG_TRY(tmap_out_2d(&pm->m[r], e.remote[r] + e.col_off, (uint64_t)e.n_out, (uint64_t)e.m_valid,
+                             (uint64_t)e.ldy));
+      e.store_mode = e.mode == EPI_GATED_RES ? STORE_TMA_ADD_PEERS : STORE_TMA_PEERS;
+      return ENVG_OK;
+    }
+  }
   if (!use_tma || e.nremote != 0) {  // N-split outputs leave through peer / multicast stores
     e.store_mode = STORE_COALESCED;
     return ENVG_OK;
@@ -605,7 +617,7 @@ int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap&
   g.group_m = 8;
   CUtensorMap tY;
   memset(&tY, 0, sizeof(tY));
-  ENVG_TRY(choose_store(d->store_tma, e, &tY));
+  ENVG_TRY(choose_store(d->store_tma, e, &tY, &g.pm));
   g.epi = e;
   if (d->use_pair && M > BM) {
     g.tiles_m = (int)cdiv(M, 2 * BM);

@@ -86,7 +86,20 @@ ENVG_DEV void out_store4(const EpiArgs& e, int64_t idx, float4 v) {
 // TMA bulk reduce (Y += tile); or (STORE_COALESCED, the default) the staged tile read back
 // transposed so that every warp store writes whole 128-byte rows, keeping the output off the
 // SM's TMA unit, which the operand loads keep busy.
-enum StoreMode : int { STORE_DIRECT = 0, STORE_TMA = 1, STORE_TMA_ADD = 2, STORE_COALESCED = 3 };
+enum StoreMode : int {
+  STORE_DIRECT = 0,
+  STORE_TMA = 1,
+  STORE_TMA_ADD = 2,
+  STORE_COALESCED = 3,
+  STORE_TMA_PEERS = 4,      // N-split: one TMA bulk store per rank's copy of Y (GemmArgs::pm)
+  STORE_TMA_ADD_PEERS = 5,  // the same with bulk reduce-add (gated residual)
+};
+
+// Tensor maps over each rank's copy of Y for STORE_TMA_PEERS, each based at this rank's column
+// shard (so the shard edge clips the tile like the local map does).
+struct PeerMaps {
+  CUtensorMap m[8];
+};
 
 struct ConvGeom {
   int tileW, tileH;   // pixel tile, tileW * tileH == BN
@@ -105,6 +118,7 @@ struct GemmArgs {
   ConvGeom conv;
   int* status;
   uint64_t wait_cap_ns;
+  PeerMaps pm;  // STORE_TMA_PEERS only
 };
 
 struct SkinnyArgs {
@@ -406,7 +420,7 @@ struct K1Smem {
 template <int BN, int STAGES, bool CONV_B, bool SILU_GATE>
 __global__ void __launch_bounds__(K1_THREADS, 1)
     k1_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-            const __grid_constant__ CUtensorMap tmY, const GemmArgs args) {
+            const __grid_constant__ CUtensorMap tmY, const __grid_constant__ GemmArgs args) {
   using L = K1Smem<BN, STAGES>;
   constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
@@ -445,7 +459,9 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (args.epi.store_mode != STORE_DIRECT) tma_prefetch_desc(&tmY);
+    if (args.epi.store_mode == STORE_TMA || args.epi.store_mode == STORE_TMA_ADD) tma_prefetch_desc(&tmY);
+    if (args.epi.store_mode >= STORE_TMA_PEERS)
+      for (int r = 0; r < args.epi.nremote; ++r) tma_prefetch_desc(&args.pm.m[r]);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), L::TMEM_COLS);
@@ -653,6 +669,11 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
             if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&tmY, smem_u32(buf), x, y, b);
             else tma_store_3d(&tmY, smem_u32(buf), x, y, b);
           }
+          else if (smode == STORE_TMA_PEERS) {
+            for (int r = 0; r < ep.nremote; ++r) tma_store_2d(&args.pm.m[r], smem_u32(buf), x, y);
+          } else if (smode == STORE_TMA_ADD_PEERS) {
+            for (int r = 0; r < ep.nremote; ++r) tma_reduce_add_2d(&args.pm.m[r], smem_u32(buf), x, y);
+          }
           else if (smode == STORE_TMA_ADD) tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
           else tma_store_2d(&tmY, smem_u32(buf), x, y);
           bulk_commit();
@@ -701,7 +722,7 @@ struct KPairSmem {
 template <int STAGES, bool CONV_B, bool SILU_GATE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
     k1_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const __grid_constant__ CUtensorMap tmY, const GemmArgs args) {
+                 const __grid_constant__ CUtensorMap tmY, const __grid_constant__ GemmArgs args) {
   using L = KPairSmem<STAGES>;
   constexpr int BN = 256;
   constexpr uint32_t IDESC = idesc_bf16_f32(2 * BM, BN);
@@ -745,7 +766,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (args.epi.store_mode != STORE_DIRECT) tma_prefetch_desc(&tmY);
+    if (args.epi.store_mode == STORE_TMA || args.epi.store_mode == STORE_TMA_ADD) tma_prefetch_desc(&tmY);
+    if (args.epi.store_mode >= STORE_TMA_PEERS)
+      for (int r = 0; r < args.epi.nremote; ++r) tma_prefetch_desc(&args.pm.m[r]);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), L::TMEM_COLS);
@@ -955,6 +978,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
           if (CONV_B) {
             if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&tmY, smem_u32(buf), x, y, b);
             else tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+          }
+          else if (smode == STORE_TMA_PEERS) {
+            for (int r = 0; r < ep.nremote; ++r) tma_store_2d(&args.pm.m[r], smem_u32(buf), x, y);
+          } else if (smode == STORE_TMA_ADD_PEERS) {
+            for (int r = 0; r < ep.nremote; ++r) tma_reduce_add_2d(&args.pm.m[r], smem_u32(buf), x, y);
           }
           else if (smode == STORE_TMA_ADD) tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
           else tma_store_2d(&tmY, smem_u32(buf), x, y);

@@ -71,6 +71,24 @@ def _worker(rank, world, port, q):
                 hdl.barrier()
                 ok = bool(torch.equal(Y, ref))
                 results.append((f"{name} {M}x{K}x{N} gate_up={gate_up}", ok))
+            if not gate_up and M > 64:
+                # gated residual: every copy of Y starts as the same residual h0
+                rng = np.random.default_rng(M)
+                h0 = torch.from_numpy(rng.standard_normal((M, half)).astype(np.float32)).to(dev)
+                gate = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).to(dev)
+                ref_r = h0.clone()
+                envg.linear(ref_r, xt, Wf, bias=torch.from_numpy(b).to(dev), epilogue=envg.EPI_GATED_RESIDUAL,
+                            gate=gate)
+                gs = gate[n0:n1].contiguous()
+                for name, peers, mc in modes:
+                    Y.copy_(h0)
+                    torch.cuda.synchronize()
+                    hdl.barrier()
+                    envg.linear_nsplit(Y, xt, Ws, n0, peers=peers, multicast=mc, bias=bt,
+                                       epilogue=envg.EPI_GATED_RESIDUAL, gate=gs)
+                    torch.cuda.synchronize()
+                    hdl.barrier()
+                    results.append((f"{name} gated residual {M}x{K}x{N}", bool(torch.equal(Y, ref_r))))
             Ws.free()
             Wf.free()
             del Y, hdl
