@@ -265,6 +265,7 @@ class Workload:
         gen = torch.Generator(device=dev)
         self.W, self.b, self.x, self.y, self.shard, self.ys, self.gbuf = {}, {}, {}, {}, {}, {}, {}
         names = [it["name"] for it in items]
+        self.consumed = {it["x_from"] for it in items if it.get("x_from")}
         for i, it in enumerate(items):
             name = it["name"]
             gen.manual_seed(1000 + i)
@@ -384,7 +385,10 @@ class Workload:
             if n1 > n0:
                 envg.linear_nsplit(ysym, x, self.W[name], n0, peers=None if mc else peers, multicast=mc,
                                    bias=self.b[name], sync=False)
-            h.barrier()
+            # the ranks meet only where a copy of Y is read next: before a linear that consumes this
+            # output, and at the end of the step (before the next step writes the copies again)
+            if name in self.consumed or it is self.items[-1]:
+                h.barrier()
             return
         if n1 - n0 == per:
             envg.linear(self.ys[name], x, self.W[name], bias=self.b[name], sync=False)
@@ -396,6 +400,24 @@ class Workload:
             gather_columns(self.ys[name], self.y[name].shape[1], out=self.y[name], buf=self.gbuf[name])
 
     def step(self, gather=True):
+        if (self.world > 1 and gather and self.batch and self.sym and
+                all(it["op"] == "linear" and it["name"] in self.sym for it in self.items)):
+            # N-split shards in envg_linear_nsplit_batch calls, one per segment that ends where a
+            # later linear reads the output (the ranks meet there) or at the end of the step
+            seg = []
+            for it in self.items:
+                name = it["name"]
+                ysym, h, peers, mc = self.sym[name]
+                n0, n1, _ = self.shard[name]
+                if n1 > n0:
+                    seg.append(dict(y=ysym, x=self.input_of(it), W=self.W[name], col0=n0, bias=self.b[name],
+                                    peers=None if mc else peers, multicast=mc))
+                if name in self.consumed or it is self.items[-1]:
+                    if seg:
+                        self.envg.linear_nsplit_batch(seg, sync=False)
+                    seg = []
+                    h.barrier()
+            return
         if self.world == 1 and self.batch and all(it["op"] == "linear" for it in self.items):
             # one envg_linear_batch call: each input cast once, casts overlapped with the GEMMs
             self.envg.linear_batch([dict(dst=self.y[it["name"]], x=self.input_of(it), W=self.W[it["name"]],
@@ -589,8 +611,9 @@ def run_ours(args, items, desc, world, rank, local):
                 "config": {"workload": desc, "config": args.config, "flops_per_step": step_flops,
                            "timing": ("one step captured as a CUDA graph and replayed" if graph is not None
                                       else "steps launched from the host"),
-                           "api": "envg_linear_batch (one call per step)" if wl.batch and world == 1 else
-                                  "envg_linear per linear",
+                           "api": ("envg_linear_batch (one call per step)" if world == 1 else
+                                   "envg_linear_nsplit_batch (one call per barrier-to-barrier segment)")
+                                  if wl.batch else "envg_linear per linear",
                            "parallelism": "single GPU" if world == 1 else (
                                f"N-split x{world}, all-gather fused into the GEMM epilogue ("
                                + ("NVLS multimem stores" if any(v[3] for v in wl.sym.values()) else "P2P stores")

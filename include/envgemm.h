@@ -189,6 +189,22 @@ int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float*
                        int64_t col0, const float* x, envg_weight W, const float* bias, int64_t M,
                        int64_t K, int64_t N, int epilogue, const float* gate, int flags);
 
+/* Several N-split shards in one call, as envg_linear_batch runs several linears: each distinct
+ * input is rounded to bf16 once, on a second stream, overlapped with the previous GEMM.  Each
+ * descriptor is envg_linear_nsplit's arguments: lin.dst = this rank's copy of Y (row stride ldy),
+ * lin.N = the shard's rows of W.  A linear that reads another's Y belongs in a later call, after
+ * the ranks' barrier. */
+typedef struct envg_nsplit_desc {
+  envg_linear_desc lin;
+  float* const* y_peers;  /* every rank's copy of Y (this rank's included), or NULL */
+  int npeers;
+  float* y_multicast;     /* NVLS multicast address of Y, or NULL */
+  int64_t ldy;
+  int64_t col0;           /* first column of this shard in Y */
+} envg_nsplit_desc;
+
+int envg_linear_nsplit_batch(const envg_nsplit_desc* descs, int n, int flags);
+
 /* dst[batch, out_ch, outH, outW] = conv(src[batch, in_ch, H, W], W) + bias, NCHW, as
  * QNNConv2d (quicknn_kernels.pas:984-1010 -> quicknncpu.pas:1958-2132); outH/outW follow
  * QNNConv2DShape (quicknn_kernels.pas:984-988).  epilogue: ENVG_EPI_NONE/BIAS or ENVG_EPI_SILU. */

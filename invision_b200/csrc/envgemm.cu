@@ -1487,13 +1487,42 @@ cudaEvent_t batch_event(Dev* d, size_t i) {
 }
 }  // namespace
 
-int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
-  std::lock_guard<std::recursive_mutex> lk(g_mu);
-  Dev* d = cur();
-  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+}  // extern "C"
+
+namespace {
+// envg_linear_batch and envg_linear_nsplit_batch.  ns[i] (optional) makes linear i an N-split
+// shard whose epilogue writes into every rank's copy of Y.
+int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns, int n, int flags) {
   if (n < 0 || (n > 0 && !descs)) return fail(ENVG_ERR_ARG, "envg_linear_batch: bad descriptor array");
   if (!(flags & ENVG_DEVICE_PTRS)) return fail(ENVG_ERR_ARG, "envg_linear_batch: needs device pointers");
   for (int i = 0; i < n; ++i) ENVG_TRY(check_linear_args(d, descs[i]));
+  auto nsplit_epi = [&](int i, EpiArgs& e) -> int {
+    if (!ns) return ENVG_OK;
+    const envg_nsplit_desc& x = ns[i];
+    const int64_t n_out = e.n_out;
+    if (x.col0 < 0 || x.col0 + n_out > x.ldy)
+      return fail(ENVG_ERR_ARG, "nsplit: columns [%lld, %lld) outside ldy %lld", (long long)x.col0,
+                  (long long)(x.col0 + n_out), (long long)x.ldy);
+    if (!x.y_multicast && (x.npeers < 1 || x.npeers > 8 || !x.y_peers))
+      return fail(ENVG_ERR_ARG, "nsplit: give a multicast address or 1..8 peer copies of Y");
+    e.ldy = x.ldy;
+    e.col_off = (int)x.col0;
+    bool aligned = (reinterpret_cast<uintptr_t>(e.Y) & 15) == 0 && x.ldy % 4 == 0 && x.col0 % 4 == 0;
+    if (x.y_multicast) {
+      e.nremote = -1;
+      e.remote[0] = x.y_multicast;
+      aligned = aligned && (reinterpret_cast<uintptr_t>(x.y_multicast) & 15) == 0;
+    } else {
+      e.nremote = x.npeers;
+      for (int r = 0; r < x.npeers; ++r) {
+        if (!x.y_peers[r]) return fail(ENVG_ERR_ARG, "nsplit: peer copy %d is NULL", r);
+        e.remote[r] = x.y_peers[r];
+        aligned = aligned && (reinterpret_cast<uintptr_t>(x.y_peers[r]) & 15) == 0;
+      }
+    }
+    e.vec_ok = (aligned && n_out % 4 == 0) ? 1 : 0;
+    return ENVG_OK;
+  };
   if (!d->aux) ENVG_CUDA(cudaStreamCreateWithFlags(&d->aux, cudaStreamNonBlocking));
   cudaStream_t s = stream_of(d);
 
@@ -1559,6 +1588,7 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
     const int64_t pn = pr.W->layout == ENVG_LAYOUT_GATE_UP ? pr.N / 2 : pr.N;
     if ((const void*)pr.dst != (const void*)q.x || pr.M != q.M || pn != q.K) continue;
     if (pr.epilogue == ENVG_EPI_GATED_RESIDUAL || pr.M <= d->skinny_max || src_of[prod] < 0) continue;
+    if (ns) continue;  // an N-split producer computes only its own columns of the consumer's input
     if (yb_copy[prod] >= 0) continue;
     fused_from[j] = prod;
     yb_copy[prod] = (int)j;
@@ -1590,6 +1620,7 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
     if (q.M == 0) continue;
     const bool gu = q.W->layout == ENVG_LAYOUT_GATE_UP;
     EpiArgs e = linear_epi(q);
+    ENVG_TRY(nsplit_epi(i, e));
     if (yb_copy[i] >= 0) {
       e.yb = reinterpret_cast<__nv_bfloat16*>(base + offset[yb_copy[i]]);
       e.ldyb = descs[first_use[yb_copy[i]]].W->Kp;
@@ -1612,6 +1643,26 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
   }
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  return batch_core(d, descs, nullptr, n, flags);
+}
+
+int envg_linear_nsplit_batch(const envg_nsplit_desc* descs, int n, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (n < 0 || (n > 0 && !descs)) return fail(ENVG_ERR_ARG, "envg_linear_nsplit_batch: bad descriptor array");
+  std::vector<envg_linear_desc> lin((size_t)n);
+  for (int i = 0; i < n; ++i) lin[i] = descs[i].lin;
+  return batch_core(d, lin.data(), descs, n, flags);
 }
 
 int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float* y_multicast, int64_t ldy,

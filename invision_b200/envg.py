@@ -63,6 +63,11 @@ class ResBlockDesc(ctypes.Structure):
                 ("skip", ctypes.c_void_p), ("skip_bias", ctypes.c_void_p)]
 
 
+class NsplitDesc(ctypes.Structure):
+    _fields_ = [("lin", LinearDesc), ("y_peers", ctypes.POINTER(ctypes.c_void_p)), ("npeers", ctypes.c_int),
+                ("y_multicast", ctypes.c_void_p), ("ldy", ctypes.c_int64), ("col0", ctypes.c_int64)]
+
+
 class Stats(ctypes.Structure):
     _fields_ = [("calls", ctypes.c_uint64), ("kernel_launches", ctypes.c_uint64), ("flops", ctypes.c_double),
                 ("h2d_bytes", ctypes.c_double), ("d2h_bytes", ctypes.c_double), ("weight_bytes", ctypes.c_uint64),
@@ -96,6 +101,7 @@ def lib():
         L.envg_linear.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_noalloc.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_batch.argtypes = [ctypes.POINTER(LinearDesc), _ci, _ci]
+        L.envg_linear_nsplit_batch.argtypes = [ctypes.POINTER(NsplitDesc), _ci, _ci]
         L.envg_linear_adaln.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_nsplit.argtypes = [_vp, ctypes.POINTER(_vp), _ci, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64,
                                          _i64, _ci, _vp, _ci]
@@ -371,6 +377,31 @@ def linear_batch(calls, sync=True):
         keep.append(c)
     flags = DEVICE_PTRS | (0 if sync else ASYNC)
     return _check(lib().envg_linear_batch(arr, len(calls), flags))
+
+
+def linear_nsplit_batch(calls, sync=True):
+    """Several N-split shards in one envg_linear_nsplit_batch call.  `calls`: dicts with keys
+    y (this rank's copy of Y), x, W (the shard), col0 and peers (list of int pointers) or
+    multicast, plus optional bias, epilogue, gate.  Synchronise the ranks before reading Y."""
+    arr = (NsplitDesc * len(calls))()
+    keep = []
+    for i, c in enumerate(calls):
+        W = c["W"]
+        bias, gate = c.get("bias"), c.get("gate")
+        epi = c.get("epilogue")
+        if epi is None:
+            epi = EPI_SILU_GATE if W.layout == LAYOUT_GATE_UP else (EPI_BIAS if bias is not None else EPI_NONE)
+        _mode(c["y"], c["x"], bias, gate)
+        M, K = c["x"].shape
+        plist = list(c.get("peers") or [])
+        parr = (_vp * max(1, len(plist)))(*[_vp(p) for p in plist]) if plist else None
+        mc = c.get("multicast") or 0
+        arr[i] = NsplitDesc(LinearDesc(_ptr(c["y"]), _ptr(c["x"]), W.h, _ptr(bias), M, K, W.N, epi, _ptr(gate)),
+                            ctypes.cast(parr, ctypes.POINTER(ctypes.c_void_p)) if parr is not None else None,
+                            len(plist), _vp(mc) if mc else None, c["y"].shape[1], c["col0"])
+        keep.append((c, parr))
+    flags = DEVICE_PTRS | (0 if sync else ASYNC)
+    return _check(lib().envg_linear_nsplit_batch(arr, len(calls), flags))
 
 
 def linear_nsplit(y_local, x, W, col0, peers=None, multicast=0, bias=None, epilogue=None, gate=None, sync=True):

@@ -92,6 +92,41 @@ def _worker(rank, world, port, q):
             Ws.free()
             Wf.free()
             del Y, hdl
+        # envg_linear_nsplit_batch: two shards (plain + SiLU-gate) in one call, bit-identical
+        # to one GPU; the second reads the same input, so it is cast once
+        M, K = 384, 512
+        x, w1, b1 = inputs(M, K, 640, seed=11)
+        _, w2, b2 = inputs(M, K, 2 * 512, seed=12)
+        xt = torch.from_numpy(x).to(dev)
+        calls, refs, keep = [], [], []
+        for w, b, gate_up in ((w1, b1, False), (w2, b2, True)):
+            N = w.shape[0]
+            half = N // 2 if gate_up else N
+            n0, n1, per = shard_bounds(half, world, rank, 128)
+            layout = envg.LAYOUT_GATE_UP if gate_up else envg.LAYOUT_PLAIN
+            Ws = envg.Weight(w, layout=layout, shard=(n0, n1))
+            bs = np.concatenate([b[n0:n1], b[half + n0:half + n1]]) if gate_up else b[n0:n1]
+            Y = symm_mem.empty(M, half, device=dev)
+            hdl = symm_mem.rendezvous(Y, dist.group.WORLD)
+            Wf = envg.Weight(w, layout=layout)
+            ref = torch.empty(M, half, device=dev)
+            envg.linear(ref, xt, Wf, bias=torch.from_numpy(b).to(dev))
+            Wf.free()
+            Y.fill_(float("nan"))
+            calls.append(dict(y=Y, x=xt, W=Ws, col0=n0, peers=list(hdl.buffer_ptrs),
+                              bias=torch.from_numpy(np.ascontiguousarray(bs)).to(dev)))
+            refs.append(ref)
+            keep.append((Ws, hdl))
+        torch.cuda.synchronize()
+        keep[-1][1].barrier()
+        envg.linear_nsplit_batch(calls)
+        torch.cuda.synchronize()
+        keep[-1][1].barrier()
+        for i, (c, ref) in enumerate(zip(calls, refs)):
+            results.append((f"nsplit batch item {i}", bool(torch.equal(c["y"], ref))))
+        for Ws, _ in keep:
+            Ws.free()
+        del calls, keep
         if rank == 0:
             q.put(results)
     finally:
