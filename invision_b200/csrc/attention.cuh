@@ -465,8 +465,7 @@ ENVG_DEV void tmem_st64(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
-// 320 threads x 192 registers = 61440 of the SM's 65536.
-__global__ void __maxnreg__(192)
+__global__ void __launch_bounds__(FA2_THREADS, 1)
     k_attention2(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const FaArgs a) {
   constexpr uint32_t IDESC = idesc_f16_f32(FA_BQ, 128);

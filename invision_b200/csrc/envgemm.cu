@@ -509,40 +509,112 @@ int launch_k2(Dev* d, int mpad, int R, const CUtensorMap& tW, const CUtensorMap&
 }
 
 // M <= 8 linear on CUDA cores straight from fp32 X (no cast).
-int launch_gemv(Dev* d, const float* X, int64_t M, int64_t K, envg_weight W, bool gu, const EpiArgs& e, double flops,
-                double bytes) {
-  GemvArgs a{};
-  a.X = X;
-  a.ldx = K;
-  a.M = (int)M;
-  a.K = (int)K;
-  a.W = W->d;
-  a.Kp = W->Kp;
-  a.rows = (int)W->rows;
-  a.gate_up = gu ? 1 : 0;
-  a.groups = (int)(gu ? cdiv(W->half, 32) : cdiv(W->rows, 64));
-  const int64_t kchunks = cdiv(K, 256);
-  // about two blocks per SM, but at least two 256-element chunks of K per split
-  int64_t splits = std::max<int64_t>(1, std::min<int64_t>(kchunks / 2, cdiv(2 * d->sms, a.groups)));
-  a.kchunk = (int)(cdiv(kchunks, splits) * 256);
-  a.splits = (int)cdiv(K, a.kchunk);
-  a.xvec = (K % 8 == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0) ? 1 : 0;
-  a.epi = e;
-  if (a.splits > 1) {
-    ENVG_TRY(ensure(d, d->part, (size_t)a.groups * a.splits * 8 * 64 * sizeof(float)));
-    ENVG_TRY(ensure(d, d->cnt, (size_t)a.groups * sizeof(int), true));
-    a.partial = reinterpret_cast<float*>(d->part.p);
-    a.counters = reinterpret_cast<int*>(d->cnt.p);
+// One M <= 8 linear for k_gemv.
+struct GemvJob {
+  const float* X;
+  int64_t M, K;
+  envg_weight W;
+  bool gu;
+  EpiArgs e;
+  double flops, bytes;
+};
+
+// Resident k_gemv<MT> blocks on the whole GPU.
+template <int MT>
+int gemv_capacity(Dev* d, int* cap) {
+  static int per_sm[64] = {};
+  if (!per_sm[d->id]) {
+    int nb = 0;
+    ENVG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemv<MT>, 256, 0));
+    per_sm[d->id] = std::max(1, nb);
   }
-  const int grid = a.groups * a.splits;
+  *cap = per_sm[d->id] * d->sms;
+  return ENVG_OK;
+}
+
+// Up to GEMV_MAX_LIN independent skinny linears in one persistent k_gemv launch.
+int launch_gemv_set(Dev* d, const GemvJob* jobs, int n) {
+  if (n <= 0) return ENVG_OK;
+  if (n > GEMV_MAX_LIN) return fail(ENVG_ERR_STATE, "launch_gemv_set: %d linears", n);
+  int64_t mt = 1;
+  double flops = 0.0, bytes = 0.0;
+  for (int i = 0; i < n; ++i) {
+    mt = std::max(mt, jobs[i].M);
+    flops += jobs[i].flops;
+    bytes += jobs[i].bytes;
+  }
+  auto capacity = [&](int64_t m, int* c) -> int {
+    if (m <= 1) return gemv_capacity<1>(d, c);
+    if (m <= 2) return gemv_capacity<2>(d, c);
+    if (m <= 4) return gemv_capacity<4>(d, c);
+    return gemv_capacity<8>(d, c);
+  };
+  int cap = 0;
+  ENVG_TRY(capacity(mt, &cap));
+  GemvSet set{};
+  set.n = n;
+  size_t part_off = 0, cnt_off = 0;
+  std::vector<size_t> po(n), co(n);
+  for (int i = 0; i < n; ++i) {
+    const GemvJob& q = jobs[i];
+    GemvArgs& a = set.lin[i];
+    a.X = q.X;
+    a.ldx = q.K;
+    a.M = (int)q.M;
+    a.K = (int)q.K;
+    a.W = q.W->d;
+    a.Kp = q.W->Kp;
+    a.rows = (int)q.W->rows;
+    a.gate_up = q.gu ? 1 : 0;
+    a.groups = (int)(q.gu ? cdiv(q.W->half, 32) : cdiv(q.W->rows, 64));
+    // About one unit per resident block for the linear on its own: one with many row groups runs
+    // without split-K (partials and their reduction cost more than a short tail); one with few
+    // groups and a long K splits it, keeping at least 1024 K elements per split.  The choice
+    // depends only on the linear (not on the rest of the set), so a batch sums in the same order
+    // as a separate call.
+    const int64_t kchunks = cdiv(q.K, 256);
+    int own_cap = 0;
+    ENVG_TRY(capacity(q.M, &own_cap));
+    const int64_t splits = std::max<int64_t>(1, std::min<int64_t>(std::max<int64_t>(1, kchunks / 4),
+                                                                    (int64_t)own_cap / a.groups));
+    a.kchunk = (int)(cdiv(kchunks, splits) * 256);
+    a.splits = (int)cdiv(q.K, a.kchunk);
+    a.xvec = (q.K % 8 == 0 && (reinterpret_cast<uintptr_t>(q.X) & 15) == 0) ? 1 : 0;
+    a.epi = q.e;
+    set.base[i] = set.total;
+    set.total += a.groups * a.splits;
+    po[i] = part_off;
+    co[i] = cnt_off;
+    if (a.splits > 1) {
+      part_off += (size_t)a.groups * a.splits * 8 * 64 * sizeof(float);
+      cnt_off += (size_t)rup(a.groups, 64) * sizeof(int);
+    }
+  }
+  set.base[n] = set.total;
+  if (part_off) {
+    ENVG_TRY(ensure(d, d->part, part_off));
+    ENVG_TRY(ensure(d, d->cnt, cnt_off, true));
+    for (int i = 0; i < n; ++i)
+      if (set.lin[i].splits > 1) {
+        set.lin[i].partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d->part.p) + po[i]);
+        set.lin[i].counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(d->cnt.p) + co[i]);
+      }
+  }
+  const int grid = std::min(set.total, cap);
   ProfScope ps(stream_of(d), KID_GEMV, flops, bytes);
-  if (M <= 1) k_gemv<1><<<grid, 256, 0, stream_of(d)>>>(a);
-  else if (M <= 2) k_gemv<2><<<grid, 256, 0, stream_of(d)>>>(a);
-  else if (M <= 4) k_gemv<4><<<grid, 256, 0, stream_of(d)>>>(a);
-  else k_gemv<8><<<grid, 256, 0, stream_of(d)>>>(a);
+  if (mt <= 1) k_gemv<1><<<grid, 256, 0, stream_of(d)>>>(set);
+  else if (mt <= 2) k_gemv<2><<<grid, 256, 0, stream_of(d)>>>(set);
+  else if (mt <= 4) k_gemv<4><<<grid, 256, 0, stream_of(d)>>>(set);
+  else k_gemv<8><<<grid, 256, 0, stream_of(d)>>>(set);
   ENVG_CUDA(cudaGetLastError());
   d->st.kernel_launches++;
   return ENVG_OK;
+}
+
+int launch_gemv(Dev* d, const float* X, int64_t M, int64_t K, envg_weight W, bool gu, const EpiArgs& e, double flops,
+                double bytes) {
+  const GemvJob j{X, M, K, W, gu, e, flops, bytes};
+  return launch_gemv_set(d, &j, 1);
 }
 
 // QNNAdaLN (EPSILON = 1e-6, quicknn_common.pas:51) fused with the bf16 cast, or into fp32.
@@ -1610,10 +1682,36 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     ENVG_CUDA(cudaEventRecord(batch_event(d, 1 + j), d->aux));
     return ENVG_OK;
   };
+  // Consecutive independent M <= gemv_max linears go out as one persistent k_gemv launch; until
+  // that launch, their events do not exist, so casts that read their outputs wait.
+  std::vector<GemvJob> gq;
+  std::vector<int> gidx;
+  auto flush_gemv = [&]() -> int {
+    if (gq.empty()) return ENVG_OK;
+    ENVG_TRY(launch_gemv_set(d, gq.data(), (int)gq.size()));
+    for (size_t k = 0; k < gidx.size(); ++k) {
+      ENVG_CUDA(cudaEventRecord(batch_event(d, 1 + ncopies + gidx[k]), s));
+      d->st.calls++;
+      d->st.flops += gq[k].flops;
+    }
+    gq.clear();
+    gidx.clear();
+    return ENVG_OK;
+  };
+  auto reads_output_of = [&](const envg_linear_desc& c, const envg_linear_desc& pr) {
+    const bool gu = pr.W->layout == ENVG_LAYOUT_GATE_UP;
+    const char* y0 = reinterpret_cast<const char*>(pr.dst);
+    const char* y1 = y0 + (size_t)(pr.M * (gu ? pr.N / 2 : pr.N)) * 4;
+    const char* x0 = reinterpret_cast<const char*>(c.x);
+    const char* x1 = x0 + (size_t)(c.M * c.K) * 4;
+    return pr.M > 0 && x0 < y1 && y0 < x1;
+  };
   for (int i = 0; i < n; ++i) {
     const envg_linear_desc& q = descs[i];
+    if (src_of[i] >= 0) ENVG_TRY(flush_gemv());  // a tcgen05 linear follows the pending skinny ones
     // casts run one linear ahead of the GEMMs, in order, as soon as their inputs exist
-    while (next_copy < ncopies && first_use[next_copy] <= i + 1 && ready(next_copy, i)) {
+    while (next_copy < ncopies && first_use[next_copy] <= i + 1 &&
+           ready(next_copy, gidx.empty() ? i : gidx.front())) {
       if (fused_from[next_copy] < 0) ENVG_TRY(issue_cast(next_copy));  // else written by its producer on s
       ++next_copy;
     }
@@ -1630,8 +1728,17 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     const double ob = 4.0 * (double)q.M * n_out + (q.bias ? 4.0 * q.N : 0.0) +
                       (q.epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)q.M * n_out + 4.0 * q.N : 0.0);
     if (src_of[i] < 0) {
-      ENVG_TRY(launch_gemv(d, q.x, q.M, q.K, q.W, gu, e, fl, 2.0 * (double)q.N * q.K + 4.0 * (double)q.M * q.K + ob));
+      for (int k : gidx)
+        if (reads_output_of(q, descs[k])) {
+          ENVG_TRY(flush_gemv());
+          break;
+        }
+      gq.push_back(GemvJob{q.x, q.M, q.K, q.W, gu, e, fl, 2.0 * (double)q.N * q.K + 4.0 * (double)q.M * q.K + ob});
+      gidx.push_back(i);
+      if ((int)gq.size() == GEMV_MAX_LIN) ENVG_TRY(flush_gemv());
+      continue;
     } else {
+      ENVG_TRY(flush_gemv());
       if ((size_t)src_of[i] >= next_copy) return fail(ENVG_ERR_STATE, "envg_linear_batch: internal schedule error");
       if (fused_from[src_of[i]] < 0) ENVG_CUDA(cudaStreamWaitEvent(s, batch_event(d, 1 + src_of[i]), 0));
       ENVG_TRY(gemm_device(d, base + offset[src_of[i]], q.M, q.W->Kp, q.W->tm256, q.W->tm128, q.W->rows, gu, e, fl,
@@ -1641,6 +1748,7 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     d->st.calls++;
     d->st.flops += fl;
   }
+  ENVG_TRY(flush_gemv());
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
 }
@@ -2031,7 +2139,15 @@ int envg_attention(float* dst, const float* Q, const float* K, const float* V, i
                                                                                                         tV, a);
     else
       k_attention<<<dim3((unsigned)(sq_pad / FA_BQ), (unsigned)heads), FA_THREADS, FaSmem::TOTAL, s>>>(tQ, tK, tV, a);
-    ENVG_CUDA(cudaGetLastError());
+    const cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess) {
+      cudaFuncAttributes fa{};
+      cudaFuncGetAttributes(&fa, two ? (const void*)k_attention2 : (const void*)k_attention);
+      return fail(ENVG_ERR_CUDA, "attention launch (%s, %d threads, %d B smem) failed: %s; kernel: %d regs, max %d "
+                  "threads, %zu B local", two ? "k_attention2" : "k_attention", two ? FA2_THREADS : FA_THREADS,
+                  two ? Fa2Smem::TOTAL : FaSmem::TOTAL, cudaGetErrorString(le), fa.numRegs, fa.maxThreadsPerBlock,
+                  fa.localSizeBytes);
+    }
     d->st.kernel_launches++;
     d->st.flops += fl;
   }

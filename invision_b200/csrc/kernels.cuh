@@ -1271,13 +1271,29 @@ ENVG_DEV uint4 ld_nc_v4(const void* p) {
   return r;
 }
 
+// Several skinny linears in one persistent launch: unit u of the set is (linear l, row group,
+// K split); block b takes units b, b + gridDim.x, ...  The host sizes the units (about one per
+// resident block, by bytes) and the launch streams every weight of the set back to back.
+constexpr int GEMV_MAX_LIN = 6;
+struct GemvSet {
+  int n;                        // linears in the set
+  int total;                    // units over all of them
+  int base[GEMV_MAX_LIN + 1];   // first unit of each linear
+  GemvArgs lin[GEMV_MAX_LIN];
+};
+
 template <int MT>
-__global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
+__global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet set) {
   __shared__ float s_sum[MT][64];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int group = blockIdx.x / a.splits;
-  const int split = blockIdx.x - group * a.splits;
+  for (int u = blockIdx.x; u < set.total; u += gridDim.x) {
+  int l = 0;
+  while (l + 1 < set.n && u >= set.base[l + 1]) ++l;
+  const GemvArgs& a = set.lin[l];
+  const int v = u - set.base[l];
+  const int group = v / a.splits;
+  const int split = v - group * a.splits;
   // the 8 device rows of this warp
   int drow[8];
 #pragma unroll
@@ -1353,7 +1369,8 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
     __syncthreads();
     if (threadIdx.x == 0) s_last = (atomicAdd(a.counters + group, 1) == a.splits - 1) ? 1 : 0;
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) continue;  // uniform across the block; s_sum is rewritten only after the next
+                            // unit's __syncthreads
     __threadfence();
     for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) {
       float v = 0.0f;
@@ -1389,6 +1406,8 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
     }
   }
   if (e.nremote != 0) __threadfence_system();
+  __syncthreads();  // every thread is done with s_sum before the next unit writes it
+  }
 }
 
 // ------------------------------------------------------------------------------------------

@@ -566,3 +566,38 @@ def test_attention_two_tile_kernel_in_subprocess():
     r = subprocess.run([sys.executable, "-c", code], env={**os.environ, "ENVG_ATTN_TILES": "2"}, capture_output=True,
                        text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
+
+
+def test_linear_batch_groups_skinny_linears(gpu):
+    """Consecutive M <= 8 linears of a batch run as one persistent k_gemv launch (several weights per
+    launch, a chained one after a flush); results are bit-identical to separate envg_linear calls and
+    within the fp32-exact bound of the reference."""
+    import torch
+
+    dev = "cuda"
+    rng = np.random.default_rng(9)
+    H, F = 2560, 1536
+
+    def wt(n, k, seed):
+        return O.f32_to_bf16_rne((0.02 * np.random.default_rng(seed).standard_normal((n, k))).astype(np.float32))
+
+    ws = {"q": wt(4096, H, 1), "k": wt(1024, H, 2), "gu": wt(2 * F, H, 3), "d": wt(H, F, 4), "o": wt(H, 4096, 5)}
+    W = {k: gpu.Weight(v, layout=gpu.LAYOUT_GATE_UP if k == "gu" else gpu.LAYOUT_PLAIN) for k, v in ws.items()}
+    x4 = torch.from_numpy(rng.standard_normal((4, H), dtype=np.float32)).to(dev)
+    x1 = torch.from_numpy(rng.standard_normal((1, 4096), dtype=np.float32)).to(dev)
+    b = torch.from_numpy((0.01 * rng.standard_normal(4096)).astype(np.float32)).to(dev)
+    outs = {"q": torch.empty(4, 4096, device=dev), "k": torch.empty(4, 1024, device=dev),
+            "gu": torch.empty(4, F, device=dev), "d": torch.empty(4, H, device=dev), "o": torch.empty(1, H, device=dev)}
+    calls = [dict(dst=outs["q"], x=x4, W=W["q"], bias=b), dict(dst=outs["k"], x=x4, W=W["k"]),
+             dict(dst=outs["gu"], x=x4, W=W["gu"]), dict(dst=outs["d"], x=outs["gu"], W=W["d"]),
+             dict(dst=outs["o"], x=x1, W=W["o"])]
+    gpu.linear_batch(calls)
+    torch.cuda.synchronize()
+    got = {k: v.cpu().numpy() for k, v in outs.items()}
+    for c in calls:
+        gpu.linear(c["dst"], c["x"], c["W"], bias=c.get("bias"))
+    torch.cuda.synchronize()
+    for k, v in outs.items():
+        np.testing.assert_array_equal(got[k], v.cpu().numpy(), err_msg=k)
+    ref = O.linear_bf16(x4.cpu().numpy(), ws["q"], b.cpu().numpy(), path=O.PATH_SCALAR)
+    assert_parity(got["q"], ref, tol_max=1e-5, tol_mean=5e-6, what="grouped gemv q")
