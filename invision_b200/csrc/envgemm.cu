@@ -586,7 +586,7 @@ int launch_gemv_set(Dev* d, const GemvJob* jobs, int n) {
     po[i] = part_off;
     co[i] = cnt_off;
     if (a.splits > 1) {
-      part_off += (size_t)a.groups * a.splits * 8 * 64 * sizeof(float);
+      part_off += (size_t)a.groups * a.splits * GEMV_PART * sizeof(float);
       cnt_off += (size_t)rup(a.groups, 64) * sizeof(int);
     }
   }
@@ -667,9 +667,10 @@ int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap&
     SkinnyArgs s{};
     s.n_tiles = (int)cdiv(rows_b, (int64_t)R * BM);
     s.num_kb = (int)num_kb;
-    // about two CTAs per SM, but at least 4 k-blocks (32 KB of W per 128 rows) per split
-    int splits = std::max(1, (2 * d->sms) / s.n_tiles);
-    splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 4));
+    // about one CTA per SM, with at least 8 k-blocks (128 KB of W per 128 rows) per split:
+    // fewer, longer splits pay the per-CTA setup and the partial reduction less often
+    int splits = std::max(1, d->sms / s.n_tiles);
+    splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 8));
     s.kb_per_split = (int)cdiv(num_kb, splits);
     s.splits = (int)cdiv(num_kb, s.kb_per_split);
     s.epi = e;

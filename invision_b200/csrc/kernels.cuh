@@ -1247,6 +1247,9 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
 // rows (32 gate + 32 up output pairs for the GATE_UP layout); split-K across blocks reduces
 // deterministically: the last block of a row group sums the partials in split order.
 // ------------------------------------------------------------------------------------------
+constexpr int GEMV_MAX_M = 8;
+constexpr int GEMV_PART = GEMV_MAX_M * 64;  // floats per (row group, split) partial
+
 struct GemvArgs {
   const float* X;
   int64_t ldx;
@@ -1259,7 +1262,7 @@ struct GemvArgs {
   int splits, kchunk;  // split-K: K elements per split (multiple of 256)
   int xvec;       // X rows 16-byte aligned and K % 8 == 0
   EpiArgs epi;
-  float* partial;  // [groups][splits][8][64]
+  float* partial;  // [groups][splits][GEMV_PART]
   int* counters;   // [groups]
 };
 
@@ -1363,7 +1366,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
   }
   __syncthreads();
   if (a.splits > 1) {
-    float* part = a.partial + ((int64_t)group * a.splits + split) * (8 * 64);
+    float* part = a.partial + ((int64_t)group * a.splits + split) * GEMV_PART;
     for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) __stcg(part + t, s_sum[t / 64][t % 64]);
     __threadfence();
     __syncthreads();
@@ -1375,7 +1378,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
     for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) {
       float v = 0.0f;
 #pragma unroll 8
-      for (int sp = 0; sp < a.splits; ++sp) v += __ldcg(a.partial + ((int64_t)group * a.splits + sp) * (8 * 64) + t);
+      for (int sp = 0; sp < a.splits; ++sp) v += __ldcg(a.partial + ((int64_t)group * a.splits + sp) * GEMV_PART + t);
       s_sum[t / 64][t % 64] = v;
     }
     if (threadIdx.x == 0) a.counters[group] = 0;  // re-arm for the next launch
