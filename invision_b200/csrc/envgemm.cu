@@ -508,6 +508,112 @@ int launch_k2(Dev* d, int mpad, int R, const CUtensorMap& tW, const CUtensorMap&
   return fail(ENVG_ERR_ARG, "skinny path: unsupported padded M %d", mpad);
 }
 
+// One 8 < M <= 64 linear for k2_set: A = its bf16 activation copy [M, Kp].
+struct K2Job {
+  const void* A;
+  int64_t M, Kp;
+  const CUtensorMap* w128;  // W, box 64 x 128 rows
+  int64_t rows_b;
+  bool gu;
+  EpiArgs e;
+  double flops, bytes;
+};
+
+// Splits of a skinny linear: about one unit per SM, at least 8 k-blocks (128 KB of W per 128
+// rows) per split; more, shorter splits cost more in partials and reductions than they gain.
+// Depends only on the linear's shape.
+void k2_plan(const Dev* d, int64_t rows_b, int64_t Kp, bool gu, SkinnyArgs& s) {
+  const int R = gu ? 2 : 1;
+  const int64_t num_kb = cdiv(Kp, BK);
+  s.n_tiles = (int)cdiv(rows_b, (int64_t)R * BM);
+  s.num_kb = (int)num_kb;
+  int splits = std::max(1, d->sms / s.n_tiles);
+  splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 8));
+  s.kb_per_split = (int)cdiv(num_kb, splits);
+  s.splits = (int)cdiv(num_kb, s.kb_per_split);
+}
+
+template <int MPAD, int R>
+int launch_k2_set_t(Dev* d, K2Set& S, double flops, double bytes) {
+  constexpr int STAGE = K2SetSmem<MPAD, R, 1>::STAGE_BYTES;
+  constexpr int ST = (110 * 1024) / STAGE < 2 ? 2 : (110 * 1024) / STAGE;  // two CTAs per SM
+  using L = K2SetSmem<MPAD, R, ST>;
+  auto kern = k2_set<MPAD, R, ST>;
+  static bool attr[64] = {};
+  if (!attr[d->id]) {
+    ENVG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    attr[d->id] = true;
+  }
+  S.status = d->d_status;
+  S.wait_cap_ns = d->wait_cap_ns;
+  const int grid = std::min(S.total, 2 * d->sms);
+  ProfScope ps(stream_of(d), KID_K2, flops, bytes);
+  kern<<<grid, K1_THREADS, L::TOTAL, stream_of(d)>>>(S);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
+// Up to K2S_MAX_LIN skinny linears with the same padded M and the same layout kind (plain, or
+// GATE_UP with the SiLU-gate) in one persistent k2_set launch.
+int launch_k2_set(Dev* d, const K2Job* jobs, int n) {
+  if (n <= 0) return ENVG_OK;
+  if (n > K2S_MAX_LIN) return fail(ENVG_ERR_STATE, "launch_k2_set: %d linears", n);
+  const int mpad = (int)rup(std::max<int64_t>(jobs[0].M, 1), 16);
+  K2Set S{};
+  S.n = n;
+  size_t part_off = 0, cnt_off = 0;
+  std::vector<size_t> po(n), co(n);
+  double flops = 0.0, bytes = 0.0;
+  for (int i = 0; i < n; ++i) {
+    const K2Job& q = jobs[i];
+    if ((int)rup(std::max<int64_t>(q.M, 1), 16) != mpad || q.gu != jobs[0].gu)
+      return fail(ENVG_ERR_STATE, "launch_k2_set: mixed padded M or layout");
+    ENVG_TRY(tmap_2d(&S.tmX[i], q.A, q.Kp, q.M, mpad));
+    S.tmW[i] = *q.w128;
+    K2Lin& L = S.lin[i];
+    L.R = q.gu ? 2 : 1;
+    k2_plan(d, q.rows_b, q.Kp, q.gu, L.s);
+    L.s.epi = q.e;
+    S.base[i] = S.total;
+    S.total += L.s.n_tiles * L.s.splits;
+    po[i] = part_off;
+    co[i] = cnt_off;
+    if (L.s.splits > 1) {
+      part_off += (size_t)L.s.n_tiles * L.s.splits * L.R * BM * mpad * sizeof(float);
+      cnt_off += (size_t)rup(L.s.n_tiles, 64) * sizeof(int);
+    }
+    flops += q.flops;
+    bytes += q.bytes;
+  }
+  S.base[n] = S.total;
+  if (part_off) {
+    ENVG_TRY(ensure(d, d->part, part_off));
+    ENVG_TRY(ensure(d, d->cnt, cnt_off, true));
+    for (int i = 0; i < n; ++i)
+      if (S.lin[i].s.splits > 1) {
+        S.lin[i].s.partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d->part.p) + po[i]);
+        S.lin[i].s.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(d->cnt.p) + co[i]);
+      }
+  }
+  if (!jobs[0].gu) {
+    switch (mpad) {
+      case 16: return launch_k2_set_t<16, 1>(d, S, flops, bytes);
+      case 32: return launch_k2_set_t<32, 1>(d, S, flops, bytes);
+      case 48: return launch_k2_set_t<48, 1>(d, S, flops, bytes);
+      case 64: return launch_k2_set_t<64, 1>(d, S, flops, bytes);
+    }
+  } else {
+    switch (mpad) {
+      case 16: return launch_k2_set_t<16, 2>(d, S, flops, bytes);
+      case 32: return launch_k2_set_t<32, 2>(d, S, flops, bytes);
+      case 48: return launch_k2_set_t<48, 2>(d, S, flops, bytes);
+      case 64: return launch_k2_set_t<64, 2>(d, S, flops, bytes);
+    }
+  }
+  return fail(ENVG_ERR_ARG, "skinny path: unsupported padded M %d", mpad);
+}
+
 // M <= 8 linear on CUDA cores straight from fp32 X (no cast).
 // One M <= 8 linear for k_gemv.
 struct GemvJob {
@@ -660,27 +766,8 @@ int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap&
                 int64_t rows_b, bool silu_gate, EpiArgs e, double flops, double bytes) {
   const int64_t num_kb = cdiv(Kp, BK);
   if (M <= d->skinny_max) {
-    const int mpad = (int)rup(std::max<int64_t>(M, 1), 16);
-    const int R = silu_gate ? 2 : 1;
-    CUtensorMap tX;
-    ENVG_TRY(tmap_2d(&tX, A, Kp, M, mpad));
-    SkinnyArgs s{};
-    s.n_tiles = (int)cdiv(rows_b, (int64_t)R * BM);
-    s.num_kb = (int)num_kb;
-    // about one CTA per SM, with at least 8 k-blocks (128 KB of W per 128 rows) per split:
-    // fewer, longer splits pay the per-CTA setup and the partial reduction less often
-    int splits = std::max(1, d->sms / s.n_tiles);
-    splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 8));
-    s.kb_per_split = (int)cdiv(num_kb, splits);
-    s.splits = (int)cdiv(num_kb, s.kb_per_split);
-    s.epi = e;
-    if (s.splits > 1) {
-      ENVG_TRY(ensure(d, d->part, (size_t)s.n_tiles * s.splits * R * BM * mpad * sizeof(float)));
-      ENVG_TRY(ensure(d, d->cnt, (size_t)s.n_tiles * sizeof(int), true));
-      s.partial = reinterpret_cast<float*>(d->part.p);
-      s.counters = reinterpret_cast<int*>(d->cnt.p);
-    }
-    return launch_k2(d, mpad, R, b128, tX, s, flops, bytes);
+    const K2Job j{A, M, Kp, &b128, rows_b, silu_gate, e, flops, bytes};
+    return launch_k2_set(d, &j, 1);
   }
   CUtensorMap tA;
   ENVG_TRY(tmap_2d(&tA, A, Kp, M, BM));
@@ -1699,6 +1786,22 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     gidx.clear();
     return ENVG_OK;
   };
+  // Consecutive independent skinny (gemv_max < M <= skinny_max) linears with the same padded M
+  // go out as one persistent k2_set launch, in the same way.
+  std::vector<K2Job> kq;
+  std::vector<int> kidx;
+  auto flush_k2 = [&]() -> int {
+    if (kq.empty()) return ENVG_OK;
+    ENVG_TRY(launch_k2_set(d, kq.data(), (int)kq.size()));
+    for (size_t k = 0; k < kidx.size(); ++k) {
+      ENVG_CUDA(cudaEventRecord(batch_event(d, 1 + ncopies + kidx[k]), s));
+      d->st.calls++;
+      d->st.flops += kq[k].flops;
+    }
+    kq.clear();
+    kidx.clear();
+    return ENVG_OK;
+  };
   auto reads_output_of = [&](const envg_linear_desc& c, const envg_linear_desc& pr) {
     const bool gu = pr.W->layout == ENVG_LAYOUT_GATE_UP;
     const char* y0 = reinterpret_cast<const char*>(pr.dst);
@@ -1709,10 +1812,15 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
   };
   for (int i = 0; i < n; ++i) {
     const envg_linear_desc& q = descs[i];
-    if (src_of[i] >= 0) ENVG_TRY(flush_gemv());  // a tcgen05 linear follows the pending skinny ones
-    // casts run one linear ahead of the GEMMs, in order, as soon as their inputs exist
-    while (next_copy < ncopies && first_use[next_copy] <= i + 1 &&
-           ready(next_copy, gidx.empty() ? i : gidx.front())) {
+    const bool is_k2 = src_of[i] >= 0 && q.M <= d->skinny_max;
+    if (src_of[i] >= 0) ENVG_TRY(flush_gemv());  // a tcgen05 linear follows the pending gemv ones
+    if (!is_k2) ENVG_TRY(flush_k2());
+    // casts run one linear ahead of the GEMMs, in order, as soon as their inputs exist; a cast
+    // that reads the output of a linear still waiting in a group waits for that group's launch
+    int first_pending = i;
+    if (!gidx.empty()) first_pending = std::min(first_pending, gidx.front());
+    if (!kidx.empty()) first_pending = std::min(first_pending, kidx.front());
+    while (next_copy < ncopies && first_use[next_copy] <= i + 1 && ready(next_copy, first_pending)) {
       if (fused_from[next_copy] < 0) ENVG_TRY(issue_cast(next_copy));  // else written by its producer on s
       ++next_copy;
     }
@@ -1738,6 +1846,26 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
       gidx.push_back(i);
       if ((int)gq.size() == GEMV_MAX_LIN) ENVG_TRY(flush_gemv());
       continue;
+    } else if (is_k2) {
+      const int mpad = (int)rup(q.M, 16);
+      bool flush = !kq.empty() && ((int)rup(kq.front().M, 16) != mpad || kq.front().gu != gu ||
+                                   (int)kq.size() == K2S_MAX_LIN);
+      for (int k : kidx) flush = flush || reads_output_of(q, descs[k]);
+      if (flush) ENVG_TRY(flush_k2());
+      if ((size_t)src_of[i] >= next_copy) {
+        // its cast waits for a linear of the pending group: launch the group, then cast
+        ENVG_TRY(flush_k2());
+        while (next_copy < ncopies && first_use[next_copy] <= i + 1 && ready(next_copy, i)) {
+          if (fused_from[next_copy] < 0) ENVG_TRY(issue_cast(next_copy));
+          ++next_copy;
+        }
+        if ((size_t)src_of[i] >= next_copy) return fail(ENVG_ERR_STATE, "envg_linear_batch: internal schedule error");
+      }
+      if (fused_from[src_of[i]] < 0) ENVG_CUDA(cudaStreamWaitEvent(s, batch_event(d, 1 + src_of[i]), 0));
+      kq.push_back(K2Job{base + offset[src_of[i]], q.M, q.W->Kp, &q.W->tm128, q.W->rows, gu, e, fl,
+                         2.0 * (double)q.N * q.K + 2.0 * (double)q.M * q.W->Kp + ob});
+      kidx.push_back(i);
+      continue;
     } else {
       ENVG_TRY(flush_gemv());
       if ((size_t)src_of[i] >= next_copy) return fail(ENVG_ERR_STATE, "envg_linear_batch: internal schedule error");
@@ -1750,6 +1878,7 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     d->st.flops += fl;
   }
   ENVG_TRY(flush_gemv());
+  ENVG_TRY(flush_k2());
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
 }

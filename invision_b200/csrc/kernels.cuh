@@ -1240,6 +1240,295 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------
+// K2 set: the skinny GEMM of k2_skinny, persistent over the units (linear, tile, split) of up to
+// K2S_MAX_LIN linears in one launch.  The producer, the UMMA thread and the epilogue warps walk
+// the same unit sequence (blockIdx.x, +gridDim.x, ...); the accumulator is double-buffered in
+// TMEM so the epilogue of one unit overlaps the main loop of the next, and the launch cost, the
+// TMEM allocation and the pipeline fill are paid once for all the weights of the set.  Each unit
+// issues the same UMMAs in the same order as k2_skinny does for that (tile, split), and the split
+// reduction sums in split order, so results do not depend on the set a linear is launched in.
+// ------------------------------------------------------------------------------------------
+constexpr int K2S_MAX_LIN = 4;
+
+struct K2Lin {
+  SkinnyArgs s;  // n_tiles, splits, kb_per_split, num_kb, epi, partial, counters
+  int R;         // 2: the unit pairs a gate tile with its up tile (SiLU-gate); one R per set
+};
+
+struct K2Set {
+  CUtensorMap tmW[K2S_MAX_LIN];  // W, box 64 x 128 rows
+  CUtensorMap tmX[K2S_MAX_LIN];  // X (bf16), box 64 x MPAD rows
+  K2Lin lin[K2S_MAX_LIN];
+  int n, total;
+  int base[K2S_MAX_LIN + 1];
+  int* status;
+  uint64_t wait_cap_ns;
+};
+
+template <int MPAD, int R, int STAGES>
+struct K2SetSmem {
+  static constexpr int W_BYTES = R * TILE_A_BYTES;
+  static constexpr int X_BYTES = MPAD * BK * 2;
+  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+  static constexpr int NBARS = 2 * STAGES + 5;       // full/empty, tfull[2], tempty[2], drain
+  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 32;
+  static constexpr uint32_t ACC_COLS = R * MPAD;      // R accumulators of MPAD columns
+  static constexpr uint32_t TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
+                                        : (2 * ACC_COLS <= 128) ? 128 : 256;
+};
+
+ENVG_DEV void k2_unit(const K2Set& S, int u, int& l, int& tile, int& split) {
+  l = 0;
+  while (l + 1 < S.n && u >= S.base[l + 1]) ++l;
+  const int v = u - S.base[l];
+  tile = v / S.lin[l].s.splits;
+  split = v - tile * S.lin[l].s.splits;
+}
+
+template <int MPAD, int R, int STAGES>
+__global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ K2Set S) {
+  using L = K2SetSmem<MPAD, R, STAGES>;
+  constexpr uint32_t IDESC = idesc_bf16_f32(BM, MPAD);
+  static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 64, "MPAD");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + STAGES * L::W_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sX + STAGES * L::X_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBARS);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_s = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * STAGES;
+  const uint32_t tfull0 = empty0 + 8 * STAGES;
+  const uint32_t tempty0 = tfull0 + 16;
+  const uint32_t drain = tempty0 + 16;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 4);
+    }
+    mbar_init(drain, 1);
+    *abort_s = 0;
+    *last_s = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane < S.n) {
+    tma_prefetch_desc(&S.tmW[lane]);
+    tma_prefetch_desc(&S.tmX[lane]);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtl wc{S.wait_cap_ns, S.status, abort_s, 0};
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t pending = 0, issue_ph = 0;
+      for (int u = blockIdx.x; u < S.total; u += gridDim.x) {
+        int l, tile, split;
+        k2_unit(S, u, l, tile, split);
+        const SkinnyArgs& a = S.lin[l].s;
+        const int kb0 = split * a.kb_per_split;
+        const int kb1 = min(kb0 + a.kb_per_split, a.num_kb);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_bounded(empty0 + 8 * stage, ph ^ 1, wc, 41)) goto producer_done;
+          const uint32_t fb = full0 + 8 * stage;
+          mbar_arrive_expect_tx(fb, R * TILE_A_BYTES + L::X_BYTES);
+          for (int r = 0; r < R; ++r)
+            tma_load_2d(smem_u32(sW + stage * L::W_BYTES + r * TILE_A_BYTES), &S.tmW[l], fb, kb * BK,
+                        (tile * R + r) * BM);
+          tma_load_2d(smem_u32(sX + stage * L::X_BYTES), &S.tmX[l], fb, kb * BK, 0);
+          pending |= 1u << stage;
+          issue_ph = (issue_ph & ~(1u << stage)) | (ph << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    producer_done:
+      if (*abort_s)
+        for (int s = 0; s < STAGES; ++s)
+          if (pending & (1u << s)) wait_drain(full0 + 8 * s, (issue_ph >> s) & 1u, S.wait_cap_ns);
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      for (int u = blockIdx.x; u < S.total; u += gridDim.x) {
+        int l, tile, split;
+        k2_unit(S, u, l, tile, split);
+        const SkinnyArgs& a = S.lin[l].s;
+        const int kb0 = split * a.kb_per_split;
+        const int kb1 = min(kb0 + a.kb_per_split, a.num_kb);
+        if (!wait_bounded(tempty0 + 8 * acc, aph ^ 1, wc, 42)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)acc * L::ACC_COLS;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_bounded(full0 + 8 * stage, ph, wc, 43)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t xd = sw128_kmajor_desc(smem_u32(sX + stage * L::X_BYTES));
+          for (int r = 0; r < R; ++r) {
+            const uint64_t wd = sw128_kmajor_desc(smem_u32(sW + stage * L::W_BYTES + r * TILE_A_BYTES));
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_bf16(d_tmem + (uint32_t)(r * MPAD), wd + 2 * k, xd + 2 * k, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(empty0 + 8 * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull0 + 8 * acc);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
+      }
+      if (*abort_s) {
+        umma_commit(drain);
+        wait_drain(drain, 0, S.wait_cap_ns);
+      }
+    }
+  } else {
+    // ---------------- epilogue: 4 warps, one TMEM lane quadrant each ----------------
+    const int q = warp & 3;
+    const int rowin = q * 32 + lane;  // W row within a 128-row tile
+    const int et = threadIdx.x - 64;  // 0..127
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int u = blockIdx.x; u < S.total; u += gridDim.x) {
+      int l, tile, split;
+      k2_unit(S, u, l, tile, split);
+      const SkinnyArgs& a = S.lin[l].s;
+      if (!wait_bounded_warp(tfull0 + 8 * acc, aph, wc, 44)) break;
+      tc_fence_after();
+      float accv[R][MPAD];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint32_t ta = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)acc * L::ACC_COLS + (uint32_t)(r * MPAD);
+#pragma unroll
+        for (int c = 0; c < MPAD / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(ta + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) accv[r][c * 32 + j] = __uint_as_float(v[j]);
+        }
+        if (MPAD % 32) {
+          uint32_t v[16];
+          tmem_ld16(ta + (MPAD / 32) * 32, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) accv[r][(MPAD / 32) * 32 + j] = __uint_as_float(v[j]);
+        }
+      }
+      // the accumulator is in registers: hand the TMEM buffer back to the UMMA thread
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+      bool finalize = true;
+      if (a.splits > 1) {
+        // every split stores its partial; the CTA that arrives last sums them in split order
+        for (int r = 0; r < R; ++r) {
+          float* p = a.partial + ((((int64_t)tile * a.splits + split) * R + r) * BM + rowin) * MPAD;
+#pragma unroll
+          for (int m = 0; m < MPAD; m += 4)
+            __stcg(reinterpret_cast<float4*>(p + m),
+                   make_float4(accv[r][m], accv[r][m + 1], accv[r][m + 2], accv[r][m + 3]));
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          const int old = atomicAdd(a.counters + tile, 1);
+          *last_s = (old == a.splits - 1) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        finalize = (*last_s != 0);
+        named_bar_sync(1, 128);  // every thread has read last_s before a later unit rewrites it
+        if (finalize) {
+          __threadfence();
+          for (int r = 0; r < R; ++r) {
+#pragma unroll
+            for (int m = 0; m < MPAD; ++m) accv[r][m] = 0.0f;
+#pragma unroll 4
+            for (int sp = 0; sp < a.splits; ++sp) {
+              const float* p = a.partial + ((((int64_t)tile * a.splits + sp) * R + r) * BM + rowin) * MPAD;
+#pragma unroll
+              for (int m = 0; m < MPAD; m += 4) {
+                const float4 t = __ldcg(reinterpret_cast<const float4*>(p + m));
+                accv[r][m] += t.x;
+                accv[r][m + 1] += t.y;
+                accv[r][m + 2] += t.z;
+                accv[r][m + 3] += t.w;
+              }
+            }
+          }
+          if (et == 0) a.counters[tile] = 0;  // re-arm for the next launch
+        }
+      }
+      if (finalize) {
+        const EpiArgs& e = a.epi;
+        const int col = tile * BM + rowin;  // output column (shard-relative)
+        if (col < e.n_out) {
+#pragma unroll
+          for (int m = 0; m < MPAD; ++m) {
+            if (m >= e.m_valid) break;
+            const int64_t idx = (int64_t)m * e.ldy + e.col_off + col;
+            float* yp = e.Y + idx;
+            float v;
+            if (R == 2) {
+              float gv = accv[0][m], uv = accv[R - 1][m];
+              if (e.bias_mode == 1) {
+                gv = __fadd_rn(gv, __ldg(e.bias + col));
+                uv = __fadd_rn(uv, __ldg(e.bias + e.half_n + col));
+              }
+              v = __fmul_rn(silu_f(gv), uv);
+            } else {
+              v = epi_value(e, accv[0][m], m, col, yp);
+            }
+            out_store1(e, idx, v);
+          }
+        }
+        if (e.nremote != 0) __threadfence_system();
+      }
+    }
+    tc_fence_before();
+  }
+  __syncwarp();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // k_gemv: linears with M <= 8 on CUDA cores.  X stays fp32 (products are exact fp32 x bf16, sums
 // in fp32, as in the reference), so no activation cast runs.  Each warp streams 8 rows of W with
 // 16-byte loads (one load instruction = 512 contiguous bytes of a row) and keeps the 8 x M dot

@@ -601,3 +601,40 @@ def test_linear_batch_groups_skinny_linears(gpu):
         np.testing.assert_array_equal(got[k], v.cpu().numpy(), err_msg=k)
     ref = O.linear_bf16(x4.cpu().numpy(), ws["q"], b.cpu().numpy(), path=O.PATH_SCALAR)
     assert_parity(got["q"], ref, tol_max=1e-5, tol_mean=5e-6, what="grouped gemv q")
+
+
+@pytest.mark.parametrize("M", [16, 48])
+def test_linear_batch_groups_skinny_tcgen05_linears(gpu, M):
+    """8 < M <= 64: consecutive independent linears of a batch share one persistent k2_set launch
+    (with a chained one after its producer's group); bit-identical to separate envg_linear calls,
+    and within the GEMM bound of the reference."""
+    import torch
+
+    dev = "cuda"
+    rng = np.random.default_rng(M)
+    H, F = 2560, 1536
+
+    def wt(n, k, seed):
+        return O.f32_to_bf16_rne((0.02 * np.random.default_rng(seed).standard_normal((n, k))).astype(np.float32))
+
+    ws = {"q": wt(4096, H, 1), "k": wt(1024, H, 2), "gu": wt(2 * F, H, 3), "d": wt(H, F, 4), "o": wt(H, 4096, 5)}
+    W = {k: gpu.Weight(v, layout=gpu.LAYOUT_GATE_UP if k == "gu" else gpu.LAYOUT_PLAIN) for k, v in ws.items()}
+    x = torch.from_numpy(rng.standard_normal((M, H), dtype=np.float32)).to(dev)
+    x2 = torch.from_numpy(rng.standard_normal((M, 4096), dtype=np.float32)).to(dev)
+    b = torch.from_numpy((0.01 * rng.standard_normal(4096)).astype(np.float32)).to(dev)
+    outs = {"q": torch.empty(M, 4096, device=dev), "k": torch.empty(M, 1024, device=dev),
+            "gu": torch.empty(M, F, device=dev), "d": torch.empty(M, H, device=dev), "o": torch.empty(M, H, device=dev)}
+    calls = [dict(dst=outs["q"], x=x, W=W["q"], bias=b), dict(dst=outs["k"], x=x, W=W["k"]),
+             dict(dst=outs["gu"], x=x, W=W["gu"]), dict(dst=outs["d"], x=outs["gu"], W=W["d"]),
+             dict(dst=outs["o"], x=x2, W=W["o"])]
+    gpu.linear_batch(calls)
+    torch.cuda.synchronize()
+    got = {k: v.cpu().numpy() for k, v in outs.items()}
+    for c in calls:
+        gpu.linear(c["dst"], c["x"], c["W"], bias=c.get("bias"))
+    torch.cuda.synchronize()
+    for k, v in outs.items():
+        np.testing.assert_array_equal(got[k], v.cpu().numpy(), err_msg=k)
+    assert_parity(got["q"], O.linear_bf16(x.cpu().numpy(), ws["q"], b.cpu().numpy(), path=O.PATH_AVX2),
+                  what=f"grouped k2 q M={M}")
+    assert_parity(got["o"], O.linear_bf16(x2.cpu().numpy(), ws["o"], None, path=O.PATH_AVX2), what=f"grouped k2 o M={M}")
