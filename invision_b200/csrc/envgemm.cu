@@ -528,6 +528,7 @@ void k2_plan(const Dev* d, int64_t rows_b, int64_t Kp, bool gu, SkinnyArgs& s) {
   s.n_tiles = (int)cdiv(rows_b, (int64_t)R * BM);
   s.num_kb = (int)num_kb;
   int splits = std::max(1, d->sms / s.n_tiles);
+  if (splits == 1 && s.n_tiles < d->sms) splits = 2;  // fewer tiles than SMs: do not leave half idle
   splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, num_kb / 8));
   s.kb_per_split = (int)cdiv(num_kb, splits);
   s.splits = (int)cdiv(num_kb, s.kb_per_split);
