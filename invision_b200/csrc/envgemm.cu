@@ -752,10 +752,18 @@ int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t 
 // fp32 [batch][R][C] -> bf16 [batch][C][Rp]
 int launch_transpose_cast(Dev* d, const float* src, int64_t lds, int64_t sbs, int R, int C, void* dst, int64_t ldd,
                           int64_t dbs, int Rp, int batch, const float2* aff = nullptr, int act = 0) {
-  dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(Rp, 64), (unsigned)batch);
   ProfScope ps(stream_of(d), KID_TRANSPOSE, 0.0, (double)batch * ((double)R * C * 4 + (double)C * Rp * 2));
-  k_transpose_cast<<<grid, 256, 0, stream_of(d)>>>(src, lds, sbs, R, C, reinterpret_cast<__nv_bfloat16*>(dst), ldd,
-                                                   dbs, Rp, aff, act);
+  const bool vec = C % 4 == 0 && lds % 4 == 0 && sbs % 4 == 0 && Rp % 8 == 0 && ldd % 8 == 0 && dbs % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+  if (vec) {
+    dim3 grid((unsigned)cdiv(C, 64), (unsigned)cdiv(Rp, 64), (unsigned)batch);
+    k_transpose_cast_v<<<grid, 256, 0, stream_of(d)>>>(src, lds, sbs, R, C, reinterpret_cast<__nv_bfloat16*>(dst),
+                                                       ldd, dbs, Rp, aff, act);
+  } else {
+    dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(Rp, 64), (unsigned)batch);
+    k_transpose_cast<<<grid, 256, 0, stream_of(d)>>>(src, lds, sbs, R, C, reinterpret_cast<__nv_bfloat16*>(dst), ldd,
+                                                     dbs, Rp, aff, act);
+  }
   ENVG_CUDA(cudaGetLastError());
   d->st.kernel_launches++;
   return ENVG_OK;
@@ -1590,6 +1598,8 @@ int launch_group_affine(Dev* d, const float* src, int batch, int C, int64_t HW, 
                         const float* beta, float2** aff_out) {
   cudaStream_t s = stream_of(d);
   const int cpg = C / groups, chunks = gn_chunks(C, HW, groups);
+  // d->gn: [0, 256) the finished-CTA counter (always at offset 0: zeroed when the buffer is
+  // allocated, re-armed by every launch), then the chunk partials, then the affine
   double* part = reinterpret_cast<double*>(d->gn.p);
   float2* aff = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(d->gn.p) +
                                           rup((int64_t)batch * groups * chunks * 24, 256));
@@ -1601,6 +1611,7 @@ int launch_group_affine(Dev* d, const float* src, int batch, int C, int64_t HW, 
     d->st.kernel_launches++;
   }
   {
+    // one warp per group, all groups in parallel (a single finishing CTA doing them all is slower)
     ProfScope ps(s, KID_GN_AFFINE, 0.0, 24.0 * batch * groups * chunks + 8.0 * C + 8.0 * batch * C);
     k_group_affine<<<(unsigned)cdiv((int64_t)batch * groups * 32, 256), 256, 0, s>>>(part, chunks, batch, C, cpg,
                                                                                      groups, gamma, beta, GN_EPS, aff);
@@ -2025,7 +2036,7 @@ int envg_group_norm(float* dst, const float* src, const float* gamma, const floa
   const int64_t HW = (int64_t)H * W_, elems = (int64_t)batch * channels * HW;
   const float* dsrc = src;
   float* dy = dst;
-  ENVG_TRY(ensure(d, d->gn, gn_bytes(batch, channels, HW, num_groups)));
+  ENVG_TRY(ensure(d, d->gn, gn_bytes(batch, channels, HW, num_groups), true));
   if (!devp) {
     ENVG_TRY(ensure(d, d->x, (size_t)elems * 4));
     ENVG_TRY(ensure(d, d->vec, (size_t)2 * rup((int64_t)channels * 4, 256)));
@@ -2087,7 +2098,7 @@ int envg_vae_resblock(float* dst, const float* src, const envg_resblock* rb, int
   const int64_t HW = (int64_t)H * W_;
   const int64_t in_elems = (int64_t)batch * Ci * HW, out_elems = (int64_t)batch * Co * HW;
   const int Cp = (int)std::max(rb->conv1->Cp, rb->conv2->Cp);
-  ENVG_TRY(ensure(d, d->gn, std::max(gn_bytes(batch, Ci, HW, num_groups), gn_bytes(batch, Co, HW, num_groups))));
+  ENVG_TRY(ensure(d, d->gn, std::max(gn_bytes(batch, Ci, HW, num_groups), gn_bytes(batch, Co, HW, num_groups)), true));
   ENVG_TRY(ensure(d, d->act, (size_t)batch * HW * Cp * 2));
   ENVG_TRY(ensure(d, d->c1, (size_t)out_elems * 4));
   const float* dsrc = src;

@@ -1818,6 +1818,66 @@ __global__ void __launch_bounds__(256) k_transpose_cast(const float* __restrict_
   }
 }
 
+// The same transpose for aligned operands (C % 4 == 0, lds % 4 == 0, Rp % 8 == 0, ldd % 8 == 0,
+// 16-byte aligned bases and batch strides): a 64 x 64 tile per CTA, 16-byte loads of 4 floats
+// along C and 16-byte stores of 8 bf16 along R.
+__global__ void __launch_bounds__(256) k_transpose_cast_v(const float* __restrict__ src, int64_t lds, int64_t sbs,
+                                                          int R, int C, __nv_bfloat16* __restrict__ dst, int64_t ldd,
+                                                          int64_t dbs, int Rp, const float2* __restrict__ aff, int act) {
+  __shared__ float t[64][65];
+  const int c0 = blockIdx.x * 64;
+  const int r0 = blockIdx.y * 64;
+  const int b = blockIdx.z;
+  const float* s = src + (int64_t)b * sbs;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int idx = threadIdx.x + 256 * i;
+    const int rr = idx >> 4, c4 = (idx & 15) * 4;
+    const int r = r0 + rr, c = c0 + c4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < R && c < C) {
+      v = __ldcs(reinterpret_cast<const float4*>(s + (int64_t)r * lds + c));
+      if (aff) {
+        const float2 a = __ldg(aff + (int64_t)b * R + r);
+        v.x = __fmaf_rn(v.x, a.x, a.y);
+        v.y = __fmaf_rn(v.y, a.x, a.y);
+        v.z = __fmaf_rn(v.z, a.x, a.y);
+        v.w = __fmaf_rn(v.w, a.x, a.y);
+      }
+      if (act) {
+        v.x = silu_f(v.x);
+        v.y = silu_f(v.y);
+        v.z = silu_f(v.z);
+        v.w = silu_f(v.w);
+      }
+    }
+    t[rr][c4] = v.x;
+    t[rr][c4 + 1] = v.y;
+    t[rr][c4 + 2] = v.z;
+    t[rr][c4 + 3] = v.w;
+  }
+  __syncthreads();
+  __nv_bfloat16* d = dst + (int64_t)b * dbs;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int idx = threadIdx.x + 256 * i;
+    const int px = idx >> 3, ch = (idx & 7) * 8;
+    const int c = c0 + px, r = r0 + ch;
+    if (c < C && r < Rp) {
+      uint4 o;
+      __nv_bfloat162 h0 = __float22bfloat162_rn(make_float2(t[ch][px], t[ch + 1][px]));
+      __nv_bfloat162 h1 = __float22bfloat162_rn(make_float2(t[ch + 2][px], t[ch + 3][px]));
+      __nv_bfloat162 h2 = __float22bfloat162_rn(make_float2(t[ch + 4][px], t[ch + 5][px]));
+      __nv_bfloat162 h3 = __float22bfloat162_rn(make_float2(t[ch + 6][px], t[ch + 7][px]));
+      o.x = *reinterpret_cast<uint32_t*>(&h0);
+      o.y = *reinterpret_cast<uint32_t*>(&h1);
+      o.z = *reinterpret_cast<uint32_t*>(&h2);
+      o.w = *reinterpret_cast<uint32_t*>(&h3);
+      *reinterpret_cast<uint4*>(d + (int64_t)c * ldd + r) = o;
+    }
+  }
+}
+
 // Explicit im2col for strided convolutions: NHWC bf16 [B][H][W][Cp] -> col bf16
 // [B][outH*outW][KH*KW*Cp] in (kh, kw, c) order, zeros outside the image.  8 channels/thread.
 __global__ void k_im2col_nhwc(const __nv_bfloat16* __restrict__ in, int B, int H, int W, int Cp, int KH, int KW,
@@ -1927,8 +1987,8 @@ ENVG_DEV double block_sum256_d(double v, double* red) {
   return red[8];
 }
 
-__global__ void __launch_bounds__(GN_THREADS) k_group_stats(const float* __restrict__ X, int C, int64_t HW, int cpg,
-                                                            int groups, double* __restrict__ part, int chunks) {
+ENVG_DEV void group_stats_block(const float* __restrict__ X, int C, int64_t HW, int cpg, int groups,
+                                double* __restrict__ part, int chunks) {
   __shared__ double red[9];
   const int bg = blockIdx.y;
   const int b = bg / groups, g = bg - b * groups;
@@ -1979,6 +2039,11 @@ __global__ void __launch_bounds__(GN_THREADS) k_group_stats(const float* __restr
   }
 }
 
+__global__ void __launch_bounds__(GN_THREADS) k_group_stats(const float* __restrict__ X, int C, int64_t HW, int cpg,
+                                                            int groups, double* __restrict__ part, int chunks) {
+  group_stats_block(X, C, HW, cpg, groups, part, chunks);
+}
+
 // Chan et al.'s pairwise update: (n, mean, m2) <- (n, mean, m2) merged with (nb, mb, qb).
 ENVG_DEV void chan_merge(double& n, double& mean, double& m2, double nb, double mb, double qb) {
   if (nb == 0.0) return;
@@ -1992,15 +2057,11 @@ ENVG_DEV void chan_merge(double& n, double& mean, double& m2, double nb, double 
   n = nn;
 }
 
-// One warp per (b, g): lane l merges chunks l, l + 32, ... in order, then a fixed shuffle tree
-// merges the lanes (deterministic); the warp writes the group's per-channel affine.
-__global__ void __launch_bounds__(256) k_group_affine(const double* __restrict__ part, int chunks, int batch, int C,
-                                                      int cpg, int groups, const float* __restrict__ gamma,
-                                                      const float* __restrict__ beta, float eps,
-                                                      float2* __restrict__ aff) {
-  const int wid = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
-  if (wid >= batch * groups) return;
+// Group wid = (b, g) by one warp: lane l merges chunks l, l + 32, ... in order, then a fixed
+// shuffle tree merges the lanes (deterministic); the warp writes the group's per-channel affine.
+ENVG_DEV void group_affine_warp(int wid, int lane, const double* __restrict__ part, int chunks, int C, int cpg,
+                                int groups, const float* __restrict__ gamma, const float* __restrict__ beta,
+                                float eps, float2* __restrict__ aff) {
   const int b = wid / groups, g = wid - b * groups;
   const double* p = part + (int64_t)wid * chunks * 3;
   double n = 0.0, mean = 0.0, m2 = 0.0;
@@ -2024,6 +2085,15 @@ __global__ void __launch_bounds__(256) k_group_affine(const double* __restrict__
     const float a = __fmul_rn(ga, std_inv);
     aff[(int64_t)b * C + c] = make_float2(a, __fsub_rn(be, __fmul_rn(__fmul_rn(mf, ga), std_inv)));
   }
+}
+
+__global__ void __launch_bounds__(256) k_group_affine(const double* __restrict__ part, int chunks, int batch, int C,
+                                                      int cpg, int groups, const float* __restrict__ gamma,
+                                                      const float* __restrict__ beta, float eps,
+                                                      float2* __restrict__ aff) {
+  const int wid = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  if (wid >= batch * groups) return;
+  group_affine_warp(wid, threadIdx.x & 31, part, chunks, C, cpg, groups, gamma, beta, eps, aff);
 }
 
 // dst[b][c][i] = act(src[b][c][i] * aff[b*C + c].x + aff[b*C + c].y), fp32 NCHW (in place allowed).
