@@ -734,29 +734,48 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
   }
 }
 
-// Max |x| per head of an fp32 [seq][ld] tensor (head h at column h * 128) into amax[h]
-// (atomicMax on the float bits; amax zeroed beforehand).  Grid (row blocks of 64, heads).
-__global__ void __launch_bounds__(256) k_absmax_heads(const float* __restrict__ X, int64_t ld, int seq,
-                                                      float* __restrict__ amax) {
+// Max |x| per head of the fp32 Q, K and V ([seq][ld], head h at column h * 128) into amax
+// (Q heads, then K heads, then V heads; atomicMax on the float bits, amax zeroed beforehand).
+// Grid (row blocks of 64, max(heads, kv_heads), 3): z picks the tensor; each warp reads whole
+// 512-byte head rows with 16-byte loads (scalar loads when a row is not 16-byte aligned).
+struct AbsmaxArgs {
+  const float* X[3];
+  int64_t ld[3];
+  int seq[3];
+  int heads[3];
+  int base[3];  // first amax slot of each tensor
+  int vec[3];
+};
+
+__global__ void __launch_bounds__(256) k_absmax_heads(const AbsmaxArgs a, float* __restrict__ amax) {
   __shared__ float red[8];
-  const int h = blockIdx.y;
+  const int z = blockIdx.z, h = blockIdx.y;
+  if (h >= a.heads[z]) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* X = a.X[z] + (int64_t)h * FA_D;
   float m = 0.0f;
   const int r0 = blockIdx.x * 64;
-  for (int i = threadIdx.x; i < 64 * 32; i += 256) {
-    const int r = r0 + (i >> 5), c = (i & 31) * 4;
-    if (r < seq) {
-      const float* p = X + (int64_t)r * ld + (int64_t)h * FA_D + c;
+#pragma unroll 4
+  for (int rr = warp; rr < 64; rr += 8) {
+    const int r = r0 + rr;
+    if (r < a.seq[z]) {
+      const float* p = X + (int64_t)r * a.ld[z] + lane * 4;
+      if (a.vec[z]) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      } else {
 #pragma unroll
-      for (int t = 0; t < 4; ++t) m = fmaxf(m, fabsf(__ldg(p + t)));
+        for (int t = 0; t < 4; ++t) m = fmaxf(m, fabsf(__ldg(p + t)));
+      }
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  if (lane == 0) red[warp] = m;
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
-    atomicMax(reinterpret_cast<unsigned int*>(amax + h), __float_as_uint(m));  // NaN sorts above inf
+    atomicMax(reinterpret_cast<unsigned int*>(amax + a.base[z] + h), __float_as_uint(m));  // NaN sorts above inf
   }
 }
 

@@ -2214,14 +2214,24 @@ int envg_attention(float* dst, const float* Q, const float* K, const float* V, i
   {
     ENVG_CUDA(cudaMemsetAsync(amax, 0, nmax * 4, s));
     ProfScope ps(s, KID_ABSMAX, 0.0, 4.0 * ((double)seq_q * wq + 2.0 * seq_k * wk));
-    k_absmax_heads<<<dim3((unsigned)cdiv(seq_q, 64), (unsigned)heads), 256, 0, s>>>(dq, lq, seq_q, amax);
+    AbsmaxArgs am{};
+    const float* xs[3] = {dq, dk, dv};
+    const int64_t lds[3] = {lq, lkk, lv};
+    const int seqs[3] = {seq_q, seq_k, seq_k};
+    const int hs[3] = {heads, kv_heads, kv_heads};
+    const int bases[3] = {0, heads, heads + kv_heads};
+    for (int z = 0; z < 3; ++z) {
+      am.X[z] = xs[z];
+      am.ld[z] = lds[z];
+      am.seq[z] = seqs[z];
+      am.heads[z] = hs[z];
+      am.base[z] = bases[z];
+      am.vec[z] = (lds[z] % 4 == 0 && (reinterpret_cast<uintptr_t>(xs[z]) & 15) == 0) ? 1 : 0;
+    }
+    k_absmax_heads<<<dim3((unsigned)cdiv(std::max(seq_q, seq_k), 64), (unsigned)std::max(heads, kv_heads), 3), 256, 0,
+                     s>>>(am, amax);
     ENVG_CUDA(cudaGetLastError());
-    k_absmax_heads<<<dim3((unsigned)cdiv(seq_k, 64), (unsigned)kv_heads), 256, 0, s>>>(dk, lkk, seq_k, amax + heads);
-    ENVG_CUDA(cudaGetLastError());
-    k_absmax_heads<<<dim3((unsigned)cdiv(seq_k, 64), (unsigned)kv_heads), 256, 0, s>>>(dv, lv, seq_k,
-                                                                                       amax + heads + kv_heads);
-    ENVG_CUDA(cudaGetLastError());
-    d->st.kernel_launches += 3;
+    d->st.kernel_launches += 1;
   }
   {
     const bool vq = (lq % 4 == 0) && ((reinterpret_cast<uintptr_t>(dq) & 15) == 0);
