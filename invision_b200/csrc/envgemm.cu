@@ -84,6 +84,8 @@ struct Dev {
   Buf gn, c1, vec;  // GroupNorm statistics + affine, ResBlock conv1 output, small parameter vectors
   Buf fa, fain;     // attention operands (bf16 Q / K / V^T + key bits), host-call staging
   cudaStream_t aux = nullptr;              // second stream of envg_linear_batch
+  cudaStream_t h2d = nullptr, d2h = nullptr;  // copy streams of pipelined host-pointer calls
+  std::vector<cudaEvent_t> pipe_events;    // reused event pool of the pipelined host calls
   std::vector<cudaEvent_t> batch_events;   // reused event pool of envg_linear_batch
   int* h_status = nullptr;  // mapped pinned: [0] status code, [1] wait site
   int* d_status = nullptr;
@@ -93,6 +95,7 @@ struct Dev {
   bool use_pair = true;  // 256x256 CTA-pair tiles for M > 128 (ENVG_K1=single selects k1_gemm)
   int max_pairs = 0;     // co-resident CTA pairs of k1_gemm_pair
   bool store_tma = true;  // TMA bulk-store epilogue; ENVG_STORE=coalesced selects warp-coalesced stores
+  bool pipe_host = true;  // pipeline large host-pointer linears in row chunks (ENVG_PIPE=0 disables)
   int attn_tiles = 0;     // query tiles per attention CTA: 0 = by grid size, ENVG_ATTN_TILES=1|2 forces
   envg_stats st{};
   size_t ws_bytes() const {
@@ -1045,6 +1048,7 @@ int envg_init(int ndev, const int* dev_ids) {
   }
   if (const char* s = getenv("ENVG_K1")) d->use_pair = strcmp(s, "single") != 0;
   if (const char* s = getenv("ENVG_STORE")) d->store_tma = strcmp(s, "coalesced") != 0;
+  if (const char* s = getenv("ENVG_PIPE")) d->pipe_host = strcmp(s, "0") != 0;
   if (const char* s = getenv("ENVG_ATTN_TILES")) {
     const int v = atoi(s);
     if (v == 1 || v == 2) d->attn_tiles = v;
@@ -1077,6 +1081,11 @@ int envg_shutdown(void) {
   }
   if (d->own) cudaStreamDestroy(d->own);
   if (d->aux) cudaStreamDestroy(d->aux);
+  if (d->h2d) cudaStreamDestroy(d->h2d);
+  if (d->d2h) cudaStreamDestroy(d->d2h);
+  d->h2d = d->d2h = nullptr;
+  for (cudaEvent_t e : d->pipe_events) cudaEventDestroy(e);
+  d->pipe_events.clear();
   for (cudaEvent_t e : d->batch_events) cudaEventDestroy(e);
   d->batch_events.clear();
   d->aux = nullptr;
@@ -1235,6 +1244,113 @@ int envg_weight_upload_safetensors(const char* path, const char* name, int layou
 }  // extern "C"
 
 namespace {
+constexpr int64_t PIPE_MIN_M = 1024;   // host calls from this many rows are pipelined
+constexpr int64_t PIPE_CHUNK = 1024;   // rows per chunk (a multiple of the 256-row pair tile)
+
+cudaEvent_t pipe_event(Dev* d, size_t i) {
+  while (d->pipe_events.size() <= i) {
+    cudaEvent_t e = nullptr;
+    cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    d->pipe_events.push_back(e);
+  }
+  return d->pipe_events[i];
+}
+
+// Host-pointer linear with M >= PIPE_MIN_M, cut into row chunks: the copy-in of chunk c + 1 (on
+// d->h2d), the cast + GEMM of chunk c (on the compute stream) and the copy-out of chunk c - 1
+// (on d->d2h) overlap, so PCIe moves X and Y in both directions at once while the GPU computes.
+// Rows are independent, so every output is computed exactly as in one launch.  Synchronous.
+int linear_host_pipelined(Dev* d, float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K,
+                          int64_t N, int epilogue, const float* gate, const float* ad_shift, const float* ad_scale) {
+  const bool gu = W->layout == ENVG_LAYOUT_GATE_UP;
+  const int64_t n_out = gu ? N / 2 : N;
+  cudaStream_t s = stream_of(d);
+  if (!d->h2d) ENVG_CUDA(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
+  if (!d->d2h) ENVG_CUDA(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
+  ENVG_TRY(ensure(d, d->x, (size_t)(M * K) * 4));
+  ENVG_TRY(ensure(d, d->y, (size_t)(M * n_out) * 4));
+  ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
+  float* dx = reinterpret_cast<float*>(d->x.p);
+  float* dy = reinterpret_cast<float*>(d->y.p);
+  // small vectors first, on the compute stream
+  const float *dbias = nullptr, *dgate = nullptr, *dshift = nullptr, *dscale = nullptr;
+  if (bias) {
+    ENVG_TRY(ensure(d, d->bias, (size_t)N * 4));
+    ENVG_CUDA(cudaMemcpyAsync(d->bias.p, bias, (size_t)N * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)N * 4;
+    dbias = reinterpret_cast<float*>(d->bias.p);
+  }
+  if (epilogue == ENVG_EPI_GATED_RESIDUAL) {
+    ENVG_TRY(ensure(d, d->gate, (size_t)N * 4));
+    ENVG_CUDA(cudaMemcpyAsync(d->gate.p, gate, (size_t)N * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)N * 4;
+    dgate = reinterpret_cast<float*>(d->gate.p);
+  }
+  if (ad_shift) {
+    ENVG_TRY(ensure(d, d->ada, (size_t)(2 * K) * 4));
+    float* a = reinterpret_cast<float*>(d->ada.p);
+    ENVG_CUDA(cudaMemcpyAsync(a, ad_shift, (size_t)K * 4, cudaMemcpyHostToDevice, s));
+    ENVG_CUDA(cudaMemcpyAsync(a + K, ad_scale, (size_t)K * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)(2 * K) * 4;
+    dshift = a;
+    dscale = a + K;
+  }
+  // chunks of PIPE_CHUNK rows, the remainder joining the last one: every chunk keeps at least
+  // PIPE_CHUNK rows, so it runs the same kernel (and sums in the same order) as one launch would
+  const int64_t nch = std::max<int64_t>(1, M / PIPE_CHUNK);
+  auto chunk = [&](int64_t c, int64_t& r0, int64_t& rows) {
+    r0 = c * PIPE_CHUNK;
+    rows = (c == nch - 1) ? M - r0 : PIPE_CHUNK;
+  };
+  // event 0: the small vectors are queued on s (the copy streams start after them)
+  ENVG_CUDA(cudaEventRecord(pipe_event(d, 0), s));
+  ENVG_CUDA(cudaStreamWaitEvent(d->h2d, pipe_event(d, 0), 0));
+  for (int64_t c = 0; c < nch; ++c) {
+    int64_t r0, rows;
+    chunk(c, r0, rows);
+    ENVG_CUDA(cudaMemcpyAsync(dx + r0 * K, x + r0 * K, (size_t)(rows * K) * 4, cudaMemcpyHostToDevice, d->h2d));
+    d->st.h2d_bytes += (double)(rows * K) * 4;
+    if (epilogue == ENVG_EPI_GATED_RESIDUAL) {
+      ENVG_CUDA(cudaMemcpyAsync(dy + r0 * n_out, dst + r0 * n_out, (size_t)(rows * n_out) * 4,
+                                cudaMemcpyHostToDevice, d->h2d));
+      d->st.h2d_bytes += (double)(rows * n_out) * 4;
+    }
+    ENVG_CUDA(cudaEventRecord(pipe_event(d, 1 + 2 * c), d->h2d));  // chunk c is on the device
+  }
+  for (int64_t c = 0; c < nch; ++c) {
+    int64_t r0, rows;
+    chunk(c, r0, rows);
+    ENVG_CUDA(cudaStreamWaitEvent(s, pipe_event(d, 1 + 2 * c), 0));
+    void* xb = reinterpret_cast<uint8_t*>(d->xb.p) + (size_t)(r0 * W->Kp) * 2;
+    if (dshift) ENVG_TRY(launch_adaln(d, dx + r0 * K, rows, K, W->Kp, dshift, dscale, xb, true));
+    else ENVG_TRY(launch_cast_rows(d, dx + r0 * K, K, rows, K, W->Kp, xb));
+    EpiArgs e{};
+    e.Y = dy + r0 * n_out;
+    e.ldy = n_out;
+    e.bias = dbias;
+    e.bias_mode = dbias ? 1 : 0;
+    e.mode = (epilogue == ENVG_EPI_GATED_RESIDUAL) ? EPI_GATED_RES : EPI_PLAIN;
+    e.gate = dgate;
+    e.alpha = 1.0f;
+    e.n_out = (int)n_out;
+    e.m_valid = (int)rows;
+    e.half_n = (int)(gu ? W->half : 0);
+    e.vec_ok = ((reinterpret_cast<uintptr_t>(e.Y) & 15) == 0 && n_out % 4 == 0) ? 1 : 0;
+    const double fl = 2.0 * (double)rows * (double)N * (double)K;
+    ENVG_TRY(gemm_device(d, xb, rows, W->Kp, W->tm256, W->tm128, W->rows, gu, e, fl,
+                         2.0 * (double)N * K + 2.0 * (double)rows * W->Kp + 4.0 * (double)rows * n_out));
+    ENVG_CUDA(cudaEventRecord(pipe_event(d, 2 + 2 * c), s));  // chunk c of Y is done
+    ENVG_CUDA(cudaStreamWaitEvent(d->d2h, pipe_event(d, 2 + 2 * c), 0));
+    ENVG_CUDA(cudaMemcpyAsync(dst + r0 * n_out, dy + r0 * n_out, (size_t)(rows * n_out) * 4, cudaMemcpyDeviceToHost,
+                              d->d2h));
+    d->st.d2h_bytes += (double)(rows * n_out) * 4;
+  }
+  d->st.calls++;
+  d->st.flops += 2.0 * (double)M * (double)N * (double)K;
+  ENVG_CUDA(cudaStreamSynchronize(d->d2h));
+  return sync_and_check(d);
+}
+
 // envg_linear and envg_linear_adaln.  With ad_shift / ad_scale set, X is first normalised per row
 // and modulated (QNNAdaLN) inside the activation-cast kernel.
 int linear_core(Dev* d, float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,
@@ -1263,6 +1379,8 @@ int linear_core(Dev* d, float* dst, const float* x, envg_weight W, const float* 
   const bool devp = (flags & ENVG_DEVICE_PTRS) != 0;
   const int64_t n_out = gu ? N / 2 : N;
   cudaStream_t s = stream_of(d);
+  if (!devp && M >= PIPE_MIN_M && d->pipe_host)
+    return linear_host_pipelined(d, dst, x, W, bias, M, K, N, epilogue, gate, ad_shift, ad_scale);
 
   const float *dx = x, *dbias = bias, *dgate = gate, *dshift = ad_shift, *dscale = ad_scale;
   float* dy = dst;
