@@ -11,9 +11,16 @@
 //   QNNMatMulNT(C, A, B, M, K, N)                           quicknn_kernels.pas:847-861
 //   QNNConv2d(dst, src, weights, bias, in_ch, out_ch, H, W, kH, kW, stride, padding, batch)
 //                                                           quicknn_kernels.pas:990-1010
-// plus the fused forms of the two element-wise ops that follow a linear in the model:
+// plus the fused forms of the element-wise ops around a linear in the model, and the other
+// compute-heavy neighbours of the path:
 //   QNNLinearSiluMul   = linear into [gate | up] then QNNSiluMul (quicknncpu.pas:2404-2419)
 //   QNNLinearGatedAdd  = linear then QNNGatedAdd (quicknncpu.pas:853-859)
+//   QNNAdaLNLinear     = QNNAdaLN then a linear (quicknncpu.pas:3042-3060)
+//   QNNGroupNorm(dst, src, gamma, beta, batch, channels, H, W, num_groups)
+//                                                           quicknncpu.pas:2259-2313
+//   QNNFlashAttention(dst, Q, K, V, heads, seq_q, seq_k, head_dim, scale)
+//                                                           quicknncpu.pas:2763-2860
+//   QNNResBlock::forward(dst, src, batch, H, W, num_groups) quicknn_vae.pas:164-187
 // The weight argument is a device-resident QNNWeight in place of the reference's fp32/bf16
 // TMemoryBlock.  Where the reference asserts (e.g. quicknn_kernels.pas:484-486), these functions
 // throw std::runtime_error carrying the library's message; host pointers are used throughout,
@@ -166,6 +173,63 @@ inline void QNNConv2d(float* dst, const float* src, const QNNWeight& weights, co
                     bias ? ENVG_EPI_BIAS : ENVG_EPI_NONE, ENVG_HOST_PTRS),
         "[Conv2D]");
 }
+
+// QNNAdaLN(xn, x, shift, scale, seqLen, inDIM) followed by QNNLinear(dst, xn, W, B, ...)
+// (quicknncpu.pas:3042-3060; quicknn_transformers.pas:1400-1456): the normalisation runs inside
+// the activation cast.
+inline void QNNAdaLNLinear(float* dst, const float* x, const float* shift, const float* scale, const QNNWeight& W,
+                           const float* B, int seqLen, int inDIM, int outDIM) {
+  check(envg_linear_adaln(dst, x, shift, scale, W.handle(), B, seqLen, inDIM, outDIM,
+                          W.layout() == ENVG_LAYOUT_GATE_UP ? ENVG_EPI_SILU_GATE : (B ? ENVG_EPI_BIAS : ENVG_EPI_NONE),
+                          nullptr, ENVG_HOST_PTRS),
+        "QNNAdaLNLinear");
+}
+
+// QNNGroupNorm(dst, src, gamma, beta, batch, channels, H, W, num_groups) (quicknncpu.pas:2259-2313).
+inline void QNNGroupNorm(float* dst, const float* src, const float* gamma, const float* beta, int batch,
+                         int channels, int H, int W, int num_groups) {
+  if (num_groups <= 0 || channels % num_groups)
+    throw std::runtime_error("ERROR [GroupNorm] : channels not divisible by groups");
+  check(envg_group_norm(dst, src, gamma, beta, batch, channels, H, W, num_groups, 0, ENVG_HOST_PTRS), "[GroupNorm]");
+}
+
+// QNNFlashAttention(dst, Q, K, V, heads, seq_q, seq_k, head_dim, scale) (quicknncpu.pas:2763-2860):
+// Q/K/V/dst [seq, heads * head_dim], head h at column h * head_dim.  head_dim 128.
+inline void QNNFlashAttention(float* dst, const float* Q, const float* K, const float* V, int heads, int seq_q,
+                              int seq_k, int head_dim, float scale) {
+  const int64_t hid = (int64_t)heads * head_dim;
+  check(envg_attention(dst, Q, K, V, seq_q, seq_k, heads, heads, head_dim, hid, hid, hid, hid, scale, 0, nullptr,
+                       ENVG_HOST_PTRS),
+        "[FlashAttention]");
+}
+
+// One VAE ResBlock (TVAEResBlock.forward, quicknn_vae.pas:164-187) with its conv weights on the
+// device; the vectors stay host pointers.
+struct QNNResBlock {
+  int in_ch = 0, out_ch = 0;
+  const float *norm1_gamma = nullptr, *norm1_beta = nullptr, *conv1_bias = nullptr;
+  const float *norm2_gamma = nullptr, *norm2_beta = nullptr, *conv2_bias = nullptr, *skip_bias = nullptr;
+  const QNNWeight* conv1 = nullptr;
+  const QNNWeight* conv2 = nullptr;
+  const QNNWeight* skip = nullptr;  // nullptr when in_ch == out_ch
+
+  void forward(float* dst, const float* src, int batch, int H, int W, int num_groups) const {
+    envg_resblock rb{};
+    rb.in_ch = in_ch;
+    rb.out_ch = out_ch;
+    rb.norm1_gamma = norm1_gamma;
+    rb.norm1_beta = norm1_beta;
+    rb.conv1 = conv1 ? conv1->handle() : nullptr;
+    rb.conv1_bias = conv1_bias;
+    rb.norm2_gamma = norm2_gamma;
+    rb.norm2_beta = norm2_beta;
+    rb.conv2 = conv2 ? conv2->handle() : nullptr;
+    rb.conv2_bias = conv2_bias;
+    rb.skip = skip ? skip->handle() : nullptr;
+    rb.skip_bias = skip_bias;
+    check(envg_vae_resblock(dst, src, &rb, batch, H, W, num_groups, ENVG_HOST_PTRS), "[VAE ResBlock]");
+  }
+};
 
 }  // namespace quicknn_cuda
 
