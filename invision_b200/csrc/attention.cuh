@@ -747,7 +747,7 @@ struct AbsmaxArgs {
   int vec[3];
 };
 
-__global__ void __launch_bounds__(256) k_absmax_heads(const AbsmaxArgs a, float* __restrict__ amax) {
+__global__ void __launch_bounds__(256) k_absmax_heads(const __grid_constant__ AbsmaxArgs a, float* __restrict__ amax) {
   __shared__ float red[8];
   const int z = blockIdx.z, h = blockIdx.y;
   if (h >= a.heads[z]) return;

@@ -97,6 +97,7 @@ struct Dev {
   bool store_tma = true;  // TMA bulk-store epilogue; ENVG_STORE=coalesced selects warp-coalesced stores
   bool pipe_host = true;  // pipeline large host-pointer linears in row chunks (ENVG_PIPE=0 disables)
   int attn_tiles = 0;     // query tiles per attention CTA: 0 = by grid size, ENVG_ATTN_TILES=1|2 forces
+  int pair_split = -1;    // k1_gemm_pair split-K: -1 by cost model, 0 off, n forces n (ENVG_PAIR_SPLIT)
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
@@ -112,14 +113,15 @@ int g_cur = -1;
 // ---- optional per-launch timing (envg_profile) ---------------------------------------------
 enum KernelId {
   KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_ADALN, KID_TRANSPOSE, KID_IM2COL,
-  KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_ATTN, KID_CAST_HEADS, KID_KEY_BITS, KID_ABSMAX, KID_COUNT
+  KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_ATTN, KID_CAST_HEADS, KID_KEY_BITS, KID_ABSMAX,
+  KID_SPLIT_REDUCE, KID_COUNT
 };
 const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate", "k1_gemm_conv",
                                              "k2_skinny",   "k_gemv",            "k_cast_rows",
                                              "k_adaln",     "k_transpose_cast",  "k_im2col_nhwc",
                                              "k_wait_selftest", "k_group_stats",     "k_group_affine",
                                              "k_group_apply",   "k_attention",       "k_cast_heads",
-                                             "k_key_bits",      "k_absmax_heads"};
+                                             "k_key_bits",      "k_absmax_heads",    "k_split_reduce"};
 struct KAcc {
   uint64_t launches = 0;
   double ms = 0, flops = 0, bytes = 0;
@@ -243,11 +245,13 @@ int tmap_nhwc(CUtensorMap* tm, const void* base, int Cp, int W, int H, int B, in
   return ENVG_OK;
 }
 
-// fp32 output maps for the TMA-store epilogue: 32 x 32 boxes, 128-byte swizzle.
-int tmap_out_2d(CUtensorMap* tm, const float* base, uint64_t cols, uint64_t rows, uint64_t ld) {
+// fp32 output maps for the TMA-store epilogue: boxes of 32 columns x box_rows rows (one warp's
+// 32 rows, or a CTA's 128), 128-byte swizzle.
+int tmap_out_2d(CUtensorMap* tm, const float* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                uint32_t box_rows = 32) {
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {ld * 4};
-  cuuint32_t box[2] = {32, 32};
+  cuuint32_t box[2] = {32, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -255,10 +259,11 @@ int tmap_out_2d(CUtensorMap* tm, const float* base, uint64_t cols, uint64_t rows
   if (r != CUDA_SUCCESS) return fail(ENVG_ERR_CUDA, "cuTensorMapEncodeTiled(out 2D) failed: %d", (int)r);
   return ENVG_OK;
 }
-int tmap_out_3d(CUtensorMap* tm, const float* base, uint64_t plane, uint64_t ch, uint64_t nb) {
+int tmap_out_3d(CUtensorMap* tm, const float* base, uint64_t plane, uint64_t ch, uint64_t nb,
+                uint32_t box_rows = 32) {
   cuuint64_t dims[3] = {plane, ch, nb};
   cuuint64_t strides[2] = {plane * 4, ch * plane * 4};
-  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t box[3] = {32, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -269,7 +274,7 @@ int tmap_out_3d(CUtensorMap* tm, const float* base, uint64_t plane, uint64_t ch,
 
 // Picks the k1_gemm store path for a row-major Y (and builds its map for the TMA paths).  With
 // peer copies of Y (N-split) and `pm` given, the chunks go out as TMA bulk stores, one per copy.
-int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = nullptr) {
+int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = nullptr, GemmArgs* big = nullptr) {
   if (use_tma && pm && e.nremote > 0 && e.mode != EPI_ALPHA_BETA) {
     bool ok = e.ldy % 4 == 0 && e.col_off % 4 == 0;
     for (int r = 0; r < e.nremote; ++r) ok = ok && (reinterpret_cast<uintptr_t>(e.remote[r] + e.col_off) & 15) == 0;
@@ -297,6 +302,11 @@ int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = null
   if (mode == STORE_DIRECT) return ENVG_OK;
   int rc = tmap_out_2d(tmY, e.Y, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy);
   if (rc != ENVG_OK) return rc;
+  if (big) {  // k1_gemm_pair's last-unit stores (CTA-high boxes)
+    rc = tmap_out_2d(&big->ybig, e.Y, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy, 128);
+    if (rc != ENVG_OK) return rc;
+    big->ybig_ok = 1;
+  }
   e.store_mode = mode;
   return ENVG_OK;
 }
@@ -432,9 +442,10 @@ int launch_k1(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const CUtens
   return ENVG_OK;
 }
 
+// Dynamic shared memory attribute and the number of co-resident CTA pairs of one
+// k1_gemm_pair instance (queried once).
 template <bool CONV_B, bool SILU_GATE>
-int launch_k1_pair(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tY, GemmArgs& a,
-                   double flops, double bytes) {
+int k1_pair_capacity(Dev* d, int* pairs) {
   using L = KPairSmem<KPAIR_STAGES>;
   auto kern = k1_gemm_pair<KPAIR_STAGES, CONV_B, SILU_GATE>;
   static bool attr = false;
@@ -460,6 +471,17 @@ int launch_k1_pair(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const C
     max_pairs = n;
     attr = true;
   }
+  *pairs = max_pairs;
+  return ENVG_OK;
+}
+
+template <bool CONV_B, bool SILU_GATE>
+int launch_k1_pair(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tY, GemmArgs& a,
+                   double flops, double bytes) {
+  using L = KPairSmem<KPAIR_STAGES>;
+  auto kern = k1_gemm_pair<KPAIR_STAGES, CONV_B, SILU_GATE>;
+  int max_pairs = 0;
+  ENVG_TRY((k1_pair_capacity<CONV_B, SILU_GATE>(d, &max_pairs)));
   a.status = d->d_status;
   a.wait_cap_ns = d->wait_cap_ns;
   const int pairs = (int)std::min<int64_t>(a.num_tiles, max_pairs);
@@ -772,6 +794,69 @@ int launch_transpose_cast(Dev* d, const float* src, int64_t lds, int64_t sbs, in
   return ENVG_OK;
 }
 
+// ---- split-K for mid-size M ----------------------------------------------------------------
+// Below SPLIT_MAX_M rows a linear has at most four 256-row pair tiles in M, and a narrow N leaves
+// most CTA pairs idle (Qwen3's k / v at 512 tokens: 8 tiles for 74 pairs).  Such a launch cuts
+// K into `splits` contiguous ranges; every (split, tile) unit stores its raw fp32 tile, and
+// k_split_reduce adds the splits in split order and applies the epilogue.  The split count
+// depends only on (M, N, K) and the device, so repeated calls give identical results.  N-split
+// shards (outputs on several ranks) never split K.
+// SPLIT_MAX_M equals PIPE_MIN_M: the row chunks of a pipelined host call (>= PIPE_MIN_M rows
+// each) never split, so they sum in the same order as one launch over all rows.
+constexpr int64_t SPLIT_MAX_M = 1024;
+constexpr int SPLIT_MIN_KB = 4;        // K blocks per split at least
+constexpr int SPLIT_MAX = 16;
+constexpr double SPLIT_US_PER_KB = 0.42;  // one 64-deep K block of a 256 x 256 pair tile, measured
+constexpr double SPLIT_REDUCE_US = 3.0;   // launch and tail of k_split_reduce
+
+int pair_splits(Dev* d, int64_t M, int tiles, int num_kb, int64_t Mp, int64_t ldp, int* splits, int* kb_per) {
+  *splits = 1;
+  *kb_per = num_kb;
+  if (d->pair_split == 0 || M >= SPLIT_MAX_M || num_kb < 2) return ENVG_OK;
+  auto eff = [&](int sp, int* kbp) {
+    *kbp = (int)cdiv(num_kb, sp);
+    return (int)cdiv(num_kb, *kbp);
+  };
+  if (d->pair_split > 0) {  // forced count (tests and sweeps)
+    *splits = eff(std::min(d->pair_split, num_kb), kb_per);
+    return ENVG_OK;
+  }
+  if (num_kb < 2 * SPLIT_MIN_KB) return ENVG_OK;
+  int P = 0;
+  ENVG_TRY((k1_pair_capacity<false, false>(d, &P)));
+  int best = 1;
+  double best_us = (double)cdiv(tiles, P) * num_kb * SPLIT_US_PER_KB;
+  for (int sp = 2; sp <= SPLIT_MAX && sp * SPLIT_MIN_KB <= num_kb; ++sp) {
+    int kbp = 0;
+    const int se = eff(sp, &kbp);
+    const double part_bytes = 4.0 * (double)se * (double)Mp * (double)ldp;
+    const double us = (double)cdiv((int64_t)tiles * se, P) * kbp * SPLIT_US_PER_KB + SPLIT_REDUCE_US +
+                      2.0 * part_bytes / 6.5e6;  // partials written and read back at HBM speed
+    if (us < best_us) {
+      best_us = us;
+      best = se;
+    }
+  }
+  if (best > 1) *splits = eff(best, kb_per);
+  return ENVG_OK;
+}
+
+int launch_split_reduce(Dev* d, const float* part, int64_t ldp, int64_t split_elems, int splits, bool silu_gate,
+                        const EpiArgs& e) {
+  const int64_t work = (int64_t)e.m_valid * cdiv(e.n_out, 4);
+  if (work == 0) return ENVG_OK;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)d->sms * 8));
+  const bool rmw = e.mode == EPI_GATED_RES || (e.mode == EPI_ALPHA_BETA && e.beta != 0.0f);
+  ProfScope ps(stream_of(d), KID_SPLIT_REDUCE, 0.0,
+               4.0 * (double)splits * e.m_valid * (silu_gate ? 2.0 * e.n_out : e.n_out) +
+                   (rmw ? 8.0 : 4.0) * (double)e.m_valid * e.n_out);
+  if (silu_gate) k_split_reduce<true><<<blocks, 256, 0, stream_of(d)>>>(part, ldp, split_elems, splits, e);
+  else k_split_reduce<false><<<blocks, 256, 0, stream_of(d)>>>(part, ldp, split_elems, splits, e);
+  ENVG_CUDA(cudaGetLastError());
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
 // Core GEMM on device operands: Y = epilogue(A[M, Kp] . B[rows, Kp]^T).
 //   A: bf16 activations (M rows);  B: bf16 weights (rows_b rows), with maps for both boxes.
 int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap& b256, const CUtensorMap& b128,
@@ -787,14 +872,46 @@ int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap&
   g.num_kb = (int)num_kb;
   g.tiles_n = (int)cdiv(rows_b, K1_BN);
   g.group_m = 8;
-  CUtensorMap tY;
-  memset(&tY, 0, sizeof(tY));
-  ENVG_TRY(choose_store(d->store_tma, e, &tY, &g.pm));
-  g.epi = e;
   if (d->use_pair && M > BM) {
     g.tiles_m = (int)cdiv(M, 2 * BM);
     g.num_tiles = g.tiles_m * g.tiles_n;
     g.group_m = 4;
+    const int64_t Mp = (int64_t)g.tiles_m * 2 * BM;
+    const int64_t ldp = rup(rows_b, 4);
+    int kbp = 0;
+    int sp = 1;
+    if (e.nremote == 0) ENVG_TRY(pair_splits(d, M, g.num_tiles, g.num_kb, Mp, ldp, &sp, &kbp));
+    if (sp > 1) {
+      // the units store raw partials [sp][Mp][ldp]; k_split_reduce finishes Y
+      ENVG_TRY(ensure(d, d->part, (size_t)(sp * Mp * ldp) * 4));
+      float* part = reinterpret_cast<float*>(d->part.p);
+      CUtensorMap tP;
+      ENVG_TRY(tmap_out_2d(&tP, part, (uint64_t)ldp, (uint64_t)(sp * Mp), (uint64_t)ldp));
+      ENVG_TRY(tmap_out_2d(&g.ybig, part, (uint64_t)ldp, (uint64_t)(sp * Mp), (uint64_t)ldp, 128));
+      g.ybig_ok = 1;
+      g.splits = sp;
+      g.kb_per_split = kbp;
+      g.tiles_per_split = g.num_tiles;
+      g.split_rows = (int)Mp;
+      g.num_tiles *= sp;
+      EpiArgs ep{};
+      ep.Y = part;
+      ep.ldy = ldp;
+      ep.mode = EPI_PLAIN;
+      ep.n_out = (int)ldp;
+      ep.m_valid = (int)(sp * Mp);
+      ep.vec_ok = 1;
+      ep.store_mode = STORE_TMA;
+      g.epi = ep;
+      ENVG_TRY((launch_k1_pair<false, false>(d, tA, b128, tP, g, flops, bytes)));
+      return launch_split_reduce(d, part, ldp, Mp * ldp, sp, silu_gate, e);
+    }
+  }
+  CUtensorMap tY;
+  memset(&tY, 0, sizeof(tY));
+  ENVG_TRY(choose_store(d->store_tma, e, &tY, &g.pm, (d->use_pair && M > BM) ? &g : nullptr));
+  g.epi = e;
+  if (d->use_pair && M > BM) {
     if (silu_gate) return launch_k1_pair<false, true>(d, tA, b128, tY, g, flops, bytes);
     return launch_k1_pair<false, false>(d, tA, b128, tY, g, flops, bytes);
   }
@@ -1049,6 +1166,10 @@ int envg_init(int ndev, const int* dev_ids) {
   if (const char* s = getenv("ENVG_K1")) d->use_pair = strcmp(s, "single") != 0;
   if (const char* s = getenv("ENVG_STORE")) d->store_tma = strcmp(s, "coalesced") != 0;
   if (const char* s = getenv("ENVG_PIPE")) d->pipe_host = strcmp(s, "0") != 0;
+  if (const char* s = getenv("ENVG_PAIR_SPLIT")) {
+    const int v = atoi(s);
+    if (v >= 0 && v <= 64) d->pair_split = v;
+  }
   if (const char* s = getenv("ENVG_ATTN_TILES")) {
     const int v = atoi(s);
     if (v == 1 || v == 2) d->attn_tiles = v;
@@ -1655,6 +1776,10 @@ int conv_core(Dev* d, envg_weight W, const void* act, float* dy, const float* db
     e.store_mode = (tw >= 32) ? STORE_COALESCED : STORE_DIRECT;  // a 32-pixel chunk stays in one row
     if (d->store_tma && (reinterpret_cast<uintptr_t>(dy) & 15) == 0 && outW % 32 == 0) {
       ENVG_TRY(tmap_out_3d(&tY, dy, (uint64_t)plane, (uint64_t)out_ch, (uint64_t)batch));
+      if (pair) {
+        ENVG_TRY(tmap_out_3d(&g.ybig, dy, (uint64_t)plane, (uint64_t)out_ch, (uint64_t)batch, 128));
+        g.ybig_ok = 1;
+      }
       e.store_mode = residual ? STORE_TMA_ADD : STORE_TMA;
     }
     g.epi = e;

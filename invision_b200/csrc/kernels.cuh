@@ -119,7 +119,31 @@ struct GemmArgs {
   int* status;
   uint64_t wait_cap_ns;
   PeerMaps pm;  // STORE_TMA_PEERS only
+  // Split-K (k1_gemm_pair, splits > 1): num_tiles counts units (split, tile), split-major, with
+  // tiles_per_split tiles in each split; split s covers K blocks [s * kb_per_split, ...) and
+  // stores its raw fp32 tile at row offset s * split_rows of the partial buffer the Y map covers.
+  int splits, kb_per_split, tiles_per_split, split_rows;
+  // k1_gemm_pair, STORE_TMA / STORE_TMA_ADD: the same output as the Y map with 32-column x
+  // 128-row boxes, one box per chunk for the CTA's 128 rows (ybig_ok = 1 when built).
+  CUtensorMap ybig;
+  int ybig_ok;
 };
+
+// Unit -> (split, tile, K-block range) of a k1_gemm_pair launch; without split-K the unit is
+// the tile and the range is all of K.
+ENVG_DEV void unit_split(int unit, const GemmArgs& a, int& tile, int& split, int& kb0, int& kb1) {
+  if (a.splits > 1) {
+    split = unit / a.tiles_per_split;
+    tile = unit - split * a.tiles_per_split;
+    kb0 = split * a.kb_per_split;
+    kb1 = min(kb0 + a.kb_per_split, a.num_kb);
+  } else {
+    split = 0;
+    tile = unit;
+    kb0 = 0;
+    kb1 = a.num_kb;
+  }
+}
 
 struct SkinnyArgs {
   int n_tiles, splits, kb_per_split, num_kb;
@@ -179,7 +203,7 @@ ENVG_DEV void load_col32(const float* p, int col0, int n_out, float (&c)[32]) {
 }
 
 // epi_pre for a whole 32-column chunk of one row, with the mode tests taken once per chunk.
-// `e` is a register copy of the kernel's EpiArgs.
+// `e` is the kernel's EpiArgs, read in place from its grid-constant parameters.
 ENVG_DEV void epi_pre_chunk(const EpiArgs& e, float (&v)[32], int row, int col0) {
   if (e.bias_mode == 1) {
     float b[32];
@@ -570,7 +594,9 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
     // ---------------- epilogue: 4 warps, one TMEM lane quadrant each ----------------
     const int q = warp & 3;
     const int smode = args.epi.store_mode;
-    const EpiArgs ep = args.epi;  // register copy: the chunk loops read it every iteration
+    // A reference into the (grid-constant) parameter space: a local copy would be placed in local
+    // memory, because the peer stores index ep.remote[] at run time.
+    const EpiArgs& ep = args.epi;
     uint8_t* stg = sStage + (warp - 2) * 8192;  // this warp's two 4 KB staging tiles
     int sb = 0;
     int acc = 0;
@@ -713,8 +739,9 @@ template <int STAGES>
 struct KPairSmem {
   static constexpr int HALF_B_BYTES = 128 * BK * 2;
   static constexpr int STAGE_BYTES = TILE_A_BYTES + HALF_B_BYTES;  // this CTA's share of a stage
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;            // A stages, then B stages
   static constexpr int STAGING_BYTES = 4 * 2 * 32 * 128;
-  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int BAR_BYTES = (2 * STAGES + 6) * 8 + 16;
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
   static constexpr uint32_t TMEM_COLS = 512;
 };
@@ -733,7 +760,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   uint8_t* sB = smem + STAGES * TILE_A_BYTES;
   uint8_t* sStage = sB + STAGES * L::HALF_B_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + L::STAGING_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -745,6 +772,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   const uint32_t tfull0 = empty0 + 8 * STAGES;
   const uint32_t tempty0 = tfull0 + 16;
   const uint32_t drain = tempty0 + 16;
+  const uint32_t staged = drain + 8;  // the four epilogue warps have staged the last unit
   const uint32_t full0_leader = mapa_shared(full0, 0);
   const uint32_t tempty0_leader = mapa_shared(tempty0, 0);
   const int pair = blockIdx.x >> 1;
@@ -760,13 +788,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       mbar_init(tempty0 + 8 * b, 8);
     }
     mbar_init(drain, 1);
+    mbar_init(staged, 4);
     *abort_s = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (args.epi.store_mode == STORE_TMA || args.epi.store_mode == STORE_TMA_ADD) tma_prefetch_desc(&tmY);
+    if (args.epi.store_mode == STORE_TMA || args.epi.store_mode == STORE_TMA_ADD) {
+      tma_prefetch_desc(&tmY);
+      if (args.ybig_ok) tma_prefetch_desc(&args.ybig);
+    }
     if (args.epi.store_mode >= STORE_TMA_PEERS)
       for (int r = 0; r < args.epi.nremote; ++r) tma_prefetch_desc(&args.pm.m[r]);
   }
@@ -785,7 +817,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       int stage = 0;
       uint32_t ph = 0;
       uint32_t pending = 0, issue_ph = 0;
-      for (int tile = pair; tile < args.num_tiles; tile += npairs) {
+      for (int unit = pair; unit < args.num_tiles; unit += npairs) {
+        int tile, split, kb0, kb1;
+        unit_split(unit, args, tile, split, kb0, kb1);
         int m_blk, n_blk;
         int b = 0, h0 = 0, w0 = 0;
         if (CONV_B) {
@@ -804,7 +838,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
         }
         const int m0 = m_blk * 2 * BM + (int)rank * BM;
         const int n0 = n_blk * BN + (int)rank * 128;
-        for (int kb = 0; kb < args.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(empty0 + 8 * stage, ph ^ 1, wc, 21)) goto producer_done;
           const uint32_t fb = full0_leader + 8 * stage;
           if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, 2 * L::STAGE_BYTES);
@@ -846,12 +880,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       uint32_t ph = 0;
       int acc = 0;
       uint32_t aph = 0;
-      for (int tile = pair; tile < args.num_tiles; tile += npairs) {
+      for (int unit = pair; unit < args.num_tiles; unit += npairs) {
+        int tile, split, kb0, kb1;
+        unit_split(unit, args, tile, split, kb0, kb1);
         if (!wait_bounded(tempty0 + 8 * acc, aph ^ 1, wc, 22)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
-        for (int kb = 0; kb < args.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(full0 + 8 * stage, ph, wc, 23)) {
             ok = false;
             break;
@@ -861,7 +897,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
           const uint64_t bd = sw128_kmajor_desc(smem_u32(sB + stage * L::HALF_B_BYTES));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            umma_bf16_pair(d_tmem, ad + 2 * k, bd + 2 * k, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_bf16_pair(d_tmem, ad + 2 * k, bd + 2 * k, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
           umma_commit_pair_mc(empty0 + 8 * stage, 0x3);
           if (++stage == STAGES) {
             stage = 0;
@@ -881,12 +917,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   } else {
     const int q = warp & 3;
     const int smode = args.epi.store_mode;
-    const EpiArgs ep = args.epi;  // register copy: the chunk loops read it every iteration
+    // A reference into the (grid-constant) parameter space: a local copy would be placed in local
+    // memory, because the peer stores index ep.remote[] at run time.
+    const EpiArgs& ep = args.epi;
     uint8_t* stg = sStage + (warp - 2) * 8192;
     int sb = 0;
     int acc = 0;
     uint32_t aph = 0;
-    for (int tile = pair; tile < args.num_tiles; tile += npairs) {
+    for (int unit = pair; unit < args.num_tiles; unit += npairs) {
+      int tile, split, kb0, kb1;
+      unit_split(unit, args, tile, split, kb0, kb1);
       int m_blk, n_blk;
       int b = 0, h0 = 0, w0 = 0;
       if (CONV_B) {
@@ -906,6 +946,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       const int row0 = m_blk * 2 * BM + (int)rank * BM + q * 32;
       const int row = row0 + lane;
       constexpr int NCHUNK = SILU_GATE ? BN / 64 : BN / 32;
+      // On the CTA's last unit no operand load is in flight or still to come, and the UMMAs have
+      // read their operands (the accumulator is complete), so each epilogue warp stages all its
+      // chunks in its own quarter of the idle operand ring, then makes them visible to the TMA
+      // unit with one proxy fence and issues every store back to back: the tail of the launch
+      // is one pass over TMEM and the store drain, with no per-chunk fence or buffer wait.
+      static_assert(L::RING_BYTES / 4 >= NCHUNK * 4096 && (L::RING_BYTES / 4) % 1024 == 0, "ring staging");
+      const bool ring_mode = unit + npairs >= args.num_tiles && smode != STORE_COALESCED && smode != STORE_DIRECT;
+      // With the 128-row map, the four warps' 32 x 32 tiles of chunk c sit one above the other
+      // (rows q * 32 ..) in a 16 KB box, and one thread stores each chunk of the CTA's 128 rows:
+      // a quarter of the TMA stores, each four times larger.
+      const bool big = ring_mode && args.ybig_ok && (smode == STORE_TMA || smode == STORE_TMA_ADD);
+      static_assert(L::RING_BYTES >= NCHUNK * 16384, "ring staging, 128-row boxes");
+      uint8_t* ring = big ? smem + q * 4096 : smem + (warp - 2) * (L::RING_BYTES / 4);
+      const int ring_stride = big ? 16384 : 4096;
+      // Y coordinates of chunk c's 32 x 32 box; false when a conv chunk lies past the row end.
+      auto chunk_xy = [&](int c, int& x, int& y) -> bool {
+        if (CONV_B) {
+          const int jj = c * 32;
+          const int w = w0 + jj % args.conv.tileW;
+          const int h = h0 + jj / args.conv.tileW;
+          x = h * args.conv.outW + w;
+          y = row0;
+          return w < args.conv.outW;
+        }
+        x = n_blk * (SILU_GATE ? BN / 2 : BN) + c * 32;
+        y = row0 + split * args.split_rows;
+        return true;
+      };
+      auto issue_store = [&](const uint8_t* buf, int x, int y) {
+        if (CONV_B) {
+          if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&tmY, smem_u32(buf), x, y, b);
+          else tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+        } else if (smode == STORE_TMA_PEERS) {
+          for (int r = 0; r < ep.nremote; ++r) tma_store_2d(&args.pm.m[r], smem_u32(buf), x, y);
+        } else if (smode == STORE_TMA_ADD_PEERS) {
+          for (int r = 0; r < ep.nremote; ++r) tma_reduce_add_2d(&args.pm.m[r], smem_u32(buf), x, y);
+        } else if (smode == STORE_TMA_ADD) {
+          tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
+        } else {
+          tma_store_2d(&tmY, smem_u32(buf), x, y);
+        }
+      };
 #pragma unroll 1
       for (int c = 0; c < NCHUNK; ++c) {
         float v[32];
@@ -936,13 +1018,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
           }
           continue;
         }
-        int x = col0, y = row0;
+        int x, y;
+        if (!chunk_xy(c, x, y)) continue;
         if (CONV_B) {
-          const int jj = c * 32;
-          const int w = w0 + jj % args.conv.tileW;
-          const int h = h0 + jj / args.conv.tileW;
-          if (w >= args.conv.outW) continue;
-          x = h * args.conv.outW + w;
           const float bv = (ep.bias_mode == 2 && row < ep.m_valid) ? __ldg(ep.bias + row) : 0.0f;
           if (ep.act) {
 #pragma unroll
@@ -969,26 +1047,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
           sb ^= 1;  // the other buffer is written next, so no wait before this one is reused
           continue;
         }
+        if (ring_mode) {
+          stage_row32(ring + c * ring_stride, lane, v);  // stored after the loop
+          continue;
+        }
         if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
         __syncwarp();
         stage_row32(buf, lane, v);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (CONV_B) {
-            if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&tmY, smem_u32(buf), x, y, b);
-            else tma_store_3d(&tmY, smem_u32(buf), x, y, b);
-          }
-          else if (smode == STORE_TMA_PEERS) {
-            for (int r = 0; r < ep.nremote; ++r) tma_store_2d(&args.pm.m[r], smem_u32(buf), x, y);
-          } else if (smode == STORE_TMA_ADD_PEERS) {
-            for (int r = 0; r < ep.nremote; ++r) tma_reduce_add_2d(&args.pm.m[r], smem_u32(buf), x, y);
-          }
-          else if (smode == STORE_TMA_ADD) tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
-          else tma_store_2d(&tmY, smem_u32(buf), x, y);
+          issue_store(buf, x, y);
           bulk_commit();
         }
         sb ^= 1;
+      }
+      if (ring_mode) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (big) {
+          if (lane == 0) mbar_arrive(staged);
+          if (warp == 2 && lane == 0 && wait_bounded(staged, 0, wc, 25)) {
+            for (int c = 0; c < NCHUNK; ++c) {
+              int x, y;
+              if (!chunk_xy(c, x, y)) continue;
+              y -= q * 32;  // the CTA's first row
+              const uint32_t src = smem_u32(smem + c * 16384);
+              if (CONV_B) {
+                if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&args.ybig, src, x, y, b);
+                else tma_store_3d(&args.ybig, src, x, y, b);
+              } else if (smode == STORE_TMA_ADD) {
+                tma_reduce_add_2d(&args.ybig, src, x, y);
+              } else {
+                tma_store_2d(&args.ybig, src, x, y);
+              }
+            }
+            bulk_commit();
+          }
+        } else if (lane == 0) {
+          for (int c = 0; c < NCHUNK; ++c) {
+            int x, y;
+            if (chunk_xy(c, x, y)) issue_store(ring + c * 4096, x, y);
+          }
+          bulk_commit();
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -1008,6 +1110,96 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// Split-K reduction of k1_gemm_pair: Y = epilogue(sum of the raw fp32 partial tiles, added in
+// split order, so the result does not depend on which split finished first).  part holds
+// [splits][split_rows][ldp] accumulators over the device weight's rows; with SILU_GATE those
+// rows interleave 128 gate rows with their 128 up rows, so output column j pairs partial
+// columns 256 (j / 128) + j % 128 (gate) and that + 128 (up).  The epilogue is the one the
+// unsplit kernel applies: bias / SiLU / gated residual / alpha-beta (epi_value) or the SiLU gate,
+// the stores to each rank's copy of Y, and the optional bf16 side output.
+// ------------------------------------------------------------------------------------------
+ENVG_DEV float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+// Sum of the partials at offset `off` of every split, added in split order; four loads are in
+// flight at a time.
+ENVG_DEV float4 split_sum4(const float* __restrict__ part, int64_t off, int64_t split_elems, int splits) {
+  float4 a = __ldcs(reinterpret_cast<const float4*>(part + off));
+  int sp = 1;
+  for (; sp + 3 < splits; sp += 4) {
+    const float* p = part + sp * split_elems + off;
+    const float4 p1 = __ldcs(reinterpret_cast<const float4*>(p));
+    const float4 p2 = __ldcs(reinterpret_cast<const float4*>(p + split_elems));
+    const float4 p3 = __ldcs(reinterpret_cast<const float4*>(p + 2 * split_elems));
+    const float4 p4 = __ldcs(reinterpret_cast<const float4*>(p + 3 * split_elems));
+    a = add4(add4(add4(add4(a, p1), p2), p3), p4);
+  }
+  for (; sp < splits; ++sp) a = add4(a, __ldcs(reinterpret_cast<const float4*>(part + sp * split_elems + off)));
+  return a;
+}
+
+template <bool SILU_GATE>
+__global__ void __launch_bounds__(256) k_split_reduce(const float* __restrict__ part, int64_t ldp,
+                                                      int64_t split_elems, int splits, const EpiArgs e) {
+  const int quads = (e.n_out + 3) >> 2;
+  const int64_t total = (int64_t)e.m_valid * quads;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(t / quads);
+    const int col = (int)(t - (int64_t)row * quads) * 4;
+    float v[4];
+    if (SILU_GATE) {
+      const int64_t pg = (int64_t)row * ldp + (col >> 7) * 256 + (col & 127);
+      const float4 g = split_sum4(part, pg, split_elems, splits);
+      const float4 u = split_sum4(part, pg + 128, split_elems, splits);
+      const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = min(col + j, e.n_out - 1);
+        v[j] = (e.bias_mode == 1)
+                   ? __fmul_rn(silu_f(__fadd_rn(gv[j], __ldg(e.bias + c))), __fadd_rn(uv[j], __ldg(e.bias + e.half_n + c)))
+                   : __fmul_rn(silu_f(gv[j]), uv[j]);
+      }
+    } else {
+      const float4 a = split_sum4(part, (int64_t)row * ldp + col, split_elems, splits);
+      v[0] = a.x;
+      v[1] = a.y;
+      v[2] = a.z;
+      v[3] = a.w;
+    }
+    EpiArgs e2 = e;
+    if (SILU_GATE) {
+      e2.bias_mode = 0;
+      e2.act = 0;
+    }
+    const int64_t idx = (int64_t)row * e.ldy + e.col_off + col;
+    const bool rmw = e.mode == EPI_GATED_RES || (e.mode == EPI_ALPHA_BETA && e.beta != 0.0f);
+    if (e.vec_ok && col + 3 < e.n_out) {
+      float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rmw) old = *reinterpret_cast<const float4*>(e.Y + idx);
+      v[0] = epi_value(e2, v[0], row, col + 0, &old.x);
+      v[1] = epi_value(e2, v[1], row, col + 1, &old.y);
+      v[2] = epi_value(e2, v[2], row, col + 2, &old.z);
+      v[3] = epi_value(e2, v[3], row, col + 3, &old.w);
+      out_store4(e, idx, make_float4(v[0], v[1], v[2], v[3]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (col + j >= e.n_out) break;
+        v[j] = epi_value(e2, v[j], row, col + j, e.Y + idx + j);
+        out_store1(e, idx + j, v[j]);
+      }
+    }
+    if (e.yb) {
+      __nv_bfloat16* p = e.yb + (int64_t)row * e.ldyb + col;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (col + j < e.n_out) p[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
 template <int MPAD, int R, int STAGES>
 struct K2Smem {
   static constexpr int W_BYTES = R * TILE_A_BYTES;
@@ -1024,7 +1216,8 @@ struct K2Smem {
 // ------------------------------------------------------------------------------------------
 template <int MPAD, int R, int STAGES>
 __global__ void __launch_bounds__(K1_THREADS, 1)
-    k2_skinny(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const SkinnyArgs args) {
+    k2_skinny(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+              const __grid_constant__ SkinnyArgs args) {
   using L = K2Smem<MPAD, R, STAGES>;
   constexpr uint32_t IDESC = idesc_bf16_f32(BM, MPAD);
   static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= 64, "MPAD");
@@ -1204,7 +1397,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
         }
       }
       if (finalize) {
-        const EpiArgs e = args.epi;
+        const EpiArgs& e = args.epi;  // in parameter space (a local copy would go to local memory)
         const int col = tile * BM + rowin;  // output column (shard-relative)
         if (col < e.n_out) {
 #pragma unroll
@@ -1673,7 +1866,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
     if (threadIdx.x == 0) a.counters[group] = 0;  // re-arm for the next launch
     __syncthreads();
   }
-  const EpiArgs e = a.epi;
+  const EpiArgs& e = a.epi;  // in parameter space (a local copy would go to local memory)
   if (a.gate_up) {
     for (int t = threadIdx.x; t < MT * 32; t += blockDim.x) {
       const int m = t / 32, c = t % 32;

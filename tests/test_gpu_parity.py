@@ -203,10 +203,11 @@ def test_errors_are_codes_not_crashes(gpu):
 
 
 @pytest.mark.parametrize("env", [{"ENVG_STORE": "coalesced"}, {"ENVG_STORE": "coalesced", "ENVG_K1": "single"},
-                                 {"ENVG_K1": "single"}])
+                                 {"ENVG_K1": "single"}, {"ENVG_PAIR_SPLIT": "3"}, {"ENVG_PAIR_SPLIT": "0"}])
 def test_alternate_kernel_paths_in_subprocess(env):
-    """The warp-coalesced store epilogue and the single-CTA k1_gemm (selected by environment at init) on a
-    few linear / SiLU-gate / gated-residual / conv cases, in a fresh process."""
+    """The warp-coalesced store epilogue, the single-CTA k1_gemm and a forced (or disabled) split-K of
+    k1_gemm_pair (selected by environment at init) on a few linear / SiLU-gate / gated-residual /
+    conv cases, in a fresh process."""
     import os
     import subprocess
     import sys
