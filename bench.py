@@ -45,8 +45,9 @@ METRIC = "block_linear_tflops"
 UNIT = "TFLOP/s"
 
 
-def lin(name, M, K, N, epi="bias", x_from=None):
-    return dict(name=name, op="linear", M=M, K=K, N=N, epi=epi, x_from=x_from)
+def lin(name, M, K, N, epi="bias", x_from=None, x_same=None):
+    """x_from: the input is that item's output; x_same: the same input tensor as that item."""
+    return dict(name=name, op="linear", M=M, K=K, N=N, epi=epi, x_from=x_from, x_same=x_same)
 
 
 def conv(name, B, C, H, W, O, k, stride, pad, epi="silu"):
@@ -62,7 +63,9 @@ def resblock(name, B, Ci, Co, H, W, G=32):
 
 
 def qwen(M):
-    return [lin("q", M, 2560, 4096, "none"), lin("k", M, 2560, 1024, "none"), lin("v", M, 2560, 1024, "none"),
+    # q, k and v all read the normalised hidden state (quicknn_qwen3.pas:712-714)
+    return [lin("q", M, 2560, 4096, "none"), lin("k", M, 2560, 1024, "none", x_same="q"),
+            lin("v", M, 2560, 1024, "none", x_same="q"),
             lin("o", M, 4096, 2560, "none"), lin("gate_up", M, 2560, 2 * 9728, "silu_gate_nobias"),
             lin("down", M, 9728, 2560, "none", x_from="gate_up")]
 
@@ -343,7 +346,9 @@ class Workload:
                     h = symm_mem.rendezvous(ysym, dist.group.WORLD)
                     mc = h.multicast_ptr if (h.has_multicast_support and not self.force_p2p) else 0
                     self.sym[name] = (ysym, h, list(h.buffer_ptrs), mc)
-            if it["x_from"] not in names:
+            if it.get("x_same"):
+                self.x[name] = self.x[it["x_same"]]
+            elif it["x_from"] not in names:
                 gen.manual_seed(2000 + i)
                 self.x[name] = torch.randn(M, K, generator=gen, device=dev)
             self.y[name] = torch.empty(M, out_cols(it), device=dev)

@@ -98,6 +98,7 @@ struct Dev {
   bool pipe_host = true;  // pipeline large host-pointer linears in row chunks (ENVG_PIPE=0 disables)
   int attn_tiles = 0;     // query tiles per attention CTA: 0 = by grid size, ENVG_ATTN_TILES=1|2 forces
   int pair_split = -1;    // k1_gemm_pair split-K: -1 by cost model, 0 off, n forces n (ENVG_PAIR_SPLIT)
+  bool pdl = true;        // programmatic dependent launch of the GEMM-chain kernels (ENVG_PDL=0 disables)
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
@@ -274,7 +275,8 @@ int tmap_out_3d(CUtensorMap* tm, const float* base, uint64_t plane, uint64_t ch,
 
 // Picks the k1_gemm store path for a row-major Y (and builds its map for the TMA paths).  With
 // peer copies of Y (N-split) and `pm` given, the chunks go out as TMA bulk stores, one per copy.
-int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = nullptr, GemmArgs* big = nullptr) {
+int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = nullptr, CUtensorMap* ybig = nullptr,
+                 int* ybig_ok = nullptr) {
   if (use_tma && pm && e.nremote > 0 && e.mode != EPI_ALPHA_BETA) {
     bool ok = e.ldy % 4 == 0 && e.col_off % 4 == 0;
     for (int r = 0; r < e.nremote; ++r) ok = ok && (reinterpret_cast<uintptr_t>(e.remote[r] + e.col_off) & 15) == 0;
@@ -302,10 +304,10 @@ int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = null
   if (mode == STORE_DIRECT) return ENVG_OK;
   int rc = tmap_out_2d(tmY, e.Y, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy);
   if (rc != ENVG_OK) return rc;
-  if (big) {  // k1_gemm_pair's last-unit stores (CTA-high boxes)
-    rc = tmap_out_2d(&big->ybig, e.Y, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy, 128);
+  if (ybig) {  // k1_gemm_pair's last-unit stores (CTA-high boxes)
+    rc = tmap_out_2d(ybig, e.Y, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy, 128);
     if (rc != ENVG_OK) return rc;
-    big->ybig_ok = 1;
+    *ybig_ok = 1;
   }
   e.store_mode = mode;
   return ENVG_OK;
@@ -421,6 +423,25 @@ int sync_and_check(Dev* d) {
 
 // ---- kernel launchers ----------------------------------------------------------------------
 
+// Launch on the library stream.  With programmatic stream serialization (Dev::pdl) the kernel may
+// start while the previous kernel of the stream finishes: every kernel launched this way calls
+// griddep_wait before its first global memory access, so only its prologue overlaps.
+template <typename... KArgs, typename... Args>
+int launch_pdl(Dev* d, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream_of(d);
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = d->pdl ? 1 : 0;
+  ENVG_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
+  return ENVG_OK;
+}
+
 template <bool CONV_B, bool SILU_GATE>
 int launch_k1(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tY, GemmArgs& a, double flops,
               double bytes) {
@@ -476,21 +497,46 @@ int k1_pair_capacity(Dev* d, int* pairs) {
 }
 
 template <bool CONV_B, bool SILU_GATE>
-int launch_k1_pair(Dev* d, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tY, GemmArgs& a,
-                   double flops, double bytes) {
+int launch_k1_pair(Dev* d, const CUtensorMap& tA, PairSet& set, double flops, double bytes) {
   using L = KPairSmem<KPAIR_STAGES>;
   auto kern = k1_gemm_pair<KPAIR_STAGES, CONV_B, SILU_GATE>;
   int max_pairs = 0;
   ENVG_TRY((k1_pair_capacity<CONV_B, SILU_GATE>(d, &max_pairs)));
-  a.status = d->d_status;
-  a.wait_cap_ns = d->wait_cap_ns;
-  const int pairs = (int)std::min<int64_t>(a.num_tiles, max_pairs);
+  set.status = d->d_status;
+  set.wait_cap_ns = d->wait_cap_ns;
+  const int pairs = (int)std::min<int64_t>(set.total, max_pairs);
   if (pairs <= 0) return ENVG_OK;
   ProfScope ps(stream_of(d), CONV_B ? KID_K1_CONV : (SILU_GATE ? KID_K1_SILU_GATE : KID_K1), flops, bytes);
-  kern<<<2 * pairs, K1_THREADS, L::TOTAL, stream_of(d)>>>(tA, tB, tY, a);
-  ENVG_CUDA(cudaGetLastError());
+  ENVG_TRY(launch_pdl(d, kern, dim3(2 * pairs), dim3(K1_THREADS), L::TOTAL, tA, set));
   d->st.kernel_launches++;
   return ENVG_OK;
+}
+
+// A pair launch of one linear (or convolution) described by GemmArgs-style fields.
+PairSet set_of_one(const GemmArgs& g, const CUtensorMap& tB, const CUtensorMap& tY) {
+  PairSet set;
+  memset(&set, 0, sizeof(set));
+  PairLin& P = set.lin[0];
+  P.num_kb = g.num_kb;
+  P.tiles_m = g.tiles_m;
+  P.tiles_n = g.tiles_n;
+  P.group_m = g.group_m;
+  P.splits = g.splits;
+  P.kb_per_split = g.kb_per_split;
+  P.tiles_per_split = g.tiles_per_split;
+  P.split_rows = g.split_rows;
+  P.ybig_ok = g.ybig_ok;
+  P.epi = g.epi;
+  set.tmB[0] = tB;
+  set.tmY[0] = tY;
+  set.ybig[0] = g.ybig;
+  set.n = 1;
+  set.total = g.num_tiles;
+  set.base[0] = 0;
+  set.base[1] = g.num_tiles;
+  set.conv = g.conv;
+  set.pm = g.pm;
+  return set;
 }
 
 template <int MPAD, int R>
@@ -574,8 +620,7 @@ int launch_k2_set_t(Dev* d, K2Set& S, double flops, double bytes) {
   S.wait_cap_ns = d->wait_cap_ns;
   const int grid = std::min(S.total, 2 * d->sms);
   ProfScope ps(stream_of(d), KID_K2, flops, bytes);
-  kern<<<grid, K1_THREADS, L::TOTAL, stream_of(d)>>>(S);
-  ENVG_CUDA(cudaGetLastError());
+  ENVG_TRY(launch_pdl(d, kern, dim3(grid), dim3(K1_THREADS), L::TOTAL, S));
   d->st.kernel_launches++;
   return ENVG_OK;
 }
@@ -734,11 +779,8 @@ int launch_gemv_set(Dev* d, const GemvJob* jobs, int n) {
   }
   const int grid = std::min(set.total, cap);
   ProfScope ps(stream_of(d), KID_GEMV, flops, bytes);
-  if (mt <= 1) k_gemv<1><<<grid, 256, 0, stream_of(d)>>>(set);
-  else if (mt <= 2) k_gemv<2><<<grid, 256, 0, stream_of(d)>>>(set);
-  else if (mt <= 4) k_gemv<4><<<grid, 256, 0, stream_of(d)>>>(set);
-  else k_gemv<8><<<grid, 256, 0, stream_of(d)>>>(set);
-  ENVG_CUDA(cudaGetLastError());
+  auto kern = mt <= 1 ? k_gemv<1> : mt <= 2 ? k_gemv<2> : mt <= 4 ? k_gemv<4> : k_gemv<8>;
+  ENVG_TRY(launch_pdl(d, kern, dim3(grid), dim3(256), 0, set));
   d->st.kernel_launches++;
   return ENVG_OK;
 }
@@ -754,8 +796,8 @@ int launch_adaln(Dev* d, const float* x, int64_t rows, int64_t K, int64_t Kp, co
                  void* out, bool bf16) {
   if (rows == 0) return ENVG_OK;
   ProfScope ps(stream_of(d), KID_ADALN, 0.0, (double)rows * K * 4 + (double)rows * Kp * (bf16 ? 2 : 4) + 8.0 * K);
-  k_adaln<<<(unsigned)rows, 256, 0, stream_of(d)>>>(x, K, (int)K, (int)Kp, shift, scale, 1e-6f, out, bf16 ? 1 : 0);
-  ENVG_CUDA(cudaGetLastError());
+  ENVG_TRY(launch_pdl(d, k_adaln, dim3((unsigned)rows), dim3(256), 0, x, K, (int)K, (int)Kp, shift, scale, 1e-6f,
+                      out, bf16 ? 1 : 0));
   d->st.kernel_launches++;
   return ENVG_OK;
 }
@@ -767,9 +809,8 @@ int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t 
   const int64_t work = vec8 ? rows * K / 8 : rows * Kp;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)d->sms * 8));
   ProfScope ps(stream_of(d), KID_CAST, 0.0, (double)rows * K * 4 + (double)rows * Kp * 2);
-  k_cast_rows<<<blocks, 256, 0, stream_of(d)>>>(x, ldx, (int)rows, (int)K, (int)Kp,
-                                                  reinterpret_cast<__nv_bfloat16*>(xb), vec8);
-  ENVG_CUDA(cudaGetLastError());
+  ENVG_TRY(launch_pdl(d, k_cast_rows, dim3(blocks), dim3(256), 0, x, ldx, (int)rows, (int)K, (int)Kp,
+                      reinterpret_cast<__nv_bfloat16*>(xb), vec8));
   d->st.kernel_launches++;
   return ENVG_OK;
 }
@@ -782,14 +823,13 @@ int launch_transpose_cast(Dev* d, const float* src, int64_t lds, int64_t sbs, in
                    (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
   if (vec) {
     dim3 grid((unsigned)cdiv(C, 64), (unsigned)cdiv(Rp, 64), (unsigned)batch);
-    k_transpose_cast_v<<<grid, 256, 0, stream_of(d)>>>(src, lds, sbs, R, C, reinterpret_cast<__nv_bfloat16*>(dst),
-                                                       ldd, dbs, Rp, aff, act);
+    ENVG_TRY(launch_pdl(d, k_transpose_cast_v, grid, dim3(256), 0, src, lds, sbs, R, C,
+                        reinterpret_cast<__nv_bfloat16*>(dst), ldd, dbs, Rp, aff, act));
   } else {
     dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(Rp, 64), (unsigned)batch);
-    k_transpose_cast<<<grid, 256, 0, stream_of(d)>>>(src, lds, sbs, R, C, reinterpret_cast<__nv_bfloat16*>(dst), ldd,
-                                                     dbs, Rp, aff, act);
+    ENVG_TRY(launch_pdl(d, k_transpose_cast, grid, dim3(256), 0, src, lds, sbs, R, C,
+                        reinterpret_cast<__nv_bfloat16*>(dst), ldd, dbs, Rp, aff, act));
   }
-  ENVG_CUDA(cudaGetLastError());
   d->st.kernel_launches++;
   return ENVG_OK;
 }
@@ -841,19 +881,124 @@ int pair_splits(Dev* d, int64_t M, int tiles, int num_kb, int64_t Mp, int64_t ld
   return ENVG_OK;
 }
 
-int launch_split_reduce(Dev* d, const float* part, int64_t ldp, int64_t split_elems, int splits, bool silu_gate,
-                        const EpiArgs& e) {
-  const int64_t work = (int64_t)e.m_valid * cdiv(e.n_out, 4);
+int launch_split_reduce(Dev* d, SplitReduceSet& rs) {
+  const int64_t work = rs.base[rs.n];
   if (work == 0) return ENVG_OK;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)d->sms * 8));
-  const bool rmw = e.mode == EPI_GATED_RES || (e.mode == EPI_ALPHA_BETA && e.beta != 0.0f);
-  ProfScope ps(stream_of(d), KID_SPLIT_REDUCE, 0.0,
-               4.0 * (double)splits * e.m_valid * (silu_gate ? 2.0 * e.n_out : e.n_out) +
-                   (rmw ? 8.0 : 4.0) * (double)e.m_valid * e.n_out);
-  if (silu_gate) k_split_reduce<true><<<blocks, 256, 0, stream_of(d)>>>(part, ldp, split_elems, splits, e);
-  else k_split_reduce<false><<<blocks, 256, 0, stream_of(d)>>>(part, ldp, split_elems, splits, e);
-  ENVG_CUDA(cudaGetLastError());
+  double bytes = 0.0;
+  for (int i = 0; i < rs.n; ++i) {
+    const EpiArgs& e = rs.e[i];
+    const bool rmw = e.mode == EPI_GATED_RES || (e.mode == EPI_ALPHA_BETA && e.beta != 0.0f);
+    bytes += 4.0 * (double)rs.splits[i] * e.m_valid * (rs.silu_gate[i] ? 2.0 * e.n_out : e.n_out) +
+             (rmw ? 8.0 : 4.0) * (double)e.m_valid * e.n_out;
+  }
+  ProfScope ps(stream_of(d), KID_SPLIT_REDUCE, 0.0, bytes);
+  ENVG_TRY(launch_pdl(d, k_split_reduce, dim3(blocks), dim3(256), 0, rs));
   d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
+// One linear of a k1_gemm_pair launch, host side.
+struct PairJob {
+  const CUtensorMap* tB;  // its weight, 128-row boxes
+  int64_t rows_b;         // weight rows on the device
+  bool gu;                // SiLU-gate (GATE_UP weight)
+  EpiArgs e;              // its epilogue
+  double flops, bytes;
+};
+
+// Linears that share the activation operand A[M, Kp] (M > 128) as k1_gemm_pair launches: one
+// launch per kernel variant present (the SiLU-gate variant for unsplit GATE_UP linears, the
+// plain one for the rest), each walking all its linears' units; then one k_split_reduce per
+// linear that splits K.  Each linear's split count is its own (pair_splits), so a linear gives
+// the same bits whether it runs alone or in a set.
+int launch_pair_set(Dev* d, const void* A, int64_t M, int64_t Kp, PairJob* jobs, int n) {
+  CUtensorMap tA;
+  ENVG_TRY(tmap_2d(&tA, A, Kp, M, BM));
+  const int num_kb = (int)cdiv(Kp, BK);
+  const int tiles_m = (int)cdiv(M, 2 * BM);
+  const int64_t Mp = (int64_t)tiles_m * 2 * BM;
+  int sp[PSET_MAX], kbp[PSET_MAX];
+  size_t off[PSET_MAX], part = 0;
+  for (int i = 0; i < n; ++i) {
+    const int tiles = tiles_m * (int)cdiv(jobs[i].rows_b, K1_BN);
+    sp[i] = 1;
+    kbp[i] = num_kb;
+    if (jobs[i].e.nremote == 0)
+      ENVG_TRY(pair_splits(d, M, tiles, num_kb, Mp, rup(jobs[i].rows_b, 4), &sp[i], &kbp[i]));
+    off[i] = part;
+    if (sp[i] > 1) part += ((size_t)(sp[i] * Mp * rup(jobs[i].rows_b, 4)) * 4 + 255) & ~size_t(255);
+  }
+  if (part) ENVG_TRY(ensure(d, d->part, part));
+  // Units are handed to CTA pairs in order (pair p takes units p, p + pairs, ...), so the
+  // linears with the longest units (most K blocks each) go first and the short ones fill in.
+  int order[PSET_MAX];
+  for (int i = 0; i < n; ++i) order[i] = i;
+  std::stable_sort(order, order + n, [&](int a, int b) { return kbp[a] > kbp[b]; });
+  for (int pass = 0; pass < 2; ++pass) {  // pass 0: plain kernel; pass 1: SiLU-gate kernel
+    PairSet set;
+    memset(&set, 0, sizeof(set));
+    double flops = 0.0, bytes = 0.0;
+    for (int oi = 0; oi < n; ++oi) {
+      const int i = order[oi];
+      const bool silu_kernel = jobs[i].gu && sp[i] == 1;
+      if (silu_kernel != (pass == 1)) continue;
+      const int j = set.n++;
+      PairLin& P = set.lin[j];
+      P.num_kb = num_kb;
+      P.tiles_m = tiles_m;
+      P.tiles_n = (int)cdiv(jobs[i].rows_b, K1_BN);
+      P.group_m = 4;
+      P.tiles_per_split = P.tiles_m * P.tiles_n;
+      set.tmB[j] = *jobs[i].tB;
+      if (sp[i] > 1) {
+        // the units store raw partials [sp][Mp][ldp]; k_split_reduce finishes Y
+        const int64_t ldp = rup(jobs[i].rows_b, 4);
+        float* p = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d->part.p) + off[i]);
+        ENVG_TRY(tmap_out_2d(&set.tmY[j], p, (uint64_t)ldp, (uint64_t)(sp[i] * Mp), (uint64_t)ldp));
+        ENVG_TRY(tmap_out_2d(&set.ybig[j], p, (uint64_t)ldp, (uint64_t)(sp[i] * Mp), (uint64_t)ldp, 128));
+        P.ybig_ok = 1;
+        P.splits = sp[i];
+        P.kb_per_split = kbp[i];
+        P.split_rows = (int)Mp;
+        EpiArgs& ep = P.epi;
+        ep.Y = p;
+        ep.ldy = ldp;
+        ep.mode = EPI_PLAIN;
+        ep.n_out = (int)ldp;
+        ep.m_valid = (int)(sp[i] * Mp);
+        ep.vec_ok = 1;
+        ep.store_mode = STORE_TMA;
+      } else {
+        P.epi = jobs[i].e;
+        ENVG_TRY(choose_store(d->store_tma, P.epi, &set.tmY[j], n == 1 ? &set.pm : nullptr, &set.ybig[j],
+                              &P.ybig_ok));
+        if (P.epi.nremote > 0 && P.epi.store_mode >= STORE_TMA_PEERS && n != 1)
+          return fail(ENVG_ERR_STATE, "internal: peer-store maps in a pair set");
+      }
+      set.base[j + 1] = set.base[j] + P.tiles_per_split * std::max(1, P.splits);
+      flops += jobs[i].flops;
+      bytes += jobs[i].bytes;
+    }
+    if (set.n == 0) continue;
+    set.total = set.base[set.n];
+    if (pass == 1) ENVG_TRY((launch_k1_pair<false, true>(d, tA, set, flops, bytes)));
+    else ENVG_TRY((launch_k1_pair<false, false>(d, tA, set, flops, bytes)));
+  }
+  SplitReduceSet rs;
+  memset(&rs, 0, sizeof(rs));
+  for (int i = 0; i < n; ++i)
+    if (sp[i] > 1) {
+      const int j = rs.n++;
+      rs.ldp[j] = rup(jobs[i].rows_b, 4);
+      rs.part[j] = reinterpret_cast<const float*>(reinterpret_cast<uint8_t*>(d->part.p) + off[i]);
+      rs.split_elems[j] = Mp * rs.ldp[j];
+      rs.splits[j] = sp[i];
+      rs.silu_gate[j] = jobs[i].gu ? 1 : 0;
+      rs.e[j] = jobs[i].e;
+      rs.base[j + 1] = rs.base[j] + (int64_t)rs.e[j].m_valid * cdiv(rs.e[j].n_out, 4);
+    }
+  if (rs.n) ENVG_TRY(launch_split_reduce(d, rs));
   return ENVG_OK;
 }
 
@@ -866,55 +1011,20 @@ int gemm_device(Dev* d, const void* A, int64_t M, int64_t Kp, const CUtensorMap&
     const K2Job j{A, M, Kp, &b128, rows_b, silu_gate, e, flops, bytes};
     return launch_k2_set(d, &j, 1);
   }
+  if (d->use_pair && M > BM) {
+    PairJob j{&b128, rows_b, silu_gate, e, flops, bytes};
+    return launch_pair_set(d, A, M, Kp, &j, 1);
+  }
   CUtensorMap tA;
   ENVG_TRY(tmap_2d(&tA, A, Kp, M, BM));
   GemmArgs g{};
   g.num_kb = (int)num_kb;
   g.tiles_n = (int)cdiv(rows_b, K1_BN);
   g.group_m = 8;
-  if (d->use_pair && M > BM) {
-    g.tiles_m = (int)cdiv(M, 2 * BM);
-    g.num_tiles = g.tiles_m * g.tiles_n;
-    g.group_m = 4;
-    const int64_t Mp = (int64_t)g.tiles_m * 2 * BM;
-    const int64_t ldp = rup(rows_b, 4);
-    int kbp = 0;
-    int sp = 1;
-    if (e.nremote == 0) ENVG_TRY(pair_splits(d, M, g.num_tiles, g.num_kb, Mp, ldp, &sp, &kbp));
-    if (sp > 1) {
-      // the units store raw partials [sp][Mp][ldp]; k_split_reduce finishes Y
-      ENVG_TRY(ensure(d, d->part, (size_t)(sp * Mp * ldp) * 4));
-      float* part = reinterpret_cast<float*>(d->part.p);
-      CUtensorMap tP;
-      ENVG_TRY(tmap_out_2d(&tP, part, (uint64_t)ldp, (uint64_t)(sp * Mp), (uint64_t)ldp));
-      ENVG_TRY(tmap_out_2d(&g.ybig, part, (uint64_t)ldp, (uint64_t)(sp * Mp), (uint64_t)ldp, 128));
-      g.ybig_ok = 1;
-      g.splits = sp;
-      g.kb_per_split = kbp;
-      g.tiles_per_split = g.num_tiles;
-      g.split_rows = (int)Mp;
-      g.num_tiles *= sp;
-      EpiArgs ep{};
-      ep.Y = part;
-      ep.ldy = ldp;
-      ep.mode = EPI_PLAIN;
-      ep.n_out = (int)ldp;
-      ep.m_valid = (int)(sp * Mp);
-      ep.vec_ok = 1;
-      ep.store_mode = STORE_TMA;
-      g.epi = ep;
-      ENVG_TRY((launch_k1_pair<false, false>(d, tA, b128, tP, g, flops, bytes)));
-      return launch_split_reduce(d, part, ldp, Mp * ldp, sp, silu_gate, e);
-    }
-  }
   CUtensorMap tY;
   memset(&tY, 0, sizeof(tY));
-  ENVG_TRY(choose_store(d->store_tma, e, &tY, &g.pm, (d->use_pair && M > BM) ? &g : nullptr));
+  ENVG_TRY(choose_store(d->store_tma, e, &tY, &g.pm));
   g.epi = e;
-  if (d->use_pair && M > BM) {
-    if (silu_gate) return launch_k1_pair<false, true>(d, tA, b128, tY, g, flops, bytes);
-    return launch_k1_pair<false, false>(d, tA, b128, tY, g, flops, bytes);
-  }
   g.tiles_m = (int)cdiv(M, BM);
   g.num_tiles = g.tiles_m * g.tiles_n;
   if (silu_gate) return launch_k1<false, true>(d, tA, b256, tY, g, flops, bytes);
@@ -1166,6 +1276,7 @@ int envg_init(int ndev, const int* dev_ids) {
   if (const char* s = getenv("ENVG_K1")) d->use_pair = strcmp(s, "single") != 0;
   if (const char* s = getenv("ENVG_STORE")) d->store_tma = strcmp(s, "coalesced") != 0;
   if (const char* s = getenv("ENVG_PIPE")) d->pipe_host = strcmp(s, "0") != 0;
+  if (const char* s = getenv("ENVG_PDL")) d->pdl = strcmp(s, "0") != 0;
   if (const char* s = getenv("ENVG_PAIR_SPLIT")) {
     const int v = atoi(s);
     if (v >= 0 && v <= 64) d->pair_split = v;
@@ -1786,7 +1897,10 @@ int conv_core(Dev* d, envg_weight W, const void* act, float* dy, const float* db
     const double cflops = 2.0 * out_ch * (double)plane * batch * (double)W->K;
     const double cbytes = 2.0 * (double)batch * H * W_ * Cp + 2.0 * out_ch * (double)W->Kp + 4.0 * (double)out_elems +
                           (dbias ? 4.0 * out_ch : 0.0);
-    if (pair) ENVG_TRY(launch_k1_pair<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
+    if (pair) {
+      PairSet set = set_of_one(g, tB, tY);
+      ENVG_TRY((launch_k1_pair<true, false>(d, W->tm128, set, cflops, cbytes)));
+    }
     else ENVG_TRY(launch_k1<true, false>(d, W->tm128, tB, tY, g, cflops, cbytes));
   } else {
     // Strided convolution: explicit bf16 im2col, then one GEMM per image.
@@ -1947,12 +2061,26 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
   std::vector<int> first_use;  // linear index of each copy's first use
   std::vector<size_t> offset;
   size_t total = 0;
+  // true when linear t writes into the fp32 input of linear c
+  auto writes_input_of = [&](int t, const envg_linear_desc& c) {
+    const envg_linear_desc& pr = descs[t];
+    const bool gu = pr.W->layout == ENVG_LAYOUT_GATE_UP;
+    const char* y0 = reinterpret_cast<const char*>(pr.dst);
+    const char* y1 = y0 + (size_t)(pr.M * (gu ? pr.N / 2 : pr.N)) * 4;
+    const char* x0 = reinterpret_cast<const char*>(c.x);
+    const char* x1 = x0 + (size_t)(c.M * c.K) * 4;
+    return pr.M > 0 && x0 < y1 && y0 < x1;
+  };
   for (int i = 0; i < n; ++i) {
     const envg_linear_desc& q = descs[i];
     if (q.M == 0 || q.M <= d->gemv_max) continue;
     for (size_t j = 0; j < first_use.size(); ++j) {
       const envg_linear_desc& p = descs[first_use[j]];
       if (p.x == q.x && p.M == q.M && p.W->Kp == q.W->Kp && p.K == q.K) {
+        // the copy holds x as it was before first_use[j]; reuse it only if nothing since wrote x
+        bool stale = false;
+        for (int t = first_use[j]; t < i && !stale; ++t) stale = writes_input_of(t, q);
+        if (stale) continue;
         src_of[i] = (int)j;
         break;
       }
@@ -2057,6 +2185,30 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     kidx.clear();
     return ENVG_OK;
   };
+  // Consecutive independent linears on the CTA-pair path (M > 128) that read the same bf16
+  // input copy go out as one pair-set launch (launch_pair_set), in the same way.
+  std::vector<PairJob> pq;
+  std::vector<int> pidx;
+  int pair_src = -1;
+  auto flush_pair = [&]() -> int {
+    if (pq.empty()) return ENVG_OK;
+    const envg_linear_desc& f = descs[pidx.front()];
+    ENVG_TRY(launch_pair_set(d, base + offset[pair_src], f.M, f.W->Kp, pq.data(), (int)pq.size()));
+    for (size_t k = 0; k < pidx.size(); ++k) {
+      ENVG_CUDA(cudaEventRecord(batch_event(d, 1 + ncopies + pidx[k]), s));
+      d->st.calls++;
+      d->st.flops += pq[k].flops;
+    }
+    pq.clear();
+    pidx.clear();
+    pair_src = -1;
+    return ENVG_OK;
+  };
+  auto out_range = [&](const envg_linear_desc& c, const char** y0, const char** y1) {
+    const bool gu = c.W->layout == ENVG_LAYOUT_GATE_UP;
+    *y0 = reinterpret_cast<const char*>(c.dst);
+    *y1 = *y0 + (size_t)(c.M * (gu ? c.N / 2 : c.N)) * 4;
+  };
   auto reads_output_of = [&](const envg_linear_desc& c, const envg_linear_desc& pr) {
     const bool gu = pr.W->layout == ENVG_LAYOUT_GATE_UP;
     const char* y0 = reinterpret_cast<const char*>(pr.dst);
@@ -2068,13 +2220,16 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
   for (int i = 0; i < n; ++i) {
     const envg_linear_desc& q = descs[i];
     const bool is_k2 = src_of[i] >= 0 && q.M <= d->skinny_max;
+    const bool is_pair = src_of[i] >= 0 && !is_k2 && d->use_pair && q.M > BM && !ns;
     if (src_of[i] >= 0) ENVG_TRY(flush_gemv());  // a tcgen05 linear follows the pending gemv ones
     if (!is_k2) ENVG_TRY(flush_k2());
+    if (!is_pair) ENVG_TRY(flush_pair());
     // casts run one linear ahead of the GEMMs, in order, as soon as their inputs exist; a cast
     // that reads the output of a linear still waiting in a group waits for that group's launch
     int first_pending = i;
     if (!gidx.empty()) first_pending = std::min(first_pending, gidx.front());
     if (!kidx.empty()) first_pending = std::min(first_pending, kidx.front());
+    if (!pidx.empty()) first_pending = std::min(first_pending, pidx.front());
     while (next_copy < ncopies && first_use[next_copy] <= i + 1 && ready(next_copy, first_pending)) {
       if (fused_from[next_copy] < 0) ENVG_TRY(issue_cast(next_copy));  // else written by its producer on s
       ++next_copy;
@@ -2121,6 +2276,30 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
                          2.0 * (double)q.N * q.K + 2.0 * (double)q.M * q.W->Kp + ob});
       kidx.push_back(i);
       continue;
+    } else if (is_pair) {
+      bool flush = !pq.empty() && (src_of[i] != pair_src || (int)pq.size() == PSET_MAX);
+      const char *qy0, *qy1;
+      out_range(q, &qy0, &qy1);
+      for (int k : pidx) {
+        const char *py0, *py1;
+        out_range(descs[k], &py0, &py1);
+        flush = flush || reads_output_of(q, descs[k]) || (qy0 < py1 && py0 < qy1);
+      }
+      if (flush) ENVG_TRY(flush_pair());
+      if ((size_t)src_of[i] >= next_copy) {
+        // its cast waits for a linear of the pending group: launch the group, then cast
+        ENVG_TRY(flush_pair());
+        while (next_copy < ncopies && first_use[next_copy] <= i + 1 && ready(next_copy, i)) {
+          if (fused_from[next_copy] < 0) ENVG_TRY(issue_cast(next_copy));
+          ++next_copy;
+        }
+        if ((size_t)src_of[i] >= next_copy) return fail(ENVG_ERR_STATE, "envg_linear_batch: internal schedule error");
+      }
+      if (fused_from[src_of[i]] < 0) ENVG_CUDA(cudaStreamWaitEvent(s, batch_event(d, 1 + src_of[i]), 0));
+      pq.push_back(PairJob{&q.W->tm128, q.W->rows, gu, e, fl, 2.0 * (double)q.N * q.K + 2.0 * (double)q.M * q.W->Kp + ob});
+      pidx.push_back(i);
+      pair_src = src_of[i];
+      continue;
     } else {
       ENVG_TRY(flush_gemv());
       if ((size_t)src_of[i] >= next_copy) return fail(ENVG_ERR_STATE, "envg_linear_batch: internal schedule error");
@@ -2134,6 +2313,7 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
   }
   ENVG_TRY(flush_gemv());
   ENVG_TRY(flush_k2());
+  ENVG_TRY(flush_pair());
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
 }

@@ -131,7 +131,8 @@ struct GemmArgs {
 
 // Unit -> (split, tile, K-block range) of a k1_gemm_pair launch; without split-K the unit is
 // the tile and the range is all of K.
-ENVG_DEV void unit_split(int unit, const GemmArgs& a, int& tile, int& split, int& kb0, int& kb1) {
+template <typename Args>
+ENVG_DEV void unit_split(int unit, const Args& a, int& tile, int& split, int& kb0, int& kb1) {
   if (a.splits > 1) {
     split = unit / a.tiles_per_split;
     tile = unit - split * a.tiles_per_split;
@@ -143,6 +144,39 @@ ENVG_DEV void unit_split(int unit, const GemmArgs& a, int& tile, int& split, int
     kb0 = 0;
     kb1 = a.num_kb;
   }
+}
+
+constexpr int PSET_MAX = 4;
+
+// One linear of a k1_gemm_pair launch (fields as in GemmArgs).
+struct PairLin {
+  int num_kb, tiles_m, tiles_n, group_m;
+  int splits, kb_per_split, tiles_per_split, split_rows;
+  int ybig_ok;
+  EpiArgs epi;
+};
+
+// A k1_gemm_pair launch: up to PSET_MAX linears that share the A operand (one activation
+// matrix), walked as one persistent sequence of units; units [base[i], base[i + 1]) belong to
+// linear i.  A convolution is a set of one, with A = its weights and B = the NHWC activations.
+struct PairSet {
+  CUtensorMap tmB[PSET_MAX];   // B operand of each linear
+  CUtensorMap tmY[PSET_MAX];   // output, 32 x 32 boxes (TMA store modes)
+  CUtensorMap ybig[PSET_MAX];  // output, 32 x 128 boxes (last-unit stores, PairLin::ybig_ok)
+  PairLin lin[PSET_MAX];
+  int n, total;
+  int base[PSET_MAX + 1];
+  ConvGeom conv;
+  int* status;
+  uint64_t wait_cap_ns;
+  PeerMaps pm;  // STORE_TMA_PEERS (a set of one)
+};
+
+// Linear of a set that owns `unit`.
+ENVG_DEV int set_linear(const PairSet& set, int unit) {
+  int li = 0;
+  while (li + 1 < set.n && unit >= set.base[li + 1]) ++li;
+  return li;
 }
 
 struct SkinnyArgs {
@@ -418,7 +452,8 @@ ENVG_DEV void epi_store_conv32(const EpiArgs& e, const ConvGeom& g, int b, int o
 
 // Tile order: groups of `group_m` M-tiles sweep all N-tiles, so CTAs that run together share
 // A rows and B rows in L2.
-ENVG_DEV void map_tile(int tile, const GemmArgs& a, int& m_blk, int& n_blk) {
+template <typename Args>
+ENVG_DEV void map_tile(int tile, const Args& a, int& m_blk, int& n_blk) {
   const int group = a.group_m * a.tiles_n;
   const int g = tile / group;
   const int first_m = g * a.group_m;
@@ -748,8 +783,7 @@ struct KPairSmem {
 
 template <int STAGES, bool CONV_B, bool SILU_GATE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
-    k1_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const __grid_constant__ CUtensorMap tmY, const __grid_constant__ GemmArgs args) {
+    k1_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ PairSet set) {
   using L = KPairSmem<STAGES>;
   constexpr int BN = 256;
   constexpr uint32_t IDESC = idesc_bf16_f32(2 * BM, BN);
@@ -794,13 +828,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
-    if (args.epi.store_mode == STORE_TMA || args.epi.store_mode == STORE_TMA_ADD) {
-      tma_prefetch_desc(&tmY);
-      if (args.ybig_ok) tma_prefetch_desc(&args.ybig);
+    for (int i = 0; i < set.n; ++i) {
+      const EpiArgs& e = set.lin[i].epi;
+      tma_prefetch_desc(&set.tmB[i]);
+      if (e.store_mode == STORE_TMA || e.store_mode == STORE_TMA_ADD) {
+        tma_prefetch_desc(&set.tmY[i]);
+        if (set.lin[i].ybig_ok) tma_prefetch_desc(&set.ybig[i]);
+      }
+      if (e.store_mode >= STORE_TMA_PEERS)
+        for (int r = 0; r < e.nremote; ++r) tma_prefetch_desc(&set.pm.m[r]);
     }
-    if (args.epi.store_mode >= STORE_TMA_PEERS)
-      for (int r = 0; r < args.epi.nremote; ++r) tma_prefetch_desc(&args.pm.m[r]);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), L::TMEM_COLS);
@@ -810,31 +847,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const WaitCtl wc{args.wait_cap_ns, args.status, abort_s, 0};
+  const WaitCtl wc{set.wait_cap_ns, set.status, abort_s, 0};
+  // everything above (barriers, TMEM, descriptor prefetch) overlaps the previous kernel's tail
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t ph = 0;
       uint32_t pending = 0, issue_ph = 0;
-      for (int unit = pair; unit < args.num_tiles; unit += npairs) {
+      for (int unit = pair; unit < set.total; unit += npairs) {
+        const int li = set_linear(set, unit);
+        const PairLin& P = set.lin[li];
         int tile, split, kb0, kb1;
-        unit_split(unit, args, tile, split, kb0, kb1);
+        unit_split(unit - set.base[li], P, tile, split, kb0, kb1);
         int m_blk, n_blk;
         int b = 0, h0 = 0, w0 = 0;
         if (CONV_B) {
-          m_blk = tile % args.tiles_m;
-          n_blk = tile / args.tiles_m;
-          const int per_img = args.conv.tiles_w * args.conv.tiles_h;
+          m_blk = tile % P.tiles_m;
+          n_blk = tile / P.tiles_m;
+          const int per_img = set.conv.tiles_w * set.conv.tiles_h;
           b = n_blk / per_img;
           const int r = n_blk - b * per_img;
-          h0 = (r / args.conv.tiles_w) * args.conv.tileH;
-          w0 = (r % args.conv.tiles_w) * args.conv.tileW;
+          h0 = (r / set.conv.tiles_w) * set.conv.tileH;
+          w0 = (r % set.conv.tiles_w) * set.conv.tileW;
           // this CTA's half of the pixel tile: half the rows, or half the row when one row
-          if (args.conv.tileH >= 2) h0 += (int)rank * (args.conv.tileH / 2);
-          else w0 += (int)rank * (args.conv.tileW / 2);
+          if (set.conv.tileH >= 2) h0 += (int)rank * (set.conv.tileH / 2);
+          else w0 += (int)rank * (set.conv.tileW / 2);
         } else {
-          map_tile(tile, args, m_blk, n_blk);
+          map_tile(tile, P, m_blk, n_blk);
         }
         const int m0 = m_blk * 2 * BM + (int)rank * BM;
         const int n0 = n_blk * BN + (int)rank * 128;
@@ -844,14 +886,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
           if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, 2 * L::STAGE_BYTES);
           tma_load_2d_pair(smem_u32(sA + stage * TILE_A_BYTES), &tmA, fb, kb * BK, m0);
           if (CONV_B) {
-            const int kpos = kb / args.conv.cblocks;
-            const int cb = kb - kpos * args.conv.cblocks;
-            const int kh = kpos / args.conv.KW;
-            const int kw = kpos - kh * args.conv.KW;
-            tma_load_4d_pair(smem_u32(sB + stage * L::HALF_B_BYTES), &tmB, fb, cb * BK, w0 + kw - args.conv.pad,
-                             h0 + kh - args.conv.pad, b);
+            const int kpos = kb / set.conv.cblocks;
+            const int cb = kb - kpos * set.conv.cblocks;
+            const int kh = kpos / set.conv.KW;
+            const int kw = kpos - kh * set.conv.KW;
+            tma_load_4d_pair(smem_u32(sB + stage * L::HALF_B_BYTES), &set.tmB[li], fb, cb * BK,
+                             w0 + kw - set.conv.pad, h0 + kh - set.conv.pad, b);
           } else {
-            tma_load_2d_pair(smem_u32(sB + stage * L::HALF_B_BYTES), &tmB, fb, kb * BK, n0);
+            tma_load_2d_pair(smem_u32(sB + stage * L::HALF_B_BYTES), &set.tmB[li], fb, kb * BK, n0);
           }
           pending |= 1u << stage;
           issue_ph = (issue_ph & ~(1u << stage)) | (ph << stage);
@@ -865,7 +907,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       if (*abort_s && pending) {
         if (leader) {
           for (int s = 0; s < STAGES; ++s)
-            if (pending & (1u << s)) wait_drain(full0 + 8 * s, (issue_ph >> s) & 1u, args.wait_cap_ns);
+            if (pending & (1u << s)) wait_drain(full0 + 8 * s, (issue_ph >> s) & 1u, set.wait_cap_ns);
         } else {
           // The odd CTA's copies signal the even CTA's barriers; give them time to land.
           const uint64_t t0 = globaltimer_ns();
@@ -880,9 +922,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       uint32_t ph = 0;
       int acc = 0;
       uint32_t aph = 0;
-      for (int unit = pair; unit < args.num_tiles; unit += npairs) {
+      for (int unit = pair; unit < set.total; unit += npairs) {
+        const int li = set_linear(set, unit);
         int tile, split, kb0, kb1;
-        unit_split(unit, args, tile, split, kb0, kb1);
+        unit_split(unit - set.base[li], set.lin[li], tile, split, kb0, kb1);
         if (!wait_bounded(tempty0 + 8 * acc, aph ^ 1, wc, 22)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -911,34 +954,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       }
       if (*abort_s) {
         umma_commit_pair(drain);
-        wait_drain(drain, 0, args.wait_cap_ns);
+        wait_drain(drain, 0, set.wait_cap_ns);
       }
     }
   } else {
     const int q = warp & 3;
-    const int smode = args.epi.store_mode;
-    // A reference into the (grid-constant) parameter space: a local copy would be placed in local
-    // memory, because the peer stores index ep.remote[] at run time.
-    const EpiArgs& ep = args.epi;
+    bool any_remote = false;
     uint8_t* stg = sStage + (warp - 2) * 8192;
     int sb = 0;
     int acc = 0;
     uint32_t aph = 0;
-    for (int unit = pair; unit < args.num_tiles; unit += npairs) {
+    for (int unit = pair; unit < set.total; unit += npairs) {
+      const int li = set_linear(set, unit);
+      const PairLin& P = set.lin[li];
+      // A reference into the (grid-constant) parameter space: a local copy would be placed in
+      // local memory, because the peer stores index ep.remote[] at run time.
+      const EpiArgs& ep = P.epi;
+      const int smode = ep.store_mode;
+      any_remote = any_remote || ep.nremote != 0;
       int tile, split, kb0, kb1;
-      unit_split(unit, args, tile, split, kb0, kb1);
+      unit_split(unit - set.base[li], P, tile, split, kb0, kb1);
       int m_blk, n_blk;
       int b = 0, h0 = 0, w0 = 0;
       if (CONV_B) {
-        m_blk = tile % args.tiles_m;
-        n_blk = tile / args.tiles_m;
-        const int per_img = args.conv.tiles_w * args.conv.tiles_h;
+        m_blk = tile % P.tiles_m;
+        n_blk = tile / P.tiles_m;
+        const int per_img = set.conv.tiles_w * set.conv.tiles_h;
         b = n_blk / per_img;
         const int r = n_blk - b * per_img;
-        h0 = (r / args.conv.tiles_w) * args.conv.tileH;
-        w0 = (r % args.conv.tiles_w) * args.conv.tileW;
+        h0 = (r / set.conv.tiles_w) * set.conv.tileH;
+        w0 = (r % set.conv.tiles_w) * set.conv.tileW;
       } else {
-        map_tile(tile, args, m_blk, n_blk);
+        map_tile(tile, P, m_blk, n_blk);
       }
       if (!wait_bounded_warp(tfull0 + 8 * acc, aph, wc, 24)) break;
       tc_fence_after();
@@ -952,11 +999,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       // unit with one proxy fence and issues every store back to back: the tail of the launch
       // is one pass over TMEM and the store drain, with no per-chunk fence or buffer wait.
       static_assert(L::RING_BYTES / 4 >= NCHUNK * 4096 && (L::RING_BYTES / 4) % 1024 == 0, "ring staging");
-      const bool ring_mode = unit + npairs >= args.num_tiles && smode != STORE_COALESCED && smode != STORE_DIRECT;
+      const bool ring_mode = unit + npairs >= set.total && smode != STORE_COALESCED && smode != STORE_DIRECT;
       // With the 128-row map, the four warps' 32 x 32 tiles of chunk c sit one above the other
       // (rows q * 32 ..) in a 16 KB box, and one thread stores each chunk of the CTA's 128 rows:
       // a quarter of the TMA stores, each four times larger.
-      const bool big = ring_mode && args.ybig_ok && (smode == STORE_TMA || smode == STORE_TMA_ADD);
+      const bool big = ring_mode && P.ybig_ok && (smode == STORE_TMA || smode == STORE_TMA_ADD);
       static_assert(L::RING_BYTES >= NCHUNK * 16384, "ring staging, 128-row boxes");
       uint8_t* ring = big ? smem + q * 4096 : smem + (warp - 2) * (L::RING_BYTES / 4);
       const int ring_stride = big ? 16384 : 4096;
@@ -964,28 +1011,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       auto chunk_xy = [&](int c, int& x, int& y) -> bool {
         if (CONV_B) {
           const int jj = c * 32;
-          const int w = w0 + jj % args.conv.tileW;
-          const int h = h0 + jj / args.conv.tileW;
-          x = h * args.conv.outW + w;
+          const int w = w0 + jj % set.conv.tileW;
+          const int h = h0 + jj / set.conv.tileW;
+          x = h * set.conv.outW + w;
           y = row0;
-          return w < args.conv.outW;
+          return w < set.conv.outW;
         }
         x = n_blk * (SILU_GATE ? BN / 2 : BN) + c * 32;
-        y = row0 + split * args.split_rows;
+        y = row0 + split * P.split_rows;
         return true;
       };
       auto issue_store = [&](const uint8_t* buf, int x, int y) {
         if (CONV_B) {
-          if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&tmY, smem_u32(buf), x, y, b);
-          else tma_store_3d(&tmY, smem_u32(buf), x, y, b);
+          if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&set.tmY[li], smem_u32(buf), x, y, b);
+          else tma_store_3d(&set.tmY[li], smem_u32(buf), x, y, b);
         } else if (smode == STORE_TMA_PEERS) {
-          for (int r = 0; r < ep.nremote; ++r) tma_store_2d(&args.pm.m[r], smem_u32(buf), x, y);
+          for (int r = 0; r < ep.nremote; ++r) tma_store_2d(&set.pm.m[r], smem_u32(buf), x, y);
         } else if (smode == STORE_TMA_ADD_PEERS) {
-          for (int r = 0; r < ep.nremote; ++r) tma_reduce_add_2d(&args.pm.m[r], smem_u32(buf), x, y);
+          for (int r = 0; r < ep.nremote; ++r) tma_reduce_add_2d(&set.pm.m[r], smem_u32(buf), x, y);
         } else if (smode == STORE_TMA_ADD) {
-          tma_reduce_add_2d(&tmY, smem_u32(buf), x, y);
+          tma_reduce_add_2d(&set.tmY[li], smem_u32(buf), x, y);
         } else {
-          tma_store_2d(&tmY, smem_u32(buf), x, y);
+          tma_store_2d(&set.tmY[li], smem_u32(buf), x, y);
         }
       };
 #pragma unroll 1
@@ -1012,7 +1059,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
             e2.act = 0;
             epi_store_row32(e2, row, col0, v);
           } else if (CONV_B) {
-            epi_store_conv32(ep, args.conv, b, row, h0, w0, c * 32, v);
+            epi_store_conv32(ep, set.conv, b, row, h0, w0, c * 32, v);
           } else {
             epi_store_row32(ep, row, col0, v);
           }
@@ -1039,8 +1086,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
           __syncwarp();
           if (CONV_B) {
             const int jj = c * 32;
-            store_tile32_conv(ep, args.conv, buf, lane, row0, b, h0 + jj / args.conv.tileW,
-                              w0 + jj % args.conv.tileW);
+            store_tile32_conv(ep, set.conv, buf, lane, row0, b, h0 + jj / set.conv.tileW,
+                              w0 + jj % set.conv.tileW);
           } else {
             store_tile32_rows(ep, buf, lane, row0, col0);
           }
@@ -1074,12 +1121,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
               y -= q * 32;  // the CTA's first row
               const uint32_t src = smem_u32(smem + c * 16384);
               if (CONV_B) {
-                if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&args.ybig, src, x, y, b);
-                else tma_store_3d(&args.ybig, src, x, y, b);
+                if (smode == STORE_TMA_ADD) tma_reduce_add_3d(&set.ybig[li], src, x, y, b);
+                else tma_store_3d(&set.ybig[li], src, x, y, b);
               } else if (smode == STORE_TMA_ADD) {
-                tma_reduce_add_2d(&args.ybig, src, x, y);
+                tma_reduce_add_2d(&set.ybig[li], src, x, y);
               } else {
-                tma_store_2d(&args.ybig, src, x, y);
+                tma_store_2d(&set.ybig[li], src, x, y);
               }
             }
             bulk_commit();
@@ -1099,7 +1146,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       if (acc == 0) aph ^= 1;
     }
     if (lane == 0) bulk_wait_all();
-    if (ep.nremote != 0) __threadfence_system();  // peer / multicast stores ordered before the caller's barrier
+    if (any_remote) __threadfence_system();  // peer / multicast stores ordered before the caller's barrier
   }
   __syncwarp();
   tc_fence_before();
@@ -1140,20 +1187,40 @@ ENVG_DEV float4 split_sum4(const float* __restrict__ part, int64_t off, int64_t 
   return a;
 }
 
-template <bool SILU_GATE>
-__global__ void __launch_bounds__(256) k_split_reduce(const float* __restrict__ part, int64_t ldp,
-                                                      int64_t split_elems, int splits, const EpiArgs e) {
-  const int quads = (e.n_out + 3) >> 2;
-  const int64_t total = (int64_t)e.m_valid * quads;
+// The split linears of one launch_pair_set call, reduced by one launch: work items (one row and
+// four output columns each) [base[i], base[i + 1]) belong to linear i.
+struct SplitReduceSet {
+  const float* part[PSET_MAX];
+  int64_t ldp[PSET_MAX], split_elems[PSET_MAX];
+  int splits[PSET_MAX];
+  int silu_gate[PSET_MAX];
+  EpiArgs e[PSET_MAX];
+  int64_t base[PSET_MAX + 1];
+  int n;
+};
+
+__global__ void __launch_bounds__(256) k_split_reduce(const __grid_constant__ SplitReduceSet rs) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int64_t total = rs.base[rs.n];
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-    const int row = (int)(t / quads);
-    const int col = (int)(t - (int64_t)row * quads) * 4;
+    int li = 0;
+    while (li + 1 < rs.n && t >= rs.base[li + 1]) ++li;
+    const EpiArgs& e = rs.e[li];
+    const float* part = rs.part[li];
+    const int64_t ldp = rs.ldp[li], split_elems = rs.split_elems[li];
+    const int splits = rs.splits[li];
+    const int quads = (e.n_out + 3) >> 2;
+    const int64_t u = t - rs.base[li];
+    const int row = (int)(u / quads);
+    const int col = (int)(u - (int64_t)row * quads) * 4;
+    const bool silu_gate = rs.silu_gate[li] != 0;
     float v[4];
-    if (SILU_GATE) {
+    if (silu_gate) {
       const int64_t pg = (int64_t)row * ldp + (col >> 7) * 256 + (col & 127);
       const float4 g = split_sum4(part, pg, split_elems, splits);
-      const float4 u = split_sum4(part, pg + 128, split_elems, splits);
-      const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+      const float4 up = split_sum4(part, pg + 128, split_elems, splits);
+      const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {up.x, up.y, up.z, up.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c = min(col + j, e.n_out - 1);
@@ -1168,26 +1235,25 @@ __global__ void __launch_bounds__(256) k_split_reduce(const float* __restrict__ 
       v[2] = a.z;
       v[3] = a.w;
     }
-    EpiArgs e2 = e;
-    if (SILU_GATE) {
-      e2.bias_mode = 0;
-      e2.act = 0;
-    }
     const int64_t idx = (int64_t)row * e.ldy + e.col_off + col;
     const bool rmw = e.mode == EPI_GATED_RES || (e.mode == EPI_ALPHA_BETA && e.beta != 0.0f);
+    // the SiLU gate already holds its bias; epi_value then adds nothing (mode SILU_GATE)
+    const bool plain = silu_gate;
     if (e.vec_ok && col + 3 < e.n_out) {
       float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
       if (rmw) old = *reinterpret_cast<const float4*>(e.Y + idx);
-      v[0] = epi_value(e2, v[0], row, col + 0, &old.x);
-      v[1] = epi_value(e2, v[1], row, col + 1, &old.y);
-      v[2] = epi_value(e2, v[2], row, col + 2, &old.z);
-      v[3] = epi_value(e2, v[3], row, col + 3, &old.w);
+      if (!plain) {
+        v[0] = epi_value(e, v[0], row, col + 0, &old.x);
+        v[1] = epi_value(e, v[1], row, col + 1, &old.y);
+        v[2] = epi_value(e, v[2], row, col + 2, &old.z);
+        v[3] = epi_value(e, v[3], row, col + 3, &old.w);
+      }
       out_store4(e, idx, make_float4(v[0], v[1], v[2], v[3]));
     } else {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (col + j >= e.n_out) break;
-        v[j] = epi_value(e2, v[j], row, col + j, e.Y + idx + j);
+        if (!plain) v[j] = epi_value(e, v[j], row, col + j, e.Y + idx + j);
         out_store1(e, idx + j, v[j]);
       }
     }
@@ -1528,6 +1594,8 @@ __global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const WaitCtl wc{S.wait_cap_ns, S.status, abort_s, 0};
+  griddep_wait();  // the prologue above overlaps the previous kernel's tail
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -1772,6 +1840,8 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
   __shared__ float s_sum[MT][64];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
   for (int u = blockIdx.x; u < set.total; u += gridDim.x) {
   int l = 0;
   while (l + 1 < set.n && u >= set.base[l + 1]) ++l;
@@ -1902,6 +1972,8 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
 // X fp32 [rows][K] (row stride ldx) -> Xb bf16 [rows][Kp] with zeros in [K, Kp).  RNE.
 __global__ void k_cast_rows(const float* __restrict__ X, int64_t ldx, int rows, int K, int Kp,
                             __nv_bfloat16* __restrict__ Xb, int vec8) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if (vec8 == 2) {
@@ -1977,6 +2049,8 @@ __global__ void __launch_bounds__(256) k_transpose_cast(const float* __restrict_
                                                         int64_t dbs, int Rp, const float2* __restrict__ aff,
                                                         int act) {
   __shared__ float t[64][33];
+  griddep_wait();
+  griddep_launch_dependents();
   const int c0 = blockIdx.x * 32;
   const int r0 = blockIdx.y * 64;
   const int b = blockIdx.z;
@@ -2018,6 +2092,8 @@ __global__ void __launch_bounds__(256) k_transpose_cast_v(const float* __restric
                                                           int R, int C, __nv_bfloat16* __restrict__ dst, int64_t ldd,
                                                           int64_t dbs, int Rp, const float2* __restrict__ aff, int act) {
   __shared__ float t[64][65];
+  griddep_wait();
+  griddep_launch_dependents();
   const int c0 = blockIdx.x * 64;
   const int r0 = blockIdx.y * 64;
   const int b = blockIdx.z;
@@ -2120,6 +2196,8 @@ __global__ void __launch_bounds__(256) k_adaln(const float* __restrict__ X, int6
                                                const float* __restrict__ shift, const float* __restrict__ scale,
                                                float eps, void* out, int out_bf16) {
   __shared__ float red[9];
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t r = blockIdx.x;
   const float* xr = X + r * ldx;
   float s = 0.0f;

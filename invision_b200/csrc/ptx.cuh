@@ -113,6 +113,12 @@ ENVG_DEV void tma_load_4d(uint32_t dst, const void* desc, uint32_t bar, int c0, 
 
 // Bulk tensor stores from shared memory (one elected thread issues; completion tracked with
 // bulk groups).  The tile must have been written with the tensor map's swizzle.
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may
+// start while the previous kernel of its stream finishes; griddep_wait blocks until that kernel
+// has completed and its memory is visible (a no-op for a normal launch), and
+// griddep_launch_dependents lets the next such kernel start its own prologue early.
+ENVG_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+ENVG_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 ENVG_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 ENVG_DEV void tma_store_2d(const void* desc, uint32_t src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(

@@ -164,3 +164,67 @@ def test_forced_split_counts_in_subprocess():
         r = subprocess.run([sys.executable, "-c", code], env={**os.environ, "ENVG_PAIR_SPLIT": n},
                            capture_output=True, text=True, timeout=300)
         assert r.returncode == 0 and "ok" in r.stdout, f"ENVG_PAIR_SPLIT={n}: " + r.stderr[-3000:]
+
+
+def test_pair_set_batch_equals_separate_calls(gpu):
+    """Qwen3's q, k, v and a gate_up on one input at M = 512 go out as pair-set launches (k and v
+    split K, q does not; the SiLU-gate linear needs the other kernel variant), plus a gated
+    residual on the same input: every output equals its separate call bit for bit."""
+    import torch
+
+    dev = "cuda"
+    M, H = 512, 2560
+    ws = {"q": _weight(4096, H, 11), "k": _weight(1024, H, 12), "v": _weight(1024, H, 13),
+          "gu": _weight(2 * 1536, H, 14), "r": _weight(768, H, 15)}
+    W = {k: gpu.Weight(v, layout=gpu.LAYOUT_GATE_UP if k == "gu" else gpu.LAYOUT_PLAIN) for k, v in ws.items()}
+    g = torch.Generator(device=dev).manual_seed(21)
+    x = torch.randn(M, H, generator=g, device=dev)
+    b = 0.01 * torch.randn(4096, generator=g, device=dev)
+    gate = torch.randn(768, generator=g, device=dev)
+    h0 = torch.randn(M, 768, generator=g, device=dev)
+    outs = {"q": torch.empty(M, 4096, device=dev), "k": torch.empty(M, 1024, device=dev),
+            "v": torch.empty(M, 1024, device=dev), "gu": torch.empty(M, 1536, device=dev), "r": h0.clone()}
+    calls = [dict(dst=outs["q"], x=x, W=W["q"], bias=b), dict(dst=outs["k"], x=x, W=W["k"]),
+             dict(dst=outs["v"], x=x, W=W["v"]), dict(dst=outs["gu"], x=x, W=W["gu"]),
+             dict(dst=outs["r"], x=x, W=W["r"], epilogue=gpu.EPI_GATED_RESIDUAL, gate=gate)]
+    gpu.linear_batch(calls)
+    torch.cuda.synchronize()
+    got = {k: v.clone() for k, v in outs.items()}
+    outs["r"].copy_(h0)
+    for c in calls:
+        kw = {k: c[k] for k in ("bias", "epilogue", "gate") if k in c}
+        gpu.linear(c["dst"], c["x"], c["W"], **kw)
+    torch.cuda.synchronize()
+    for k in outs:
+        assert torch.equal(got[k], outs[k]), k
+    ref = O.linear_bf16(x[:16].cpu().numpy(), ws["k"], path=O.PATH_AVX2)
+    assert_parity(got["k"][:16].cpu().numpy(), ref, what="pair set k, 16 rows")
+    for w in W.values():
+        w.free()
+
+
+def test_batch_rereads_an_input_that_an_earlier_linear_overwrote(gpu):
+    """[y1 = x W1; x = h W2; y3 = x W3]: the third linear reads x after the second rewrote it, so
+    it must not reuse the bf16 copy made for the first (equal to three separate calls)."""
+    import torch
+
+    dev = "cuda"
+    M, K = 300, 512
+    w1, w2, w3 = _weight(640, K, 31), _weight(K, 384, 32), _weight(256, K, 33)
+    W1, W2, W3 = gpu.Weight(w1), gpu.Weight(w2), gpu.Weight(w3)
+    g = torch.Generator(device=dev).manual_seed(5)
+    x0 = torch.randn(M, K, generator=g, device=dev)
+    h = torch.randn(M, 384, generator=g, device=dev)
+    x = x0.clone()
+    y1, y3 = torch.empty(M, 640, device=dev), torch.empty(M, 256, device=dev)
+    gpu.linear_batch([dict(dst=y1, x=x, W=W1), dict(dst=x, x=h, W=W2), dict(dst=y3, x=x, W=W3)])
+    torch.cuda.synchronize()
+    xr = x0.clone()
+    r1, r3 = torch.empty_like(y1), torch.empty_like(y3)
+    gpu.linear(r1, xr, W1)
+    gpu.linear(xr, h, W2)
+    gpu.linear(r3, xr, W3)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, r1) and torch.equal(x, xr) and torch.equal(y3, r3)
+    for w in (W1, W2, W3):
+        w.free()
