@@ -117,8 +117,10 @@ enum KernelId {
   KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_ATTN, KID_CAST_HEADS, KID_KEY_BITS, KID_ABSMAX,
   KID_SPLIT_REDUCE, KID_COUNT
 };
+// Profile names are per family: "k1_gemm*" counts k1_gemm and k1_gemm_pair launches (plain,
+// SiLU-gate, conv), "k2_set" counts k2_set and the no-alloc path's k2_skinny.
 const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate", "k1_gemm_conv",
-                                             "k2_skinny",   "k_gemv",            "k_cast_rows",
+                                             "k2_set",      "k_gemv",            "k_cast_rows",
                                              "k_adaln",     "k_transpose_cast",  "k_im2col_nhwc",
                                              "k_wait_selftest", "k_group_stats",     "k_group_affine",
                                              "k_group_apply",   "k_attention",       "k_cast_heads",
@@ -425,7 +427,9 @@ int sync_and_check(Dev* d) {
 
 // Launch on the library stream.  With programmatic stream serialization (Dev::pdl) the kernel may
 // start while the previous kernel of the stream finishes: every kernel launched this way calls
-// griddep_wait before its first global memory access, so only its prologue overlaps.
+// griddep_wait before its first global memory access, so only its prologue overlaps.  While
+// per-launch timing (envg_profile) is on, launches are plainly serialized, so that each kernel's
+// events bracket that kernel alone and not its wait for the previous one.
 template <typename... KArgs, typename... Args>
 int launch_pdl(Dev* d, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -437,7 +441,7 @@ int launch_pdl(Dev* d, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = d->pdl ? 1 : 0;
+  cfg.numAttrs = (d->pdl && !g_prof_on) ? 1 : 0;
   ENVG_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
   return ENVG_OK;
 }
