@@ -585,7 +585,8 @@ def run_ours(args, items, desc, world, rank, local):
         p = envg.profile_read()
         envg.profile(False)
         main = {k: v for k, v in p.items()
-                if k.startswith("k1") or k.startswith("k2") or k in ("k_gemv", "k_attention", "k_split_reduce")}
+                if k.startswith("k1") or k.startswith("k2") or
+                k in ("k_gemv", "k_attention", "k_split_reduce", "k_skinny_reduce")}
         mms = sum(v["ms"] for v in main.values()) / reps
         mbytes = sum(v["bytes"] for v in main.values()) / reps
         rank_flops = item_flops(it) / (world if it["op"] == "linear" else 1)  # this rank's shard

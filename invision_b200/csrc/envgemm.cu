@@ -115,7 +115,7 @@ int g_cur = -1;
 enum KernelId {
   KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_ADALN, KID_TRANSPOSE, KID_IM2COL,
   KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_ATTN, KID_CAST_HEADS, KID_KEY_BITS, KID_ABSMAX,
-  KID_SPLIT_REDUCE, KID_COUNT
+  KID_SPLIT_REDUCE, KID_SKINNY_REDUCE, KID_COUNT
 };
 // Profile names are per family: "k1_gemm*" counts k1_gemm and k1_gemm_pair launches (plain,
 // SiLU-gate, conv), "k2_set" counts k2_set and the no-alloc path's k2_skinny.
@@ -124,7 +124,8 @@ const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate",
                                              "k_adaln",     "k_transpose_cast",  "k_im2col_nhwc",
                                              "k_wait_selftest", "k_group_stats",     "k_group_affine",
                                              "k_group_apply",   "k_attention",       "k_cast_heads",
-                                             "k_key_bits",      "k_absmax_heads",    "k_split_reduce"};
+                                             "k_key_bits",      "k_absmax_heads",    "k_split_reduce",
+                                             "k_skinny_reduce"};
 struct KAcc {
   uint64_t launches = 0;
   double ms = 0, flops = 0, bytes = 0;
@@ -609,8 +610,9 @@ void k2_plan(const Dev* d, int64_t rows_b, int64_t Kp, bool gu, SkinnyArgs& s) {
   s.splits = (int)cdiv(num_kb, s.kb_per_split);
 }
 
+// k2_set over the set, then (when a linear splits K) k_skinny_reduce over its split linears.
 template <int MPAD, int R>
-int launch_k2_set_t(Dev* d, K2Set& S, double flops, double bytes) {
+int launch_k2_set_t(Dev* d, K2Set& S, const SkinnyReduceSet& rs, double flops, double bytes) {
   constexpr int STAGE = K2SetSmem<MPAD, R, 1>::STAGE_BYTES;
   constexpr int ST = (110 * 1024) / STAGE < 2 ? 2 : (110 * 1024) / STAGE;  // two CTAs per SM
   using L = K2SetSmem<MPAD, R, ST>;
@@ -623,9 +625,20 @@ int launch_k2_set_t(Dev* d, K2Set& S, double flops, double bytes) {
   S.status = d->d_status;
   S.wait_cap_ns = d->wait_cap_ns;
   const int grid = std::min(S.total, 2 * d->sms);
-  ProfScope ps(stream_of(d), KID_K2, flops, bytes);
-  ENVG_TRY(launch_pdl(d, kern, dim3(grid), dim3(K1_THREADS), L::TOTAL, S));
-  d->st.kernel_launches++;
+  {
+    ProfScope ps(stream_of(d), KID_K2, flops, bytes);
+    ENVG_TRY(launch_pdl(d, kern, dim3(grid), dim3(K1_THREADS), L::TOTAL, S));
+    d->st.kernel_launches++;
+  }
+  if (rs.n) {
+    double rb = 0.0;
+    for (int i = 0; i < rs.n; ++i)
+      rb += 16.0 * R * (double)(rs.base[i + 1] - rs.base[i]) * rs.splits[i] +
+            4.0 * (double)rs.e[i].m_valid * rs.e[i].n_out;
+    ProfScope ps(stream_of(d), KID_SKINNY_REDUCE, 0.0, rb);
+    ENVG_TRY(launch_pdl(d, k_skinny_reduce<MPAD, R>, dim3((unsigned)cdiv(rs.base[rs.n], 256)), dim3(256), 0, rs));
+    d->st.kernel_launches++;
+  }
   return ENVG_OK;
 }
 
@@ -637,8 +650,8 @@ int launch_k2_set(Dev* d, const K2Job* jobs, int n) {
   const int mpad = (int)rup(std::max<int64_t>(jobs[0].M, 1), 16);
   K2Set S{};
   S.n = n;
-  size_t part_off = 0, cnt_off = 0;
-  std::vector<size_t> po(n), co(n);
+  size_t part_off = 0;
+  std::vector<size_t> po(n);
   double flops = 0.0, bytes = 0.0;
   for (int i = 0; i < n; ++i) {
     const K2Job& q = jobs[i];
@@ -653,40 +666,38 @@ int launch_k2_set(Dev* d, const K2Job* jobs, int n) {
     S.base[i] = S.total;
     S.total += L.s.n_tiles * L.s.splits;
     po[i] = part_off;
-    co[i] = cnt_off;
-    if (L.s.splits > 1) {
-      part_off += (size_t)L.s.n_tiles * L.s.splits * L.R * BM * mpad * sizeof(float);
-      cnt_off += (size_t)rup(L.s.n_tiles, 64) * sizeof(int);
-    }
+    if (L.s.splits > 1) part_off += (size_t)L.s.n_tiles * L.s.splits * L.R * BM * mpad * sizeof(float);
     flops += q.flops;
     bytes += q.bytes;
   }
   S.base[n] = S.total;
+  SkinnyReduceSet rs;
+  memset(&rs, 0, sizeof(rs));
   if (part_off) {
     ENVG_TRY(ensure(d, d->part, part_off));
-    ENVG_TRY(ensure(d, d->cnt, cnt_off, true));
     for (int i = 0; i < n; ++i)
       if (S.lin[i].s.splits > 1) {
         S.lin[i].s.partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d->part.p) + po[i]);
-        S.lin[i].s.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(d->cnt.p) + co[i]);
+        const int j = rs.n++;
+        rs.partial[j] = S.lin[i].s.partial;
+        rs.splits[j] = S.lin[i].s.splits;
+        rs.e[j] = S.lin[i].s.epi;
+        rs.base[j + 1] = rs.base[j] + S.lin[i].s.n_tiles * BM * (mpad / 4);
       }
   }
-  if (!jobs[0].gu) {
-    switch (mpad) {
-      case 16: return launch_k2_set_t<16, 1>(d, S, flops, bytes);
-      case 32: return launch_k2_set_t<32, 1>(d, S, flops, bytes);
-      case 48: return launch_k2_set_t<48, 1>(d, S, flops, bytes);
-      case 64: return launch_k2_set_t<64, 1>(d, S, flops, bytes);
-    }
-  } else {
-    switch (mpad) {
-      case 16: return launch_k2_set_t<16, 2>(d, S, flops, bytes);
-      case 32: return launch_k2_set_t<32, 2>(d, S, flops, bytes);
-      case 48: return launch_k2_set_t<48, 2>(d, S, flops, bytes);
-      case 64: return launch_k2_set_t<64, 2>(d, S, flops, bytes);
-    }
+  const bool gu = jobs[0].gu;
+  switch (mpad * 2 + (gu ? 1 : 0)) {
+    case 32: ENVG_TRY((launch_k2_set_t<16, 1>(d, S, rs, flops, bytes))); break;
+    case 64: ENVG_TRY((launch_k2_set_t<32, 1>(d, S, rs, flops, bytes))); break;
+    case 96: ENVG_TRY((launch_k2_set_t<48, 1>(d, S, rs, flops, bytes))); break;
+    case 128: ENVG_TRY((launch_k2_set_t<64, 1>(d, S, rs, flops, bytes))); break;
+    case 33: ENVG_TRY((launch_k2_set_t<16, 2>(d, S, rs, flops, bytes))); break;
+    case 65: ENVG_TRY((launch_k2_set_t<32, 2>(d, S, rs, flops, bytes))); break;
+    case 97: ENVG_TRY((launch_k2_set_t<48, 2>(d, S, rs, flops, bytes))); break;
+    case 129: ENVG_TRY((launch_k2_set_t<64, 2>(d, S, rs, flops, bytes))); break;
+    default: return fail(ENVG_ERR_ARG, "skinny path: unsupported padded M %d", mpad);
   }
-  return fail(ENVG_ERR_ARG, "skinny path: unsupported padded M %d", mpad);
+  return ENVG_OK;
 }
 
 // M <= 8 linear on CUDA cores straight from fp32 X (no cast).

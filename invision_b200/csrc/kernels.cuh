@@ -1557,7 +1557,6 @@ __global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ 
   uint64_t* bars = reinterpret_cast<uint64_t*>(sX + STAGES * L::X_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBARS);
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_s = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1578,7 +1577,6 @@ __global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ 
     }
     mbar_init(drain, 1);
     *abort_s = 0;
-    *last_s = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane < S.n) {
@@ -1713,9 +1711,8 @@ __global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ 
       if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
       acc ^= 1;
       if (acc == 0) aph ^= 1;
-      bool finalize = true;
       if (a.splits > 1) {
-        // every split stores its partial; the CTA that arrives last sums them in split order
+        // a split stores its partial; k_skinny_reduce sums a tile's partials in split order
         for (int r = 0; r < R; ++r) {
           float* p = a.partial + ((((int64_t)tile * a.splits + split) * R + r) * BM + rowin) * MPAD;
 #pragma unroll
@@ -1723,37 +1720,9 @@ __global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ 
             __stcg(reinterpret_cast<float4*>(p + m),
                    make_float4(accv[r][m], accv[r][m + 1], accv[r][m + 2], accv[r][m + 3]));
         }
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (et == 0) {
-          const int old = atomicAdd(a.counters + tile, 1);
-          *last_s = (old == a.splits - 1) ? 1 : 0;
-        }
-        named_bar_sync(1, 128);
-        finalize = (*last_s != 0);
-        named_bar_sync(1, 128);  // every thread has read last_s before a later unit rewrites it
-        if (finalize) {
-          __threadfence();
-          for (int r = 0; r < R; ++r) {
-#pragma unroll
-            for (int m = 0; m < MPAD; ++m) accv[r][m] = 0.0f;
-#pragma unroll 4
-            for (int sp = 0; sp < a.splits; ++sp) {
-              const float* p = a.partial + ((((int64_t)tile * a.splits + sp) * R + r) * BM + rowin) * MPAD;
-#pragma unroll
-              for (int m = 0; m < MPAD; m += 4) {
-                const float4 t = __ldcg(reinterpret_cast<const float4*>(p + m));
-                accv[r][m] += t.x;
-                accv[r][m + 1] += t.y;
-                accv[r][m + 2] += t.z;
-                accv[r][m + 3] += t.w;
-              }
-            }
-          }
-          if (et == 0) a.counters[tile] = 0;  // re-arm for the next launch
-        }
+        continue;
       }
-      if (finalize) {
+      {
         const EpiArgs& e = a.epi;
         const int col = tile * BM + rowin;  // output column (shard-relative)
         if (col < e.n_out) {
@@ -1787,6 +1756,83 @@ __global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ 
     tc_fence_after();
     tmem_dealloc(tmem_base, L::TMEM_COLS);
   }
+}
+
+// Split-K finish of a k2_set launch: one thread per four outputs (four tokens m of one output
+// column, i.e. of one W row of a 128-row tile) of each split linear.  It loads up to eight
+// splits' partials at once and adds them in split order, from 0, as one CTA would, then applies
+// the linear's epilogue.  Work items [base[i], base[i + 1]) belong to linear i:
+// n_tiles * 128 * MPAD / 4 of them, the four tokens fastest (the partials' layout).
+struct SkinnyReduceSet {
+  const float* partial[K2S_MAX_LIN];  // [tile][split][R][128][MPAD]
+  int splits[K2S_MAX_LIN];
+  EpiArgs e[K2S_MAX_LIN];
+  int base[K2S_MAX_LIN + 1];
+  int n;
+};
+
+template <int MPAD, int R>
+__global__ void __launch_bounds__(256) k_skinny_reduce(const __grid_constant__ SkinnyReduceSet rs) {
+  griddep_wait();
+  griddep_launch_dependents();
+  constexpr int Q = MPAD / 4;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= rs.base[rs.n]) return;
+  int li = 0;
+  while (li + 1 < rs.n && t >= rs.base[li + 1]) ++li;
+  const int v = t - rs.base[li];
+  const int quad = v % Q, rv = v / Q;
+  const int tile = rv / BM, rowin = rv - tile * BM;
+  const EpiArgs& e = rs.e[li];
+  const int col = tile * BM + rowin;  // output column (shard-relative)
+  const int m0 = quad * 4;
+  if (col >= e.n_out || m0 >= e.m_valid) return;
+  const int splits = rs.splits[li];
+  const float* base = rs.partial[li] + ((int64_t)tile * splits * R * BM + rowin) * MPAD + m0;
+  const int64_t sstride = (int64_t)R * BM * MPAD;  // floats between splits
+  float4 acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < splits; s0 += 8) {
+    float4 p[8][R];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (s0 + j < splits)
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          p[j][r] = __ldcs(reinterpret_cast<const float4*>(base + (s0 + j) * sstride + r * BM * MPAD));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (s0 + j < splits)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          acc[r].x += p[j][r].x;
+          acc[r].y += p[j][r].y;
+          acc[r].z += p[j][r].z;
+          acc[r].w += p[j][r].w;
+        }
+  }
+  const float g4[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
+  const float u4[4] = {acc[R - 1].x, acc[R - 1].y, acc[R - 1].z, acc[R - 1].w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int m = m0 + j;
+    if (m >= e.m_valid) break;
+    const int64_t idx = (int64_t)m * e.ldy + e.col_off + col;
+    float val;
+    if (R == 2) {
+      float gv = g4[j], uv = u4[j];
+      if (e.bias_mode == 1) {
+        gv = __fadd_rn(gv, __ldg(e.bias + col));
+        uv = __fadd_rn(uv, __ldg(e.bias + e.half_n + col));
+      }
+      val = __fmul_rn(silu_f(gv), uv);
+    } else {
+      val = epi_value(e, g4[j], m, col, e.Y + idx);
+    }
+    out_store1(e, idx, val);
+  }
+  if (e.nremote != 0) __threadfence_system();
 }
 
 // ------------------------------------------------------------------------------------------
