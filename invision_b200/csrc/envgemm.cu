@@ -205,7 +205,10 @@ int ensure(Dev* d, Buf& b, size_t bytes, bool zero = false) {
     cudaGetLastError();
     return fail(ENVG_ERR_OOM, "device workspace allocation of %zu bytes failed", want);
   }
-  if (zero) ENVG_CUDA(cudaMemset(b.p, 0, want));
+  if (zero) {  // zero before any stream, blocking or not, can use the buffer
+    ENVG_CUDA(cudaMemset(b.p, 0, want));
+    ENVG_CUDA(cudaDeviceSynchronize());
+  }
   b.bytes = want;
   d->st.workspace_bytes = d->ws_bytes();
   return ENVG_OK;
