@@ -62,12 +62,37 @@ struct FaArgs {
   int causal;
   float sl2;                 // scale * log2(e)
   const uint32_t* kbits;     // key validity bits
+  int full_blocks;           // leading key blocks whose keys are all valid (no mask, inside seq_k)
   const float* amax;         // max |x| per head: Q [heads], then K [kv_heads], then V [kv_heads]
   float* out;                // fp32 [seq_q][ldo], head h at column h * 128
   int64_t ldo;
   int* status;
   uint64_t wait_cap_ns;
 };
+
+// Three-input max and packed fp32 pairs (sm_100): each lane of fma/add.rn.f32x2 rounds exactly
+// as the scalar instruction does.
+ENVG_DEV float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+ENVG_DEV uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+ENVG_DEV void f2_unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+ENVG_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+ENVG_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 
 // D[tmem] <- 32 registers per thread (32 lanes x 32 columns); completion by tmem_st_wait.
 ENVG_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -312,11 +337,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       tmem_ld64_nowait(sb, r);
       tmem_ld64_nowait(sb + 64, r + 64);
       tmem_ld_wait();
-      // masks only where the block is not fully visible to every row of the warp
-      const uint32_t w0 = __ldg(a.kbits + (kc0 >> 5)), w1 = __ldg(a.kbits + (kc0 >> 5) + 1);
-      const uint32_t w2 = __ldg(a.kbits + (kc0 >> 5) + 2), w3 = __ldg(a.kbits + (kc0 >> 5) + 3);
-      const bool full = (w0 & w1 & w2 & w3) == 0xffffffffu && (int64_t)kc0 + FA_BKV - 1 <= climit;
+      // masks only where the block is not fully visible to every row of the warp; blocks before
+      // full_blocks need no validity bits (no key mask, inside seq_k)
+      const bool full = j < a.full_blocks && (int64_t)kc0 + FA_BKV - 1 <= climit;
       if (!__all_sync(0xffffffffu, full)) {
+        const uint32_t w0 = __ldg(a.kbits + (kc0 >> 5)), w1 = __ldg(a.kbits + (kc0 >> 5) + 1);
+        const uint32_t w2 = __ldg(a.kbits + (kc0 >> 5) + 2), w3 = __ldg(a.kbits + (kc0 >> 5) + 3);
         const uint32_t wd[4] = {w0, w1, w2, w3};
 #pragma unroll
         for (int t = 0; t < 128; ++t) {
@@ -324,14 +350,18 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           if (!vis) r[t] = 0xff800000u;  // -inf
         }
       }
-      // row maximum, eight independent chains
-      float mx8[8];
+      // row maximum: four chains of three-input maxima
+      float mx4[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mx8[u] = __uint_as_float(r[u]);
+      for (int u = 0; u < 4; ++u) mx4[u] = __uint_as_float(r[u]);
 #pragma unroll
-      for (int t = 8; t < 128; ++t) mx8[t & 7] = fmaxf(mx8[t & 7], __uint_as_float(r[t]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int t = 4; t < 124; t += 8)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          mx4[u] = fmax3(mx4[u], __uint_as_float(r[t + 2 * u]), __uint_as_float(r[t + 2 * u + 1]));
+      const float mx = fmax3(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3],
+                             fmax3(__uint_as_float(r[124]), __uint_as_float(r[125]),
+                                   fmaxf(__uint_as_float(r[126]), __uint_as_float(r[127]))));
       const float m_cand = mx * sl2;
       float factor = 1.0f;
       bool rescale = false;
@@ -346,15 +376,23 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           lsum *= factor;
         }
       }
-      // p = 2^(s * sl2 - m) in place, eight partial sums
+      // p = 2^(s * sl2 - m) in place, a pair of columns per step: one packed FMA, two ex2, one
+      // packed add into four pair accumulators (lane-wise the same sums as eight scalar ones)
       const float msub = (m_use == -INFINITY) ? 0.0f : m_use;
-      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const uint64_t sl2_2 = f2_pack(sl2, sl2), nm_2 = f2_pack(-msub, -msub);
+      uint64_t ps2[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int t = 0; t < 128; ++t) {
-        const float pv = ex2_approx(__fmaf_rn(__uint_as_float(r[t]), sl2, -msub));
-        ps8[t & 7] += pv;
-        r[t] = __float_as_uint(pv);
+      for (int t = 0; t < 128; t += 2) {
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r[t]), __uint_as_float(r[t + 1])), sl2_2, nm_2), x0, x1);
+        const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+        ps2[(t >> 1) & 3] = f2_add(ps2[(t >> 1) & 3], f2_pack(p0, p1));
+        r[t] = __float_as_uint(p0);
+        r[t + 1] = __float_as_uint(p1);
       }
+      float ps8[8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) f2_unpack(ps2[u], ps8[2 * u], ps8[2 * u + 1]);
       lsum += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       if (j > 0) {
         // P and O are free once PV_{j-1} is complete
@@ -652,10 +690,11 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
       tmem_ld64_nowait(s_addr, r);
       tmem_ld64_nowait(s_addr + 64, r + 64);
       tmem_ld_wait();
-      const uint32_t w0 = __ldg(a.kbits + (kc0 >> 5)), w1 = __ldg(a.kbits + (kc0 >> 5) + 1);
-      const uint32_t w2 = __ldg(a.kbits + (kc0 >> 5) + 2), w3 = __ldg(a.kbits + (kc0 >> 5) + 3);
-      const bool full = (w0 & w1 & w2 & w3) == 0xffffffffu && (int64_t)kc0 + FA_BKV - 1 <= climit;
+      // blocks before full_blocks need no validity bits (no key mask, inside seq_k)
+      bool full = j < a.full_blocks && (int64_t)kc0 + FA_BKV - 1 <= climit;
       if (!__all_sync(0xffffffffu, full)) {
+        const uint32_t w0 = __ldg(a.kbits + (kc0 >> 5)), w1 = __ldg(a.kbits + (kc0 >> 5) + 1);
+        const uint32_t w2 = __ldg(a.kbits + (kc0 >> 5) + 2), w3 = __ldg(a.kbits + (kc0 >> 5) + 3);
         const uint32_t wd[4] = {w0, w1, w2, w3};
 #pragma unroll
         for (int c = 0; c < 128; ++c) {
@@ -663,13 +702,18 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
           if (!vis) r[c] = 0xff800000u;
         }
       }
-      float mx8[8];
+      // row max: four chains of three-input maxima
+      float mx4[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mx8[u] = __uint_as_float(r[u]);
+      for (int u = 0; u < 4; ++u) mx4[u] = __uint_as_float(r[u]);
 #pragma unroll
-      for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(r[c]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int c = 4; c < 124; c += 8)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          mx4[u] = fmax3(mx4[u], __uint_as_float(r[c + 2 * u]), __uint_as_float(r[c + 2 * u + 1]));
+      const float mx = fmax3(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3],
+                             fmax3(__uint_as_float(r[124]), __uint_as_float(r[125]),
+                                   fmaxf(__uint_as_float(r[126]), __uint_as_float(r[127]))));
       const float m_cand = mx * sl2;
       if (j == 0) {
         m_use = m_cand;
@@ -689,17 +733,23 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
         }
       }
       const float msub = (m_use == -INFINITY) ? 0.0f : m_use;
-      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // p = 2^(s * sl2 - msub) for a pair of columns per step: one packed FMA, two ex2, one
+      // packed add into four pair accumulators (lane-wise the same sums as eight scalar ones)
+      const uint64_t sl2_2 = f2_pack(sl2, sl2), nm_2 = f2_pack(-msub, -msub);
+      uint64_t ps2[4] = {0, 0, 0, 0};
       uint32_t ph[64];
 #pragma unroll
       for (int c = 0; c < 128; c += 2) {
-        const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[c]), sl2, -msub));
-        const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[c + 1]), sl2, -msub));
-        ps8[c & 7] += p0;
-        ps8[(c + 1) & 7] += p1;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sl2_2, nm_2), x0, x1);
+        const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+        ps2[(c >> 1) & 3] = f2_add(ps2[(c >> 1) & 3], f2_pack(p0, p1));
         __half2 hp = __floats2half2_rn(p0, p1);
         ph[c >> 1] = *reinterpret_cast<uint32_t*>(&hp);
       }
+      float ps8[8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) f2_unpack(ps2[u], ps8[2 * u], ps8[2 * u + 1]);
       lsum += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       tmem_st64(s_addr, ph);  // P_t over the first 64 columns of S_t
       tmem_st_wait();

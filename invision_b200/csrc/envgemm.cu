@@ -2710,6 +2710,7 @@ int envg_attention(float* dst, const float* Q, const float* K, const float* V, i
   a.causal = causal ? 1 : 0;
   a.sl2 = scale * 1.4426950408889634f;
   a.kbits = bits;
+  a.full_blocks = dm ? 0 : seq_k / FA_BKV;  // without a key mask every whole block inside seq_k is valid
   a.amax = amax;
   a.out = dout;
   a.ldo = lo;
