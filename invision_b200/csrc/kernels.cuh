@@ -1678,7 +1678,6 @@ __global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ 
     // ---------------- epilogue: 4 warps, one TMEM lane quadrant each ----------------
     const int q = warp & 3;
     const int rowin = q * 32 + lane;  // W row within a 128-row tile
-    const int et = threadIdx.x - 64;  // 0..127
     int acc = 0;
     uint32_t aph = 0;
     for (int u = blockIdx.x; u < S.total; u += gridDim.x) {
