@@ -99,6 +99,7 @@ struct Dev {
   int attn_tiles = 0;     // query tiles per attention CTA: 0 = by grid size, ENVG_ATTN_TILES=1|2 forces
   int pair_split = -1;    // k1_gemm_pair split-K: -1 by cost model, 0 off, n forces n (ENVG_PAIR_SPLIT)
   bool pdl = true;        // programmatic dependent launch of the GEMM-chain kernels (ENVG_PDL=0 disables)
+  bool no_split = false;  // set while a pipelined host call launches its row chunks
   envg_stats st{};
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
@@ -859,8 +860,9 @@ int launch_transpose_cast(Dev* d, const float* src, int64_t lds, int64_t sbs, in
 // k_split_reduce adds the splits in split order and applies the epilogue.  The split count
 // depends only on (M, N, K) and the device, so repeated calls give identical results.  N-split
 // shards (outputs on several ranks) never split K.
-// SPLIT_MAX_M equals PIPE_MIN_M: the row chunks of a pipelined host call (>= PIPE_MIN_M rows
-// each) never split, so they sum in the same order as one launch over all rows.
+// A call of M >= SPLIT_MAX_M rows never splits; the row chunks of a pipelined host call (such a
+// call, cut into chunks of PIPE_CHUNK rows) are launched with splitting off (Dev::no_split), so
+// they sum in the same order as one launch over all rows.
 constexpr int64_t SPLIT_MAX_M = 1024;
 constexpr int SPLIT_MIN_KB = 4;        // K blocks per split at least
 constexpr int SPLIT_MAX = 16;
@@ -870,7 +872,7 @@ constexpr double SPLIT_REDUCE_US = 3.0;   // launch and tail of k_split_reduce
 int pair_splits(Dev* d, int64_t M, int tiles, int num_kb, int64_t Mp, int64_t ldp, int* splits, int* kb_per) {
   *splits = 1;
   *kb_per = num_kb;
-  if (d->pair_split == 0 || M >= SPLIT_MAX_M || num_kb < 2) return ENVG_OK;
+  if (d->pair_split == 0 || d->no_split || M >= SPLIT_MAX_M || num_kb < 2) return ENVG_OK;
   auto eff = [&](int sp, int* kbp) {
     *kbp = (int)cdiv(num_kb, sp);
     return (int)cdiv(num_kb, *kbp);
@@ -1495,7 +1497,7 @@ int envg_weight_upload_safetensors(const char* path, const char* name, int layou
 
 namespace {
 constexpr int64_t PIPE_MIN_M = 1024;   // host calls from this many rows are pipelined
-constexpr int64_t PIPE_CHUNK = 1024;   // rows per chunk (a multiple of the 256-row pair tile)
+constexpr int64_t PIPE_CHUNK = 512;    // rows per chunk (a multiple of the 256-row pair tile)
 
 cudaEvent_t pipe_event(Dev* d, size_t i) {
   while (d->pipe_events.size() <= i) {
@@ -1545,9 +1547,16 @@ int linear_host_pipelined(Dev* d, float* dst, const float* x, envg_weight W, con
     dshift = a;
     dscale = a + K;
   }
-  // chunks of PIPE_CHUNK rows, the remainder joining the last one: every chunk keeps at least
-  // PIPE_CHUNK rows, so it runs the same kernel (and sums in the same order) as one launch would
+  // chunks of PIPE_CHUNK rows, the remainder joining the last one.  Small chunks shorten the
+  // pipeline's fill (the first copy-in) and drain (the last copy-out).  Every chunk has more
+  // than 128 rows and runs without split-K, so it takes the CTA-pair kernel with the same
+  // per-tile summation order as one launch over all M >= PIPE_MIN_M rows (which never splits).
   const int64_t nch = std::max<int64_t>(1, M / PIPE_CHUNK);
+  struct NoSplit {
+    Dev* d;
+    ~NoSplit() { d->no_split = false; }
+  } no_split_guard{d};
+  d->no_split = true;
   auto chunk = [&](int64_t c, int64_t& r0, int64_t& rows) {
     r0 = c * PIPE_CHUNK;
     rows = (c == nch - 1) ? M - r0 : PIPE_CHUNK;

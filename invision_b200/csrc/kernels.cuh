@@ -1504,13 +1504,14 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
 // the same unit sequence (blockIdx.x, +gridDim.x, ...); the accumulator is double-buffered in
 // TMEM so the epilogue of one unit overlaps the main loop of the next, and the launch cost, the
 // TMEM allocation and the pipeline fill are paid once for all the weights of the set.  Each unit
-// issues the same UMMAs in the same order as k2_skinny does for that (tile, split), and the split
-// reduction sums in split order, so results do not depend on the set a linear is launched in.
+// issues the same UMMAs in the same order as k2_skinny does for that (tile, split); a unit of a
+// split linear stores its partial and k_skinny_reduce sums a tile's partials in split order, so
+// results do not depend on the set a linear is launched in.
 // ------------------------------------------------------------------------------------------
 constexpr int K2S_MAX_LIN = 4;
 
 struct K2Lin {
-  SkinnyArgs s;  // n_tiles, splits, kb_per_split, num_kb, epi, partial, counters
+  SkinnyArgs s;  // n_tiles, splits, kb_per_split, num_kb, epi, partial (counters unused here)
   int R;         // 2: the unit pairs a gate tile with its up tile (SiLU-gate); one R per set
 };
 
