@@ -269,6 +269,17 @@ int envg_linear_adaln(float* dst, const float* x, const float* shift, const floa
                       const float* bias, int64_t M, int64_t K, int64_t N, int epilogue, const float* gate,
                       int flags);
 
+/* The normalised linear of the Qwen3 layer: QNNRMSNormRows (quicknncpu.pas:2159-2198; call sites
+ * quicknn_qwen3.pas:802 input_layernorm and :817 post_attention_layernorm, whose outputs feed the
+ * q/k/v and gate/up projections) followed by QNNLinear, with the normalisation fused into the
+ * activation cast:
+ *   xn[r][k] = x[r][k] * weight[k] / sqrt(sum_k x[r][k]^2 / K + 1e-6)   (weight NULL: x * inv)
+ *   dst = epilogue(xn . W^T)
+ * 1e-6 is EPSILON (quicknn_common.pas:51).  weight: fp32 [K] or NULL; other arguments and flags as
+ * envg_linear. */
+int envg_linear_rmsnorm(float* dst, const float* x, const float* weight, envg_weight W, const float* bias,
+                        int64_t M, int64_t K, int64_t N, int epilogue, const float* gate, int flags);
+
 /* Allocation-free linear for skinny M.  This entry point has no counterpart in the reference.
  *
  * envg_linear grows a device workspace on demand (cudaMalloc, and cudaFree of the smaller

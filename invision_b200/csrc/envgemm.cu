@@ -116,7 +116,7 @@ int g_cur = -1;
 enum KernelId {
   KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_ADALN, KID_TRANSPOSE, KID_IM2COL,
   KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_ATTN, KID_CAST_HEADS, KID_KEY_BITS, KID_ABSMAX,
-  KID_SPLIT_REDUCE, KID_SKINNY_REDUCE, KID_COUNT
+  KID_SPLIT_REDUCE, KID_SKINNY_REDUCE, KID_RMSNORM, KID_COUNT
 };
 // Profile names are per family: "k1_gemm*" counts k1_gemm and k1_gemm_pair launches (plain,
 // SiLU-gate, conv), "k2_set" counts k2_set and the no-alloc path's k2_skinny.
@@ -126,7 +126,7 @@ const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate",
                                              "k_wait_selftest", "k_group_stats",     "k_group_affine",
                                              "k_group_apply",   "k_attention",       "k_cast_heads",
                                              "k_key_bits",      "k_absmax_heads",    "k_split_reduce",
-                                             "k_skinny_reduce"};
+                                             "k_skinny_reduce", "k_rmsnorm"};
 struct KAcc {
   uint64_t launches = 0;
   double ms = 0, flops = 0, bytes = 0;
@@ -821,6 +821,18 @@ int launch_adaln(Dev* d, const float* x, int64_t rows, int64_t K, int64_t Kp, co
   return ENVG_OK;
 }
 
+// QNNRMSNorm (EPSILON = 1e-6, quicknn_common.pas:51) fused with the bf16 cast, or into fp32.
+int launch_rmsnorm(Dev* d, const float* x, int64_t rows, int64_t K, int64_t Kp, const float* weight, void* out,
+                   bool bf16) {
+  if (rows == 0) return ENVG_OK;
+  ProfScope ps(stream_of(d), KID_RMSNORM, 0.0,
+               (double)rows * K * 4 + (double)rows * Kp * (bf16 ? 2 : 4) + (weight ? 4.0 * K : 0.0));
+  ENVG_TRY(launch_pdl(d, k_rmsnorm, dim3((unsigned)rows), dim3(256), 0, x, K, (int)K, (int)Kp, weight, 1e-6f, out,
+                      bf16 ? 1 : 0));
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
 int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t K, int64_t Kp, void* xb) {
   if (rows == 0) return ENVG_OK;
   int vec8 = (K == Kp && K % 8 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
@@ -1508,12 +1520,53 @@ cudaEvent_t pipe_event(Dev* d, size_t i) {
   return d->pipe_events[i];
 }
 
+// Row normalisation fused into the activation cast of a linear: none, QNNAdaLN (shift, scale) or
+// QNNRMSNorm (weight, which may be NULL).
+struct Prologue {
+  enum Kind { NONE = 0, ADALN, RMS } kind = NONE;
+  const float* shift = nullptr;
+  const float* scale = nullptr;
+  const float* rms_w = nullptr;
+};
+
+// Copies a host prologue's K-long vectors into d->ada on stream s; out is the device-side prologue.
+int stage_prologue(Dev* d, const Prologue& p, int64_t K, cudaStream_t s, Prologue& out) {
+  out = p;
+  if (p.kind == Prologue::ADALN) {
+    ENVG_TRY(ensure(d, d->ada, (size_t)(2 * K) * 4));
+    float* a = reinterpret_cast<float*>(d->ada.p);
+    ENVG_CUDA(cudaMemcpyAsync(a, p.shift, (size_t)K * 4, cudaMemcpyHostToDevice, s));
+    ENVG_CUDA(cudaMemcpyAsync(a + K, p.scale, (size_t)K * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)(2 * K) * 4;
+    out.shift = a;
+    out.scale = a + K;
+  } else if (p.kind == Prologue::RMS && p.rms_w) {
+    ENVG_TRY(ensure(d, d->ada, (size_t)K * 4));
+    float* a = reinterpret_cast<float*>(d->ada.p);
+    ENVG_CUDA(cudaMemcpyAsync(a, p.rms_w, (size_t)K * 4, cudaMemcpyHostToDevice, s));
+    d->st.h2d_bytes += (double)K * 4;
+    out.rms_w = a;
+  }
+  return ENVG_OK;
+}
+
+// Normalises (or only casts) rows of x into out: bf16 padded to Kp, or fp32 with K columns
+// (bf16 = false, only for a prologue other than NONE).
+int launch_prologue(Dev* d, const Prologue& p, const float* x, int64_t rows, int64_t K, int64_t Kp, void* out,
+                    bool bf16) {
+  switch (p.kind) {
+    case Prologue::ADALN: return launch_adaln(d, x, rows, K, Kp, p.shift, p.scale, out, bf16);
+    case Prologue::RMS: return launch_rmsnorm(d, x, rows, K, Kp, p.rms_w, out, bf16);
+    default: return launch_cast_rows(d, x, K, rows, K, Kp, out);
+  }
+}
+
 // Host-pointer linear with M >= PIPE_MIN_M, cut into row chunks: the copy-in of chunk c + 1 (on
 // d->h2d), the cast + GEMM of chunk c (on the compute stream) and the copy-out of chunk c - 1
 // (on d->d2h) overlap, so PCIe moves X and Y in both directions at once while the GPU computes.
 // Rows are independent, so every output is computed exactly as in one launch.  Synchronous.
 int linear_host_pipelined(Dev* d, float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K,
-                          int64_t N, int epilogue, const float* gate, const float* ad_shift, const float* ad_scale) {
+                          int64_t N, int epilogue, const float* gate, const Prologue& pro) {
   const bool gu = W->layout == ENVG_LAYOUT_GATE_UP;
   const int64_t n_out = gu ? N / 2 : N;
   cudaStream_t s = stream_of(d);
@@ -1525,7 +1578,7 @@ int linear_host_pipelined(Dev* d, float* dst, const float* x, envg_weight W, con
   float* dx = reinterpret_cast<float*>(d->x.p);
   float* dy = reinterpret_cast<float*>(d->y.p);
   // small vectors first, on the compute stream
-  const float *dbias = nullptr, *dgate = nullptr, *dshift = nullptr, *dscale = nullptr;
+  const float *dbias = nullptr, *dgate = nullptr;
   if (bias) {
     ENVG_TRY(ensure(d, d->bias, (size_t)N * 4));
     ENVG_CUDA(cudaMemcpyAsync(d->bias.p, bias, (size_t)N * 4, cudaMemcpyHostToDevice, s));
@@ -1538,15 +1591,8 @@ int linear_host_pipelined(Dev* d, float* dst, const float* x, envg_weight W, con
     d->st.h2d_bytes += (double)N * 4;
     dgate = reinterpret_cast<float*>(d->gate.p);
   }
-  if (ad_shift) {
-    ENVG_TRY(ensure(d, d->ada, (size_t)(2 * K) * 4));
-    float* a = reinterpret_cast<float*>(d->ada.p);
-    ENVG_CUDA(cudaMemcpyAsync(a, ad_shift, (size_t)K * 4, cudaMemcpyHostToDevice, s));
-    ENVG_CUDA(cudaMemcpyAsync(a + K, ad_scale, (size_t)K * 4, cudaMemcpyHostToDevice, s));
-    d->st.h2d_bytes += (double)(2 * K) * 4;
-    dshift = a;
-    dscale = a + K;
-  }
+  Prologue dpro;
+  ENVG_TRY(stage_prologue(d, pro, K, s, dpro));
   // chunks of PIPE_CHUNK rows, the remainder joining the last one.  Small chunks shorten the
   // pipeline's fill (the first copy-in) and drain (the last copy-out).  Every chunk has more
   // than 128 rows and runs without split-K, so it takes the CTA-pair kernel with the same
@@ -1581,8 +1627,7 @@ int linear_host_pipelined(Dev* d, float* dst, const float* x, envg_weight W, con
     chunk(c, r0, rows);
     ENVG_CUDA(cudaStreamWaitEvent(s, pipe_event(d, 1 + 2 * c), 0));
     void* xb = reinterpret_cast<uint8_t*>(d->xb.p) + (size_t)(r0 * W->Kp) * 2;
-    if (dshift) ENVG_TRY(launch_adaln(d, dx + r0 * K, rows, K, W->Kp, dshift, dscale, xb, true));
-    else ENVG_TRY(launch_cast_rows(d, dx + r0 * K, K, rows, K, W->Kp, xb));
+    ENVG_TRY(launch_prologue(d, dpro, dx + r0 * K, rows, K, W->Kp, xb, true));
     EpiArgs e{};
     e.Y = dy + r0 * n_out;
     e.ldy = n_out;
@@ -1610,10 +1655,10 @@ int linear_host_pipelined(Dev* d, float* dst, const float* x, envg_weight W, con
   return sync_and_check(d);
 }
 
-// envg_linear and envg_linear_adaln.  With ad_shift / ad_scale set, X is first normalised per row
-// and modulated (QNNAdaLN) inside the activation-cast kernel.
+// envg_linear, envg_linear_adaln and envg_linear_rmsnorm.  With a prologue, X is first normalised
+// per row (QNNAdaLN or QNNRMSNorm) inside the activation-cast kernel.
 int linear_core(Dev* d, float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,
-                int epilogue, const float* gate, int flags, const float* ad_shift, const float* ad_scale) {
+                int epilogue, const float* gate, int flags, const Prologue& pro) {
   ENVG_TRY(check_weight(d, W));
   if (W->conv) return fail(ENVG_ERR_ARG, "envg_linear: handle holds a convolution weight");
   if (M < 0) return fail(ENVG_ERR_ARG, "envg_linear: M=%lld < 0", (long long)M);
@@ -1639,20 +1684,13 @@ int linear_core(Dev* d, float* dst, const float* x, envg_weight W, const float* 
   const int64_t n_out = gu ? N / 2 : N;
   cudaStream_t s = stream_of(d);
   if (!devp && M >= PIPE_MIN_M && d->pipe_host)
-    return linear_host_pipelined(d, dst, x, W, bias, M, K, N, epilogue, gate, ad_shift, ad_scale);
+    return linear_host_pipelined(d, dst, x, W, bias, M, K, N, epilogue, gate, pro);
 
-  const float *dx = x, *dbias = bias, *dgate = gate, *dshift = ad_shift, *dscale = ad_scale;
+  const float *dx = x, *dbias = bias, *dgate = gate;
   float* dy = dst;
+  Prologue dpro = pro;
   if (!devp) {
-    if (ad_shift) {
-      ENVG_TRY(ensure(d, d->ada, (size_t)(2 * K) * 4));
-      float* a = reinterpret_cast<float*>(d->ada.p);
-      ENVG_CUDA(cudaMemcpyAsync(a, ad_shift, (size_t)K * 4, cudaMemcpyHostToDevice, s));
-      ENVG_CUDA(cudaMemcpyAsync(a + K, ad_scale, (size_t)K * 4, cudaMemcpyHostToDevice, s));
-      d->st.h2d_bytes += (double)(2 * K) * 4;
-      dshift = a;
-      dscale = a + K;
-    }
+    ENVG_TRY(stage_prologue(d, pro, K, s, dpro));
     ENVG_TRY(ensure(d, d->x, (size_t)(M * K) * 4));
     ENVG_TRY(ensure(d, d->y, (size_t)(M * n_out) * 4));
     ENVG_CUDA(cudaMemcpyAsync(d->x.p, x, (size_t)(M * K) * 4, cudaMemcpyHostToDevice, s));
@@ -1691,17 +1729,16 @@ int linear_core(Dev* d, float* dst, const float* x, envg_weight W, const float* 
   const double out_bytes = 4.0 * (double)M * n_out + (dbias ? 4.0 * N : 0.0) +
                            (epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)M * n_out + 4.0 * N : 0.0);
   if (M <= d->gemv_max) {
-    if (dshift) {  // normalised X kept in fp32 for the CUDA-core path
+    if (dpro.kind != Prologue::NONE) {  // normalised X kept in fp32 for the CUDA-core path
       ENVG_TRY(ensure(d, d->xn, (size_t)(M * K) * 4));
-      ENVG_TRY(launch_adaln(d, dx, M, K, K, dshift, dscale, d->xn.p, false));
+      ENVG_TRY(launch_prologue(d, dpro, dx, M, K, K, d->xn.p, false));
       dx = reinterpret_cast<const float*>(d->xn.p);
     }
     // fp32 X read directly: W once, X once per 64-row group (from L2)
     ENVG_TRY(launch_gemv(d, dx, M, K, W, gu, e, lin_flops, 2.0 * (double)N * K + 4.0 * (double)M * K + out_bytes));
   } else {
     ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
-    if (dshift) ENVG_TRY(launch_adaln(d, dx, M, K, W->Kp, dshift, dscale, d->xb.p, true));
-    else ENVG_TRY(launch_cast_rows(d, dx, K, M, K, W->Kp, d->xb.p));
+    ENVG_TRY(launch_prologue(d, dpro, dx, M, K, W->Kp, d->xb.p, true));
     ENVG_TRY(gemm_device(d, d->xb.p, M, W->Kp, W->tm256, W->tm128, W->rows, gu, e, lin_flops,
                          2.0 * (double)N * K + 2.0 * (double)M * W->Kp + out_bytes));
   }
@@ -1725,7 +1762,7 @@ int envg_linear(float* dst, const float* x, envg_weight W, const float* bias, in
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   Dev* d = cur();
   if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
-  return linear_core(d, dst, x, W, bias, M, K, N, epilogue, gate, flags, nullptr, nullptr);
+  return linear_core(d, dst, x, W, bias, M, K, N, epilogue, gate, flags, Prologue{});
 }
 
 int envg_linear_adaln(float* dst, const float* x, const float* shift, const float* scale, envg_weight W,
@@ -1734,7 +1771,22 @@ int envg_linear_adaln(float* dst, const float* x, const float* shift, const floa
   Dev* d = cur();
   if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
   if (!shift || !scale) return fail(ENVG_ERR_ARG, "envg_linear_adaln: shift and scale are required");
-  return linear_core(d, dst, x, W, bias, M, K, N, epilogue, gate, flags, shift, scale);
+  Prologue p;
+  p.kind = Prologue::ADALN;
+  p.shift = shift;
+  p.scale = scale;
+  return linear_core(d, dst, x, W, bias, M, K, N, epilogue, gate, flags, p);
+}
+
+int envg_linear_rmsnorm(float* dst, const float* x, const float* weight, envg_weight W, const float* bias, int64_t M,
+                        int64_t K, int64_t N, int epilogue, const float* gate, int flags) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Dev* d = cur();
+  if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  Prologue p;
+  p.kind = Prologue::RMS;
+  p.rms_w = weight;
+  return linear_core(d, dst, x, W, bias, M, K, N, epilogue, gate, flags, p);
 }
 
 int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,

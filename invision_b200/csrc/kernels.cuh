@@ -2275,6 +2275,34 @@ __global__ void __launch_bounds__(256) k_adaln(const float* __restrict__ X, int6
   }
 }
 
+// QNNRMSNorm per row (src/quicknncpu.pas:2159-2185), fused with the activation cast: one CTA per
+// row; inv = 1 / sqrt(sum(x^2) / K + eps), out = (x * weight) * inv, or x * inv when weight is
+// NULL.  bf16 output is zero-padded to Kp columns (the GEMM operand), fp32 output has K columns.
+__global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ X, int64_t ldx, int K, int Kp,
+                                                 const float* __restrict__ weight, float eps, void* out, int out_bf16) {
+  __shared__ float red[9];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int64_t r = blockIdx.x;
+  const float* xr = X + r * ldx;
+  float q = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) q = fmaf(xr[k], xr[k], q);
+  const float ms = block_sum256(q, red) / (float)K;
+  const float inv = 1.0f / sqrtf(ms + eps);
+  if (out_bf16) {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + r * Kp;
+    for (int k = threadIdx.x; k < Kp; k += 256) {
+      float v = 0.0f;
+      if (k < K) v = weight ? __fmul_rn(__fmul_rn(xr[k], __ldg(weight + k)), inv) : __fmul_rn(xr[k], inv);
+      o[k] = __float2bfloat16_rn(v);
+    }
+  } else {
+    float* o = reinterpret_cast<float*>(out) + r * K;
+    for (int k = threadIdx.x; k < K; k += 256)
+      o[k] = weight ? __fmul_rn(__fmul_rn(xr[k], __ldg(weight + k)), inv) : __fmul_rn(xr[k], inv);
+  }
+}
+
 // ---- GroupNorm (QNNGroupNorm, src/quicknncpu.pas:2259-2313) --------------------------------
 // Group (b, g) of an NCHW tensor is the contiguous run of cpg * HW floats starting at
 // (b*C + g*cpg) * HW.  Statistics are taken in two launches:

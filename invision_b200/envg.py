@@ -103,6 +103,7 @@ def lib():
         L.envg_linear_batch.argtypes = [ctypes.POINTER(LinearDesc), _ci, _ci]
         L.envg_linear_nsplit_batch.argtypes = [ctypes.POINTER(NsplitDesc), _ci, _ci]
         L.envg_linear_adaln.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
+        L.envg_linear_rmsnorm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _ci, _vp, _ci]
         L.envg_linear_nsplit.argtypes = [_vp, ctypes.POINTER(_vp), _ci, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64,
                                          _i64, _ci, _vp, _ci]
         L.envg_conv2d.argtypes = [_vp, _vp, _vp, _vp] + [_ci] * 11
@@ -359,6 +360,19 @@ def linear_adaln(dst, x, shift, scale, W, bias=None, epilogue=None, gate=None, s
                                           epilogue, _ptr(gate), flags))
 
 
+def linear_rmsnorm(dst, x, W, weight=None, bias=None, epilogue=None, gate=None, sync=True):
+    """dst = epilogue(RMSNorm(x; weight) . W^T): envg_linear_rmsnorm (QNNRMSNormRows fused into the
+    cast); weight None normalises without a per-column scale."""
+    if epilogue is None:
+        epilogue = EPI_SILU_GATE if W.layout == LAYOUT_GATE_UP else (EPI_BIAS if bias is not None else EPI_NONE)
+    flags = _mode(dst, x, weight, bias, gate)
+    if flags == DEVICE_PTRS and not sync:
+        flags |= ASYNC
+    M, K = x.shape
+    return _check(lib().envg_linear_rmsnorm(_ptr(dst), _ptr(x), _ptr(weight), W.h, _ptr(bias), M, K, W.N, epilogue,
+                                            _ptr(gate), flags))
+
+
 def linear_batch(calls, sync=True):
     """Several linears in one envg_linear_batch call (torch CUDA tensors only).  `calls` is a list
     of dicts with keys dst, x, W and optionally bias, epilogue, gate; each distinct x is cast once
@@ -578,6 +592,15 @@ def QNNAdaLNLinear(dst, src, shift, scale, W, B, seqLen, inDIM, outDIM):
     _assert(W.N == outDIM and W.K == inDIM, "ERROR : QNNLinear weight shape mismatch")
     return linear_adaln(dst[:seqLen], src[:seqLen], shift, scale, W, bias=B,
                         epilogue=EPI_BIAS if B is not None else EPI_NONE)
+
+
+def QNNRMSNormLinear(dst, src, norm_weight, W, B, seqLen, inDIM, outDIM):
+    """QNNRMSNormRows(norm, src, norm_weight, seq, hidden) (quicknncpu.pas:2159-2198) followed by
+    QNNLinear(dst, norm, W, B, seq, hidden, outDIM), fused as in the Qwen3 layer
+    (quicknn_qwen3.pas:802, 817); a GATE_UP weight gives the SiLU-gated MLP input."""
+    _assert(W.K == inDIM and (W.N == outDIM or (W.layout == LAYOUT_GATE_UP and W.N == 2 * outDIM)),
+            "ERROR : QNNLinear weight shape mismatch")
+    return linear_rmsnorm(dst[:seqLen], src[:seqLen], W, weight=norm_weight, bias=B)
 
 
 def QNNGroupNorm(dst, src, gamma, beta, batch, channels, H, W, num_groups):

@@ -401,6 +401,21 @@ void envo_adaln(float* dst, const float* src, const float* bias, const float* sc
   }
 }
 
+// QNNRMSNorm applied per row (QNNRMSNormRows, quicknncpu.pas:2187-2198 -> 2159-2185):
+// inv = 1 / sqrt(sum(x^2) / N + 1e-6), then x * weight * inv (QNNFusedMulScale), or x * inv when
+// no weight is given.  Scalar sums in index order.
+void envo_rms_norm(float* dst, const float* src, const float* weight, int64_t seq, int64_t hidden) {
+  const float EPS = 1e-6f;
+  for (int64_t i = 0; i < seq; ++i) {
+    const float* in = src + i * hidden;
+    float* out = dst + i * hidden;
+    float ss = 0.0f;
+    for (int64_t j = 0; j < hidden; ++j) ss = ss + in[j] * in[j];
+    const float inv = 1.0f / sqrtf((hidden ? ss / (float)hidden : 0.0f) + EPS);
+    for (int64_t j = 0; j < hidden; ++j) out[j] = weight ? (in[j] * weight[j]) * inv : in[j] * inv;
+  }
+}
+
 // QNNGroupNorm (quicknncpu.pas:2259-2313), scalar build: per (batch, group) over the contiguous
 // run of channels_per_group * H * W floats, mean = QNNMean (sequential fp32 sum / n, :536-547 and
 // :679-685), variance = QNNVariance population form (sequential sum of squared differences / n,

@@ -63,6 +63,7 @@ def lib():
         L.envo_gated_add.argtypes = [_f32p, _f32p, _f32p, _i64, _i64]
         L.envo_conv2d.argtypes = [ctypes.c_int, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 9
         L.envo_adaln.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64]
+        L.envo_rms_norm.argtypes = [_f32p, _f32p, ctypes.c_void_p, _i64, _i64]
         L.envo_group_norm.argtypes = [_f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 6
         L.envo_attention.argtypes = [ctypes.c_int, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 5 + \
             [_i64] * 4 + [ctypes.c_float, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)]
@@ -180,6 +181,19 @@ def gated_add(dst, gate, proj):
     seq, hidden = d.shape
     lib().envo_gated_add(_p(d), _p(g), _p(p), seq, hidden)
     return d
+
+
+def rms_norm(src, weight=None):
+    """QNNRMSNormRows: per row x * weight / sqrt(mean(x^2) + 1e-6) (returns a new array)."""
+    src = _chk(np.ascontiguousarray(src), np.float32)
+    seq, hidden = src.shape
+    out = np.empty_like(src)
+    wp = None
+    if weight is not None:
+        weight = _chk(np.ascontiguousarray(weight), np.float32)
+        wp = weight.ctypes.data
+    lib().envo_rms_norm(_p(out), _p(src), wp, seq, hidden)
+    return out
 
 
 def adaln(src, shift, scale):

@@ -339,6 +339,47 @@ def test_adaln_linear_vs_oracle(gpu, M, K, N):
         assert_parity(y, ref, what=f"adaln {M}x{K}x{N}")
 
 
+@pytest.mark.parametrize("M,K,N,wt", [(512, 2560, 1024, True), (4, 2560, 640, True), (16, 2560, 512, True),
+                                      (130, 200, 264, False), (1, 200, 96, False)])
+def test_rmsnorm_linear_vs_oracle(gpu, M, K, N, wt):
+    """QNNRMSNormRows + QNNLinear fused (envg_linear_rmsnorm) against the oracle's QNNRMSNormRows then
+    linear: the gemv path (M <= 8, fp32 normalised input), k2 (M = 16) and the pair kernel."""
+    rng = np.random.default_rng(M + K + 7)
+    x = (0.3 + 3 * rng.standard_normal((M, K))).astype(np.float32)
+    nw = (1 + 0.2 * rng.standard_normal(K)).astype(np.float32) if wt else None
+    _, w, b = inputs(M, K, N, seed=K + N + 1)
+    W = gpu.Weight(w)
+    y = np.zeros((M, N), np.float32)
+    gpu.QNNRMSNormLinear(y, x, nw, W, b, M, K, N)
+    ref = O.linear_bf16(O.rms_norm(x, nw), w, b, path=O.PATH_SCALAR if K % 8 else O.PATH_AVX2)
+    if M <= 8:
+        assert_parity(y, ref, 1e-4, 2e-5, what=f"rmsnorm gemv {M}x{K}x{N}")
+    else:
+        assert_parity(y, ref, what=f"rmsnorm {M}x{K}x{N}")
+
+
+@pytest.mark.parametrize("M", [3, 200])
+def test_rmsnorm_gate_up_vs_oracle(gpu, M):
+    """The Qwen3 MLP input: post_attention_layernorm fused into the gate/up linear with SiLU-gate."""
+    K, H = 512, 384
+    rng = np.random.default_rng(M + 5)
+    x = (2 * rng.standard_normal((M, K))).astype(np.float32)
+    nw = (1 + 0.2 * rng.standard_normal(K)).astype(np.float32)
+    _, w, _ = inputs(M, K, 2 * H, seed=M + 9, bias=False)
+    W = gpu.Weight(w, layout=gpu.LAYOUT_GATE_UP)
+    y = np.zeros((M, H), np.float32)
+    gpu.QNNRMSNormLinear(y, x, nw, W, None, M, K, H)
+    gu = O.linear_bf16(O.rms_norm(x, nw), w)
+    ref = O.silu_mul(np.ascontiguousarray(gu[:, :H]), np.ascontiguousarray(gu[:, H:]))
+    yg = np.zeros((M, 2 * H), np.float32)
+    gpu.linear_rmsnorm(yg, x, gpu.Weight(w), weight=nw)
+    assert_parity(yg, gu, what=f"rmsnorm gate_up halves M={M}")
+    np.testing.assert_allclose(y, O.silu_mul(np.ascontiguousarray(yg[:, :H]), np.ascontiguousarray(yg[:, H:])),
+                               rtol=2e-5, atol=2e-6)
+    # silu(g) * u compounds the two halves' errors: the product bound of the SiLU-gate tests
+    assert_parity(y, ref, TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT, what=f"rmsnorm gate_up M={M}")
+
+
 def test_safetensors_upload_matches_array_upload(gpu, tmp_path):
     """Weights uploaded straight from a .safetensors file (BF16, F16, F32; plain, GATE_UP, a shard
     and a 4-D conv weight) give the same outputs, bit for bit, as the same values uploaded from
@@ -641,7 +682,7 @@ def test_linear_batch_groups_skinny_tcgen05_linears(gpu, M):
     assert_parity(got["o"], O.linear_bf16(x2.cpu().numpy(), ws["o"], None, path=O.PATH_AVX2), what=f"grouped k2 o M={M}")
 
 
-@pytest.mark.parametrize("epi", ["bias", "silu_gate", "gated_residual", "adaln"])
+@pytest.mark.parametrize("epi", ["bias", "silu_gate", "gated_residual", "adaln", "rmsnorm"])
 def test_host_pipelined_linear_equals_device_call(gpu, epi):
     """Host-pointer linears with M >= 1024 run in row chunks with copies overlapped; the result is
     bit-identical to the same linear on device pointers (one launch), and within the GEMM bound."""
@@ -663,6 +704,9 @@ def test_host_pipelined_linear_equals_device_call(gpu, epi):
     if epi == "adaln":
         gpu.linear_adaln(yh, x, shift, scale, W, bias=b)
         gpu.linear_adaln(yd, xd, torch.from_numpy(shift).cuda(), torch.from_numpy(scale).cuda(), W, bias=bd)
+    elif epi == "rmsnorm":
+        gpu.linear_rmsnorm(yh, x, W, weight=1 + scale, bias=b)
+        gpu.linear_rmsnorm(yd, xd, W, weight=torch.from_numpy(1 + scale).cuda(), bias=bd)
     elif epi == "gated_residual":
         gpu.linear(yh, x, W, bias=b, epilogue=gpu.EPI_GATED_RESIDUAL, gate=gate)
         gpu.linear(yd, xd, W, bias=bd, epilogue=gpu.EPI_GATED_RESIDUAL, gate=torch.from_numpy(gate).cuda())

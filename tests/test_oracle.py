@@ -151,6 +151,16 @@ def test_conv2d_stride1_valid_padding_quirk():
     np.testing.assert_allclose(y1, conv_f64(src, w, None, 1, 1), rtol=1e-4, atol=1e-4)
 
 
+def test_rms_norm_vs_fp64():
+    rng = np.random.default_rng(10)
+    x = (0.5 + 2 * rng.standard_normal((5, 2560))).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(2560)).astype(np.float32)
+    xd = x.astype(np.float64)
+    inv = 1 / np.sqrt((xd * xd).mean(1, keepdims=True) + 1e-6)
+    np.testing.assert_allclose(O.rms_norm(x, w), xd * w * inv, rtol=2e-5, atol=2e-5)
+    np.testing.assert_allclose(O.rms_norm(x), xd * inv, rtol=2e-5, atol=2e-5)
+
+
 def test_adaln_vs_fp64():
     rng = np.random.default_rng(9)
     x = (3 + 2 * rng.standard_normal((7, 3072))).astype(np.float32)
