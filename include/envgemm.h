@@ -294,8 +294,10 @@ int envg_linear_rmsnorm(float* dst, const float* x, const float* weight, envg_we
  *    pointers: flags must contain ENVG_DEVICE_PTRS (ENVG_ASYNC optional).
  *  - Limits: 1 <= M <= 64 and M * Kp * 2 <= 2 MiB (Kp = K rounded up to 8), i.e. K <= 16384
  *    at M = 64; larger requests return ENVG_ERR_ARG with the limit in envg_last_error().
- *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress)
- *    with that device current; make that first call before any stream capture.
+ *  - envg_init prepares everything this entry point uses: it loads the code of every kernel it
+ *    launches (which, with lazy module loading, would otherwise happen at the first launch and
+ *    can map device memory), reserves their local memory, and looks up the array's device
+ *    address (cudaGetSymbolAddress).  So the first call allocates no more than later ones.
  *  - Every call shares the one array, which keeps the last call's contents; the counters are
  *    cleared on every call.  Calls whose kernels overlap on the GPU (different streams without
  *    ordering) race on the array and must be serialised by the caller. */

@@ -225,6 +225,30 @@ int get_encode() {
   return ENVG_OK;
 }
 
+// Loads a kernel's code on the current device now (cuFuncLoad, CUDA 12.4+) rather than at its
+// first launch, which is when the runtime loads it under lazy module loading.
+int load_kernel(const void* sym) {
+  using PfnFuncLoad = CUresult (*)(CUfunction);
+  static PfnFuncLoad func_load = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    looked_up = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuFuncLoad", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      func_load = reinterpret_cast<PfnFuncLoad>(fn);
+    else
+      cudaGetLastError();
+  }
+  if (!func_load) return fail(ENVG_ERR_CUDA, "cuFuncLoad unavailable (driver older than CUDA 12.4)");
+  cudaFunction_t f = nullptr;
+  ENVG_CUDA(cudaGetFuncBySymbol(&f, sym));
+  const CUresult r = func_load(reinterpret_cast<CUfunction>(f));
+  if (r != CUDA_SUCCESS) return fail(ENVG_ERR_CUDA, "cuFuncLoad failed: %d", (int)r);
+  return ENVG_OK;
+}
+
 // 2D bf16 K-major map: dims {inner, rows}, 64 x box_rows boxes, 128-byte swizzle, zero fill.
 int tmap_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16)
@@ -549,16 +573,37 @@ PairSet set_of_one(const GemmArgs& g, const CUtensorMap& tB, const CUtensorMap& 
 }
 
 template <int MPAD, int R>
-int launch_k2_t(Dev* d, const CUtensorMap& tW, const CUtensorMap& tX, SkinnyArgs& a, double flops, double bytes) {
-  constexpr int STAGE_BYTES = K2Smem<MPAD, R, 1>::STAGE_BYTES;
-  constexpr int ST = (110 * 1024) / STAGE_BYTES < 2 ? 2 : (110 * 1024) / STAGE_BYTES;  // two CTAs per SM
+struct K2Skinny {
+  static constexpr int STAGE_BYTES = K2Smem<MPAD, R, 1>::STAGE_BYTES;
+  static constexpr int ST = (110 * 1024) / STAGE_BYTES < 2 ? 2 : (110 * 1024) / STAGE_BYTES;  // two CTAs per SM
   using L = K2Smem<MPAD, R, ST>;
-  auto kern = k2_skinny<MPAD, R, ST>;
+  static constexpr auto kern = k2_skinny<MPAD, R, ST>;
+};
+
+// Sets k2_skinny<MPAD, R>'s shared-memory attribute once.  With local set, also loads the
+// kernel's code on the device now and returns its local memory per thread.
+template <int MPAD, int R>
+int k2_prepare(size_t* local) {
+  using K = K2Skinny<MPAD, R>;
   static bool attr = false;
   if (!attr) {
-    ENVG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    ENVG_CUDA(cudaFuncSetAttribute(K::kern, cudaFuncAttributeMaxDynamicSharedMemorySize, K::L::TOTAL));
     attr = true;
   }
+  if (local) {
+    ENVG_TRY(load_kernel(reinterpret_cast<const void*>(K::kern)));
+    cudaFuncAttributes fa;
+    ENVG_CUDA(cudaFuncGetAttributes(&fa, K::kern));
+    *local = fa.localSizeBytes;
+  }
+  return ENVG_OK;
+}
+
+template <int MPAD, int R>
+int launch_k2_t(Dev* d, const CUtensorMap& tW, const CUtensorMap& tX, SkinnyArgs& a, double flops, double bytes) {
+  using L = typename K2Skinny<MPAD, R>::L;
+  const auto kern = K2Skinny<MPAD, R>::kern;
+  ENVG_TRY((k2_prepare<MPAD, R>(nullptr)));
   a.status = d->d_status;
   a.wait_cap_ns = d->wait_cap_ns;
   ProfScope ps(stream_of(d), KID_K2, flops, bytes);
@@ -1266,6 +1311,37 @@ int noalloc_scratch(Dev* d, uint8_t** out) {
   return ENVG_OK;
 }
 
+// Run by envg_init: everything envg_linear_noalloc would otherwise set up on first use, some of
+// which takes device memory.  With lazy module loading the runtime loads a kernel's code on its
+// first use and may map a new block of device memory for it, and a kernel that needs more local
+// memory per thread than the context holds grows that reservation at its first launch.  So this
+// loads every kernel the entry point launches (the eight k2_skinny shapes and k_cast_rows),
+// raises the context's stack limit to their largest local-memory need, looks up the scratch
+// array and issues one memset into it.
+int noalloc_preload(Dev* d) {
+  size_t need = 0, l = 0;
+  ENVG_TRY((k2_prepare<16, 1>(&l))); need = std::max(need, l);
+  ENVG_TRY((k2_prepare<32, 1>(&l))); need = std::max(need, l);
+  ENVG_TRY((k2_prepare<48, 1>(&l))); need = std::max(need, l);
+  ENVG_TRY((k2_prepare<64, 1>(&l))); need = std::max(need, l);
+  ENVG_TRY((k2_prepare<16, 2>(&l))); need = std::max(need, l);
+  ENVG_TRY((k2_prepare<32, 2>(&l))); need = std::max(need, l);
+  ENVG_TRY((k2_prepare<48, 2>(&l))); need = std::max(need, l);
+  ENVG_TRY((k2_prepare<64, 2>(&l))); need = std::max(need, l);
+  ENVG_TRY(load_kernel(reinterpret_cast<const void*>(k_cast_rows)));
+  cudaFuncAttributes fa;
+  ENVG_CUDA(cudaFuncGetAttributes(&fa, k_cast_rows));
+  need = std::max(need, fa.localSizeBytes);
+  size_t have = 0;
+  ENVG_CUDA(cudaDeviceGetLimit(&have, cudaLimitStackSize));
+  if (need > have) ENVG_CUDA(cudaDeviceSetLimit(cudaLimitStackSize, need));
+  uint8_t* scratch = nullptr;
+  ENVG_TRY(noalloc_scratch(d, &scratch));
+  ENVG_CUDA(cudaMemsetAsync(scratch + NOALLOC_XB_BYTES + NOALLOC_PART_BYTES, 0, sizeof(int), d->own));
+  ENVG_CUDA(cudaStreamSynchronize(d->own));
+  return ENVG_OK;
+}
+
 // =============================================================================================
 // C ABI
 // =============================================================================================
@@ -1327,6 +1403,7 @@ int envg_init(int ndev, const int* dev_ids) {
   }
   d->st = envg_stats{};
   d->st.device = id;
+  ENVG_TRY(noalloc_preload(d));
   d->ready = true;
   return ENVG_OK;
 }
@@ -2192,7 +2269,7 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     const char* x1 = x0 + (size_t)(q.M * q.K) * 4;
     return pr.M > 0 && x0 < y1 && y0 < x1;
   };
-  // A copy whose input is exactly the output of one earlier linear on the tcgen05 path (same
+  // A copy whose input is exactly the output of one earlier linear on the tcgen05 path (k1 or k2; same
   // [M, K] shape, K % 8 == 0, overwrite epilogue) is written by that linear's epilogue as a bf16
   // side output instead of by a cast: fused_from[j] = the producer, yb_copy[p] = the copy.
   std::vector<int> fused_from(ncopies, -1), yb_copy(n, -1);
@@ -2209,7 +2286,7 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     const envg_linear_desc& pr = descs[prod];
     const int64_t pn = pr.W->layout == ENVG_LAYOUT_GATE_UP ? pr.N / 2 : pr.N;
     if ((const void*)pr.dst != (const void*)q.x || pr.M != q.M || pn != q.K) continue;
-    if (pr.epilogue == ENVG_EPI_GATED_RESIDUAL || pr.M <= d->skinny_max || src_of[prod] < 0) continue;
+    if (pr.epilogue == ENVG_EPI_GATED_RESIDUAL || src_of[prod] < 0) continue;
     if (ns) continue;  // an N-split producer computes only its own columns of the consumer's input
     if (yb_copy[prod] >= 0) continue;
     fused_from[j] = prod;

@@ -55,7 +55,8 @@ struct EpiArgs {
   int col_off;
   // Optional bf16 copy of the finished output (row stride ldyb elements, ldyb % 8 == 0): the
   // activation operand of a following linear that reads this Y, written here instead of by a
-  // separate cast (row-major linears on the TMA / coalesced store paths only).
+  // separate cast (row-major linears on the TMA / coalesced store paths, the split reduces and
+  // the skinny k2_set path).
   __nv_bfloat16* yb;
   int64_t ldyb;
 };
@@ -1743,6 +1744,7 @@ __global__ void __launch_bounds__(K1_THREADS, 1) k2_set(const __grid_constant__ 
               v = epi_value(e, accv[0][m], m, col, yp);
             }
             out_store1(e, idx, v);
+            if (e.yb) e.yb[(int64_t)m * e.ldyb + col] = __float2bfloat16_rn(v);
           }
         }
         if (e.nremote != 0) __threadfence_system();
@@ -1831,6 +1833,7 @@ __global__ void __launch_bounds__(256) k_skinny_reduce(const __grid_constant__ S
       val = epi_value(e, g4[j], m, col, e.Y + idx);
     }
     out_store1(e, idx, val);
+    if (e.yb) e.yb[(int64_t)m * e.ldyb + col] = __float2bfloat16_rn(val);
   }
   if (e.nremote != 0) __threadfence_system();
 }

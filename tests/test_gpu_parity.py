@@ -277,13 +277,15 @@ def test_gemv_silu_gate_and_gated_residual(gpu, M):
     assert_parity(h - h0, ref - h0, 1e-5, 1e-5, what=f"gemv gated residual M={M}")
 
 
-def test_linear_batch_equals_separate_calls(gpu):
+@pytest.mark.parametrize("M", [300, 40])
+def test_linear_batch_equals_separate_calls(gpu, M):
     """envg_linear_batch (one cast per distinct input, casts overlapped on a second stream, a
-    chained input waiting for its producer) gives bit-identical results to envg_linear calls."""
+    chained input waiting for its producer) gives bit-identical results to envg_linear calls, on
+    the CTA-pair path (M = 300) and the skinny k2_set path (M = 40)."""
     import torch
 
     dev = "cuda"
-    M, H, F = 300, 256, 384
+    H, F = 256, 384
     rng = np.random.default_rng(5)
     x = torch.from_numpy(rng.standard_normal((M, H), dtype=np.float32)).to(dev)
     x2 = torch.from_numpy(rng.standard_normal((M, H), dtype=np.float32)).to(dev)
@@ -318,6 +320,33 @@ def test_linear_batch_equals_separate_calls(gpu):
     torch.cuda.synchronize()
     for k, v in outs.items():
         np.testing.assert_array_equal(got[k], v.cpu().numpy(), err_msg=k)
+
+
+@pytest.mark.parametrize("M", [16, 64])
+def test_skinny_chain_batch_split_producer(gpu, M):
+    """A skinny gate_up whose K splits (its k_skinny_reduce writes down's bf16 input) chained into
+    down, in one batch: bit-identical to separate calls, and within the bound of the oracle."""
+    import torch
+
+    K, F, H = 2048, 1024, 256
+    rng = np.random.default_rng(M + 3)
+    x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+    wgu = O.f32_to_bf16_rne((0.02 * rng.standard_normal((2 * F, K))).astype(np.float32))
+    wd = O.f32_to_bf16_rne((0.02 * rng.standard_normal((H, F))).astype(np.float32))
+    Wgu, Wd = gpu.Weight(wgu, layout=gpu.LAYOUT_GATE_UP), gpu.Weight(wd)
+    g, y = torch.empty(M, F, device="cuda"), torch.empty(M, H, device="cuda")
+    gpu.linear_batch([dict(dst=g, x=x, W=Wgu), dict(dst=y, x=g, W=Wd)])
+    torch.cuda.synchronize()
+    gb, yb = g.cpu().numpy(), y.cpu().numpy()
+    gpu.linear(g, x, Wgu)
+    gpu.linear(y, g, Wd)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(gb, g.cpu().numpy())
+    np.testing.assert_array_equal(yb, y.cpu().numpy())
+    gu = O.linear_bf16(x.cpu().numpy(), wgu)
+    gref = O.silu_mul(np.ascontiguousarray(gu[:, :F]), np.ascontiguousarray(gu[:, F:]))
+    assert_parity(gb, gref, TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT, what=f"skinny chain gate_up M={M}")
+    assert_parity(yb, O.linear_bf16(gb, wd), what=f"skinny chain down M={M}")
 
 
 @pytest.mark.parametrize("M,K,N", [(512, 3072, 1024), (4, 3072, 768), (130, 200, 264)])

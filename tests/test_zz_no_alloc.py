@@ -95,3 +95,47 @@ def test_noalloc_rejects_what_it_cannot_hold(gpu):
     assert rc == envg.ERR_ARG and "scratch" in envg.last_error()
     W.free()
     W2.free()
+
+
+_FRESH = r"""
+import sys
+import torch
+from invision_b200 import envg
+from tests.common import inputs
+envg.init(0)
+cases = []
+for M, K, N, kind in %r:
+    x, w, b = inputs(M, K, N, seed=M + K)
+    silu = kind == "silu_gate"
+    W = envg.Weight(w, layout=envg.LAYOUT_GATE_UP if silu else envg.LAYOUT_PLAIN)
+    epi = envg.EPI_SILU_GATE if silu else (envg.EPI_BIAS if kind == "bias" else envg.EPI_NONE)
+    bias = torch.from_numpy(b).cuda() if kind == "bias" else None
+    y = torch.empty(M, N // 2 if silu else N, device="cuda")
+    cases.append((y, torch.from_numpy(x).cuda(), W, bias, epi))
+torch.cuda.synchronize()
+free_before = torch.cuda.mem_get_info()[0]
+L = envg.lib()
+for y, x, W, bias, epi in cases:
+    rc = L.envg_linear_noalloc(y.data_ptr(), x.data_ptr(), W.h, bias.data_ptr() if bias is not None else None,
+                               x.shape[0], x.shape[1], W.N, epi, None, envg.DEVICE_PTRS)
+    if rc != envg.OK:
+        sys.exit("rc %%d: %%s" %% (rc, envg.last_error()))
+torch.cuda.synchronize()
+free_after = torch.cuda.mem_get_info()[0]
+print("free", free_before, free_after)
+sys.exit(0 if free_after == free_before else "device memory dropped by %%d bytes" %% (free_before - free_after))
+"""
+
+
+def test_noalloc_first_calls_in_a_fresh_process(gpu):
+    """The first call of each kernel shape in a new process allocates nothing either: envg_init has
+    already loaded the code of every kernel the entry point launches."""
+    import os
+    import subprocess
+    import sys
+
+    cases = CASES + [(33, 1024, 256, "none"), (48, 512, 2 * 128, "silu_gate"), (64, 256, 2 * 64, "silu_gate")]
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _FRESH % (cases,)], cwd=root, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
