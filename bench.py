@@ -14,7 +14,8 @@ X ~ N(0,1) fp32, W = bf16(0.02 N(0,1)), b = 0.01 N(0,1) fp32, all synthetic and 
 weights exist in this environment).  One step = the five linears.  The working set (weights
 358 MB + activations) exceeds the 126 MB L2, so no flush is needed between steps.
 `--config c1|c3|c3_m16|c3_m1|c4|c5` runs the other BASELINE shapes (per-config figures; the
-headline stays config 2).
+headline stays config 2); `--config f2|f3|f4` runs the fused neighbours (RMSNorm / AdaLN
+prologues), the VAE ResBlock and attention.
 
 Arms:
   (default)          libenvgemm through its C ABI.  `value` = device-resident throughput
@@ -45,9 +46,10 @@ METRIC = "block_linear_tflops"
 UNIT = "TFLOP/s"
 
 
-def lin(name, M, K, N, epi="bias", x_from=None, x_same=None):
-    """x_from: the input is that item's output; x_same: the same input tensor as that item."""
-    return dict(name=name, op="linear", M=M, K=K, N=N, epi=epi, x_from=x_from, x_same=x_same)
+def lin(name, M, K, N, epi="bias", x_from=None, x_same=None, norm=None):
+    """x_from: the input is that item's output; x_same: the same input tensor as that item;
+    norm: "rms" (envg_linear_rmsnorm) or "adaln" (envg_linear_adaln) normalises X in the cast."""
+    return dict(name=name, op="linear", M=M, K=K, N=N, epi=epi, x_from=x_from, x_same=x_same, norm=norm)
 
 
 def conv(name, B, C, H, W, O, k, stride, pad, epi="silu"):
@@ -92,6 +94,12 @@ WORKLOADS = {
     "f3": ("VAE-decoder ResBlocks (GroupNorm 32 + SiLU + 3x3 conv, twice, + residual): 512 ch at 128x128 and "
            "256 ch at 256x256",
            [resblock("rb512", 1, 512, 512, 128, 128), resblock("rb256", 1, 256, 256, 256, 256)]),
+    "f2": ("fused prologues: Qwen3-4B q 2560->4096 and gate_up 2560->2x9728 (SiLU-gate) at M=512 behind "
+           "QNNRMSNormRows (envg_linear_rmsnorm), and the FLUX2-Klein-4B qkv 3072->9216 + b at M=4608 behind "
+           "QNNAdaLN (envg_linear_adaln); one call per linear",
+           [lin("rms_q", 512, 2560, 4096, "none", norm="rms"),
+            lin("rms_gate_up", 512, 2560, 2 * 9728, "silu_gate_nobias", norm="rms"),
+            lin("adaln_qkv", M_TOK, 3072, 9216, norm="adaln")]),
     "f4": ("attention: FLUX2-Klein-4B joint attention (4608 tokens, 24 heads x 128, non-causal) and Qwen3-4B "
            "prefill (512 tokens, 32 query / 8 kv heads x 128, causal)",
            [attn("flux", M_TOK, M_TOK, 24, 24), attn("qwen3", 512, 512, 32, 8, causal=True)]),
@@ -120,6 +128,11 @@ def is_gate(it):
 
 def out_cols(it):
     return it["N"] // 2 if is_gate(it) else it["N"]
+
+
+def plain_linear(it):
+    """A linear the batch, N-split, end-to-end and CPU-baseline paths take (no fused prologue)."""
+    return it["op"] == "linear" and not it.get("norm")
 
 
 def has_bias(it):
@@ -267,12 +280,13 @@ class Workload:
         self.sym = {}
         gen = torch.Generator(device=dev)
         self.W, self.b, self.x, self.y, self.shard, self.ys, self.gbuf = {}, {}, {}, {}, {}, {}, {}
+        self.nv = {}  # normalisation vectors of the items with a fused prologue
         names = [it["name"] for it in items]
         self.consumed = {it["x_from"] for it in items if it.get("x_from")}
         for i, it in enumerate(items):
             name = it["name"]
             gen.manual_seed(1000 + i)
-            if it["op"] in ("attn", "resblock") and world > 1:
+            if (it["op"] in ("attn", "resblock") or it.get("norm")) and world > 1:
                 raise SystemExit(f"{it['op']} workloads run on one GPU")
             if it["op"] == "attn":
                 D = 128
@@ -352,6 +366,11 @@ class Workload:
                 gen.manual_seed(2000 + i)
                 self.x[name] = torch.randn(M, K, generator=gen, device=dev)
             self.y[name] = torch.empty(M, out_cols(it), device=dev)
+            if it.get("norm") == "rms":
+                self.nv[name] = (1 + 0.1 * torch.randn(K, generator=gen, device=dev),)
+            elif it.get("norm") == "adaln":
+                self.nv[name] = (0.1 * torch.randn(K, generator=gen, device=dev),
+                                 0.1 * torch.randn(K, generator=gen, device=dev))
 
     def input_of(self, it):
         if it["name"] in self.x:
@@ -376,6 +395,13 @@ class Workload:
             self.W[name].forward(self.y[name], self.x[name], it["G"], vecs=self.b[name], sync=False)
             return
         x = self.input_of(it)
+        if it.get("norm") == "rms":
+            envg.linear_rmsnorm(self.y[name], x, self.W[name], weight=self.nv[name][0], bias=self.b[name], sync=False)
+            return
+        if it.get("norm") == "adaln":
+            shift, scale = self.nv[name]
+            envg.linear_adaln(self.y[name], x, shift, scale, self.W[name], bias=self.b[name], sync=False)
+            return
         if self.world == 1:
             envg.linear(self.y[name], x, self.W[name], bias=self.b[name], sync=False)
             return
@@ -406,7 +432,7 @@ class Workload:
 
     def step(self, gather=True):
         if (self.world > 1 and gather and self.batch and self.sym and
-                all(it["op"] == "linear" and it["name"] in self.sym for it in self.items)):
+                all(plain_linear(it) and it["name"] in self.sym for it in self.items)):
             # N-split shards in envg_linear_nsplit_batch calls, one per segment that ends where a
             # later linear reads the output (the ranks meet there) or at the end of the step
             seg = []
@@ -423,7 +449,7 @@ class Workload:
                     seg = []
                     h.barrier()
             return
-        if self.world == 1 and self.batch and all(it["op"] == "linear" for it in self.items):
+        if self.world == 1 and self.batch and all(plain_linear(it) for it in self.items):
             # one envg_linear_batch call: each input cast once, casts overlapped with the GEMMs
             self.envg.linear_batch([dict(dst=self.y[it["name"]], x=self.input_of(it), W=self.W[it["name"]],
                                          bias=self.b[it["name"]]) for it in self.items], sync=False)
@@ -603,11 +629,11 @@ def run_ours(args, items, desc, world, rank, local):
         per_item[it["name"]] = rec
 
     e2e = None
-    if not args.no_e2e and world == 1 and all(it["op"] == "linear" for it in items):
+    if not args.no_e2e and world == 1 and all(plain_linear(it) for it in items):
         e2e = run_e2e(args, envg, torch, dev, wl, step_flops)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and all(it["op"] == "linear" for it in items):
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and all(plain_linear(it) for it in items):
         cpu = cpu_baseline(items, sample_seconds=args.cpu_seconds)
 
     if rank == 0:
@@ -786,7 +812,7 @@ def run_reference(args, items, desc, world, rank):
     """--impl reference: the reference's CPU GEMM path on the host cores (rank 0 only)."""
     if rank != 0:
         return
-    if not all(it["op"] == "linear" for it in items):
+    if not all(plain_linear(it) for it in items):
         print(json.dumps({"impl": "reference", "unavailable": "the CPU arm covers linear workloads only"}))
         return
     threads = use_all_host_threads()
