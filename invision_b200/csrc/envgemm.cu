@@ -2326,7 +2326,9 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     return ENVG_OK;
   };
   // Consecutive independent skinny (gemv_max < M <= skinny_max) linears with the same padded M
-  // go out as one persistent k2_set launch, in the same way.
+  // and layout kind go out as one persistent k2_set launch, in the same way.  (Keeping a plain
+  // and a GATE_UP queue open side by side, so that a Qwen3 layer runs as {gate_up} then
+  // {q, k, v, o, down}, measured slower: the merged set's static unit assignment is unbalanced.)
   std::vector<K2Job> kq;
   std::vector<int> kidx;
   auto flush_k2 = [&]() -> int {
@@ -2403,11 +2405,16 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     const double ob = 4.0 * (double)q.M * n_out + (q.bias ? 4.0 * q.N : 0.0) +
                       (q.epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)q.M * n_out + 4.0 * q.N : 0.0);
     if (src_of[i] < 0) {
-      for (int k : gidx)
-        if (reads_output_of(q, descs[k])) {
+      const char *qy0, *qy1;
+      out_range(q, &qy0, &qy1);
+      for (int k : gidx) {  // a set runs its linears at once: no reads of, or writes over, its outputs
+        const char *ky0, *ky1;
+        out_range(descs[k], &ky0, &ky1);
+        if (reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1)) {
           ENVG_TRY(flush_gemv());
           break;
         }
+      }
       gq.push_back(GemvJob{q.x, q.M, q.K, q.W, gu, e, fl, 2.0 * (double)q.N * q.K + 4.0 * (double)q.M * q.K + ob});
       gidx.push_back(i);
       if ((int)gq.size() == GEMV_MAX_LIN) ENVG_TRY(flush_gemv());
@@ -2416,7 +2423,13 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
       const int mpad = (int)rup(q.M, 16);
       bool flush = !kq.empty() && ((int)rup(kq.front().M, 16) != mpad || kq.front().gu != gu ||
                                    (int)kq.size() == K2S_MAX_LIN);
-      for (int k : kidx) flush = flush || reads_output_of(q, descs[k]);
+      const char *qy0, *qy1;
+      out_range(q, &qy0, &qy1);
+      for (int k : kidx) {  // a set runs its linears at once: no reads of, or writes over, its outputs
+        const char *ky0, *ky1;
+        out_range(descs[k], &ky0, &ky1);
+        flush = flush || reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1);
+      }
       if (flush) ENVG_TRY(flush_k2());
       if ((size_t)src_of[i] >= next_copy) {
         // its cast waits for a linear of the pending group: launch the group, then cast

@@ -1525,6 +1525,7 @@ struct K2Set {
   int* status;
   uint64_t wait_cap_ns;
 };
+static_assert(sizeof(K2Set) <= 4096, "K2Set is a kernel parameter");
 
 template <int MPAD, int R, int STAGES>
 struct K2SetSmem {
@@ -1772,6 +1773,7 @@ struct SkinnyReduceSet {
   int base[K2S_MAX_LIN + 1];
   int n;
 };
+static_assert(sizeof(SkinnyReduceSet) <= 4096, "SkinnyReduceSet is a kernel parameter");
 
 template <int MPAD, int R>
 __global__ void __launch_bounds__(256) k_skinny_reduce(const __grid_constant__ SkinnyReduceSet rs) {

@@ -349,6 +349,44 @@ def test_skinny_chain_batch_split_producer(gpu, M):
     assert_parity(yb, O.linear_bf16(gb, wd), what=f"skinny chain down M={M}")
 
 
+@pytest.mark.parametrize("M", [16, 1])
+def test_skinny_batch_queue_hazards(gpu, M):
+    """A batch of skinny plain and gate/up linears that overwrite each other's inputs (write after
+    read) and outputs (write after write, within one kind and across kinds) gives the same
+    results as the calls one by one: a k2_set or k_gemv launch never holds two linears that write
+    the same output, nor runs a linear before an earlier one has read what it overwrites."""
+    import torch
+
+    H, F = 256, 384
+    rng = np.random.default_rng(21)
+
+    def wt(n, k):
+        return O.f32_to_bf16_rne((0.02 * rng.standard_normal((n, k))).astype(np.float32))
+
+    Wa, Wc = gpu.Weight(wt(H, F)), gpu.Weight(wt(F, H))
+    Wgu = gpu.Weight(wt(2 * F, H), layout=gpu.LAYOUT_GATE_UP)
+    x0 = torch.from_numpy(rng.standard_normal((M, F), dtype=np.float32)).cuda()
+    x2 = torch.from_numpy(rng.standard_normal((M, H), dtype=np.float32)).cuda()
+    x = x0.clone()
+    ya, yc, yd = torch.empty(M, H, device="cuda"), torch.empty(M, F, device="cuda"), torch.empty(M, F, device="cuda")
+    calls = [dict(dst=ya, x=x, W=Wa),     # plain, reads x
+             dict(dst=x, x=x2, W=Wgu),    # gate/up, then overwrites x (write after read)
+             dict(dst=yc, x=x2, W=Wc),    # plain, writes yc
+             dict(dst=yc, x=ya, W=Wc),    # plain, writes yc again (write after write, same kind)
+             dict(dst=yd, x=x2, W=Wgu),   # gate/up, writes yd
+             dict(dst=yd, x=x2, W=Wc)]    # plain over yd (write after write, other kind)
+    gpu.linear_batch(calls)
+    torch.cuda.synchronize()
+    outs = (ya, x, yc, yd)
+    got = [t.cpu().numpy() for t in outs]
+    x.copy_(x0)
+    for c in calls:
+        gpu.linear(c["dst"], c["x"], c["W"])
+    torch.cuda.synchronize()
+    for g, t, name in zip(got, outs, ("ya", "x", "yc", "yd")):
+        np.testing.assert_array_equal(g, t.cpu().numpy(), err_msg=name)
+
+
 @pytest.mark.parametrize("M,K,N", [(512, 3072, 1024), (4, 3072, 768), (130, 200, 264)])
 def test_adaln_linear_vs_oracle(gpu, M, K, N):
     """QNNAdaLN + QNNLinear fused (envg_linear_adaln) against the oracle's QNNAdaLN then linear."""
