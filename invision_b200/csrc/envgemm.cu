@@ -2407,10 +2407,12 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     if (src_of[i] < 0) {
       const char *qy0, *qy1;
       out_range(q, &qy0, &qy1);
-      for (int k : gidx) {  // a set runs its linears at once: no reads of, or writes over, its outputs
+      // a set runs its linears at once: none may read or write over another's output, and since
+      // k_gemv reads fp32 X directly (no cast copy), none may write over another's input either
+      for (int k : gidx) {
         const char *ky0, *ky1;
         out_range(descs[k], &ky0, &ky1);
-        if (reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1)) {
+        if (reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1) || writes_input_of(i, descs[k])) {
           ENVG_TRY(flush_gemv());
           break;
         }
