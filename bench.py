@@ -255,8 +255,25 @@ def dist_setup():
         from datetime import timedelta
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        # stdout carries only the one JSON result line.  With NCCL_DEBUG set, NCCL writes its
+        # debug lines to stdout (sent to a file per process here) and prints its version banner
+        # there when the first communicator starts (sent to stderr below).
+        if os.environ.get("NCCL_DEBUG") and "NCCL_DEBUG_FILE" not in os.environ:
+            os.environ["NCCL_DEBUG_FILE"] = f"/tmp/nccl_debug.{os.getpid()}.log"
+            print(f"rank {rank}: NCCL_DEBUG output in {os.environ['NCCL_DEBUG_FILE']}", file=sys.stderr)
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        import ctypes
+
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            ctypes.CDLL(None).fflush(None)  # the C library's buffered stdout goes to stderr too
+            os.dup2(saved, 1)
+            os.close(saved)
     return world, rank, local
 
 
