@@ -1,28 +1,32 @@
 """Benchmark of the Envision dense-linear hot path on B200 (one JSON line on rank 0).
 
-Default workload (the configuration the headline metric is quoted on): the
-linears of one FLUX2-Klein-4B-shaped double-stream block at 1024x1024, M = 4096 image + 512
-text tokens = 4608, hidden 3072:
+Default workload: BASELINE config 4, the configuration the metric's "at 1/2/4/8 B200" figure is
+quoted on (N-split across 1/2/4/8 GPUs) and the largest that fits one GPU: the two linears of a
+FLUX2-Klein-9B-shaped single-stream block, batch of 4 images at 1024x1024
+(quicknn_transformers.pas:1503 linear1 and :1528 linear2):
 
-    qkv      [4608, 3072] -> 9216   + bias
-    out      [4608, 3072] -> 3072   + bias
-    gate_up  [4608, 3072] -> 18432  + bias, SiLU-gate epilogue -> [4608, 9216]
-    down     [4608, 9216] -> 3072   + bias   (input: the gate_up output)
-    adaln    [1, 3072]    -> 18432  + bias   (adaptive-norm modulation, skinny M)
+    fused_in  [18432, 4096]  -> 36864   QKV (3 x 4096) and gate/up (2 x 12288), no bias
+    out       [18432, 16384] -> 4096    no bias
 
-X ~ N(0,1) fp32, W = bf16(0.02 N(0,1)), b = 0.01 N(0,1) fp32, all synthetic and seeded (no model
-weights exist in this environment).  One step = the five linears.  The working set (weights
-358 MB + activations) exceeds the 126 MB L2, so no flush is needed between steps.
-`--config c1|c3|c3_m16|c3_m1|c4|c5` runs the other BASELINE shapes (per-config figures; the
-headline stays config 2); `--config f2|f3|f4` runs the fused neighbours (RMSNorm / AdaLN
-prologues), the VAE ResBlock and attention.
+X ~ N(0,1) fp32, W = bf16(0.02 N(0,1)), all synthetic and seeded (no model weights exist in this
+environment).  One step = both linears, 8.04 TFLOP.  The working set (weights 436 MB, activations
+and outputs 4.5 GB) is far above the 126 MB L2, so no flush is needed between steps.
+With N > 1 GPUs (one process per GPU, torchrun) each rank holds a head-aligned output-column
+shard of every weight (N-split, strong scaling):
+  fused_in  the shard holds whole heads of Q, K and V and whole gate/up pairs; its consumers
+            (per-head attention, the per-pair SiLU gate) are column-local, so its output stays
+            sharded on the rank (ENVG_KEEP_SHARDED: no transfer);
+  out       its output is the residual stream, which every rank needs whole: each rank's columns
+            go to every rank's copy of Y from the GEMM epilogue (all-gather fused into the
+            epilogue; --gather nccl for NCCL's all-gather instead).
+`--config c1|c2|c3|c3_m16|c3_m1|c5` run the other BASELINE shapes (per-config figures);
+`--config f2|f3|f4` the fused neighbours (RMSNorm / AdaLN prologues), the VAE ResBlock and
+attention.  `--gather-all` gathers fused_in's output too (every linear's Y assembled on every rank).
 
 Arms:
   (default)          libenvgemm through its C ABI.  `value` = device-resident throughput
                      (TFLOP/s, whole job); `e2e` = the same through host buffers (pinned), every
-                     call copying its inputs H2D and its output D2H.  With N > 1 GPUs the weights
-                     are N-split by output column and every output is all-gathered over NCCL
-                     (strong scaling; the gather is part of the timed step).
+                     call copying its inputs H2D and its output D2H.
   --impl reference   the reference's own CPU GEMM (src/sgemm2.cpp compiled from the reference
                      tree into oracle/_ref, else the C++ restatement of its Pascal qgemm) on the
                      host cores, on a bounded M-slice of the same workload.
@@ -46,10 +50,14 @@ METRIC = "block_linear_tflops"
 UNIT = "TFLOP/s"
 
 
-def lin(name, M, K, N, epi="bias", x_from=None, x_same=None, norm=None):
+def lin(name, M, K, N, epi="bias", x_from=None, x_same=None, norm=None, segments=None, keep=False):
     """x_from: the input is that item's output; x_same: the same input tensor as that item;
-    norm: "rms" (envg_linear_rmsnorm) or "adaln" (envg_linear_adaln) normalises X in the cast."""
-    return dict(name=name, op="linear", M=M, K=K, N=N, epi=epi, x_from=x_from, x_same=x_same, norm=norm)
+    norm: "rms" (envg_linear_rmsnorm) or "adaln" (envg_linear_adaln) normalises X in the cast;
+    segments: W's row blocks (Q, K, V heads, gate, up) that an N-split shards each in the same
+    proportion, so a rank holds whole heads and gate/up pairs; keep: with N > 1 the output stays
+    sharded on its rank (its consumers are column-local)."""
+    return dict(name=name, op="linear", M=M, K=K, N=N, epi=epi, x_from=x_from, x_same=x_same, norm=norm,
+                segments=segments, keep=keep)
 
 
 def conv(name, B, C, H, W, O, k, stride, pad, epi="silu"):
@@ -85,9 +93,10 @@ WORKLOADS = {
     "c3": ("BASELINE config 3: Qwen3-4B layer linears at M=512 (no bias)", qwen(512)),
     "c3_m16": ("BASELINE config 3 at M=16 (skinny)", qwen(16)),
     "c3_m1": ("BASELINE config 3 at M=1 (skinny)", qwen(1)),
-    "c4": ("BASELINE config 4: FLUX2-Klein-9B single-stream fused input linear M=18432, K=4096, N=36864, then "
-           "the output linear K=16384, N=4096 (no bias)",
-           [lin("fused_in", 18432, 4096, 36864, "none"), lin("out", 18432, 16384, 4096, "none")]),
+    "c4": ("BASELINE config 4: FLUX2-Klein-9B single-stream fused input linear M=18432 (4 x (4096+512) tokens), "
+           "K=4096, N=36864 (QKV 3x4096 + gate/up 2x12288), then the output linear K=16384, N=4096 (no bias)",
+           [lin("fused_in", 18432, 4096, 36864, "none", segments=(4096, 4096, 4096, 12288, 12288), keep=True),
+            lin("out", 18432, 16384, 4096, "none")]),
     "c5": ("BASELINE config 5: VAE-decoder 3x3 conv, [1,512,128,128] -> 512 ch, and [1,256,256,256] -> 256 ch, "
            "fused bias + SiLU",
            [conv("conv512", 1, 512, 128, 128, 512, 3, 1, 1), conv("conv256", 1, 256, 256, 256, 256, 3, 1, 1)]),
@@ -139,21 +148,26 @@ def has_bias(it):
     return it["epi"] in ("bias", "silu_gate", "silu")
 
 
-# DRAM bytes (read + write) per k1_gemm_pair launch of the config-2 step: mean of the four launches
-# of one step in the ncu capture summarised in profiles/k1_gemm_pair_config2.md (single pass,
-# full-size workload).
-K1_TRAFFIC_BYTES_PER_LAUNCH = 385.4e6
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per k1_gemm launch of one step of the
+# default workload at one GPU, from an ncu capture of the current kernels (one pass,
+# gpu__time_duration and the two dram counters; per-launch mean over the step's launches).
+K1_TRAFFIC_BYTES_PER_LAUNCH = {}
 
 
-def peaks():
-    """(bf16 TFLOP/s, HBM GB/s, source).  The k1 kernels are timed inside a long, power-capped
-    step, so the denominator is the sustained cuBLAS figure of MEASURED_PEAKS.json."""
+def peaks(clocks=None, region_ms=0.0):
+    """(bf16 TFLOP/s, HBM GB/s, which).  The burst cuBLAS figure of MEASURED_PEAKS.json is the
+    denominator for a short or unthrottled timed region; the sustained one (cuBLAS looped for
+    seconds under the 1 kW power cap) when the clock record shows sw_power_cap over a region of a
+    second or more."""
+    capped = bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or []) and region_ms >= 1000.0
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), float(p["hbm_gbs"]), "measured"
+        if capped and "bf16_tflops_sustained" in p:
+            return float(p["bf16_tflops_sustained"]), float(p["hbm_gbs"]), "measured, sustained"
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured, burst"
     except Exception:
-        return 1400.0, 6650.0, "fallback"
+        return (1400.0, 6650.0, "fallback, sustained") if capped else (1590.0, 6650.0, "fallback, burst")
 
 
 # ---------------------------------------------------------------------------------------------
@@ -255,26 +269,33 @@ def dist_setup():
         from datetime import timedelta
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        # stdout carries only the one JSON result line.  With NCCL_DEBUG set, NCCL writes its
-        # debug lines to stdout (sent to a file per process here) and prints its version banner
-        # there when the first communicator starts (sent to stderr below).
-        if os.environ.get("NCCL_DEBUG") and "NCCL_DEBUG_FILE" not in os.environ:
-            os.environ["NCCL_DEBUG_FILE"] = f"/tmp/nccl_debug.{os.getpid()}.log"
-            print(f"rank {rank}: NCCL_DEBUG output in {os.environ['NCCL_DEBUG_FILE']}", file=sys.stderr)
+        # stdout carries only the one JSON result line: NCCL's version banner and, with NCCL_DEBUG
+        # set, its debug lines, which it prints to stdout while the communicator starts, go to
+        # stderr (below), where they stay visible.
         torch.cuda.set_device(local)
-        import ctypes
-
-        sys.stdout.flush()
-        saved = os.dup(1)
-        os.dup2(2, 1)
-        try:
-            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-            dist.barrier()
-        finally:
-            ctypes.CDLL(None).fflush(None)  # the C library's buffered stdout goes to stderr too
-            os.dup2(saved, 1)
-            os.close(saved)
+        stdout_to_stderr()
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.barrier()
     return world, rank, local
+
+
+_json_out = None
+
+
+def stdout_to_stderr():
+    """From here on, file descriptor 1 is stderr (NCCL and other libraries print to it); the JSON
+    result line goes to the original stdout through emit()."""
+    global _json_out
+    if _json_out is None:
+        sys.stdout.flush()
+        _json_out = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(line):
+    out = _json_out if _json_out is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 
 # ---------------------------------------------------------------------------------------------
@@ -283,11 +304,11 @@ def dist_setup():
 class Workload:
     """Device-resident weights, inputs and outputs of one workload on this rank."""
 
-    def __init__(self, items, world, rank, dev, gather="peer", force_p2p=False):
+    def __init__(self, items, world, rank, dev, gather="peer", force_p2p=False, gather_all=False):
         import torch
 
         from invision_b200 import envg
-        from invision_b200.nsplit import shard_bounds
+        from invision_b200.nsplit import segment_rows, shard_bounds
 
         self.items, self.world, self.rank, self.dev = items, world, rank, dev
         self.envg = envg
@@ -295,6 +316,7 @@ class Workload:
         self.gather = gather
         self.force_p2p = force_p2p
         self.sym = {}
+        self.keep = set()  # N-split items whose output stays sharded on the rank (no transfer)
         gen = torch.Generator(device=dev)
         self.W, self.b, self.x, self.y, self.shard, self.ys, self.gbuf = {}, {}, {}, {}, {}, {}, {}
         self.nv = {}  # normalisation vectors of the items with a fused prologue
@@ -360,16 +382,26 @@ class Workload:
                 self.b[name] = b
             else:
                 half = N // 2 if gate else N
-                n0, n1, per = shard_bounds(half, world, rank, 128)
-                self.W[name] = envg.Weight(w_host, layout=layout, shard=(n0, n1))
-                if b is not None:
-                    self.b[name] = (torch.cat([b[n0:n1], b[half + n0:half + n1]]) if gate else b[n0:n1]).contiguous()
+                if it.get("segments") and not gate:
+                    # head-aligned shard: this rank's heads of Q, K, V and its gate/up rows
+                    rows = segment_rows(it["segments"], world, rank, 128)
+                    self.W[name] = envg.Weight(np.ascontiguousarray(w_host[rows]), layout=layout)
+                    self.b[name] = b[torch.from_numpy(rows).to(dev)].contiguous() if b is not None else None
+                    n0, n1, per = 0, len(rows), len(rows)
                 else:
-                    self.b[name] = None
+                    n0, n1, per = shard_bounds(half, world, rank, 128)
+                    self.W[name] = envg.Weight(w_host, layout=layout, shard=(n0, n1))
+                    if b is not None:
+                        self.b[name] = (torch.cat([b[n0:n1], b[half + n0:half + n1]]) if gate else b[n0:n1]).contiguous()
+                    else:
+                        self.b[name] = None
                 self.shard[name] = (n0, n1, per)
                 self.ys[name] = torch.zeros(M, per, device=dev)
-                self.gbuf[name] = torch.empty(world, M, per, device=dev)
-                if self.gather == "peer":
+                if it.get("keep") and not gather_all and name not in self.consumed:
+                    self.keep.add(name)
+                elif self.gather == "nccl":
+                    self.gbuf[name] = torch.empty(world, M, per, device=dev)
+                if name not in self.keep and self.gather == "peer":
                     import torch.distributed as dist
                     import torch.distributed._symmetric_memory as symm_mem
 
@@ -395,6 +427,8 @@ class Workload:
         return self.sym[it["x_from"]][0] if it["x_from"] in self.sym else self.y[it["x_from"]]
 
     def out_of(self, name):
+        if name in self.keep:
+            return self.ys[name]
         return self.sym[name][0] if name in self.sym else self.y[name]
 
     def run_item(self, it, gather=True):
@@ -427,6 +461,9 @@ class Workload:
         from invision_b200.nsplit import gather_columns
 
         n0, n1, per = self.shard[name]
+        if name in self.keep:  # the output stays on this rank: its shard is all there is to compute
+            envg.linear(self.ys[name], x, self.W[name], bias=self.b[name], sync=False)
+            return
         if gather and name in self.sym:
             # all-gather fused into the epilogue: this rank's columns go to every rank's copy of Y
             ysym, h, peers, mc = self.sym[name]
@@ -448,23 +485,29 @@ class Workload:
             gather_columns(self.ys[name], self.y[name].shape[1], out=self.y[name], buf=self.gbuf[name])
 
     def step(self, gather=True):
-        if (self.world > 1 and gather and self.batch and self.sym and
-                all(plain_linear(it) and it["name"] in self.sym for it in self.items)):
+        if (self.world > 1 and gather and self.batch and (self.sym or self.keep) and
+                all(plain_linear(it) and (it["name"] in self.sym or it["name"] in self.keep) for it in self.items)):
             # N-split shards in envg_linear_nsplit_batch calls, one per segment that ends where a
-            # later linear reads the output (the ranks meet there) or at the end of the step
+            # later linear reads a gathered output (the ranks meet there) or at the end of the step.
+            # A kept shard names no peers: its epilogue stores into this rank's buffer only.
             seg = []
+            handle = next(iter(self.sym.values()))[1] if self.sym else None
             for it in self.items:
                 name = it["name"]
-                ysym, h, peers, mc = self.sym[name]
                 n0, n1, _ = self.shard[name]
-                if n1 > n0:
-                    seg.append(dict(y=ysym, x=self.input_of(it), W=self.W[name], col0=n0, bias=self.b[name],
-                                    peers=None if mc else peers, multicast=mc))
-                if name in self.consumed or it is self.items[-1]:
+                if name in self.keep:
+                    seg.append(dict(y=self.ys[name], x=self.input_of(it), W=self.W[name], col0=0, bias=self.b[name]))
+                else:
+                    ysym, h, peers, mc = self.sym[name]
+                    if n1 > n0:
+                        seg.append(dict(y=ysym, x=self.input_of(it), W=self.W[name], col0=n0, bias=self.b[name],
+                                        peers=None if mc else peers, multicast=mc))
+                if (name in self.consumed and name not in self.keep) or it is self.items[-1]:
                     if seg:
                         self.envg.linear_nsplit_batch(seg, sync=False)
                     seg = []
-                    h.barrier()
+                    if handle is not None:
+                        handle.barrier()
             return
         if self.world == 1 and self.batch and all(plain_linear(it) for it in self.items):
             # one envg_linear_batch call: each input cast once, casts overlapped with the GEMMs
@@ -483,6 +526,22 @@ class Workload:
             else:
                 w.free()
         self.sym.clear()  # symmetric buffers go before the process group
+
+
+def workload_config(args, desc, items):
+    """The workload, identical on both arms (the driver compares the arms' config objects)."""
+    ws = 0.0
+    for it in items:
+        if it["op"] == "linear":
+            ws += 2.0 * it["N"] * it["K"] + 4.0 * it["M"] * (it["K"] + out_cols(it))
+    cfg = {"workload": desc, "config": args.config + (f" (only {args.only})" if args.only else ""),
+           "flops_per_step": float(sum(item_flops(it) for it in items))}
+    if ws:
+        cfg["l2"] = (f"working set {ws / 1e9:.2f} GB of weights, inputs and outputs > 126 MB L2: no flush between "
+                     "steps")
+    else:
+        cfg["l2"] = "inputs larger than the 126 MB L2: no flush between steps"
+    return cfg
 
 
 def capture(torch, fn):
@@ -505,7 +564,8 @@ def run_ours(args, items, desc, world, rank, local):
     torch.cuda.set_device(local)
     envg.init(local)
     dev = torch.device("cuda", local)
-    wl = Workload(items, world, rank, dev, gather=args.gather, force_p2p=not args.multicast)
+    wl = Workload(items, world, rank, dev, gather=args.gather, force_p2p=not args.multicast,
+                  gather_all=args.gather_all)
     wl.batch = not args.no_batch
     step_flops = float(sum(item_flops(it) for it in items))
 
@@ -568,11 +628,19 @@ def run_ours(args, items, desc, world, rank, local):
     gemm_phase = None
     if world > 1:
         gms = timed(lambda: wl.step(gather=False), args.steps)
+        gathered = [it for it in items if it["name"] not in wl.keep]
+        gbytes = sum(4.0 * it["M"] * out_cols(it) * (world - 1) / world for it in gathered)
         gemm_phase = {"value": round(step_flops / (gms * 1e-3) / 1e12, 2), "ms_per_step": round(gms, 4),
-                      "note": "same step without the all-gather of Y"}
+                      "note": "the same step with every rank computing its shards into local buffers: no "
+                              "transfer, no barrier",
+                      "gathered": [it["name"] for it in gathered], "kept_sharded": sorted(wl.keep),
+                      "nvlink_bytes_in_per_rank": gbytes,
+                      "nvlink_floor_ms": round(gbytes / 770e9 * 1e3, 4),
+                      "nvlink_floor_note": "bytes each rank must receive / 770 GB/s (measured peer copy per "
+                                          "direction on this pool)"}
 
     # per-kernel device time: CUDA events the library records around each launch
-    pk, hbm, src = peaks()
+    pk, hbm, src = peaks(clocks, ms * args.steps)
     envg.profile(True)
     prof_steps = max(3, min(args.steps, 10))
     for _ in range(prof_steps):
@@ -591,19 +659,19 @@ def run_ours(args, items, desc, world, rank, local):
         roofline = {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s",
                     "frac": round(ach / pk, 4), "traffic": None,
                     "kernel": "k_attention (tcgen05 flash-attention forward, fp16 operands)",
-                    "peak_source": ("measured: MEASURED_PEAKS.json bf16_tflops_sustained (fp16 runs at the bf16 "
-                                    "rate)" if src == "measured" else "fallback: 1.4 PFLOP/s sustained"),
+                    "peak_source": src + " (MEASURED_PEAKS.json cuBLAS bf16; fp16 runs at the bf16 rate)",
                     "algorithmic_flops_per_launch": fa["flops"] / fa["launches"],
                     "avg_launch_ms": round(fa["ms"] / fa["launches"], 5)}
     if k1["launches"]:
         ach = k1["flops"] / (k1["ms"] * 1e-3) / 1e12
         roofline = {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s",
                     "frac": round(ach / pk, 4),
-                    "traffic": K1_TRAFFIC_BYTES_PER_LAUNCH if args.config == "c2" and not args.only else None,
+                    "traffic": (K1_TRAFFIC_BYTES_PER_LAUNCH.get(args.config)
+                                if world == 1 and not args.only else None),
                     "kernel": "k1_gemm family (tcgen05 CTA-pair GEMM; plain, SiLU-gate and conv variants)",
-                    "peak_source": ("measured: MEASURED_PEAKS.json bf16_tflops_sustained (cuBLAS bf16 8192^3 looped "
-                                    "4 s under the 1 kW power cap)" if src == "measured"
-                                    else "fallback: 1.4 PFLOP/s sustained"),
+                    "peak_source": src + (" (MEASURED_PEAKS.json: cuBLAS bf16 8192^3, burst = best of 10, sustained = "
+                                          "looped 4 s under the 1 kW power cap; sustained is used when sw_power_cap "
+                                          "was active over a timed region of 1 s or more)"),
                     "algorithmic_flops_per_launch": k1["flops"] / k1["launches"],
                     "avg_launch_ms": round(k1["ms"] / k1["launches"], 5)}
     tot = sum(v["ms"] for v in prof.values()) or 1.0
@@ -654,26 +722,31 @@ def run_ours(args, items, desc, world, rank, local):
         cpu = cpu_baseline(items, sample_seconds=args.cpu_seconds)
 
     if rank == 0:
+        if world == 1:
+            par = "single GPU"
+        elif args.gather == "peer":
+            par = (f"N-split x{world}, head-aligned shards; "
+                   + (f"{', '.join(sorted(wl.keep))} kept sharded (column-local consumers); " if wl.keep else "")
+                   + "all-gather of the rest fused into the GEMM epilogue ("
+                   + ("NVLS multimem stores" if any(v[3] for v in wl.sym.values()) else "P2P TMA stores") + ")")
+        else:
+            par = f"N-split x{world} + NCCL all-gather"
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": desc, "config": args.config, "flops_per_step": step_flops,
-                           "timing": ("one step captured as a CUDA graph and replayed" if graph is not None
-                                      else "steps launched from the host"),
-                           "api": ("envg_linear_batch (one call per step)" if world == 1 else
-                                   "envg_linear_nsplit_batch (one call per barrier-to-barrier segment)")
-                                  if wl.batch else "envg_linear per linear",
-                           "parallelism": "single GPU" if world == 1 else (
-                               f"N-split x{world}, all-gather fused into the GEMM epilogue ("
-                               + ("NVLS multimem stores" if any(v[3] for v in wl.sym.values()) else "P2P stores")
-                               + ")" if args.gather == "peer" else f"N-split x{world} + NCCL all-gather"),
-                           "arith": "fp32 activations rounded to bf16 (RNE), bf16 weights, fp32 accumulate",
-                           "l2": "working set > 126 MB L2 (config 2: ~0.6 GB); no flush"},
+                "config": workload_config(args, desc, items),
+                "arm": {"timing": ("one step captured as a CUDA graph and replayed" if graph is not None
+                                   else "steps launched from the host"),
+                        "api": ("envg_linear_batch (one call per step)" if world == 1 else
+                                "envg_linear_nsplit_batch (one call per barrier-to-barrier segment)")
+                               if wl.batch else "envg_linear per linear",
+                        "parallelism": par,
+                        "arith": "fp32 activations rounded to bf16 (RNE), bf16 weights, fp32 accumulate"},
                 "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "roofline": roofline,
                 "cpu_baseline": cpu, "kernels": kernels, "per_item": per_item}
         if gemm_phase:
             line["gemm_phase"] = gemm_phase
-        print(json.dumps(line), flush=True)
+        emit(line)
     wl.free()
 
 
@@ -730,9 +803,13 @@ def run_e2e(args, envg, torch, dev, wl, step_flops):
 # CPU side: the reference's own GEMM on the host cores
 # ---------------------------------------------------------------------------------------------
 class CpuWorkload:
-    """Seeded host copies of a linear workload: fp32-widened bf16 weights (the reference widens at
-    load, src/safetensor.pas:584-647), fp32 biases and inputs.  A step runs an M-slice of `rows`
-    rows of every linear whose M exceeds it (M = 1 linears run in full)."""
+    """Seeded host copies of a linear workload: bf16 weight bits and their fp32 widening (the
+    reference widens at load, src/safetensor.pas:584-647, or per call, src/quicknncpu.pas:1830-1847),
+    fp32 biases and inputs.  A step runs an M-slice of `rows` rows of every linear whose M exceeds
+    it (M = 1 linears run in full) through one of the reference's CPU GEMMs:
+      "sgemm2"  src/sgemm2.cpp cpp_sgemm, compiled unmodified from the reference tree (oracle/_ref);
+      "o1"      the C++ restatement of the shipped Pascal qgemm -> gemm_nt with sDot_x4_avx2
+                (quicknncpu.pas:1241-1337, ops_avx2.inc:1407-1508) on pre-widened fp32 weights."""
 
     def __init__(self, items):
         import torch
@@ -742,52 +819,64 @@ class CpuWorkload:
         self.O = O
         self.items = items
         g = torch.Generator().manual_seed(7)
-        self.w, self.b, self.x = {}, {}, {}
+        self.w, self.wb, self.b, self.x = {}, {}, {}, {}
         names = [it["name"] for it in items]
         for it in items:
             n, M, K, N = it["name"], it["M"], it["K"], it["N"]
-            self.w[n] = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+            wb = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+            self.wb[n] = wb.view(torch.int16).numpy().view(np.uint16)
+            self.w[n] = wb.float().numpy()
             self.b[n] = (torch.randn(N, generator=g) * 0.01).numpy() if has_bias(it) else None
             if it["x_from"] not in names:
                 self.x[n] = torch.randn(M, K, generator=g).numpy()
-        self.use_ref = O.ref_lib() is not None
+        self.has_ref = O.ref_lib() is not None
 
-    def gemm(self, x, w):
+    def gemm(self, x, n, kind):
         m, K = x.shape
-        N = w.shape[0]
-        if self.use_ref:
-            return self.O.sgemm2_nt(x, w, m, N, K)
-        return self.O.linear_f32(x, w)
+        N = self.w[n].shape[0]
+        if kind == "sgemm2":
+            return self.O.sgemm2_nt(x, self.w[n], m, N, K)
+        return self.O.linear_f32(x, self.w[n])
 
-    def step(self, rows):
+    def step(self, rows, kind, times=None):
         O = self.O
         flops = 0.0
         y = {}
         for it in self.items:
             n, M, K, N = it["name"], it["M"], it["K"], it["N"]
+            t0 = time.perf_counter()
             x = np.ascontiguousarray(self.x[n][: min(M, rows)]) if n in self.x else y[it["x_from"]]
-            out = self.gemm(x, self.w[n])
+            out = self.gemm(x, n, kind)
             if self.b[n] is not None:
                 out += self.b[n]  # QNNAddInplace per row (quicknncpu.pas:1816-1819)
             if is_gate(it):
                 h = N // 2
                 out = O.silu_mul(np.ascontiguousarray(out[:, :h]), np.ascontiguousarray(out[:, h:]))
             y[n] = out
+            if times is not None:
+                times[n] = (time.perf_counter() - t0, x.shape[0])
             flops += 2.0 * x.shape[0] * K * N
         return flops
 
-    def pick_rows(self, target_s):
+    def widen_seconds(self):
+        """One BF16ToSingle widening of every weight (the per-call work of QNNLinearNoBias_BF16)."""
+        t = time.perf_counter()
+        for n in self.wb:
+            self.O.bf16_to_f32(self.wb[n])
+        return time.perf_counter() - t
+
+    def pick_rows(self, target_s, kind):
         """Largest M-slice (multiple of 64, <= the largest M) whose step takes about target_s seconds."""
         mmax = max(it["M"] for it in self.items)
         t = time.perf_counter()
-        self.step(min(64, mmax))
+        self.step(min(64, mmax), kind)
         dt = time.perf_counter() - t
         rows = int(64 * target_s / max(dt, 1e-3))
         return max(min(64, mmax), min(mmax, (rows // 64) * 64))
 
-    def describe(self):
-        return ("reference src/sgemm2.cpp cpp_sgemm (compiled from the reference tree, OpenMP)" if self.use_ref else
-                "C++ restatement of the reference Pascal qgemm/gemm_nt (oracle/envg_oracle.cpp)")
+    def describe(self, kind):
+        return ("reference src/sgemm2.cpp cpp_sgemm (compiled from the reference tree, OpenMP)" if kind == "sgemm2" else
+                "C++ restatement of the reference Pascal qgemm/gemm_nt with sDot_x4_avx2 (oracle/envg_oracle.cpp)")
 
 
 def cpu_threads():
@@ -795,6 +884,17 @@ def cpu_threads():
         return len(os.sched_getaffinity(0))
     except Exception:
         return os.cpu_count() or 1
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def use_all_host_threads():
@@ -811,18 +911,46 @@ def use_all_host_threads():
     return threads
 
 
-def cpu_baseline(items, sample_seconds=12.0):
+def cpu_baseline(items, sample_seconds=8.0):
+    """The reference's CPU GEMMs on the host cores, each on a bounded M-slice of the workload:
+    sgemm2 (the compiled reference C++, when built) as the headline `value`, and the restated
+    shipped Pascal qgemm (O1) without and with the per-call bf16 -> fp32 widening of
+    QNNLinearNoBias_BF16.  The widened figure is for the whole workload: the slice's GEMM time
+    scaled to all rows, plus one widening of every weight per step (it does not shrink with the
+    slice)."""
     threads = use_all_host_threads()
     wl = CpuWorkload(items)
-    rows = wl.pick_rows(sample_seconds)
-    t = time.perf_counter()
-    flops = wl.step(rows)
-    dt = time.perf_counter() - t
     mmax = max(it["M"] for it in items)
-    return {"value": round(flops / dt / 1e12, 5), "unit": UNIT, "cores": threads,
-            "kind": "reference" if wl.use_ref else "port",
-            "sample": f"one step of the workload on an M-slice of {rows} of {mmax} token rows (M=1 linears in full); "
-                      f"{dt:.1f} s; {wl.describe()}"}
+    full_flops = float(sum(item_flops(it) for it in items))
+
+    def run(kind):
+        rows = wl.pick_rows(sample_seconds, kind)
+        times = {}
+        t = time.perf_counter()
+        flops = wl.step(rows, kind, times)
+        dt = time.perf_counter() - t
+        full_s = sum(ts * it["M"] / r for it in items for ts, r in [times[it["name"]]])
+        return rows, flops, dt, full_s
+
+    o1_rows, o1_flops, o1_dt, o1_full = run("o1")
+    widen = wl.widen_seconds()
+    o1 = {"value": round(o1_flops / o1_dt / 1e12, 5), "unit": UNIT, "kind": "port", "cores": threads,
+          "sample": f"M-slice of {o1_rows} of {mmax} rows, {o1_dt:.1f} s; {wl.describe('o1')}; weights pre-widened "
+                    "(the path the shipped FLUX code takes, use_bf16 = false)"}
+    o1w = {"value": round(full_flops / (o1_full + widen) / 1e12, 5), "unit": UNIT, "kind": "port", "cores": threads,
+           "sample": f"O1 GEMM time of the slice scaled to all {mmax} rows plus {widen:.2f} s of single-threaded "
+                     "BF16ToSingle widening of every weight per step (QNNLinearNoBias_BF16, quicknncpu.pas:1830-1847)"}
+    if wl.has_ref:
+        rows, flops, dt, _ = run("sgemm2")
+        out = {"value": round(flops / dt / 1e12, 5), "unit": UNIT, "cores": threads, "kind": "reference",
+               "sample": f"one step of the workload on an M-slice of {rows} of {mmax} token rows (M=1 linears in "
+                         f"full); {dt:.1f} s; {wl.describe('sgemm2')}"}
+    else:
+        out = dict(o1)
+    out["cpu_model"] = f"{cpu_model()}, {threads} threads"
+    out["o1_qgemm"] = o1
+    out["o1_qgemm_widened_per_call"] = o1w
+    return out
 
 
 def run_reference(args, items, desc, world, rank):
@@ -830,32 +958,33 @@ def run_reference(args, items, desc, world, rank):
     if rank != 0:
         return
     if not all(plain_linear(it) for it in items):
-        print(json.dumps({"impl": "reference", "unavailable": "the CPU arm covers linear workloads only"}))
+        emit({"impl": "reference", "unavailable": "the CPU arm covers linear workloads only"})
         return
     threads = use_all_host_threads()
     per_step = max(0.5, min(15.0, 150.0 / max(1, args.steps + args.warmup)))
     wl = CpuWorkload(items)
-    rows = wl.pick_rows(per_step)
+    kind = "sgemm2" if wl.has_ref else "o1"
+    rows = wl.pick_rows(per_step, kind)
     for _ in range(args.warmup):
-        wl.step(rows)
+        wl.step(rows, kind)
     t = time.perf_counter()
     flops = 0.0
     for _ in range(args.steps):
-        flops += wl.step(rows)
+        flops += wl.step(rows, kind)
     dt = time.perf_counter() - t
     value = flops / dt / 1e12
-    kind = "reference" if wl.use_ref else "port"
     mmax = max(it["M"] for it in items)
     sample = (f"each step: the workload on an M-slice of {rows} of {mmax} token rows (M=1 linears in full); "
-              f"{wl.describe()}")
+              f"{wl.describe(kind)}")
     line = {"metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": desc, "config": args.config, "M_slice": rows,
-                       "parallelism": f"{threads} host threads"},
-            "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
+            "config": workload_config(args, desc, items),
+            "arm": {"parallelism": f"{threads} host threads ({cpu_model()})", "M_slice": rows},
+            "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads,
+                             "kind": "reference" if kind == "sgemm2" else "port", "sample": sample},
             "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
@@ -864,7 +993,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--config", default="c4", choices=sorted(WORKLOADS))
     ap.add_argument("--only", default=None, help="run one item of the workload (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
@@ -875,7 +1004,9 @@ def main():
                     help="N>1 peer gather through an NVLS multicast address (default: P2P stores, which load each "
                          "GPU's NVLink ingress less: multicast also returns the local copy through the switch)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU time per baseline variant")
+    ap.add_argument("--gather-all", action="store_true",
+                    help="N>1: gather every linear's output, also those whose consumers are column-local")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     desc, items = WORKLOADS[args.config]
@@ -888,6 +1019,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
+        if world > 1:
+            stdout_to_stderr()
         run_reference(args, items, desc, world, rank)
         return
     world, rank, local = dist_setup()

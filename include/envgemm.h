@@ -48,6 +48,8 @@ extern "C" {
 #define ENVG_LAYOUT_GATE_UP 1 /* W [N, K], rows [0, N/2) = gate, [N/2, N) = up (the fused     */
                               /* FLUX linear_in / Qwen3 gate+up tensor, quicknn_transformers.pas */
                               /* :595-597); re-laid out once at upload for ENVG_EPI_SILU_GATE   */
+#define ENVG_LAYOUT_ROUND_BF16 4 /* OR-ed in: round an fp32 / fp16 weight to bf16 (RNE) even when */
+                                 /* its values are not all bf16 numbers (see envg_weight_upload)  */
 
 /* ---- epilogues (envg_linear.epilogue, envg_conv2d.epilogue) -------------------------------- */
 #define ENVG_EPI_NONE 0           /* Y = X.W^T (+ bias if bias != NULL)                         */
@@ -61,6 +63,8 @@ extern "C" {
 #define ENVG_HOST_PTRS 0    /* x, dst, bias, gate are host pointers (pinned or pageable)       */
 #define ENVG_DEVICE_PTRS 1  /* x, dst, bias, gate are device pointers on the current device   */
 #define ENVG_ASYNC 2        /* with ENVG_DEVICE_PTRS: do not wait for completion               */
+#define ENVG_KEEP_SHARDED 4 /* envg_linear_nsplit(_batch): the shard's columns stay on this     */
+                            /* rank (y_local only; no transfer), for column-local consumers     */
 
 /* Opaque device-resident weight (bf16 in HBM, laid out for the kernels). */
 typedef struct envg_weight_s* envg_weight;
@@ -89,9 +93,16 @@ int envg_shutdown(void);
 
 /* Upload a weight once into HBM (replaces the per-call widening of QNNLinearNoBias_BF16,
  * quicknncpu.pas:1830-1847, and the per-step mmap re-reads of quicknn_transformers.pas:1581-1602).
- * Exactly one of w_bf16 (raw bf16 bits, the safetensors dtype BF16) or w_f32 (rounded to bf16
- * with RNE) is non-NULL; both are host pointers to W[N, K] row-major.  After return the host
- * memory may be unmapped (safetensor.pas mmap views). */
+ * Exactly one of w_bf16 (raw bf16 bits, the safetensors dtype BF16) or w_f32 is non-NULL; both
+ * are host pointers to W[N, K] row-major.  After return the host memory may be unmapped
+ * (safetensor.pas mmap views).
+ * An fp32 weight whose values are all bf16 numbers (a widened bf16 checkpoint, the reference's
+ * usual case, safetensor.pas:584-647) is stored as bf16, exactly.  Any other fp32 weight keeps
+ * its precision as a bf16x3 split: each value v becomes hi = bf16_rn(v) and lo = bf16_rn(v - hi),
+ * and the linear multiplies x_hi w_hi + x_hi w_lo + x_lo w_hi on the tensor cores, which matches
+ * the reference's fp32 GEMM (QNNLinearNoBias, quicknncpu.pas:1822-1828) to about 1e-5 relative.
+ * Such a weight holds 6 bytes per value and costs three times the tensor-core work; with
+ * ENVG_LAYOUT_ROUND_BF16 in layout_flags it is rounded to bf16 (RNE) instead, like activations. */
 int envg_weight_upload(const uint16_t* w_bf16, const float* w_f32, int64_t N, int64_t K,
                        int layout_flags, envg_weight* out);
 
@@ -184,6 +195,10 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags);
  * y_local is this rank's copy (read for ENVG_EPI_GATED_RESIDUAL).  The transfer overlaps the
  * remaining tiles, replacing the separate all-gather + reorder of the N-split.  Device pointers
  * only; the caller synchronises the ranks (e.g. a symmetric-memory barrier) before Y is read.
+ * With ENVG_KEEP_SHARDED in flags (or npeers == 0 and y_multicast == NULL) the shard's columns
+ * are written to y_local only: the output stays column-sharded across the ranks, for a consumer
+ * that reads only its own columns (per-head attention after head-aligned Q/K/V shards, the
+ * per-pair SiLU gate after gate/up shards; quicknn_transformers.pas:1402-1405 -> :1174-1183).
  * New with this library (the reference runs on one CPU). */
 int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float* y_multicast, int64_t ldy,
                        int64_t col0, const float* x, envg_weight W, const float* bias, int64_t M,
@@ -192,8 +207,9 @@ int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float*
 /* Several N-split shards in one call, as envg_linear_batch runs several linears: each distinct
  * input is rounded to bf16 once, on a second stream, overlapped with the previous GEMM.  Each
  * descriptor is envg_linear_nsplit's arguments: lin.dst = this rank's copy of Y (row stride ldy),
- * lin.N = the shard's rows of W.  A linear that reads another's Y belongs in a later call, after
- * the ranks' barrier. */
+ * lin.N = the shard's rows of W.  A descriptor with npeers == 0 and y_multicast == NULL (or every
+ * descriptor, with ENVG_KEEP_SHARDED in flags) keeps its shard on this rank.  A linear that reads
+ * another's gathered Y belongs in a later call, after the ranks' barrier. */
 typedef struct envg_nsplit_desc {
   envg_linear_desc lin;
   float* const* y_peers;  /* every rank's copy of Y (this rank's included), or NULL */
@@ -292,8 +308,9 @@ int envg_linear_rmsnorm(float* dst, const float* x, const float* weight, envg_we
  *
  *  - Same arguments and epilogues as envg_linear, but x, dst, bias and gate must be device
  *    pointers: flags must contain ENVG_DEVICE_PTRS (ENVG_ASYNC optional).
- *  - Limits: 1 <= M <= 64 and M * Kp * 2 <= 2 MiB (Kp = K rounded up to 8), i.e. K <= 16384
- *    at M = 64; larger requests return ENVG_ERR_ARG with the limit in envg_last_error().
+ *  - Limits: 0 <= M <= 64 (M = 0 is a no-op) and M * Kp * 2 <= 2 MiB (Kp = K rounded up to 8,
+ *    times 3 for a bf16x3 weight), i.e. K <= 16384 at M = 64; larger requests return
+ *    ENVG_ERR_ARG with the limit in envg_last_error().  dst must not alias x.
  *  - envg_init prepares everything this entry point uses: it loads the code of every kernel it
  *    launches (which, with lazy module loading, would otherwise happen at the first launch and
  *    can map device memory), reserves their local memory, and looks up the array's device
@@ -309,8 +326,9 @@ int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* 
  * slot TQNNSingleOPS.cblas_sgemm (quicknncpu.pas:102-109; enums quicknn_common.pas:54-58:
  * RowMajor = 101, NoTrans = 111, Trans = 112).  Re-pointing that slot to this entry moves
  * every cblas_gemm call (attention products included) to the GPU without model edits.  Both
- * operands are rounded to bf16 (RNE) on the device; C = alpha*A.op(B) + beta*C.  RowMajor,
- * NN/NT/TN only (as qgemm, quicknncpu.pas:1476). */
+ * fp32 operands are split into bf16x3 parts on the device (see envg_weight_upload), so the
+ * tensor-core product matches an fp32 GEMM to about 1e-5 relative; C = alpha*A.op(B) + beta*C.
+ * RowMajor, NN/NT/TN only (as qgemm, quicknncpu.pas:1476). */
 int envg_sgemm(int order, int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,
                const float* A, int64_t lda, const float* B, int64_t ldb, float beta, float* C,
                int64_t ldc);

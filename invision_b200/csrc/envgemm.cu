@@ -22,6 +22,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -116,7 +117,7 @@ int g_cur = -1;
 enum KernelId {
   KID_K1 = 0, KID_K1_SILU_GATE, KID_K1_CONV, KID_K2, KID_GEMV, KID_CAST, KID_ADALN, KID_TRANSPOSE, KID_IM2COL,
   KID_SELFTEST, KID_GN_STATS, KID_GN_AFFINE, KID_GN_APPLY, KID_ATTN, KID_CAST_HEADS, KID_KEY_BITS, KID_ABSMAX,
-  KID_SPLIT_REDUCE, KID_SKINNY_REDUCE, KID_RMSNORM, KID_COUNT
+  KID_SPLIT_REDUCE, KID_SKINNY_REDUCE, KID_RMSNORM, KID_CAST_X3, KID_COUNT
 };
 // Profile names are per family: "k1_gemm*" counts k1_gemm and k1_gemm_pair launches (plain,
 // SiLU-gate, conv), "k2_set" counts k2_set and the no-alloc path's k2_skinny.
@@ -126,7 +127,7 @@ const char* const kKernelNames[KID_COUNT] = {"k1_gemm",     "k1_gemm_silu_gate",
                                              "k_wait_selftest", "k_group_stats",     "k_group_affine",
                                              "k_group_apply",   "k_attention",       "k_cast_heads",
                                              "k_key_bits",      "k_absmax_heads",    "k_split_reduce",
-                                             "k_skinny_reduce", "k_rmsnorm"};
+                                             "k_skinny_reduce", "k_rmsnorm",      "k_cast_x3"};
 struct KAcc {
   uint64_t launches = 0;
   double ms = 0, flops = 0, bytes = 0;
@@ -324,7 +325,9 @@ int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = null
     return ENVG_OK;
   }
   e.store_mode = STORE_DIRECT;
-  const bool aligned = (reinterpret_cast<uintptr_t>(e.Y) & 15) == 0 && e.ldy % 4 == 0;
+  // the maps start at the output's first column (col_off > 0: a kept N-split shard inside a wider Y)
+  const float* ybase = e.Y + e.col_off;
+  const bool aligned = (reinterpret_cast<uintptr_t>(ybase) & 15) == 0 && e.ldy % 4 == 0;
   if (!aligned) {
     if (e.yb) e.store_mode = STORE_COALESCED;  // the bf16 side output is written on the staged paths
     return ENVG_OK;
@@ -333,10 +336,10 @@ int choose_store(bool use_tma, EpiArgs& e, CUtensorMap* tmY, PeerMaps* pm = null
   if (e.mode == EPI_GATED_RES) mode = STORE_TMA_ADD;
   else if (e.mode == EPI_ALPHA_BETA) mode = e.beta == 0.0f ? STORE_TMA : (e.beta == 1.0f ? STORE_TMA_ADD : STORE_DIRECT);
   if (mode == STORE_DIRECT) return ENVG_OK;
-  int rc = tmap_out_2d(tmY, e.Y, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy);
+  int rc = tmap_out_2d(tmY, ybase, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy);
   if (rc != ENVG_OK) return rc;
   if (ybig) {  // k1_gemm_pair's last-unit stores (CTA-high boxes)
-    rc = tmap_out_2d(ybig, e.Y, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy, 128);
+    rc = tmap_out_2d(ybig, ybase, (uint64_t)e.n_out, (uint64_t)e.m_valid, (uint64_t)e.ldy, 128);
     if (rc != ENVG_OK) return rc;
     *ybig_ok = 1;
   }
@@ -353,6 +356,13 @@ uint16_t f32_to_bf16_rne(float f) {
   if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return (uint16_t)((u >> 16) | 0x40);
   u += 0x7FFFu + ((u >> 16) & 1u);
   return (uint16_t)(u >> 16);
+}
+
+float bf16_to_f32(uint16_t b) {
+  const uint32_t u = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
 }
 
 // IEEE binary16 -> binary32 (exact; subnormals normalised, Inf/NaN kept).
@@ -391,6 +401,27 @@ struct WSrc {
     if (h) return f32_to_bf16_rne(f16_to_f32(h[r * ld + k]));
     return f32_to_bf16_rne(f[r * ld + k]);
   }
+  float value(int64_t r, int64_t k) const {
+    if (b) return bf16_to_f32(b[r * ld + k]);
+    if (h) return f16_to_f32(h[r * ld + k]);
+    return f[r * ld + k];
+  }
+  // The low bf16 part of the bf16x3 form (k_cast_x3): bf16_rn(v - hi), 0 for an infinite hi.
+  uint16_t lo_at(int64_t r, int64_t k) const {
+    const float v = value(r, k);
+    const float hv = bf16_to_f32(f32_to_bf16_rne(v));
+    return std::isinf(hv) ? 0 : f32_to_bf16_rne(v - hv);
+  }
+  // true when every value of rows [r0, r1) is exactly a bf16 (then all lo parts are zero)
+  bool bf16_exact(int64_t r0, int64_t r1, int64_t K) const {
+    if (b) return true;
+    for (int64_t r = r0; r < r1; ++r)
+      for (int64_t k = 0; k < K; ++k) {
+        const float v = value(r, k);
+        if (!(bf16_to_f32(f32_to_bf16_rne(v)) == v) && !std::isnan(v)) return false;
+      }
+    return true;
+  }
 };
 
 }  // namespace
@@ -402,7 +433,9 @@ struct envg_weight_s {
   size_t bytes;
   int64_t rows;   // rows stored on the device (padding included)
   int64_t N;      // rows seen by envg_linear (N argument)
-  int64_t K, Kp;  // logical and padded reduction length
+  int64_t K, Kp;  // logical reduction length; device row length (3 * Ks for a bf16x3 weight)
+  int64_t Ks;     // K rounded up to 8: the padded length of one K-segment
+  bool x3;        // bf16x3: rows hold hi | lo | hi segments of the fp32 weight (k_cast_x3)
   int layout;
   int64_t half;   // GATE_UP: gate rows (N/2)
   bool conv;
@@ -891,6 +924,33 @@ int launch_cast_rows(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t 
   return ENVG_OK;
 }
 
+// bf16x3 operand layouts (k_cast_x3): activations hi|hi|lo, weights hi|lo|hi.
+constexpr int X3_ACT = 4;
+constexpr int X3_WEIGHT = 2;
+
+// x fp32 [rows][K] (row stride ldx) -> bf16 [rows][3 * Ks] in the bf16x3 layout lo_mask.
+int launch_cast_x3(Dev* d, const float* x, int64_t ldx, int64_t rows, int64_t K, int64_t Ks, void* out,
+                      int lo_mask) {
+  if (rows == 0) return ENVG_OK;
+  const int64_t work = rows * (Ks / 2);
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(work, 256), (int64_t)d->sms * 8));
+  ProfScope ps(stream_of(d), KID_CAST_X3, 0.0, (double)rows * K * 4 + (double)rows * 3 * Ks * 2);
+  ENVG_TRY(launch_pdl(d, k_cast_x3, dim3(blocks), dim3(256), 0, x, ldx, (int)rows, (int)K, (int)Ks,
+                      reinterpret_cast<__nv_bfloat16*>(out), lo_mask));
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
+// src fp32 [R][C] (row stride lds) -> bf16 [C][3 * Rs], the transpose in the bf16x3 layout lo_mask.
+int launch_transpose_x3(Dev* d, const float* src, int64_t lds, int R, int C, void* dst, int Rs, int lo_mask) {
+  ProfScope ps(stream_of(d), KID_CAST_X3, 0.0, (double)R * C * 4 + (double)C * 3 * Rs * 2);
+  dim3 grid((unsigned)cdiv(C, 32), (unsigned)cdiv(Rs, 64), 1);
+  ENVG_TRY(launch_pdl(d, k_transpose_cast_x3, grid, dim3(256), 0, src, lds, R, C,
+                      reinterpret_cast<__nv_bfloat16*>(dst), Rs, lo_mask));
+  d->st.kernel_launches++;
+  return ENVG_OK;
+}
+
 // fp32 [batch][R][C] -> bf16 [batch][C][Rp]
 int launch_transpose_cast(Dev* d, const float* src, int64_t lds, int64_t sbs, int R, int C, void* dst, int64_t ldd,
                           int64_t dbs, int Rp, int batch, const float2* aff = nullptr, int act = 0) {
@@ -1112,6 +1172,8 @@ int upload_common(Dev* d, WSrc src, int64_t N, int64_t K, int64_t n0, int64_t n1
   if (!out) return fail(ENVG_ERR_ARG, "out handle pointer is NULL");
   *out = nullptr;
   if (N <= 0 || K <= 0) return fail(ENVG_ERR_ARG, "weight shape [%lld, %lld] invalid", (long long)N, (long long)K);
+  const bool round_bf16 = (layout & ENVG_LAYOUT_ROUND_BF16) != 0;
+  layout &= ~ENVG_LAYOUT_ROUND_BF16;
   if (layout != ENVG_LAYOUT_PLAIN && layout != ENVG_LAYOUT_GATE_UP)
     return fail(ENVG_ERR_ARG, "unknown layout flag %d", layout);
   const bool gu = layout == ENVG_LAYOUT_GATE_UP;
@@ -1119,21 +1181,38 @@ int upload_common(Dev* d, WSrc src, int64_t N, int64_t K, int64_t n0, int64_t n1
   const int64_t lim = gu ? N / 2 : N;
   if (n0 < 0 || n1 > lim || n0 >= n1)
     return fail(ENVG_ERR_ARG, "shard [%lld, %lld) outside [0, %lld)", (long long)n0, (long long)n1, (long long)lim);
+  // An fp32 / fp16 weight whose values are not all bf16 numbers keeps its low parts: the bf16x3
+  // form (k_cast_x3), unless the caller asked for plain RNE rounding.
+  bool x3 = !round_bf16 && !src.b;
+  if (x3) x3 = !(src.bf16_exact(n0, n1, K) && (!gu || src.bf16_exact(N / 2 + n0, N / 2 + n1, K)));
   auto* w = new envg_weight_s();
   w->magic = WEIGHT_MAGIC;
   w->dev = d->id;
   w->K = K;
-  w->Kp = rup(K, 8);
+  w->Ks = rup(K, 8);
+  w->x3 = x3;
+  w->Kp = x3 ? 3 * w->Ks : w->Ks;
   w->layout = layout;
   w->conv = false;
   std::vector<uint16_t> host;
+  // device row rd <- source row rs: hi parts, or hi | lo | hi for a bf16x3 weight
+  auto put = [&](int64_t rd, int64_t rs) {
+    uint16_t* row = &host[(size_t)(rd * w->Kp)];
+    for (int64_t k = 0; k < K; ++k) {
+      const uint16_t hb = src.at(rs, k);
+      row[k] = hb;
+      if (x3) {
+        row[w->Ks + k] = src.lo_at(rs, k);
+        row[2 * w->Ks + k] = hb;
+      }
+    }
+  };
   const int64_t cnt = n1 - n0;
   if (!gu) {
     w->N = cnt;
     w->rows = cnt;
     host.assign((size_t)(w->rows * w->Kp), 0);
-    for (int64_t r = 0; r < cnt; ++r)
-      for (int64_t k = 0; k < K; ++k) host[(size_t)(r * w->Kp + k)] = src.at(n0 + r, k);
+    for (int64_t r = 0; r < cnt; ++r) put(r, n0 + r);
   } else {
     // Interleave per 128-row block: device rows [256t, 256t+128) = gate rows [128t, 128t+128),
     // rows [256t+128, 256t+256) = the matching up rows; missing rows are zero.
@@ -1146,10 +1225,8 @@ int upload_common(Dev* d, WSrc src, int64_t N, int64_t K, int64_t n0, int64_t n1
     for (int64_t j = 0; j < cnt; ++j) {
       const int64_t t = j / BM, i = j % BM;
       const int64_t rg = 2 * BM * t + i, ru = rg + BM;
-      for (int64_t k = 0; k < K; ++k) {
-        host[(size_t)(rg * w->Kp + k)] = src.at(n0 + j, k);
-        host[(size_t)(ru * w->Kp + k)] = src.at(half + n0 + j, k);
-      }
+      put(rg, n0 + j);
+      put(ru, half + n0 + j);
     }
   }
   int rc = finish_weight(d, w, host);
@@ -1181,6 +1258,7 @@ int conv_upload_common(Dev* d, WSrc src, int out_ch, int in_ch, int kH, int kW, 
   w->Cp = (int)rup(in_ch, BK);
   w->K = (int64_t)in_ch * kH * kW;
   w->Kp = (int64_t)kH * kW * w->Cp;
+  w->Ks = w->Kp;
   w->N = out_ch;
   w->rows = out_ch;
   w->layout = ENVG_LAYOUT_PLAIN;
@@ -1315,7 +1393,8 @@ int noalloc_scratch(Dev* d, uint8_t** out) {
 // which takes device memory.  With lazy module loading the runtime loads a kernel's code on its
 // first use and may map a new block of device memory for it, and a kernel that needs more local
 // memory per thread than the context holds grows that reservation at its first launch.  So this
-// loads every kernel the entry point launches (the eight k2_skinny shapes and k_cast_rows),
+// loads every kernel the entry point launches (the eight k2_skinny shapes, k_cast_rows and, for
+// bf16x3 weights, k_cast_x3),
 // raises the context's stack limit to their largest local-memory need, looks up the scratch
 // array and issues one memset into it.
 int noalloc_preload(Dev* d) {
@@ -1329,8 +1408,11 @@ int noalloc_preload(Dev* d) {
   ENVG_TRY((k2_prepare<48, 2>(&l))); need = std::max(need, l);
   ENVG_TRY((k2_prepare<64, 2>(&l))); need = std::max(need, l);
   ENVG_TRY(load_kernel(reinterpret_cast<const void*>(k_cast_rows)));
+  ENVG_TRY(load_kernel(reinterpret_cast<const void*>(k_cast_x3)));
   cudaFuncAttributes fa;
   ENVG_CUDA(cudaFuncGetAttributes(&fa, k_cast_rows));
+  need = std::max(need, fa.localSizeBytes);
+  ENVG_CUDA(cudaFuncGetAttributes(&fa, k_cast_x3));
   need = std::max(need, fa.localSizeBytes);
   size_t have = 0;
   ENVG_CUDA(cudaDeviceGetLimit(&have, cudaLimitStackSize));
@@ -1628,9 +1710,20 @@ int stage_prologue(Dev* d, const Prologue& p, int64_t K, cudaStream_t s, Prologu
 }
 
 // Normalises (or only casts) rows of x into out: bf16 padded to Kp, or fp32 with K columns
-// (bf16 = false, only for a prologue other than NONE).
+// (bf16 = false, only for a prologue other than NONE).  For a bf16x3 weight (x3), Kp is its
+// device row length 3 * Ks and out receives the activation layout hi|hi|lo; a prologue first
+// writes its fp32 rows into the workspace d->xn.
 int launch_prologue(Dev* d, const Prologue& p, const float* x, int64_t rows, int64_t K, int64_t Kp, void* out,
-                    bool bf16) {
+                    bool bf16, bool x3 = false) {
+  if (x3) {
+    const float* src = x;
+    if (p.kind != Prologue::NONE) {
+      ENVG_TRY(ensure(d, d->xn, (size_t)(rows * K) * 4));
+      ENVG_TRY(launch_prologue(d, p, x, rows, K, K, d->xn.p, false));
+      src = reinterpret_cast<const float*>(d->xn.p);
+    }
+    return launch_cast_x3(d, src, K, rows, K, Kp / 3, out, X3_ACT);
+  }
   switch (p.kind) {
     case Prologue::ADALN: return launch_adaln(d, x, rows, K, Kp, p.shift, p.scale, out, bf16);
     case Prologue::RMS: return launch_rmsnorm(d, x, rows, K, Kp, p.rms_w, out, bf16);
@@ -1704,7 +1797,7 @@ int linear_host_pipelined(Dev* d, float* dst, const float* x, envg_weight W, con
     chunk(c, r0, rows);
     ENVG_CUDA(cudaStreamWaitEvent(s, pipe_event(d, 1 + 2 * c), 0));
     void* xb = reinterpret_cast<uint8_t*>(d->xb.p) + (size_t)(r0 * W->Kp) * 2;
-    ENVG_TRY(launch_prologue(d, dpro, dx + r0 * K, rows, K, W->Kp, xb, true));
+    ENVG_TRY(launch_prologue(d, dpro, dx + r0 * K, rows, K, W->Kp, xb, true, W->x3));
     EpiArgs e{};
     e.Y = dy + r0 * n_out;
     e.ldy = n_out;
@@ -1805,7 +1898,7 @@ int linear_core(Dev* d, float* dst, const float* x, envg_weight W, const float* 
   const double lin_flops = 2.0 * (double)M * (double)N * (double)K;
   const double out_bytes = 4.0 * (double)M * n_out + (dbias ? 4.0 * N : 0.0) +
                            (epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)M * n_out + 4.0 * N : 0.0);
-  if (M <= d->gemv_max) {
+  if (M <= d->gemv_max && !W->x3) {
     if (dpro.kind != Prologue::NONE) {  // normalised X kept in fp32 for the CUDA-core path
       ENVG_TRY(ensure(d, d->xn, (size_t)(M * K) * 4));
       ENVG_TRY(launch_prologue(d, dpro, dx, M, K, K, d->xn.p, false));
@@ -1815,7 +1908,7 @@ int linear_core(Dev* d, float* dst, const float* x, envg_weight W, const float* 
     ENVG_TRY(launch_gemv(d, dx, M, K, W, gu, e, lin_flops, 2.0 * (double)N * K + 4.0 * (double)M * K + out_bytes));
   } else {
     ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
-    ENVG_TRY(launch_prologue(d, dpro, dx, M, K, W->Kp, d->xb.p, true));
+    ENVG_TRY(launch_prologue(d, dpro, dx, M, K, W->Kp, d->xb.p, true, W->x3));
     ENVG_TRY(gemm_device(d, d->xb.p, M, W->Kp, W->tm256, W->tm128, W->rows, gu, e, lin_flops,
                          2.0 * (double)N * K + 2.0 * (double)M * W->Kp + out_bytes));
   }
@@ -1866,6 +1959,10 @@ int envg_linear_rmsnorm(float* dst, const float* x, const float* weight, envg_we
   return linear_core(d, dst, x, W, bias, M, K, N, epilogue, gate, flags, p);
 }
 
+namespace {
+EpiArgs linear_epi(const envg_linear_desc& q);  // the epilogue arguments of one linear (below)
+}  // namespace
+
 int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* bias, int64_t M, int64_t K, int64_t N,
                         int epilogue, const float* gate, int flags) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
@@ -1900,6 +1997,7 @@ int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* 
                 (long long)n_tiles, NOALLOC_CNT_BYTES / sizeof(int));
   if (M == 0) return ENVG_OK;
   if (!dst || !x) return fail(ENVG_ERR_ARG, "envg_linear_noalloc: dst or x is NULL");
+  if ((const void*)dst == (const void*)x) return fail(ENVG_ERR_ARG, "envg_linear_noalloc: dst aliases x");
   uint8_t* scratch = nullptr;
   ENVG_TRY(noalloc_scratch(d, &scratch));
   uint8_t* xb = scratch;
@@ -1908,7 +2006,8 @@ int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* 
   cudaStream_t s = stream_of(d);
   const int64_t n_out = gu ? N / 2 : N;
 
-  ENVG_TRY(launch_cast_rows(d, x, K, M, K, W->Kp, xb));
+  if (W->x3) ENVG_TRY(launch_cast_x3(d, x, K, M, K, W->Ks, xb, X3_ACT));
+  else ENVG_TRY(launch_cast_rows(d, x, K, M, K, W->Kp, xb));
   const int mpad = (int)rup(M, 16);
   const int64_t num_kb = cdiv(W->Kp, BK);
   SkinnyArgs a{};
@@ -1925,18 +2024,7 @@ int envg_linear_noalloc(float* dst, const float* x, envg_weight W, const float* 
     a.partial = part;
     a.counters = cnt;
   }
-  EpiArgs e{};
-  e.Y = dst;
-  e.ldy = n_out;
-  e.bias = bias;
-  e.bias_mode = bias ? 1 : 0;
-  e.mode = (epilogue == ENVG_EPI_GATED_RESIDUAL) ? EPI_GATED_RES : EPI_PLAIN;
-  e.gate = gate;
-  e.alpha = 1.0f;
-  e.n_out = (int)n_out;
-  e.m_valid = (int)M;
-  e.half_n = (int)(gu ? W->half : 0);
-  a.epi = e;
+  a.epi = linear_epi(envg_linear_desc{dst, x, W, bias, M, K, N, epilogue, gate});
   CUtensorMap tX;
   ENVG_TRY(tmap_2d(&tX, xb, W->Kp, M, mpad));
   ENVG_TRY(launch_k2(d, mpad, R, W->tm128, tX, a, 2.0 * (double)M * N * K,
@@ -2181,6 +2269,11 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
   if (n < 0 || (n > 0 && !descs)) return fail(ENVG_ERR_ARG, "envg_linear_batch: bad descriptor array");
   if (!(flags & ENVG_DEVICE_PTRS)) return fail(ENVG_ERR_ARG, "envg_linear_batch: needs device pointers");
   for (int i = 0; i < n; ++i) ENVG_TRY(check_linear_args(d, descs[i]));
+  // An N-split shard keeps its output on this rank (columns [col0, col0 + width) of y_local only)
+  // with ENVG_KEEP_SHARDED, or when the descriptor names no peer copies and no multicast address.
+  auto keeps_shard = [&](int i) {
+    return ns && ((flags & ENVG_KEEP_SHARDED) || (ns[i].npeers == 0 && !ns[i].y_multicast));
+  };
   auto nsplit_epi = [&](int i, EpiArgs& e) -> int {
     if (!ns) return ENVG_OK;
     const envg_nsplit_desc& x = ns[i];
@@ -2188,12 +2281,15 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     if (x.col0 < 0 || x.col0 + n_out > x.ldy)
       return fail(ENVG_ERR_ARG, "nsplit: columns [%lld, %lld) outside ldy %lld", (long long)x.col0,
                   (long long)(x.col0 + n_out), (long long)x.ldy);
-    if (!x.y_multicast && (x.npeers < 1 || x.npeers > 8 || !x.y_peers))
+    const bool keep = keeps_shard(i);
+    if (!keep && !x.y_multicast && (x.npeers < 1 || x.npeers > 8 || !x.y_peers))
       return fail(ENVG_ERR_ARG, "nsplit: give a multicast address or 1..8 peer copies of Y");
     e.ldy = x.ldy;
     e.col_off = (int)x.col0;
     bool aligned = (reinterpret_cast<uintptr_t>(e.Y) & 15) == 0 && x.ldy % 4 == 0 && x.col0 % 4 == 0;
-    if (x.y_multicast) {
+    if (keep) {
+      e.nremote = 0;  // the epilogue stores into this rank's y_local only
+    } else if (x.y_multicast) {
       e.nremote = -1;
       e.remote[0] = x.y_multicast;
       aligned = aligned && (reinterpret_cast<uintptr_t>(x.y_multicast) & 15) == 0;
@@ -2229,7 +2325,7 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
   };
   for (int i = 0; i < n; ++i) {
     const envg_linear_desc& q = descs[i];
-    if (q.M == 0 || q.M <= d->gemv_max) continue;
+    if (q.M == 0 || q.M <= d->gemv_max || q.W->x3) continue;  // k_gemv reads fp32 x; bf16x3: below
     for (size_t j = 0; j < first_use.size(); ++j) {
       const envg_linear_desc& p = descs[first_use[j]];
       if (p.x == q.x && p.M == q.M && p.W->Kp == q.W->Kp && p.K == q.K) {
@@ -2375,11 +2471,28 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     const char* x1 = x0 + (size_t)(c.M * c.K) * 4;
     return pr.M > 0 && x0 < y1 && y0 < x1;
   };
+  // Every epilogue reads its linear's bias (N floats) and, for the gated residual, its gate
+  // (N floats).  Inside one launch a member must neither read a vector that another member
+  // writes nor write over one that another member reads.
+  auto vectors_meet_output = [&](const envg_linear_desc& c, const envg_linear_desc& pr) {
+    if (pr.M <= 0 || c.M <= 0) return false;
+    const char *y0, *y1;
+    out_range(pr, &y0, &y1);
+    auto hits = [&](const float* v) {
+      const char* v0 = reinterpret_cast<const char*>(v);
+      return v && v0 < y1 && y0 < v0 + (size_t)c.N * 4;
+    };
+    return hits(c.bias) || (c.epilogue == ENVG_EPI_GATED_RESIDUAL && hits(c.gate));
+  };
+  auto vector_hazard = [&](const envg_linear_desc& a, const envg_linear_desc& b) {
+    return vectors_meet_output(a, b) || vectors_meet_output(b, a);
+  };
   for (int i = 0; i < n; ++i) {
     const envg_linear_desc& q = descs[i];
     const bool is_k2 = src_of[i] >= 0 && q.M <= d->skinny_max;
-    const bool is_pair = src_of[i] >= 0 && !is_k2 && d->use_pair && q.M > BM && !ns;
-    if (src_of[i] >= 0) ENVG_TRY(flush_gemv());  // a tcgen05 linear follows the pending gemv ones
+    const bool is_pair = src_of[i] >= 0 && !is_k2 && d->use_pair && q.M > BM && (!ns || keeps_shard(i));
+    const bool is_x3 = q.M > 0 && q.W->x3;
+    if (src_of[i] >= 0 || is_x3) ENVG_TRY(flush_gemv());  // a tcgen05 linear follows the pending gemv ones
     if (!is_k2) ENVG_TRY(flush_k2());
     if (!is_pair) ENVG_TRY(flush_pair());
     // casts run one linear ahead of the GEMMs, in order, as soon as their inputs exist; a cast
@@ -2404,7 +2517,14 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
     const double fl = 2.0 * (double)q.M * (double)q.N * (double)q.K;
     const double ob = 4.0 * (double)q.M * n_out + (q.bias ? 4.0 * q.N : 0.0) +
                       (q.epilogue == ENVG_EPI_GATED_RESIDUAL ? 4.0 * (double)q.M * n_out + 4.0 * q.N : 0.0);
-    if (src_of[i] < 0) {
+    if (is_x3) {
+      // A bf16x3 weight (fp32 values kept as hi / lo parts) takes its own activation layout
+      // hi|hi|lo, made here on s after every earlier linear, then runs alone.
+      ENVG_TRY(ensure(d, d->xb, (size_t)(q.M * q.W->Kp) * 2));
+      ENVG_TRY(launch_cast_x3(d, q.x, q.K, q.M, q.K, q.W->Ks, d->xb.p, X3_ACT));
+      ENVG_TRY(gemm_device(d, d->xb.p, q.M, q.W->Kp, q.W->tm256, q.W->tm128, q.W->rows, gu, e, fl,
+                           2.0 * (double)q.N * q.K + 2.0 * (double)q.M * q.W->Kp + ob));
+    } else if (src_of[i] < 0) {
       const char *qy0, *qy1;
       out_range(q, &qy0, &qy1);
       // a set runs its linears at once: none may read or write over another's output, and since
@@ -2412,7 +2532,8 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
       for (int k : gidx) {
         const char *ky0, *ky1;
         out_range(descs[k], &ky0, &ky1);
-        if (reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1) || writes_input_of(i, descs[k])) {
+        if (reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1) || writes_input_of(i, descs[k]) ||
+            vector_hazard(q, descs[k])) {
           ENVG_TRY(flush_gemv());
           break;
         }
@@ -2430,7 +2551,7 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
       for (int k : kidx) {  // a set runs its linears at once: no reads of, or writes over, its outputs
         const char *ky0, *ky1;
         out_range(descs[k], &ky0, &ky1);
-        flush = flush || reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1);
+        flush = flush || reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1) || vector_hazard(q, descs[k]);
       }
       if (flush) ENVG_TRY(flush_k2());
       if ((size_t)src_of[i] >= next_copy) {
@@ -2454,7 +2575,7 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
       for (int k : pidx) {
         const char *py0, *py1;
         out_range(descs[k], &py0, &py1);
-        flush = flush || reads_output_of(q, descs[k]) || (qy0 < py1 && py0 < qy1);
+        flush = flush || reads_output_of(q, descs[k]) || (qy0 < py1 && py0 < qy1) || vector_hazard(q, descs[k]);
       }
       if (flush) ENVG_TRY(flush_pair());
       if ((size_t)src_of[i] >= next_copy) {
@@ -2522,14 +2643,17 @@ int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float*
   const int64_t n_out = gu ? N / 2 : N;
   if (col0 < 0 || col0 + n_out > ldy) return fail(ENVG_ERR_ARG, "envg_linear_nsplit: columns [%lld, %lld) outside ldy %lld",
                                                   (long long)col0, (long long)(col0 + n_out), (long long)ldy);
-  if (!y_multicast && (npeers < 1 || npeers > 8 || !y_peers))
+  const bool keep = (flags & ENVG_KEEP_SHARDED) || (npeers == 0 && !y_multicast);
+  if (!keep && !y_multicast && (npeers < 1 || npeers > 8 || !y_peers))
     return fail(ENVG_ERR_ARG, "envg_linear_nsplit: give a multicast address or 1..8 peer copies of Y");
   if (M == 0) return ENVG_OK;
   EpiArgs e = linear_epi(q);
   e.ldy = ldy;
   e.col_off = (int)col0;
   bool aligned = (reinterpret_cast<uintptr_t>(y_local) & 15) == 0 && ldy % 4 == 0 && col0 % 4 == 0;
-  if (y_multicast) {
+  if (keep) {
+    e.nremote = 0;  // the epilogue stores into this rank's y_local only
+  } else if (y_multicast) {
     e.nremote = -1;
     e.remote[0] = y_multicast;
     aligned = aligned && (reinterpret_cast<uintptr_t>(y_multicast) & 15) == 0;
@@ -2544,11 +2668,12 @@ int envg_linear_nsplit(float* y_local, float* const* y_peers, int npeers, float*
   e.vec_ok = (aligned && n_out % 4 == 0) ? 1 : 0;
   const double fl = 2.0 * (double)M * (double)N * (double)K;
   const double ob = 4.0 * (double)M * n_out + (bias ? 4.0 * N : 0.0);
-  if (M <= d->gemv_max) {
+  if (M <= d->gemv_max && !W->x3) {
     ENVG_TRY(launch_gemv(d, x, M, K, W, gu, e, fl, 2.0 * (double)N * K + 4.0 * (double)M * K + ob));
   } else {
     ENVG_TRY(ensure(d, d->xb, (size_t)(M * W->Kp) * 2));
-    ENVG_TRY(launch_cast_rows(d, x, K, M, K, W->Kp, d->xb.p));
+    if (W->x3) ENVG_TRY(launch_cast_x3(d, x, K, M, K, W->Ks, d->xb.p, X3_ACT));
+    else ENVG_TRY(launch_cast_rows(d, x, K, M, K, W->Kp, d->xb.p));
     ENVG_TRY(gemm_device(d, d->xb.p, M, W->Kp, W->tm256, W->tm128, W->rows, gu, e, fl,
                          2.0 * (double)N * K + 2.0 * (double)M * W->Kp + ob));
   }
@@ -2928,7 +3053,10 @@ int envg_sgemm(int order, int transA, int transB, int64_t M, int64_t N, int64_t 
     return fail(ENVG_ERR_ARG, "envg_sgemm: leading dimension too small");
   if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return fail(ENVG_ERR_ARG, "envg_sgemm: size too large");
   cudaStream_t s = stream_of(d);
-  const int64_t Kp = rup(std::max<int64_t>(K, 1), 8);
+  // Both operands in the bf16x3 layout (k_cast_x3): A as hi|hi|lo, B as hi|lo|hi, so the
+  // tensor-core GEMM over Kp = 3 * Ks sums a_hi b_hi + a_hi b_lo + a_lo b_hi.
+  const int64_t Ks = rup(std::max<int64_t>(K, 1), 8);
+  const int64_t Kp = 3 * Ks;
   ENVG_TRY(ensure(d, d->x, (size_t)(arows * acols) * 4));
   ENVG_TRY(ensure(d, d->b32, (size_t)(brows * bcols) * 4));
   ENVG_TRY(ensure(d, d->y, (size_t)(M * N) * 4));
@@ -2949,10 +3077,10 @@ int envg_sgemm(int order, int transA, int transB, int64_t M, int64_t N, int64_t 
     ENVG_CUDA(cudaMemsetAsync(d->xb.p, 0, (size_t)(M * Kp) * 2, s));
     ENVG_CUDA(cudaMemsetAsync(d->wb.p, 0, (size_t)(N * Kp) * 2, s));
   } else {
-    if (!ta) ENVG_TRY(launch_cast_rows(d, a32, K, M, K, Kp, d->xb.p));
-    else ENVG_TRY(launch_transpose_cast(d, a32, M, 0, (int)K, (int)M, d->xb.p, Kp, 0, (int)Kp, 1));
-    if (tb) ENVG_TRY(launch_cast_rows(d, b32, K, N, K, Kp, d->wb.p));
-    else ENVG_TRY(launch_transpose_cast(d, b32, N, 0, (int)K, (int)N, d->wb.p, Kp, 0, (int)Kp, 1));
+    if (!ta) ENVG_TRY(launch_cast_x3(d, a32, K, M, K, Ks, d->xb.p, X3_ACT));
+    else ENVG_TRY(launch_transpose_x3(d, a32, M, (int)K, (int)M, d->xb.p, (int)Ks, X3_ACT));
+    if (tb) ENVG_TRY(launch_cast_x3(d, b32, K, N, K, Ks, d->wb.p, X3_WEIGHT));
+    else ENVG_TRY(launch_transpose_x3(d, b32, N, (int)K, (int)N, d->wb.p, (int)Ks, X3_WEIGHT));
   }
   CUtensorMap b256, b128;
   ENVG_TRY(tmap_2d(&b256, d->wb.p, Kp, N, 256));

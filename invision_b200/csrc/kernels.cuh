@@ -2198,6 +2198,82 @@ __global__ void __launch_bounds__(256) k_transpose_cast_v(const float* __restric
   }
 }
 
+// ---- bf16x3 operands for fp32 inputs ----------------------------------------------------------
+// An fp32 value v is held as two bf16 parts, hi = bf16_rn(v) and lo = bf16_rn(v - hi); hi + lo
+// equals v to about 2^-17 relative (v - hi is exact in fp32).  An operand row of K values becomes
+// three K-segments of Ks = K rounded up to 8 (zeros in [K, Ks)), each holding the hi or the lo
+// parts; bit s of lo_mask marks segment s as lo.  One bf16 GEMM over the 3 * Ks columns of an
+// activation laid out hi|hi|lo (mask 4) and a weight laid out hi|lo|hi (mask 2) accumulates
+//   x_hi w_hi + x_hi w_lo + x_lo w_hi
+// in fp32: the bf16x3 product of Henry, Tang and Heinecke ("Leveraging the bfloat16 Artificial
+// Intelligence Datatype For Higher-Precision Computations", ARITH 2019).  The dropped x_lo w_lo
+// term and the two residuals are each about 2^-16 of the product, so the GEMM matches an fp32
+// GEMM to fp32-accumulation accuracy instead of carrying the 2^-9 rounding of bf16 operands.
+// (An infinite hi, from an infinite v or one that rounds up past the bf16 range, takes lo = 0 so
+// that the sum stays infinite instead of becoming inf - inf.)
+ENVG_DEV void split_bf16(float v, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(v);
+  const float h = __bfloat162float(hi);
+  lo = __float2bfloat16_rn(isinf(h) ? 0.0f : v - h);
+}
+
+// X fp32 [rows][K] (row stride ldx) -> Xs bf16 [rows][3 * Ks], segments per lo_mask.  One thread
+// per pair of columns (Ks is even).
+__global__ void __launch_bounds__(256) k_cast_x3(const float* __restrict__ X, int64_t ldx, int rows, int K,
+                                                    int Ks, __nv_bfloat16* __restrict__ Xs, int lo_mask) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int64_t pairs = (int64_t)rows * (Ks / 2);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += stride) {
+    const int64_t r = i / (Ks / 2);
+    const int c = (int)(i - r * (Ks / 2)) * 2;
+    const float v0 = c < K ? X[r * ldx + c] : 0.0f;
+    const float v1 = c + 1 < K ? X[r * ldx + c + 1] : 0.0f;
+    __nv_bfloat162 hi, lo;
+    split_bf16(v0, hi.x, lo.x);
+    split_bf16(v1, hi.y, lo.y);
+    __nv_bfloat16* row = Xs + r * 3 * (int64_t)Ks + c;
+#pragma unroll
+    for (int s = 0; s < 3; ++s)
+      *reinterpret_cast<__nv_bfloat162*>(row + (int64_t)s * Ks) = ((lo_mask >> s) & 1) ? lo : hi;
+  }
+}
+
+// src fp32 [R][C] (row stride lds) -> dst bf16 [C][3 * Rs] (the transpose, split as k_cast_x3;
+// zeros for R <= r < Rs).  Rs must be even.  64 x 32 tiles through shared memory.
+__global__ void __launch_bounds__(256) k_transpose_cast_x3(const float* __restrict__ src, int64_t lds, int R, int C,
+                                                         __nv_bfloat16* __restrict__ dst, int Rs, int lo_mask) {
+  __shared__ float t[64][33];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int c0 = blockIdx.x * 32;
+  const int r0 = blockIdx.y * 64;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = ty + i * 8;
+    const int r = r0 + rr, c = c0 + tx;
+    t[rr][tx] = (r < R && c < C) ? src[(int64_t)r * lds + c] : 0.0f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int idx = threadIdx.x + i * 256;
+    const int cc = idx >> 5, rp = idx & 31;
+    const int c = c0 + cc, r = r0 + 2 * rp;
+    if (c < C && r < Rs) {
+      __nv_bfloat162 hi, lo;
+      split_bf16(t[2 * rp][cc], hi.x, lo.x);
+      split_bf16(t[2 * rp + 1][cc], hi.y, lo.y);
+      __nv_bfloat16* row = dst + (int64_t)c * 3 * Rs + r;
+#pragma unroll
+      for (int s = 0; s < 3; ++s)
+        *reinterpret_cast<__nv_bfloat162*>(row + (int64_t)s * Rs) = ((lo_mask >> s) & 1) ? lo : hi;
+    }
+  }
+}
+
 // Explicit im2col for strided convolutions: NHWC bf16 [B][H][W][Cp] -> col bf16
 // [B][outH*outW][KH*KW*Cp] in (kh, kw, c) order, zeros outside the image.  8 channels/thread.
 __global__ void k_im2col_nhwc(const __nv_bfloat16* __restrict__ in, int B, int H, int W, int Cp, int KH, int KW,

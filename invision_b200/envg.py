@@ -24,9 +24,9 @@ HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "envgemm.h")
 
 OK = 0
 ERR_ARG, ERR_OOM, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_STATE, ERR_UNSUPPORTED = -1, -2, -3, -4, -5, -6, -7
-LAYOUT_PLAIN, LAYOUT_GATE_UP = 0, 1
+LAYOUT_PLAIN, LAYOUT_GATE_UP, LAYOUT_ROUND_BF16 = 0, 1, 4
 EPI_NONE, EPI_BIAS, EPI_SILU_GATE, EPI_GATED_RESIDUAL, EPI_SILU = 0, 1, 2, 3, 4
-HOST_PTRS, DEVICE_PTRS, ASYNC = 0, 1, 2
+HOST_PTRS, DEVICE_PTRS, ASYNC, KEEP_SHARDED = 0, 1, 2, 4
 ROW_MAJOR, NO_TRANS, TRANS = 101, 111, 112
 DTYPE_OTHER, DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2, 3
 CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
@@ -169,9 +169,9 @@ def profile(enable):
 
 def profile_read():
     """{kernel family: {launches, ms, flops, bytes}} accumulated since profile(True)."""
-    arr = (KernelStat * 16)()
+    arr = (KernelStat * 32)()
     n = _ci(0)
-    _check(lib().envg_profile_read(arr, 16, ctypes.byref(n)))
+    _check(lib().envg_profile_read(arr, 32, ctypes.byref(n)))
     return {arr[i].name.decode(): {"launches": arr[i].launches, "ms": arr[i].ms, "flops": arr[i].flops,
                                    "bytes": arr[i].bytes} for i in range(n.value)}
 
@@ -247,8 +247,11 @@ def _mode(*arrays):
 class Weight:
     """A device-resident bf16 weight (envg_weight handle).
 
-    ``w`` is W[N, K] row-major as numpy uint16 (raw bf16 bits) or float32 (rounded to bf16 with
-    round-to-nearest-even at upload).  ``shard=(n0, n1)`` uploads only output rows [n0, n1)
+    ``w`` is W[N, K] row-major as numpy uint16 (raw bf16 bits) or float32.  A float32 weight
+    whose values are all bf16 numbers is stored as bf16; any other keeps its precision as a
+    bf16x3 split (hi / lo parts, three times the tensor-core work), unless ``layout`` has
+    ``LAYOUT_ROUND_BF16`` OR-ed in, which rounds it to bf16 (RNE).  ``shard=(n0, n1)`` uploads only
+    output rows [n0, n1)
     (for GATE_UP: gate rows [n0, n1) and the same up rows).  ``conv=(out_ch, in_ch, kH, kW)``
     uploads a convolution weight [out_ch, in_ch, kH, kW].
     """
@@ -266,6 +269,7 @@ class Weight:
             raise TypeError("weight must be uint16 (bf16 bits) or float32")
         h = _vp()
         L = lib()
+        kind = layout & ~LAYOUT_ROUND_BF16
         if conv is not None:
             O, C, kH, kW = conv
             assert w.size == O * C * kH * kW, "ERROR : conv weight size mismatch"
@@ -279,9 +283,9 @@ class Weight:
             else:
                 n0, n1 = shard
                 _check(L.envg_weight_upload_shard(pb, pf, N, K, n0, n1, layout, ctypes.byref(h)))
-                self.N = (n1 - n0) * (2 if layout == LAYOUT_GATE_UP else 1)
+                self.N = (n1 - n0) * (2 if kind == LAYOUT_GATE_UP else 1)
             self.K = K
-        self.layout = layout
+        self.layout = kind
         self.conv = conv
         self.h = h
 
@@ -303,9 +307,9 @@ class Weight:
             self.N, self.K = shape[0], shape[1] * shape[2] * shape[3]
         else:
             self.conv = None
-            rows = shape[0] if shard is None else (n1 - n0) * (2 if layout == LAYOUT_GATE_UP else 1)
+            rows = shape[0] if shard is None else (n1 - n0) * (2 if layout & 3 == LAYOUT_GATE_UP else 1)
             self.N, self.K = rows, shape[1]
-        self.layout = layout
+        self.layout = layout & ~LAYOUT_ROUND_BF16
         self.h = h
         return self
 
@@ -371,6 +375,21 @@ def linear_rmsnorm(dst, x, W, weight=None, bias=None, epilogue=None, gate=None, 
     M, K = x.shape
     return _check(lib().envg_linear_rmsnorm(_ptr(dst), _ptr(x), _ptr(weight), W.h, _ptr(bias), M, K, W.N, epilogue,
                                             _ptr(gate), flags))
+
+
+def linear_noalloc(dst, x, W, bias=None, epilogue=None, gate=None, sync=True):
+    """dst = epilogue(x . W^T) through envg_linear_noalloc, which allocates no device memory (its
+    scratch is a fixed array in the library).  Torch CUDA tensors only; M <= 64."""
+    if epilogue is None:
+        epilogue = EPI_SILU_GATE if W.layout == LAYOUT_GATE_UP else (EPI_BIAS if bias is not None else EPI_NONE)
+    flags = _mode(dst, x, bias, gate)
+    if flags != DEVICE_PTRS:
+        raise TypeError("linear_noalloc takes torch CUDA tensors (device pointers) only")
+    if not sync:
+        flags |= ASYNC
+    M, K = x.shape
+    return _check(lib().envg_linear_noalloc(_ptr(dst), _ptr(x), W.h, _ptr(bias), M, K, W.N, epilogue, _ptr(gate),
+                                            flags))
 
 
 def linear_batch(calls, sync=True):

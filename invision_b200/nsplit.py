@@ -17,6 +17,23 @@ def shard_bounds(n, world, rank, align=128):
     return n0, n1, per
 
 
+def segment_rows(segments, world, rank, align=128):
+    """Rows of a weight made of row blocks `segments` (e.g. Q, K, V heads, gate, up of the FLUX
+    single-stream linear1, quicknn_transformers.pas:1503) that rank holds when each block is
+    N-split in the same proportion: block s contributes its rows shard_bounds(segments[s], ...).
+    With align = head_dim, every rank holds whole heads of Q, K and V and matching gate/up rows,
+    so attention per head and the SiLU gate per pair need only the rank's own columns.  Returns the
+    row indices in the rank's local order (block by block)."""
+    import numpy as np
+
+    parts, off = [], 0
+    for n in segments:
+        n0, n1, _ = shard_bounds(n, world, rank, align)
+        parts.append(np.arange(off + n0, off + n1, dtype=np.int64))
+        off += n
+    return np.concatenate(parts)
+
+
 def gather_columns(y_shard, n, group=None, out=None, buf=None):
     """All-gather the per-rank [M, per] shards (zero-padded past n1 - n0) into out [M, n]."""
     import torch

@@ -119,11 +119,24 @@ float sdot_avx2(int64_t n, const float* a, const float* b) {
   int64_t blocks32 = n >> 5;
   const float* A = a;
   const float* B = b;
+#if defined(__AVX2__) && defined(__FMA__)
+  {
+    __m256 c[4];
+    for (int r = 0; r < 4; ++r) c[r] = _mm256_setzero_ps();
+    for (int64_t i = 0; i < blocks32; ++i) {
+      for (int r = 0; r < 4; ++r) c[r] = _mm256_fmadd_ps(_mm256_loadu_ps(A + 8 * r), _mm256_loadu_ps(B + 8 * r), c[r]);
+      A += 32;
+      B += 32;
+    }
+    for (int r = 0; r < 4; ++r) _mm256_storeu_ps(acc[r].l, c[r]);
+  }
+#else
   for (int64_t i = 0; i < blocks32; ++i) {
     for (int r = 0; r < 4; ++r) v8_fma(acc[r], A + 8 * r, B + 8 * r);
     A += 32;
     B += 32;
   }
+#endif
   V8 acc0 = acc[0];
   if (blocks32) {
     // vaddps ymm0,ymm0,ymm1 ; vaddps ymm2,ymm2,ymm3 ; vaddps ymm0,ymm0,ymm2
@@ -154,10 +167,31 @@ void sdot_x4_avx2(const float* A, const float* B, float* C, int64_t K, int64_t l
   for (int j = 0; j < 4; ++j) v8_zero(acc[j]);
   int64_t kb = K >> 3;
   int64_t r10 = 0;
+#if defined(__AVX2__) && defined(__FMA__)
+  // The same lane-wise vfmadd231ps chain with the instructions themselves (identical bits to
+  // v8_fma, whose per-lane fmaf the compiler may not vectorise), so the O1 timing is the
+  // reference's instruction mix rather than a scalar emulation of it.
+  {
+    __m256 c0 = _mm256_setzero_ps(), c1 = c0, c2 = c0, c3 = c0;
+    for (int64_t i = 0; i < kb; ++i) {
+      const __m256 a = _mm256_loadu_ps(A + r10);
+      c0 = _mm256_fmadd_ps(a, _mm256_loadu_ps(B + r10), c0);
+      c1 = _mm256_fmadd_ps(a, _mm256_loadu_ps(B + r10 + ldb), c1);
+      c2 = _mm256_fmadd_ps(a, _mm256_loadu_ps(B + r10 + 2 * ldb), c2);
+      c3 = _mm256_fmadd_ps(a, _mm256_loadu_ps(B + r10 + 3 * ldb), c3);
+      r10 += 8;
+    }
+    _mm256_storeu_ps(acc[0].l, c0);
+    _mm256_storeu_ps(acc[1].l, c1);
+    _mm256_storeu_ps(acc[2].l, c2);
+    _mm256_storeu_ps(acc[3].l, c3);
+  }
+#else
   for (int64_t i = 0; i < kb; ++i) {
     for (int j = 0; j < 4; ++j) v8_fma(acc[j], A + r10, B + r10 + j * ldb);
     r10 += 8;
   }
+#endif
   int64_t rem = K & 7;
   if (rem) {
     // Restated literally: vmaskmovps ymm1..4 <- B tails (overwriting the accumulators),

@@ -117,11 +117,25 @@ def _worker(rank, world, port, q):
                               bias=torch.from_numpy(np.ascontiguousarray(bs)).to(dev)))
             refs.append(ref)
             keep.append((Ws, hdl))
+        # a third shard kept on its rank (no peers: ENVG_KEEP_SHARDED semantics), head-aligned
+        from invision_b200.nsplit import segment_rows
+
+        _, w3, _ = inputs(M, K, 4 * 256, seed=13)
+        rows = segment_rows((256, 256, 256, 256), world, rank, 128)
+        W3 = envg.Weight(np.ascontiguousarray(w3[rows]))
+        Wf3 = envg.Weight(w3)
+        ref3 = torch.empty(M, 4 * 256, device=dev)
+        envg.linear(ref3, xt, Wf3)
+        Wf3.free()
+        y3 = torch.full((M, len(rows)), float("nan"), device=dev)
+        calls.append(dict(y=y3, x=xt, W=W3, col0=0))
+        refs.append(ref3[:, torch.from_numpy(rows).to(dev)])
+        keep.append((W3, None))
         torch.cuda.synchronize()
-        keep[-1][1].barrier()
+        keep[1][1].barrier()
         envg.linear_nsplit_batch(calls)
         torch.cuda.synchronize()
-        keep[-1][1].barrier()
+        keep[1][1].barrier()
         for i, (c, ref) in enumerate(zip(calls, refs)):
             results.append((f"nsplit batch item {i}", bool(torch.equal(c["y"], ref))))
         for Ws, _ in keep:
@@ -156,3 +170,39 @@ def test_nsplit_fused_gather_two_ranks():
     res = q.get(timeout=5)
     bad = [name for name, ok in res if not ok]
     assert not bad and len(res) >= 4, res
+
+
+@pytest.mark.parametrize("M", [2048, 300, 16, 4])
+def test_kept_shard_writes_only_its_columns(gpu, M):
+    """ENVG_KEEP_SHARDED on one GPU: the shard's columns land in [col0, col0 + width) of the
+    rank's own Y (every GEMM path: CTA-pair, k2_set, k_gemv), bit-identical to the same columns of
+    the unsplit linear, and nothing else of Y is written."""
+    import torch
+
+    from tests.common import inputs
+
+    envg = gpu
+    K, N = 512, 1024
+    x, w, b = inputs(M, K, N, seed=M + 3)
+    n0, n1 = 256, 640
+    Ws = envg.Weight(w, shard=(n0, n1))
+    Wf = envg.Weight(w)
+    xt = torch.from_numpy(x).cuda()
+    bt = torch.from_numpy(b).cuda()
+    ref = torch.empty(M, N, device="cuda")
+    envg.linear(ref, xt, Wf, bias=bt)
+    for how in ("flag", "no peers"):
+        Y = torch.full((M, N), 7.0, device="cuda")
+        if how == "flag":
+            L = envg.lib()
+            rc = L.envg_linear_nsplit(Y.data_ptr(), None, 0, None, N, n0, xt.data_ptr(), Ws.h,
+                                      bt[n0:n1].contiguous().data_ptr(), M, K, n1 - n0, envg.EPI_BIAS, None,
+                                      envg.DEVICE_PTRS | envg.KEEP_SHARDED)
+            assert rc == envg.OK, envg.last_error()
+        else:
+            envg.linear_nsplit_batch([dict(y=Y, x=xt, W=Ws, col0=n0, bias=bt[n0:n1].contiguous())])
+        torch.cuda.synchronize()
+        assert torch.equal(Y[:, n0:n1], ref[:, n0:n1]), how
+        assert bool((Y[:, :n0] == 7.0).all()) and bool((Y[:, n1:] == 7.0).all()), how
+    Ws.free()
+    Wf.free()

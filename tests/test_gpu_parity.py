@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests.common import TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT, assert_parity, inputs
+from tests.common import TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT, TOL_X3_MAX, TOL_X3_MEAN, assert_parity, inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -55,16 +55,99 @@ def test_linear_k_not_multiple_of_8(gpu, M, K, N):
     assert_parity(y, ref, what=f"K%8 {M}x{K}x{N}")
 
 
-def test_linear_f32_weight_upload_rounds_rne(gpu):
-    M, K, N = 96, 256, 192
-    rng = np.random.default_rng(11)
+F32_WEIGHT_CASES = [
+    # (M, K, N, gate_up): every GEMM path (k2_set for M <= 64 (M <= 8 included), CTA-pair above)
+    (96, 256, 192, False),
+    (1, 2560, 1024, False),     # Qwen3 k at M = 1 (fp32 weights, quicknn_qwen3.pas:712-714)
+    (16, 1000, 300, False),     # ragged K (padded segments)
+    (300, 512, 640, False),
+    (512, 2560, 1024, False),   # Qwen3 k at M = 512
+    (40, 512, 2 * 200, True),   # gate/up pair with the SiLU-gate epilogue
+    (260, 384, 2 * 136, True),
+]
+
+
+@pytest.mark.parametrize("M,K,N,gate_up", F32_WEIGHT_CASES)
+def test_linear_f32_weight_vs_oracle(gpu, M, K, N, gate_up):
+    """An fp32 weight that is not made of bf16 numbers (QNNLinearNoBias on fp32 W,
+    quicknncpu.pas:1822-1828): the oracle multiplies the same unrounded W and X the reference
+    does.  The upload keeps W as bf16x3 hi/lo parts, so the result holds the acceptance bounds and
+    the much tighter bf16x3 bounds."""
+    rng = np.random.default_rng(11 + M + K + N)
     x = rng.standard_normal((M, K), dtype=np.float32)
     wf = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
-    W = gpu.Weight(wf)
-    y = np.zeros((M, N), np.float32)
-    gpu.linear(y, x, W)
-    ref = O.linear_bf16(x, O.f32_to_bf16_rne(wf))
-    assert_parity(y, ref)
+    b = (0.01 * rng.standard_normal(N)).astype(np.float32)
+    W = gpu.Weight(wf, layout=gpu.LAYOUT_GATE_UP if gate_up else gpu.LAYOUT_PLAIN)
+    if gate_up:
+        y = np.full((M, N // 2), np.nan, np.float32)
+        gpu.linear(y, x, W, bias=b, epilogue=gpu.EPI_SILU_GATE)
+        g = O.linear_f32(x, wf, b)
+        ref = O.silu_mul(np.ascontiguousarray(g[:, :N // 2]), np.ascontiguousarray(g[:, N // 2:]))
+    else:
+        y = np.full((M, N), np.nan, np.float32)
+        gpu.linear(y, x, W, bias=b)
+        ref = O.linear_f32(x, wf, b, path=O.PATH_AVX2 if K % 8 == 0 else O.PATH_SCALAR)
+    what = f"f32 weight {M}x{K}x{N} gate_up={gate_up}"
+    assert_parity(y, ref, what=what)
+    assert_parity(y, ref, TOL_X3_MAX, TOL_X3_MEAN, what=what + " (bf16x3 bounds)")
+    W.free()
+
+
+def test_linear_f32_weight_upload_forms(gpu):
+    """fp32 weights made of bf16 numbers (the reference's widened bf16 checkpoints,
+    safetensor.pas:584-647) are stored as plain bf16 and give exactly the bf16 upload's bits;
+    LAYOUT_ROUND_BF16 rounds any fp32 weight to bf16 (RNE), again bit for bit the bf16 upload of
+    the rounded bits."""
+    M, K, N = 96, 256, 192
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    wf = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
+    wb = O.f32_to_bf16_rne(wf)
+    ys = {}
+    for name, w, layout in (("bits", wb, gpu.LAYOUT_PLAIN), ("widened", O.bf16_to_f32(wb), gpu.LAYOUT_PLAIN),
+                            ("rounded", wf, gpu.LAYOUT_PLAIN | gpu.LAYOUT_ROUND_BF16)):
+        W = gpu.Weight(w, layout=layout)
+        ys[name] = np.zeros((M, N), np.float32)
+        gpu.linear(ys[name], x, W)
+        W.free()
+    np.testing.assert_array_equal(ys["widened"], ys["bits"])
+    np.testing.assert_array_equal(ys["rounded"], ys["bits"])
+    assert_parity(ys["bits"], O.linear_bf16(x, wb))
+
+
+def test_f32_weight_in_batch_and_noalloc(gpu):
+    """A bf16x3 weight inside envg_linear_batch (between linears that share and chain inputs) and
+    through envg_linear_noalloc gives the bits of its own envg_linear call."""
+    import torch
+
+    rng = np.random.default_rng(13)
+    K, N = 512, 384
+    wf = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
+    wb = O.f32_to_bf16_rne((0.02 * rng.standard_normal((K, N))).astype(np.float32))
+    Wf, Wb = gpu.Weight(wf), gpu.Weight(wb)
+    for M in (4, 16, 300):
+        x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+        y1, y2, y3 = (torch.empty(M, N, device="cuda"), torch.empty(M, K, device="cuda"),
+                      torch.empty(M, N, device="cuda"))
+        gpu.linear_batch([dict(dst=y1, x=x, W=Wf), dict(dst=y2, x=y1, W=Wb), dict(dst=y3, x=y2, W=Wf)])
+        torch.cuda.synchronize()
+        got = [t.cpu().numpy() for t in (y1, y2, y3)]
+        r1, r2, r3 = torch.empty_like(y1), torch.empty_like(y2), torch.empty_like(y3)
+        gpu.linear(r1, x, Wf)
+        gpu.linear(r2, r1, Wb)
+        gpu.linear(r3, r2, Wf)
+        torch.cuda.synchronize()
+        for g, r in zip(got, (r1, r2, r3)):
+            np.testing.assert_array_equal(g, r.cpu().numpy())
+        assert_parity(got[0], O.linear_f32(x.cpu().numpy(), wf), TOL_X3_MAX, TOL_X3_MEAN, what=f"batch x3 M={M}")
+        if M <= 64:
+            yn = torch.empty(M, N, device="cuda")
+            gpu.linear_noalloc(yn, x, Wf)
+            torch.cuda.synchronize()
+            assert_parity(yn.cpu().numpy(), O.linear_f32(x.cpu().numpy(), wf), TOL_X3_MAX, TOL_X3_MEAN,
+                          what=f"noalloc x3 M={M}")
+    Wf.free()
+    Wb.free()
 
 
 @pytest.mark.parametrize("M,K,H", [(256, 512, 384), (4608 // 8, 3072, 1152), (1, 3072, 640), (16, 512, 200), (130, 256, 130)])
@@ -135,21 +218,25 @@ def test_conv2d_vs_oracle(gpu, B, C, H, Wd, O_, k, stride, pad, silu):
 
 
 @pytest.mark.parametrize("ta,tb", [(111, 112), (111, 111), (112, 111)])
-@pytest.mark.parametrize("M,N,K", [(96, 80, 72), (8, 300, 128), (257, 129, 64)])
+@pytest.mark.parametrize("M,N,K", [(96, 80, 72), (8, 300, 128), (257, 129, 64), (512, 512, 128), (200, 96, 45)])
 def test_sgemm_vs_oracle(gpu, ta, tb, M, N, K):
+    """The cblas_sgemm slot on the reference's own fp32 operands (cblas_gemm -> qgemm,
+    quicknncpu.pas:335-365,1398-1496): the oracle multiplies the unrounded A and B.  512x512x128
+    is a head of the FLUX attention score product Q.K^T (quicknn_transformers.pas:1174-1183)."""
     rng = np.random.default_rng(M + N + K + ta + tb)
     A = rng.standard_normal((K, M) if ta == 112 else (M, K), dtype=np.float32)
     B = rng.standard_normal((N, K) if tb == 112 else (K, N), dtype=np.float32)
     C0 = rng.standard_normal((M, N), dtype=np.float32)
     lda, ldb = A.shape[1], B.shape[1]
+    path = O.PATH_AVX2 if K % 8 == 0 else O.PATH_SCALAR
     for alpha, beta in ((1.0, 0.0), (0.5, 2.0), (1.5, 1.0)):
         C = C0.copy()
         gpu.sgemm(101, ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, N)
         ref = C0.copy()
-        Ab = O.bf16_to_f32(O.f32_to_bf16_rne(A))
-        Bb = O.bf16_to_f32(O.f32_to_bf16_rne(B))
-        O.qgemm(ta, tb, M, N, K, alpha, Ab, lda, Bb, ldb, beta, ref, N, path=O.PATH_SCALAR)
-        assert_parity(C, ref, what=f"sgemm {ta},{tb} a={alpha} b={beta}")
+        O.qgemm(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, ref, N, path=path)
+        what = f"sgemm {ta},{tb} {M}x{N}x{K} a={alpha} b={beta}"
+        assert_parity(C, ref, what=what)
+        assert_parity(C, ref, TOL_X3_MAX, TOL_X3_MEAN, what=what + " (bf16x3 bounds)")
 
 
 def test_m_zero_is_noop(gpu):
@@ -385,6 +472,44 @@ def test_skinny_batch_queue_hazards(gpu, M):
     torch.cuda.synchronize()
     for g, t, name in zip(got, outs, ("ya", "x", "yc", "yd")):
         np.testing.assert_array_equal(g, t.cpu().numpy(), err_msg=name)
+
+
+@pytest.mark.parametrize("M", [1, 16, 300])
+def test_batch_vector_hazards(gpu, M):
+    """Linears of one k_gemv (M = 1), k2_set (M = 16) or CTA-pair (M = 300) launch run at once, so a
+    batch must not put into one launch a linear whose bias or gate is another member's output (read
+    after write: the adaLN modulation feeding a gated residual), nor one that overwrites a vector
+    another member reads (write after read).  The batch equals the calls one by one."""
+    import torch
+
+    K, N = 256, 384
+    rng = np.random.default_rng(31 + M)
+
+    def wt(n, k):
+        return gpu.Weight(O.f32_to_bf16_rne((0.02 * rng.standard_normal((n, k))).astype(np.float32)))
+
+    Wb, Wg, Wr, Wo = wt(N, K), wt(N, K), wt(N, K), wt(N, K)
+    x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()  # one input: one pair set
+    h0 = torch.from_numpy(rng.standard_normal((M, N), dtype=np.float32)).cuda()
+    yb, yg, yo = (torch.empty(M, N, device="cuda") for _ in range(3))
+    h = h0.clone()
+    bias_v, gate_v = yb.view(-1)[:N], yg.view(-1)[:N]  # first N floats of two outputs
+    calls = [dict(dst=yb, x=x, W=Wb),                                  # writes the bias vector
+             dict(dst=yg, x=x, W=Wg),                                  # writes the gate vector
+             dict(dst=h, x=x, W=Wr, bias=bias_v, gate=gate_v,          # reads both (read after write)
+                  epilogue=gpu.EPI_GATED_RESIDUAL),
+             dict(dst=yb, x=x, W=Wo)]                                  # overwrites the bias (write after read)
+    gpu.linear_batch(calls)
+    torch.cuda.synchronize()
+    got = [t.cpu().numpy() for t in (yb, yg, h)]
+    h.copy_(h0)
+    for c in calls:
+        gpu.linear(c["dst"], c["x"], c["W"], bias=c.get("bias"), epilogue=c.get("epilogue"), gate=c.get("gate"))
+    torch.cuda.synchronize()
+    for g, t, name in zip(got, (yb, yg, h), ("yb", "yg", "h")):
+        np.testing.assert_array_equal(g, t.cpu().numpy(), err_msg=name)
+    for W in (Wb, Wg, Wr, Wo):
+        W.free()
 
 
 @pytest.mark.parametrize("M,K,N", [(512, 3072, 1024), (4, 3072, 768), (130, 200, 264)])
