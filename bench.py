@@ -27,9 +27,10 @@ Arms:
   (default)          libenvgemm through its C ABI.  `value` = device-resident throughput
                      (TFLOP/s, whole job); `e2e` = the same through host buffers (pinned), every
                      call copying its inputs H2D and its output D2H.
-  --impl reference   the reference's own CPU GEMM (src/sgemm2.cpp compiled from the reference
-                     tree into oracle/_ref, else the C++ restatement of its Pascal qgemm) on the
-                     host cores, on a bounded M-slice of the same workload.
+  --impl reference   the reference's own CPU GEMM path: the C++ restatement of the Pascal
+                     qgemm -> gemm_nt with sDot_x4_avx2 that the Envision binary runs (same
+                     tiling, threading and AVX2 instructions), on all host cores, on a bounded
+                     M-slice of the same workload.
 """
 import argparse
 import json
@@ -912,12 +913,13 @@ def use_all_host_threads():
 
 
 def cpu_baseline(items, sample_seconds=8.0):
-    """The reference's CPU GEMMs on the host cores, each on a bounded M-slice of the workload:
-    sgemm2 (the compiled reference C++, when built) as the headline `value`, and the restated
-    shipped Pascal qgemm (O1) without and with the per-call bf16 -> fp32 widening of
-    QNNLinearNoBias_BF16.  The widened figure is for the whole workload: the slice's GEMM time
-    scaled to all rows, plus one widening of every weight per step (it does not shrink with the
-    slice)."""
+    """The reference's CPU GEMMs on the host cores, each on a bounded M-slice of the workload.
+    `value` is O1, the restated shipped Pascal qgemm -> gemm_nt (the GEMM the Envision binary
+    runs; sgemm2.cpp is not linked into it) on pre-widened weights, FLUX's path (use_bf16 is never
+    set).  Beside it: O1 with the per-call bf16 -> fp32 widening of QNNLinearNoBias_BF16, and the
+    reference's standalone sgemm2.cpp compiled from its tree.  The widened figure is for the whole
+    workload: the slice's GEMM time scaled to all rows, plus one widening of every weight per step
+    (it does not shrink with the slice)."""
     threads = use_all_host_threads()
     wl = CpuWorkload(items)
     mmax = max(it["M"] for it in items)
@@ -940,16 +942,13 @@ def cpu_baseline(items, sample_seconds=8.0):
     o1w = {"value": round(full_flops / (o1_full + widen) / 1e12, 5), "unit": UNIT, "kind": "port", "cores": threads,
            "sample": f"O1 GEMM time of the slice scaled to all {mmax} rows plus {widen:.2f} s of single-threaded "
                      "BF16ToSingle widening of every weight per step (QNNLinearNoBias_BF16, quicknncpu.pas:1830-1847)"}
+    out = dict(o1)
+    out["cpu_model"] = f"{cpu_model()}, {threads} threads"
+    out["o1_qgemm_widened_per_call"] = o1w
     if wl.has_ref:
         rows, flops, dt, _ = run("sgemm2")
-        out = {"value": round(flops / dt / 1e12, 5), "unit": UNIT, "cores": threads, "kind": "reference",
-               "sample": f"one step of the workload on an M-slice of {rows} of {mmax} token rows (M=1 linears in "
-                         f"full); {dt:.1f} s; {wl.describe('sgemm2')}"}
-    else:
-        out = dict(o1)
-    out["cpu_model"] = f"{cpu_model()}, {threads} threads"
-    out["o1_qgemm"] = o1
-    out["o1_qgemm_widened_per_call"] = o1w
+        out["sgemm2"] = {"value": round(flops / dt / 1e12, 5), "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"M-slice of {rows} of {mmax} rows, {dt:.1f} s; {wl.describe('sgemm2')}"}
     return out
 
 
@@ -963,7 +962,8 @@ def run_reference(args, items, desc, world, rank):
     threads = use_all_host_threads()
     per_step = max(0.5, min(15.0, 150.0 / max(1, args.steps + args.warmup)))
     wl = CpuWorkload(items)
-    kind = "sgemm2" if wl.has_ref else "o1"
+    # O1: the restated Pascal qgemm the shipped binary runs (faster here than the unlinked sgemm2.cpp)
+    kind = "o1"
     rows = wl.pick_rows(per_step, kind)
     for _ in range(args.warmup):
         wl.step(rows, kind)

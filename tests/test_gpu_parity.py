@@ -43,6 +43,21 @@ def test_linear_vs_oracle(gpu, M, K, N, with_bias):
     assert_parity(y, ref, what=f"linear {M}x{K}x{N} bias={with_bias}")
 
 
+# BASELINE config 3 (Qwen3-4B layer) at M = 512, whole outputs: q, o, the fused gate+up
+# tensor as one plain linear, and down (quicknn_qwen3.pas:712-714,772,782-789).
+CONFIG3_M512 = [(512, 2560, 4096), (512, 4096, 2560), (512, 2560, 2 * 9728), (512, 9728, 2560)]
+
+
+@pytest.mark.parametrize("M,K,N", CONFIG3_M512)
+def test_config3_m512_vs_oracle(gpu, M, K, N):
+    x, w, _ = inputs(M, K, N, seed=M + K + 3 * N, bias=False)
+    W = gpu.Weight(w)
+    y = np.full((M, N), np.nan, np.float32)
+    gpu.linear(y, x, W)
+    assert_parity(y, O.linear_bf16(x, w, path=O.PATH_AVX2), what=f"config 3 {M}x{K}x{N}")
+    W.free()
+
+
 @pytest.mark.parametrize("M,K,N", [(70, 131, 96), (5, 45, 33), (130, 1001, 260)])
 def test_linear_k_not_multiple_of_8(gpu, M, K, N):
     """K % 8 != 0: the AVX2 build of the reference discards its main-loop sum here
