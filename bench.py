@@ -628,6 +628,9 @@ def run_ours(args, items, desc, world, rank, local):
     # GEMM-phase only (no gather) for N > 1: what the N-split itself scales like
     gemm_phase = None
     if world > 1:
+        for _ in range(2):  # the per-linear calls size their own workspace on first use
+            wl.step(gather=False)
+        torch.cuda.synchronize()
         gms = timed(lambda: wl.step(gather=False), args.steps)
         gathered = [it for it in items if it["name"] not in wl.keep]
         gbytes = sum(4.0 * it["M"] * out_cols(it) * (world - 1) / world for it in gathered)
@@ -995,6 +998,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c4", choices=sorted(WORKLOADS))
     ap.add_argument("--only", default=None, help="run one item of the workload (profiling)")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="profiling: set M of every linear with M > 64 to this many rows (a smaller case of the same "
+                         "kernels for ncu captures; not a bench figure)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
     ap.add_argument("--no-batch", action="store_true", help="one envg_linear call per linear")
@@ -1016,6 +1022,9 @@ def main():
             ap.error(f"--only: no item {args.only} in {args.config}")
         items = keep
         desc = f"{args.config}: only {args.only}"
+    if args.rows:
+        items = [dict(it, M=args.rows) if it["op"] == "linear" and it["M"] > 64 else it for it in items]
+        desc = f"{desc} [profiling case: M = {args.rows}]"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

@@ -99,6 +99,8 @@ struct Dev {
   bool pipe_host = true;  // pipeline large host-pointer linears in row chunks (ENVG_PIPE=0 disables)
   int attn_tiles = 0;     // query tiles per attention CTA: 0 = by grid size, ENVG_ATTN_TILES=1|2 forces
   int pair_split = -1;    // k1_gemm_pair split-K: -1 by cost model, 0 off, n forces n (ENVG_PAIR_SPLIT)
+  int pair_group_m = 0;   // k1_gemm_pair M-tiles per raster group: 0 by L2 budget (ENVG_PAIR_GROUP_M)
+  bool l2_hints = true;   // k1_gemm_pair L2 eviction priorities (ENVG_L2_HINTS=0 disables)
   bool pdl = true;        // programmatic dependent launch of the GEMM-chain kernels (ENVG_PDL=0 disables)
   bool no_split = false;  // set while a pipelined host call launches its row chunks
   envg_stats st{};
@@ -570,6 +572,7 @@ int launch_k1_pair(Dev* d, const CUtensorMap& tA, PairSet& set, double flops, do
   ENVG_TRY((k1_pair_capacity<CONV_B, SILU_GATE>(d, &max_pairs)));
   set.status = d->d_status;
   set.wait_cap_ns = d->wait_cap_ns;
+  set.l2_hints = d->l2_hints ? 1 : 0;
   const int pairs = (int)std::min<int64_t>(set.total, max_pairs);
   if (pairs <= 0) return ENVG_OK;
   ProfScope ps(stream_of(d), CONV_B ? KID_K1_CONV : (SILU_GATE ? KID_K1_SILU_GATE : KID_K1), flops, bytes);
@@ -1044,6 +1047,15 @@ struct PairJob {
   double flops, bytes;
 };
 
+// M-tiles (256-row A panels) per raster group of k1_gemm_pair.  A group's units sweep all of W's
+// column panels while its A panels stay in L2, so each W panel is read from HBM tiles_m / group_m
+// times: as many panels as fit a 32 MB share of the 126 MB L2, from 4 to 16.
+int pair_group_m(const Dev* d, int64_t Kp) {
+  if (d->pair_group_m > 0) return d->pair_group_m;
+  const int64_t panel = 2 * (int64_t)BM * Kp * 2;
+  return (int)std::max<int64_t>(4, std::min<int64_t>(16, (32ll << 20) / panel));
+}
+
 // Linears that share the activation operand A[M, Kp] (M > 128) as k1_gemm_pair launches: one
 // launch per kernel variant present (the SiLU-gate variant for unsplit GATE_UP linears, the
 // plain one for the rest), each walking all its linears' units; then one k_split_reduce per
@@ -1085,7 +1097,7 @@ int launch_pair_set(Dev* d, const void* A, int64_t M, int64_t Kp, PairJob* jobs,
       P.num_kb = num_kb;
       P.tiles_m = tiles_m;
       P.tiles_n = (int)cdiv(jobs[i].rows_b, K1_BN);
-      P.group_m = 4;
+      P.group_m = pair_group_m(d, Kp);
       P.tiles_per_split = P.tiles_m * P.tiles_n;
       set.tmB[j] = *jobs[i].tB;
       if (sp[i] > 1) {
@@ -1467,6 +1479,11 @@ int envg_init(int ndev, const int* dev_ids) {
   if (const char* s = getenv("ENVG_STORE")) d->store_tma = strcmp(s, "coalesced") != 0;
   if (const char* s = getenv("ENVG_PIPE")) d->pipe_host = strcmp(s, "0") != 0;
   if (const char* s = getenv("ENVG_PDL")) d->pdl = strcmp(s, "0") != 0;
+  if (const char* s = getenv("ENVG_L2_HINTS")) d->l2_hints = strcmp(s, "0") != 0;
+  if (const char* s = getenv("ENVG_PAIR_GROUP_M")) {
+    const int v = atoi(s);
+    if (v >= 1 && v <= 64) d->pair_group_m = v;
+  }
   if (const char* s = getenv("ENVG_PAIR_SPLIT")) {
     const int v = atoi(s);
     if (v >= 0 && v <= 64) d->pair_split = v;

@@ -170,6 +170,7 @@ struct PairSet {
   ConvGeom conv;
   int* status;
   uint64_t wait_cap_ns;
+  int l2_hints;  // activation loads evict_last, local output stores evict_first
   PeerMaps pm;  // STORE_TMA_PEERS (a set of one)
 };
 
@@ -858,6 +859,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       int stage = 0;
       uint32_t ph = 0;
       uint32_t pending = 0, issue_ph = 0;
+      const uint64_t pol_a = l2_policy_evict_last();
       for (int unit = pair; unit < set.total; unit += npairs) {
         const int li = set_linear(set, unit);
         const PairLin& P = set.lin[li];
@@ -885,7 +887,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
           if (!wait_bounded(empty0 + 8 * stage, ph ^ 1, wc, 21)) goto producer_done;
           const uint32_t fb = full0_leader + 8 * stage;
           if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, 2 * L::STAGE_BYTES);
-          tma_load_2d_pair(smem_u32(sA + stage * TILE_A_BYTES), &tmA, fb, kb * BK, m0);
+          if (!CONV_B && set.l2_hints)
+            tma_load_2d_pair_hint(smem_u32(sA + stage * TILE_A_BYTES), &tmA, fb, kb * BK, m0, pol_a);
+          else
+            tma_load_2d_pair(smem_u32(sA + stage * TILE_A_BYTES), &tmA, fb, kb * BK, m0);
           if (CONV_B) {
             const int kpos = kb / set.conv.cblocks;
             const int cb = kb - kpos * set.conv.cblocks;
@@ -965,6 +970,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
     int sb = 0;
     int acc = 0;
     uint32_t aph = 0;
+    const uint64_t pol_y = l2_policy_evict_first();
     for (int unit = pair; unit < set.total; unit += npairs) {
       const int li = set_linear(set, unit);
       const PairLin& P = set.lin[li];
@@ -1032,6 +1038,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
           for (int r = 0; r < ep.nremote; ++r) tma_reduce_add_2d(&set.pm.m[r], smem_u32(buf), x, y);
         } else if (smode == STORE_TMA_ADD) {
           tma_reduce_add_2d(&set.tmY[li], smem_u32(buf), x, y);
+        } else if (set.l2_hints) {
+          tma_store_2d_hint(&set.tmY[li], smem_u32(buf), x, y, pol_y);
         } else {
           tma_store_2d(&set.tmY[li], smem_u32(buf), x, y);
         }
@@ -1126,6 +1134,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
                 else tma_store_3d(&set.ybig[li], src, x, y, b);
               } else if (smode == STORE_TMA_ADD) {
                 tma_reduce_add_2d(&set.ybig[li], src, x, y);
+              } else if (set.l2_hints) {
+                tma_store_2d_hint(&set.ybig[li], src, x, y, pol_y);
               } else {
                 tma_store_2d(&set.ybig[li], src, x, y);
               }

@@ -126,6 +126,25 @@ ENVG_DEV void tma_store_2d(const void* desc, uint32_t src, int c0, int c1) {
                "r"(src), "r"(c0), "r"(c1)
                : "memory");
 }
+// L2 eviction priorities for cache-hinted copies: evict_last for data the launch reads again
+// (activation panels reused across W column panels), evict_first for data it never reads again
+// (the output), so that the output stream does not push the reused operands out of L2.
+ENVG_DEV uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+ENVG_DEV uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+ENVG_DEV void tma_store_2d_hint(const void* desc, uint32_t src, int c0, int c1, uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(src), "r"(c0), "r"(c1), "l"(policy)
+               : "memory");
+}
 ENVG_DEV void tma_store_3d(const void* desc, uint32_t src, int c0, int c1, int c2) {
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(desc)),
@@ -257,6 +276,14 @@ ENVG_DEV void tma_load_4d_pair(uint32_t dst, const void* desc, uint32_t bar, int
       "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+// The same load with an L2 eviction priority (a policy from l2_policy_*).
+ENVG_DEV void tma_load_2d_pair_hint(uint32_t dst, const void* desc, uint32_t bar, int c0, int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(c0), "r"(c1), "l"(policy)
       : "memory");
 }
 // TMEM allocation for a CTA pair: one warp of each CTA executes these together.

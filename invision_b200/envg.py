@@ -585,9 +585,34 @@ def QNNLINEAR_BF16_OR_F32(dst, src, weight, weight_bf16, seq, srcDim, dstDim):
 
 
 def QNNMatMulNT(C, A, B, M, K, N):
-    """quicknn_kernels.pas:847-861 -> quicknncpu.pas:1773-1784 with B a device weight [N, K]."""
-    _assert(B.N == N and B.K == K, "ERROR : QNNMatMul out of bound [B]")
-    return linear(C[:M], A[:M], B, epilogue=EPI_NONE)
+    """quicknn_kernels.pas:847-861 -> quicknncpu.pas:1773-1784: C[M, N] = A[M, K] . B[N, K]^T.
+    B is a device-resident Weight [N, K] (the Z-Image linears' use), or a host fp32 array [N, K],
+    which goes through the cblas_gemm slot (envg_sgemm) with the reference's arguments."""
+    if isinstance(B, Weight):
+        _assert(B.N == N and B.K == K, "ERROR : QNNMatMul out of bound [B]")
+        return linear(C[:M], A[:M], B, epilogue=EPI_NONE)
+    _assert(A.size >= M * K, "ERROR : QNNMatMul out of bound [A]")
+    _assert(B.size >= N * K, "ERROR : QNNMatMul out of bound [B]")
+    _assert(C.size >= M * N, "ERROR : QNNMatMul out of bound [C]")
+    return sgemm(ROW_MAJOR, NO_TRANS, TRANS, M, N, K, 1.0, A, K, B, K, 0.0, C, N)
+
+
+def QNNMatMulNN(C, A, B, M, K, N):
+    """quicknncpu.pas:1760-1771: C[M, N] = A[M, K] . B[K, N] through the cblas_gemm slot."""
+    _assert(A.size >= M * K, "ERROR : QNNMatMul out of bound [A]")
+    _assert(B.size >= K * N, "ERROR : QNNMatMul out of bound [B]")
+    _assert(C.size >= M * N, "ERROR : QNNMatMul out of bound [C]")
+    return sgemm(ROW_MAJOR, NO_TRANS, NO_TRANS, M, N, K, 1.0, A, K, B, N, 0.0, C, N)
+
+
+def QNNMatMulTN(C, A, B, M, K, N):
+    """quicknncpu.pas:1786-1797: C[M, N] = A^T . B with A stored [K, M] and B [K, N], called with
+    the reference's leading dimensions lda = K and ldb = K (right when M = K = N, the square
+    products it is used for; envg_sgemm refuses a leading dimension below the row length)."""
+    _assert(A.size >= K * M, "ERROR : QNNMatMul out of bound [A]")
+    _assert(B.size >= N * K, "ERROR : QNNMatMul out of bound [B]")
+    _assert(C.size >= M * N, "ERROR : QNNMatMul out of bound [C]")
+    return sgemm(ROW_MAJOR, TRANS, NO_TRANS, M, N, K, 1.0, A, K, B, K, 0.0, C, N)
 
 
 def QNNLinearSiluMul(dst, x, W_gate_up, seqLen, inDIM, mlpDIM):

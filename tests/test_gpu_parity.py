@@ -254,6 +254,38 @@ def test_sgemm_vs_oracle(gpu, ta, tb, M, N, K):
         assert_parity(C, ref, TOL_X3_MAX, TOL_X3_MEAN, what=what + " (bf16x3 bounds)")
 
 
+def test_qnn_matmul_mirror_vs_oracle(gpu):
+    """The QNNMatMulNT / NN / TN mirror (quicknncpu.pas:1760-1797) with the reference's own
+    arguments: NT with a device weight (bf16 W, fp32 X) and NT / NN / TN on fp32 host operands
+    through the cblas_gemm slot, each against the oracle's qgemm on the same unrounded inputs."""
+    rng = np.random.default_rng(41)
+    M, K, N = 200, 256, 320
+    x, w, _ = inputs(M, K, N, seed=41, bias=False)
+    W = gpu.Weight(w)
+    C = np.full((M, N), np.nan, np.float32)
+    gpu.QNNMatMulNT(C, x, W, M, K, N)
+    assert_parity(C, O.linear_bf16(x, w), what="QNNMatMulNT device weight")
+    W.free()
+    A = rng.standard_normal((M, K), dtype=np.float32)
+    Bnt = rng.standard_normal((N, K), dtype=np.float32)
+    Bnn = rng.standard_normal((K, N), dtype=np.float32)
+    for name, fn, B, ta, tb, ldb in (("NT", gpu.QNNMatMulNT, Bnt, 111, 112, K),
+                                     ("NN", gpu.QNNMatMulNN, Bnn, 111, 111, N)):
+        C = np.full((M, N), np.nan, np.float32)
+        fn(C, A, B, M, K, N)
+        ref = np.zeros((M, N), np.float32)
+        O.qgemm(ta, tb, M, N, K, 1.0, A, K, B, ldb, 0.0, ref, N)
+        assert_parity(C, ref, TOL_X3_MAX, TOL_X3_MEAN, what=f"QNNMatMul{name} fp32 operands")
+    S = 192  # TN with the reference's lda = ldb = K: square products
+    At = rng.standard_normal((S, S), dtype=np.float32)
+    Bs = rng.standard_normal((S, S), dtype=np.float32)
+    C = np.full((S, S), np.nan, np.float32)
+    gpu.QNNMatMulTN(C, At, Bs, S, S, S)
+    ref = np.zeros((S, S), np.float32)
+    O.qgemm(112, 111, S, S, S, 1.0, At, S, Bs, S, 0.0, ref, S)
+    assert_parity(C, ref, TOL_X3_MAX, TOL_X3_MEAN, what="QNNMatMulTN fp32 operands")
+
+
 def test_m_zero_is_noop(gpu):
     x, w, _ = inputs(4, 64, 64, seed=1, bias=False)
     W = gpu.Weight(w)
