@@ -720,6 +720,8 @@ def run_ours(args, items, desc, world, rank, local):
     e2e = None
     if not args.no_e2e and world == 1 and all(plain_linear(it) for it in items):
         e2e = run_e2e(args, envg, torch, dev, wl, step_flops)
+    elif not args.no_e2e and world > 1 and all(plain_linear(it) for it in items):
+        e2e = run_e2e_nsplit(args, torch, dev, wl, step_flops, timed)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and all(plain_linear(it) for it in items):
@@ -752,6 +754,53 @@ def run_ours(args, items, desc, world, rank, local):
             line["gemm_phase"] = gemm_phase
         emit(line)
     wl.free()
+
+
+def run_e2e_nsplit(args, torch, dev, wl, step_flops, timed):
+    """N > 1: the N-split step through the public API (envg_linear_nsplit_batch), with every
+    step's inputs copied in from pinned host memory on every rank (each rank needs the whole X)
+    and each rank reading its part of the results back: its kept shard, and its block of rows
+    of every gathered output (together the ranks read each output once)."""
+    world, rank = wl.world, wl.rank
+    hx, seen = {}, set()
+    for k, v in wl.x.items():
+        if v.data_ptr() in seen:  # an input shared by several linears is copied once
+            continue
+        seen.add(v.data_ptr())
+        h = torch.empty(v.shape, dtype=torch.float32, pin_memory=True)
+        h.copy_(v)
+        hx[k] = h
+    outs = []
+    for it in wl.items:
+        n = it["name"]
+        if n in wl.keep:
+            src = wl.ys[n]
+        else:
+            y = wl.out_of(n)
+            r0 = rank * y.shape[0] // world
+            r1 = (rank + 1) * y.shape[0] // world
+            src = y[r0:r1]
+        outs.append((src, torch.empty(src.shape, dtype=torch.float32, pin_memory=True)))
+    h2d = sum(h.numel() * 4 for h in hx.values())
+    d2h = sum(h.numel() * 4 for _, h in outs)
+
+    def step():
+        for k, h in hx.items():
+            wl.x[k].copy_(h, non_blocking=True)
+        wl.step()
+        for src, h in outs:
+            h.copy_(src, non_blocking=True)
+
+    steps = max(2, min(args.steps, 5))
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    ms = timed(step, steps)
+    return {"value": round(step_flops / (ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(ms, 3),
+            "steps": steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": ("per rank: inputs from pinned host memory (torch copy), envg_linear_nsplit_batch step, its "
+                     "kept shards and its row block of every gathered output back to pinned host memory; max over "
+                     "ranks; bytes are this rank's")}
 
 
 def run_e2e(args, envg, torch, dev, wl, step_flops):

@@ -14,7 +14,9 @@
  *   - The activation X is rounded fp32 -> bf16 with round-to-nearest-even on the device and
  *     multiplied with fp32 accumulation.  (The reference widens W to fp32 and runs an fp32 GEMM,
  *     quicknncpu.pas:1830-1847; the difference is bounded by the tests at max|d|/max|ref| <= 1e-2
- *     and sum|d|/sum|ref| <= 2e-3.)
+ *     and sum|d|/sum|ref| <= 2e-3.)  An fp32 weight that is not made of bf16 numbers, and both
+ *     operands of envg_sgemm, are split into bf16 hi/lo parts instead (bf16x3, see
+ *     envg_weight_upload), which matches the fp32 GEMM to about 1e-5.
  *   - M == 0 is a no-op returning ENVG_OK.  dst must not alias x.
  *   - Errors never throw: a negative ENVG_ERR_* code is returned and envg_last_error() gives a
  *     thread-local message.  The Pascal shim turns a non-zero code into assert(false, msg), which
@@ -114,7 +116,7 @@ int envg_weight_upload_shard(const uint16_t* w_bf16, const float* w_f32, int64_t
                              int64_t n0, int64_t n1, int layout_flags, envg_weight* out);
 
 /* Upload a convolution weight W[out_ch, in_ch, kH, kW] (the layout QNNConv2d reads,
- * quicknncpu.pas:1958-2132) for envg_conv2d. */
+ * quicknncpu.pas:1958-2132) for envg_conv2d.  w_f32 is rounded to bf16 (RNE). */
 int envg_conv_weight_upload(const uint16_t* w_bf16, const float* w_f32, int out_ch, int in_ch,
                             int kH, int kW, envg_weight* out);
 
@@ -153,7 +155,9 @@ int envg_safetensors_read_f32(const char* path, const char* name, float* dst, in
 /* Uploads tensor `name` as a device weight.  2-D tensors [N, K] become a linear weight with
  * `layout_flags` (shard rows [n0, n1) as envg_weight_upload_shard; n0 = n1 = 0 means all rows);
  * 4-D tensors [out_ch, in_ch, kH, kW] become a convolution weight (n0 = n1 = 0 required).
- * BF16 bits are kept; F16 and F32 are rounded to bf16 (RNE), as envg_weight_upload does. */
+ * BF16 bits are kept; F16 and F32 are stored as envg_weight_upload stores an fp32 weight (bf16
+ * when every value is a bf16 number, else bf16x3 hi/lo parts, or RNE bf16 with
+ * ENVG_LAYOUT_ROUND_BF16); convolution weights are rounded to bf16 (RNE). */
 int envg_weight_upload_safetensors(const char* path, const char* name, int layout_flags, int64_t n0,
                                    int64_t n1, envg_weight* out);
 

@@ -1672,12 +1672,13 @@ int envg_weight_upload_safetensors(const char* path, const char* name, int layou
   ENVG_TRY(st_source(path, ti, K, &mf, &copy, &src));
   if (nd == 4) {
     if (n0 != 0 || n1 != 0) return fail(ENVG_ERR_ARG, "convolution weights are uploaded whole (n0 = n1 = 0)");
-    if (layout_flags != ENVG_LAYOUT_PLAIN) return fail(ENVG_ERR_ARG, "convolution weights take ENVG_LAYOUT_PLAIN");
+    if ((layout_flags & ~ENVG_LAYOUT_ROUND_BF16) != ENVG_LAYOUT_PLAIN)
+      return fail(ENVG_ERR_ARG, "convolution weights take ENVG_LAYOUT_PLAIN");
     for (int i = 0; i < 4; ++i)
       if (ti.shape[i] <= 0 || ti.shape[i] > INT32_MAX) return fail(ENVG_ERR_ARG, "conv weight %s: bad shape", name);
     return conv_upload_common(d, src, (int)ti.shape[0], (int)ti.shape[1], (int)ti.shape[2], (int)ti.shape[3], out);
   }
-  if (n0 == 0 && n1 == 0) n1 = layout_flags == ENVG_LAYOUT_GATE_UP ? N / 2 : N;
+  if (n0 == 0 && n1 == 0) n1 = (layout_flags & ~ENVG_LAYOUT_ROUND_BF16) == ENVG_LAYOUT_GATE_UP ? N / 2 : N;
   return upload_common(d, src, N, K, n0, n1, layout_flags, out);
 }
 
