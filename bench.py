@@ -712,7 +712,7 @@ def run_ours(args, items, desc, world, rank, local):
             # An HBM-bound (skinny) linear is timed over enough copies of its weight that one
             # replay streams more than twice the 126 MB L2, so no call finds its weight in L2.
             name = it["name"]
-            copies = [wl.W[name]]
+            copies = [wl.W.get(name)]
             if it["op"] == "linear" and it["M"] <= 64:
                 wbytes = 2.0 * it["N"] * it["K"]
                 ncopy = int(min(64, -(-2 * 126e6 // wbytes)))
@@ -723,9 +723,11 @@ def run_ours(args, items, desc, world, rank, local):
 
             def replay_body():
                 for c in range(calls):
-                    wl.W[name] = copies[c % len(copies)]
+                    if len(copies) > 1:
+                        wl.W[name] = copies[c % len(copies)]
                     wl.run_item(it, gather=False)
-                wl.W[name] = copies[0]
+                if len(copies) > 1:
+                    wl.W[name] = copies[0]
 
             g = capture(torch, replay_body)
             gms = timed(g.replay, 5) / calls
