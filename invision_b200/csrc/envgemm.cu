@@ -1049,11 +1049,13 @@ struct PairJob {
 
 // M-tiles (256-row A panels) per raster group of k1_gemm_pair.  A group's units sweep all of W's
 // column panels while its A panels stay in L2, so each W panel is read from HBM tiles_m / group_m
-// times: as many panels as fit a 32 MB share of the 126 MB L2, from 4 to 16.
+// times: as many panels as fit a 64 MB share of the 126 MB L2, from 4 to 16.  Measured on config
+// 4 (ncu DRAM bytes per launch): the 18432x4096x36864 linear reads 11.1 GB at 4 panels and 2.9 GB
+// at 16 (4.33 -> 3.78 ms); the K = 16384 one reads 4.6 GB at 4 and 3.6 GB at 8.
 int pair_group_m(const Dev* d, int64_t Kp) {
   if (d->pair_group_m > 0) return d->pair_group_m;
   const int64_t panel = 2 * (int64_t)BM * Kp * 2;
-  return (int)std::max<int64_t>(4, std::min<int64_t>(16, (32ll << 20) / panel));
+  return (int)std::max<int64_t>(4, std::min<int64_t>(16, (64ll << 20) / panel));
 }
 
 // Linears that share the activation operand A[M, Kp] (M > 128) as k1_gemm_pair launches: one
