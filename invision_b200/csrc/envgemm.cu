@@ -41,6 +41,7 @@ constexpr int K1_BN = 256;
 constexpr int K1_STAGES = 4;
 constexpr int KPAIR_STAGES = 6;
 constexpr int SKINNY_MAX = 64;
+constexpr unsigned SCHED_SLOTS = 64;  // k1_gemm_pair schedules in flight
 constexpr uint64_t DEFAULT_WAIT_CAP_NS = 2000000000ull;  // 2 s
 
 thread_local std::string t_err;
@@ -101,11 +102,14 @@ struct Dev {
   int pair_split = -1;    // k1_gemm_pair split-K: -1 by cost model, 0 off, n forces n (ENVG_PAIR_SPLIT)
   int pair_group_m = 0;   // k1_gemm_pair M-tiles per raster group: 0 by L2 budget (ENVG_PAIR_GROUP_M)
   bool l2_hints = true;   // k1_gemm_pair L2 eviction priorities (ENVG_L2_HINTS=0 disables)
+  bool pair_dyn = true;   // k1_gemm_pair dynamic unit order (ENVG_PAIR_SCHED=static disables)
+  Buf sched;              // k1_gemm_pair schedules: SCHED_SLOTS x {next unit, pairs done}, zeroed
+  unsigned sched_seq = 0; // slot of the next launch
   bool pdl = true;        // programmatic dependent launch of the GEMM-chain kernels (ENVG_PDL=0 disables)
   bool no_split = false;  // set while a pipelined host call launches its row chunks
   envg_stats st{};
   size_t ws_bytes() const {
-    return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + bias.bytes + gate.bytes + act.bytes +
+    return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + sched.bytes + bias.bytes + gate.bytes + act.bytes +
            col.bytes + b32.bytes + xbatch.bytes + ada.bytes + xn.bytes + gn.bytes + c1.bytes + vec.bytes +
            fa.bytes + fain.bytes;
   }
@@ -476,6 +480,7 @@ int check_status(Dev* d) {
     hs[0] = 0;
     hs[1] = 0;
     if (d->cnt.p) cudaMemsetAsync(d->cnt.p, 0, d->cnt.bytes, stream_of(d));  // re-arm split-K counters
+    if (d->sched.p) cudaMemsetAsync(d->sched.p, 0, d->sched.bytes, stream_of(d));  // and the schedules
     d->st.last_status = st;
     return fail(st, "device-side wait exceeded its bound (site %d); pipeline abandoned", site);
   }
@@ -573,6 +578,13 @@ int launch_k1_pair(Dev* d, const CUtensorMap& tA, PairSet& set, double flops, do
   set.status = d->d_status;
   set.wait_cap_ns = d->wait_cap_ns;
   set.l2_hints = d->l2_hints ? 1 : 0;
+  set.sched = nullptr;
+  if (d->pair_dyn) {
+    // each launch takes the next of SCHED_SLOTS zeroed schedules (launches on different streams
+    // may run at once); the launch's last pair zeroes its slot again
+    ENVG_TRY(ensure(d, d->sched, SCHED_SLOTS * 2 * sizeof(int), true));
+    set.sched = reinterpret_cast<int*>(d->sched.p) + 2 * (d->sched_seq++ % SCHED_SLOTS);
+  }
   const int pairs = (int)std::min<int64_t>(set.total, max_pairs);
   if (pairs <= 0) return ENVG_OK;
   ProfScope ps(stream_of(d), CONV_B ? KID_K1_CONV : (SILU_GATE ? KID_K1_SILU_GATE : KID_K1), flops, bytes);
@@ -1482,6 +1494,7 @@ int envg_init(int ndev, const int* dev_ids) {
   if (const char* s = getenv("ENVG_PIPE")) d->pipe_host = strcmp(s, "0") != 0;
   if (const char* s = getenv("ENVG_PDL")) d->pdl = strcmp(s, "0") != 0;
   if (const char* s = getenv("ENVG_L2_HINTS")) d->l2_hints = strcmp(s, "0") != 0;
+  if (const char* s = getenv("ENVG_PAIR_SCHED")) d->pair_dyn = strcmp(s, "static") != 0;
   if (const char* s = getenv("ENVG_PAIR_GROUP_M")) {
     const int v = atoi(s);
     if (v >= 1 && v <= 64) d->pair_group_m = v;
@@ -1516,7 +1529,7 @@ int envg_shutdown(void) {
   cudaStreamSynchronize(stream_of(d));
   Buf* bufs[] = {&d->x,    &d->y,   &d->xb,  &d->wb,  &d->part,  &d->cnt,
                  &d->bias, &d->gate, &d->act, &d->col, &d->b32, &d->xbatch, &d->ada, &d->xn,
-                 &d->gn,   &d->c1,   &d->vec,  &d->fa,  &d->fain};
+                 &d->gn,   &d->c1,   &d->vec,  &d->fa,  &d->fain, &d->sched};
   for (Buf* b : bufs) {
     if (b->p) cudaFree(b->p);
     *b = Buf{};

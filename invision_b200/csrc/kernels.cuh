@@ -171,6 +171,9 @@ struct PairSet {
   int* status;
   uint64_t wait_cap_ns;
   int l2_hints;  // activation loads evict_last, local output stores evict_first
+  // Dynamic unit order (NULL: static, pair p takes units p, p + pairs, ...): [0] the next unit
+  // to hand out, [1] pairs done.  Both are zero at launch; the last pair to finish zeroes them.
+  int* sched;
   PeerMaps pm;  // STORE_TMA_PEERS (a set of one)
 };
 
@@ -778,7 +781,8 @@ struct KPairSmem {
   static constexpr int STAGE_BYTES = TILE_A_BYTES + HALF_B_BYTES;  // this CTA's share of a stage
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;            // A stages, then B stages
   static constexpr int STAGING_BYTES = 4 * 2 * 32 * 128;
-  static constexpr int BAR_BYTES = (2 * STAGES + 6) * 8 + 16;
+  static constexpr int UNIT_RING = 4;  // units handed out ahead (dynamic unit order)
+  static constexpr int BAR_BYTES = (2 * STAGES + 6 + 2 * UNIT_RING) * 8 + 16 + 4 * UNIT_RING;
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
   static constexpr uint32_t TMEM_COLS = 512;
 };
@@ -796,8 +800,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   uint8_t* sB = smem + STAGES * TILE_A_BYTES;
   uint8_t* sStage = sB + STAGES * L::HALF_B_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + L::STAGING_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+  uint64_t* ubars = bars + 2 * STAGES + 6;  // unit_full[UNIT_RING], unit_empty[UNIT_RING]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ubars + 2 * L::UNIT_RING);
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* uring = reinterpret_cast<volatile int*>(tmem_slot + 2);  // the units handed out
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -813,6 +819,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   const uint32_t tempty0_leader = mapa_shared(tempty0, 0);
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
+  // Dynamic unit order: the even CTA's producer takes each next unit from set.sched[0] and writes
+  // it into slot it % UNIT_RING of both CTAs' rings (ufull); the consumers (the UMMA thread and the
+  // four epilogue warps of the even CTA, the producer and the four epilogue warps of the odd one:
+  // 10 arrivals) release the slot on the even CTA's uempty.  Consecutive units then run on
+  // whichever pairs are free, so the pairs at work always hold a contiguous run of the raster and
+  // its A panels are read while they are still in L2.
+  constexpr int UR = L::UNIT_RING;
+  const bool dyn = set.sched != nullptr;
+  const uint32_t ufull0 = smem_u32(ubars);
+  const uint32_t uempty0 = ufull0 + 8 * UR;
+  const uint32_t uempty0_leader = mapa_shared(uempty0, 0);
+  const uint32_t ufull0_peer = mapa_shared(ufull0, 1);
+  const uint32_t uring_peer = mapa_shared(smem_u32(const_cast<int*>(uring)), 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -825,6 +844,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
     }
     mbar_init(drain, 1);
     mbar_init(staged, 4);
+    for (int s = 0; s < UR; ++s) {
+      mbar_init(ufull0 + 8 * s, 1);
+      mbar_init(uempty0 + 8 * s, 10);
+    }
     *abort_s = 0;
     fence_mbar_init();
   }
@@ -854,13 +877,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   griddep_wait();
   if (threadIdx.x == 0) griddep_launch_dependents();
 
+  // The it-th unit of this pair (set.total ends the sequence).  publish_unit: the even CTA's
+  // producer; take_unit: every other role (one thread each); peek_unit reads a slot without
+  // releasing it.  false: a bounded wait gave up.
+  auto publish_unit = [&](int it, int& unit) -> bool {
+    if (!dyn) {
+      unit = min(pair + it * npairs, set.total);
+      return true;
+    }
+    const int slot = it % UR;
+    if (!wait_bounded_cluster(uempty0 + 8 * slot, ((it / UR) & 1) ^ 1, wc, 26)) return false;
+    const int u = min(atomicAdd(set.sched, 1), set.total);
+    uring[slot] = u;
+    st_shared_cluster_u32(uring_peer + 4 * slot, (uint32_t)u);
+    mbar_arrive(ufull0 + 8 * slot);
+    mbar_arrive_cluster(ufull0_peer + 8 * slot);
+    unit = u;
+    return true;
+  };
+  auto peek_unit = [&](int it, int& unit) -> bool {
+    if (!dyn) {
+      unit = min(pair + it * npairs, set.total);
+      return true;
+    }
+    const int slot = it % UR;
+    if (!wait_bounded_cluster(ufull0 + 8 * slot, (it / UR) & 1, wc, 27)) return false;
+    unit = uring[slot];
+    return true;
+  };
+  auto take_unit = [&](int it, int& unit) -> bool {
+    if (!peek_unit(it, unit)) return false;
+    if (dyn) mbar_arrive_cluster(uempty0_leader + 8 * (it % UR));
+    return true;
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t ph = 0;
       uint32_t pending = 0, issue_ph = 0;
       const uint64_t pol_a = l2_policy_evict_last();
-      for (int unit = pair; unit < set.total; unit += npairs) {
+      for (int it = 0;; ++it) {
+        int unit;
+        if (!(leader ? publish_unit(it, unit) : take_unit(it, unit))) goto producer_done;
+        if (unit >= set.total) break;
         const int li = set_linear(set, unit);
         const PairLin& P = set.lin[li];
         int tile, split, kb0, kb1;
@@ -910,6 +970,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
         }
       }
     producer_done:
+      if (dyn && leader && !*abort_s) {
+        // every unit this pair took has been fetched: count the pair done; the last pair zeroes
+        // the schedule for the next launch (a stream-ordered launch reads it only after
+        // griddep_wait, once this grid has finished)
+        __threadfence();
+        if (atomicAdd(set.sched + 1, 1) == npairs - 1) {
+          set.sched[0] = 0;
+          set.sched[1] = 0;
+          __threadfence();
+        }
+      }
       if (*abort_s && pending) {
         if (leader) {
           for (int s = 0; s < STAGES; ++s)
@@ -928,7 +999,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       uint32_t ph = 0;
       int acc = 0;
       uint32_t aph = 0;
-      for (int unit = pair; unit < set.total; unit += npairs) {
+      for (int it = 0;; ++it) {
+        int unit;
+        if (!take_unit(it, unit) || unit >= set.total) break;
         const int li = set_linear(set, unit);
         int tile, split, kb0, kb1;
         unit_split(unit - set.base[li], set.lin[li], tile, split, kb0, kb1);
@@ -971,7 +1044,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
     int acc = 0;
     uint32_t aph = 0;
     const uint64_t pol_y = l2_policy_evict_first();
-    for (int unit = pair; unit < set.total; unit += npairs) {
+    for (int it = 0;; ++it) {
+      int unit = 0, next = 0;
+      int ok = 1;
+      if (lane == 0) ok = take_unit(it, unit) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      unit = __shfl_sync(0xffffffffu, unit, 0);
+      if (!ok || unit >= set.total) break;
       const int li = set_linear(set, unit);
       const PairLin& P = set.lin[li];
       // A reference into the (grid-constant) parameter space: a local copy would be placed in
@@ -1006,7 +1085,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
       // unit with one proxy fence and issues every store back to back: the tail of the launch
       // is one pass over TMEM and the store drain, with no per-chunk fence or buffer wait.
       static_assert(L::RING_BYTES / 4 >= NCHUNK * 4096 && (L::RING_BYTES / 4) % 1024 == 0, "ring staging");
-      const bool ring_mode = unit + npairs >= set.total && smode != STORE_COALESCED && smode != STORE_DIRECT;
+      // the CTA's last unit: the next one this pair gets is the end of the sequence
+      if (lane == 0) ok = peek_unit(it + 1, next) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      next = __shfl_sync(0xffffffffu, next, 0);
+      const bool ring_mode = ok && next >= set.total && smode != STORE_COALESCED && smode != STORE_DIRECT;
       // With the 128-row map, the four warps' 32 x 32 tiles of chunk c sit one above the other
       // (rows q * 32 ..) in a 16 KB box, and one thread stores each chunk of the CTA's 128 rows:
       // a quarter of the TMA stores, each four times larger.

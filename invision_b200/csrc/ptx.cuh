@@ -47,6 +47,20 @@ ENVG_DEV uint32_t mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok;
 }
 
+// try_wait with cluster-scope acquire: for barriers that another CTA of the cluster arrives on
+// (release.cluster) after writing data this thread then reads.
+ENVG_DEV uint32_t mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+
 // Shared state of the bounded waits of one CTA.
 struct WaitCtl {
   uint64_t cap_ns;         // time bound per wait
@@ -64,6 +78,26 @@ ENVG_DEV bool wait_bounded(uint32_t bar, uint32_t parity, const WaitCtl& w, int 
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
+    if (*w.abort_s) return false;
+    if (globaltimer_ns() - t0 > w.cap_ns) {
+      *w.abort_s = 1;
+      if (w.status) {
+        atomicExch(w.status, -5);  // ENVG_ERR_TIMEOUT
+        atomicExch(w.status + 1, site);
+      }
+      return false;
+    }
+  }
+}
+
+// wait_bounded with cluster-scope acquire (mbar_try_wait_cluster).
+ENVG_DEV bool wait_bounded_cluster(uint32_t bar, uint32_t parity, const WaitCtl& w, int site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*w.abort_s) return false;
     if (globaltimer_ns() - t0 > w.cap_ns) {
       *w.abort_s = 1;
@@ -257,6 +291,10 @@ ENVG_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 }
 ENVG_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 32-bit store into the shared memory of a CTA of this cluster (a shared::cluster address).
+ENVG_DEV void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 // Arrive on an mbarrier that may live in another CTA of the cluster.
 ENVG_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {

@@ -337,7 +337,8 @@ def test_errors_are_codes_not_crashes(gpu):
 
 
 @pytest.mark.parametrize("env", [{"ENVG_STORE": "coalesced"}, {"ENVG_STORE": "coalesced", "ENVG_K1": "single"},
-                                 {"ENVG_K1": "single"}, {"ENVG_PAIR_SPLIT": "3"}, {"ENVG_PAIR_SPLIT": "0"}])
+                                 {"ENVG_K1": "single"}, {"ENVG_PAIR_SPLIT": "3"}, {"ENVG_PAIR_SPLIT": "0"},
+                                 {"ENVG_PAIR_SCHED": "static"}, {"ENVG_PAIR_GROUP_M": "4", "ENVG_L2_HINTS": "0"}])
 def test_alternate_kernel_paths_in_subprocess(env):
     """The warp-coalesced store epilogue, the single-CTA k1_gemm and a forced (or disabled) split-K of
     k1_gemm_pair (selected by environment at init) on a few linear / SiLU-gate / gated-residual /
@@ -377,6 +378,47 @@ def test_alternate_kernel_paths_in_subprocess(env):
     r = subprocess.run([sys.executable, "-c", code], env={**os.environ, **env}, capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-3000:]
+
+
+_SCHED_CASE = r"""
+import sys
+import numpy as np
+from invision_b200 import envg
+from tests.common import inputs
+envg.init(0)
+out = {}
+for (M, K, N) in [(2048, 1024, 4096), (600, 512, 1040), (4608, 3072, 768)]:
+    x, w, b = inputs(M, K, N, seed=M + K)
+    W = envg.Weight(w)
+    y = np.zeros((M, N), np.float32)
+    envg.linear(y, x, W, bias=b)
+    out["%d_%d_%d" % (M, K, N)] = y
+np.savez(sys.argv[1], **out)
+"""
+
+
+def test_pair_unit_order_does_not_change_results(tmp_path):
+    """The CTA-pair GEMM hands out its units dynamically (the next free pair takes the next unit)
+    or statically (ENVG_PAIR_SCHED=static): every tile is computed the same way, so the outputs are
+    bit-identical, with and without split-K, for one tile wave and for many."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    res = {}
+    for mode in ("dynamic", "static"):
+        env = dict(os.environ)
+        env.pop("ENVG_PAIR_SCHED", None)
+        if mode == "static":
+            env["ENVG_PAIR_SCHED"] = "static"
+        f = str(tmp_path / f"{mode}.npz")
+        r = subprocess.run([sys.executable, "-c", _SCHED_CASE, f], cwd=root, env=env, capture_output=True,
+                           text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-3000:]
+        res[mode] = np.load(f)
+    for k in res["static"].files:
+        np.testing.assert_array_equal(res["dynamic"][k], res["static"][k], err_msg=k)
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 3072, 18432), (8, 2560, 1024), (3, 131, 257), (5, 4096, 2560), (2, 64, 70)])
