@@ -103,6 +103,7 @@ struct Dev {
   int pair_group_m = 0;   // k1_gemm_pair M-tiles per raster group: 0 by L2 budget (ENVG_PAIR_GROUP_M)
   bool l2_hints = true;   // k1_gemm_pair L2 eviction priorities (ENVG_L2_HINTS=0 disables)
   bool pair_dyn = true;   // k1_gemm_pair dynamic unit order (ENVG_PAIR_SCHED=static disables)
+  bool gemv_chain = true; // k_gemv runs a linear chained to another's output in one launch (ENVG_GEMV_CHAIN=0)
   Buf sched;              // k1_gemm_pair schedules: SCHED_SLOTS x {next unit, pairs done}, zeroed
   unsigned sched_seq = 0; // slot of the next launch
   bool pdl = true;        // programmatic dependent launch of the GEMM-chain kernels (ENVG_PDL=0 disables)
@@ -806,6 +807,7 @@ struct GemvJob {
   bool gu;
   EpiArgs e;
   double flops, bytes;
+  int dep = -1;  // index in the set of the linear whose output is X (chained in the launch), or -1
 };
 
 // Resident k_gemv<MT> blocks on the whole GPU.
@@ -842,8 +844,15 @@ int launch_gemv_set(Dev* d, const GemvJob* jobs, int n) {
   ENVG_TRY(capacity(mt, &cap));
   GemvSet set{};
   set.n = n;
+  set.status = d->d_status;
+  set.wait_cap_ns = d->wait_cap_ns;
   size_t part_off = 0, cnt_off = 0;
-  std::vector<size_t> po(n), co(n);
+  std::vector<size_t> po(n), co(n), doff(n, 0);
+  std::vector<bool> produces(n, false);
+  for (int i = 0; i < n; ++i) {
+    if (jobs[i].dep >= i) return fail(ENVG_ERR_STATE, "launch_gemv_set: linear %d depends on %d", i, jobs[i].dep);
+    if (jobs[i].dep >= 0) produces[jobs[i].dep] = true;
+  }
   for (int i = 0; i < n; ++i) {
     const GemvJob& q = jobs[i];
     GemvArgs& a = set.lin[i];
@@ -878,17 +887,27 @@ int launch_gemv_set(Dev* d, const GemvJob* jobs, int n) {
       part_off += (size_t)a.groups * a.splits * GEMV_PART * sizeof(float);
       cnt_off += (size_t)rup(a.groups, 64) * sizeof(int);
     }
+    if (produces[i]) {  // completion counters read by the chained linear
+      doff[i] = cnt_off;
+      cnt_off += 64 * sizeof(int);
+    }
   }
   set.base[n] = set.total;
-  if (part_off) {
-    ENVG_TRY(ensure(d, d->part, part_off));
-    ENVG_TRY(ensure(d, d->cnt, cnt_off, true));
-    for (int i = 0; i < n; ++i)
-      if (set.lin[i].splits > 1) {
-        set.lin[i].partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d->part.p) + po[i]);
-        set.lin[i].counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(d->cnt.p) + co[i]);
-      }
+  if (part_off) ENVG_TRY(ensure(d, d->part, part_off));
+  if (cnt_off) ENVG_TRY(ensure(d, d->cnt, cnt_off, true));
+  uint8_t* cnt_base = reinterpret_cast<uint8_t*>(d->cnt.p);
+  for (int i = 0; i < n; ++i) {
+    if (set.lin[i].splits > 1) {
+      set.lin[i].partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(d->part.p) + po[i]);
+      set.lin[i].counters = reinterpret_cast<int*>(cnt_base + co[i]);
+    }
+    if (produces[i]) set.lin[i].done = reinterpret_cast<int*>(cnt_base + doff[i]);
   }
+  for (int i = 0; i < n; ++i)
+    if (jobs[i].dep >= 0) {
+      set.lin[i].wait_on = set.lin[jobs[i].dep].done;
+      set.lin[i].wait_groups = set.lin[jobs[i].dep].groups;
+    }
   const int grid = std::min(set.total, cap);
   ProfScope ps(stream_of(d), KID_GEMV, flops, bytes);
   auto kern = mt <= 1 ? k_gemv<1> : mt <= 2 ? k_gemv<2> : mt <= 4 ? k_gemv<4> : k_gemv<8>;
@@ -1495,6 +1514,7 @@ int envg_init(int ndev, const int* dev_ids) {
   if (const char* s = getenv("ENVG_PDL")) d->pdl = strcmp(s, "0") != 0;
   if (const char* s = getenv("ENVG_L2_HINTS")) d->l2_hints = strcmp(s, "0") != 0;
   if (const char* s = getenv("ENVG_PAIR_SCHED")) d->pair_dyn = strcmp(s, "static") != 0;
+  if (const char* s = getenv("ENVG_GEMV_CHAIN")) d->gemv_chain = strcmp(s, "0") != 0;
   if (const char* s = getenv("ENVG_PAIR_GROUP_M")) {
     const int v = atoi(s);
     if (v >= 1 && v <= 64) d->pair_group_m = v;
@@ -2561,17 +2581,44 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
       const char *qy0, *qy1;
       out_range(q, &qy0, &qy1);
       // a set runs its linears at once: none may read or write over another's output, and since
-      // k_gemv reads fp32 X directly (no cast copy), none may write over another's input either
-      for (int k : gidx) {
+      // k_gemv reads fp32 X directly (no cast copy), none may write over another's input either.
+      // One exception: a linear whose X is exactly the whole output of one pending linear (Qwen3's
+      // down after gate_up at M = 1) joins the set chained to it; its units wait in the kernel
+      // until that linear's outputs are all stored.
+      int dep = -1;
+      for (size_t j = 0; j < gidx.size(); ++j) {
+        const envg_linear_desc& pk = descs[gidx[j]];
         const char *ky0, *ky1;
-        out_range(descs[k], &ky0, &ky1);
-        if (reads_output_of(q, descs[k]) || (qy0 < ky1 && ky0 < qy1) || writes_input_of(i, descs[k]) ||
-            vector_hazard(q, descs[k])) {
+        out_range(pk, &ky0, &ky1);
+        const int64_t pn = pk.W->layout == ENVG_LAYOUT_GATE_UP ? pk.N / 2 : pk.N;
+        bool chain = dep < 0 && !ns && (const void*)q.x == (const void*)pk.dst && q.M == pk.M && q.K == pn;
+        for (const GemvJob& g : gq) chain = chain && g.dep != (int)j;  // one reader per producer
+        if (reads_output_of(q, pk) && chain) {
+          dep = (int)j;
+          if ((qy0 < ky1 && ky0 < qy1) || writes_input_of(i, pk) || vector_hazard(q, pk)) {
+            ENVG_TRY(flush_gemv());
+            dep = -1;
+            break;
+          }
+          continue;
+        }
+        if (reads_output_of(q, pk) || (qy0 < ky1 && ky0 < qy1) || writes_input_of(i, pk) || vector_hazard(q, pk)) {
           ENVG_TRY(flush_gemv());
+          dep = -1;
           break;
         }
       }
-      gq.push_back(GemvJob{q.x, q.M, q.K, q.W, gu, e, fl, 2.0 * (double)q.N * q.K + 4.0 * (double)q.M * q.K + ob});
+      if (!d->gemv_chain) dep = -1;
+      if (dep < 0) {  // a pending linear it reads (not chainable) was flushed above; recheck
+        for (int k : gidx)
+          if (reads_output_of(q, descs[k])) {
+            ENVG_TRY(flush_gemv());
+            break;
+          }
+      }
+      GemvJob gj{q.x, q.M, q.K, q.W, gu, e, fl, 2.0 * (double)q.N * q.K + 4.0 * (double)q.M * q.K + ob};
+      gj.dep = dep;
+      gq.push_back(gj);
       gidx.push_back(i);
       if ((int)gq.size() == GEMV_MAX_LIN) ENVG_TRY(flush_gemv());
       continue;

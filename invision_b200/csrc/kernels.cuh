@@ -1958,6 +1958,15 @@ struct GemvArgs {
   EpiArgs epi;
   float* partial;  // [groups][splits][GEMV_PART]
   int* counters;   // [groups]
+  // In-launch chaining (a linear whose X is the output of an earlier linear of the same set):
+  //   done:     this linear's completion count, when a later linear reads its output:
+  //             [0] row groups whose outputs are stored, [1] units of the reader past their wait;
+  //   wait_on:  the producer's `done`; this linear's units start once [0] reaches wait_groups,
+  //             and read X through L2 (it was written during this launch), not the
+  //             non-coherent read-only path.  The reader's last unit past the wait zeroes both.
+  int* done;
+  int* wait_on;
+  int wait_groups;
 };
 
 ENVG_DEV uint4 ld_nc_v4(const void* p) {
@@ -1976,8 +1985,11 @@ struct GemvSet {
   int n;                        // linears in the set
   int total;                    // units over all of them
   int base[GEMV_MAX_LIN + 1];   // first unit of each linear
+  int* status;                  // device status word (a chained unit's wait that ran out)
+  uint64_t wait_cap_ns;
   GemvArgs lin[GEMV_MAX_LIN];
 };
+static_assert(sizeof(GemvSet) <= 4096, "GemvSet is a kernel parameter");
 
 template <int MT>
 __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet set) {
@@ -1993,6 +2005,32 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
   const int v = u - set.base[l];
   const int group = v / a.splits;
   const int split = v - group * a.splits;
+  if (a.wait_on) {
+    // X is an earlier linear's output from this launch: wait (bounded) until all its row groups
+    // are stored.  Units run in increasing order on every block and the producer's units all come
+    // first, so every unit waited for is running or done.
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_gpu(a.wait_on) < a.wait_groups) {
+        if (globaltimer_ns() - t0 > set.wait_cap_ns) {
+          ok = 0;
+          if (set.status) {
+            atomicExch(set.status, -5);  // ENVG_ERR_TIMEOUT
+            atomicExch(set.status + 1, 61);
+          }
+          break;
+        }
+      }
+      if (ok && atomicAdd(a.wait_on + 1, 1) == set.base[l + 1] - set.base[l] - 1) {
+        a.wait_on[0] = 0;  // the last unit past the wait re-arms the counters for the next launch
+        a.wait_on[1] = 0;
+      }
+      s_last = ok;
+    }
+    __syncthreads();
+    if (!s_last) continue;
+  }
   // the 8 device rows of this warp
   int drow[8];
 #pragma unroll
@@ -2022,7 +2060,15 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
       if (m >= a.M) break;
       float xv[8];
       const float* xp = a.X + (int64_t)m * a.ldx + k0;
-      if (a.xvec && k0 + 8 <= a.K) {
+      if (a.wait_on && k0 + 8 <= a.K && a.xvec) {
+        const float4 x0 = __ldcg(reinterpret_cast<const float4*>(xp));
+        const float4 x1 = __ldcg(reinterpret_cast<const float4*>(xp + 4));
+        xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
+        xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
+      } else if (a.wait_on) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[e] = (k0 + e < a.K) ? __ldcg(xp + e) : 0.0f;
+      } else if (a.xvec && k0 + 8 <= a.K) {
         const float4 x0 = __ldg(reinterpret_cast<const float4*>(xp));
         const float4 x1 = __ldg(reinterpret_cast<const float4*>(xp + 4));
         xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
@@ -2105,7 +2151,9 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
     }
   }
   if (e.nremote != 0) __threadfence_system();
+  if (a.done) __threadfence();  // this group's outputs are visible before it is counted
   __syncthreads();  // every thread is done with s_sum before the next unit writes it
+  if (a.done && threadIdx.x == 0) red_release_gpu_add(a.done, 1);
   }
 }
 

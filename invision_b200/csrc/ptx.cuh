@@ -292,6 +292,15 @@ ENVG_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 ENVG_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Global flags between blocks of one launch: an acquire load and a release add at GPU scope.
+ENVG_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+ENVG_DEV void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 // 32-bit store into the shared memory of a CTA of this cluster (a shared::cluster address).
 ENVG_DEV void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");

@@ -525,6 +525,51 @@ def test_skinny_chain_batch_split_producer(gpu, M):
     assert_parity(yb, O.linear_bf16(gb, wd), what=f"skinny chain down M={M}")
 
 
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_gemv_chained_in_one_launch(gpu, M):
+    """M <= 8: a linear whose input is exactly the output of an earlier linear of the batch runs in
+    the same persistent k_gemv launch, its units waiting in the kernel for the producer's outputs
+    (Qwen3 gate_up -> down, quicknn_qwen3.pas:782-789), and chains of chains (a -> b -> c, one with
+    split-K); a producer read by two later linears chains only the first.  Bit-identical to
+    separate calls, and within the bounds of the oracle."""
+    import torch
+
+    rng = np.random.default_rng(50 + M)
+
+    def wt(n, k):
+        return O.f32_to_bf16_rne((0.02 * rng.standard_normal((n, k))).astype(np.float32))
+
+    K, F, H = 2560, 1536, 2048
+    wgu, wd, wc, we = wt(2 * F, K), wt(H, F), wt(640, H), wt(384, H)
+    Wgu, Wd, Wc, We = (gpu.Weight(wgu, layout=gpu.LAYOUT_GATE_UP), gpu.Weight(wd), gpu.Weight(wc),
+                       gpu.Weight(we))
+    x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+    g, y, c, e = (torch.empty(M, n, device="cuda") for n in (F, H, 640, 384))
+    calls = [dict(dst=g, x=x, W=Wgu), dict(dst=y, x=g, W=Wd), dict(dst=c, x=y, W=Wc), dict(dst=e, x=y, W=We)]
+    launches0 = gpu.stats()["kernel_launches"]
+    gpu.linear_batch(calls)
+    torch.cuda.synchronize()
+    launches = gpu.stats()["kernel_launches"] - launches0
+    got = [t.cpu().numpy() for t in (g, y, c, e)]
+    for t in (g, y, c, e):
+        t.fill_(float("nan"))
+    for cl in calls:
+        gpu.linear(cl["dst"], cl["x"], cl["W"])
+    torch.cuda.synchronize()
+    for a_, t, name in zip(got, (g, y, c, e), "gyce"):
+        np.testing.assert_array_equal(a_, t.cpu().numpy(), err_msg=name)
+    # gate_up, down and the first reader of down in one launch; the second reader in another
+    assert launches == 2, launches
+    gu = O.linear_f32(x.cpu().numpy(), O.bf16_to_f32(wgu))
+    gref = O.silu_mul(np.ascontiguousarray(gu[:, :F]), np.ascontiguousarray(gu[:, F:]))
+    assert_parity(got[0], gref, TOL_MAX_PRODUCT, TOL_MEAN_PRODUCT, what=f"chain gate_up M={M}")
+    assert_parity(got[1], O.linear_bf16(got[0], wd), what=f"chain down M={M}")
+    assert_parity(got[2], O.linear_bf16(got[1], wc), what=f"chain c M={M}")
+    assert_parity(got[3], O.linear_bf16(got[1], we), what=f"chain e M={M}")
+    for W in (Wgu, Wd, Wc, We):
+        W.free()
+
+
 @pytest.mark.parametrize("M", [16, 1])
 def test_skinny_batch_queue_hazards(gpu, M):
     """A batch of skinny plain and gate/up linears that overwrite each other's inputs (write after
