@@ -2005,6 +2005,17 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
   const int v = u - set.base[l];
   const int group = v / a.splits;
   const int split = v - group * a.splits;
+  // the 8 device rows of this warp
+  int drow[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (a.gate_up) {
+      const int c = group * 32 + warp * 4 + (j & 3);  // output column of the pair
+      drow[j] = 256 * (c >> 7) + (c & 127) + (j >= 4 ? 128 : 0);
+    } else {
+      drow[j] = group * 64 + warp * 8 + j;
+    }
+  }
   if (a.wait_on) {
     // X is an earlier linear's output from this launch: wait (bounded) until all its row groups
     // are stored.  Units run in increasing order on every block and the producer's units all come
@@ -2030,17 +2041,6 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
     }
     __syncthreads();
     if (!s_last) continue;
-  }
-  // the 8 device rows of this warp
-  int drow[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    if (a.gate_up) {
-      const int c = group * 32 + warp * 4 + (j & 3);  // output column of the pair
-      drow[j] = 256 * (c >> 7) + (c & 127) + (j >= 4 ? 128 : 0);
-    } else {
-      drow[j] = group * 64 + warp * 8 + j;
-    }
   }
   float acc[MT][8];
 #pragma unroll
