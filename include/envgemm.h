@@ -181,12 +181,17 @@ typedef struct envg_linear_desc {
   const float* gate;
 } envg_linear_desc;
 
-/* Several linears in one call, in order, on device pointers (flags must contain ENVG_DEVICE_PTRS;
- * ENVG_ASYNC optional).  Equivalent to n envg_linear calls, but each distinct input x is rounded
- * to bf16 once (the FLUX Q/K/V and Qwen3 q/k/v projections read the same normalised input,
+/* Several linears in one call, in order.  Equivalent to n envg_linear calls.
+ * ENVG_DEVICE_PTRS (ENVG_ASYNC optional): each distinct input x is rounded to bf16 once (the FLUX
+ * Q/K/V and Qwen3 q/k/v projections read the same normalised input,
  * quicknn_transformers.pas:1402-1414, quicknn_qwen3.pas:712-714), and the rounding of the next
  * input runs on a second stream while the current GEMM runs.  An input that is the output of an
- * earlier linear of the batch waits for it. */
+ * earlier linear of the batch waits for it.
+ * ENVG_HOST_PTRS (synchronous): every linear is computed as envg_linear computes it from host
+ * pointers, but the linears' copies in and out and their GEMMs overlap one another, so the call
+ * costs about the larger of its total host->device and device->host bytes over PCIe rather than
+ * the sum of each linear's.  A linear whose output overlaps another's output, or an input of a
+ * later one, makes the call run them one after another. */
 int envg_linear_batch(const envg_linear_desc* descs, int n, int flags);
 
 /* One rank's part of an N-split linear, with the all-gather fused into the GEMM epilogue.  The

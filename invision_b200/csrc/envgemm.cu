@@ -105,6 +105,7 @@ struct Dev {
   bool pair_dyn = true;   // k1_gemm_pair dynamic unit order (ENVG_PAIR_SCHED=static disables)
   bool gemv_chain = true; // k_gemv runs a linear chained to another's output in one launch (ENVG_GEMV_CHAIN=0)
   Buf sched;              // k1_gemm_pair schedules: SCHED_SLOTS x {next unit, pairs done}, zeroed
+  Buf hb;                 // host-pointer batches: the device copies of every linear's x, Y and vectors
   unsigned sched_seq = 0; // slot of the next launch
   bool pdl = true;        // programmatic dependent launch of the GEMM-chain kernels (ENVG_PDL=0 disables)
   bool no_split = false;  // set while a pipelined host call launches its row chunks
@@ -112,7 +113,7 @@ struct Dev {
   size_t ws_bytes() const {
     return x.bytes + y.bytes + xb.bytes + wb.bytes + part.bytes + cnt.bytes + sched.bytes + bias.bytes + gate.bytes + act.bytes +
            col.bytes + b32.bytes + xbatch.bytes + ada.bytes + xn.bytes + gn.bytes + c1.bytes + vec.bytes +
-           fa.bytes + fain.bytes;
+           fa.bytes + fain.bytes + hb.bytes;
   }
 };
 
@@ -1549,7 +1550,7 @@ int envg_shutdown(void) {
   cudaStreamSynchronize(stream_of(d));
   Buf* bufs[] = {&d->x,    &d->y,   &d->xb,  &d->wb,  &d->part,  &d->cnt,
                  &d->bias, &d->gate, &d->act, &d->col, &d->b32, &d->xbatch, &d->ada, &d->xn,
-                 &d->gn,   &d->c1,   &d->vec,  &d->fa,  &d->fain, &d->sched};
+                 &d->gn,   &d->c1,   &d->vec,  &d->fa,  &d->fain, &d->sched, &d->hb};
   for (Buf* b : bufs) {
     if (b->p) cudaFree(b->p);
     *b = Buf{};
@@ -2689,6 +2690,145 @@ int batch_core(Dev* d, const envg_linear_desc* descs, const envg_nsplit_desc* ns
   if (!(flags & ENVG_ASYNC)) return sync_and_check(d);
   return ENVG_OK;
 }
+// envg_linear_batch on host pointers.  The linears' copies and GEMMs are queued back to back and
+// the call synchronises once, so the copy-in of one linear, the GEMMs and the copy-out of an
+// earlier one overlap (PCIe carries both directions at once): the call costs about the larger of
+// its total copy-in and copy-out instead of the sum over the linears of each one's larger
+// direction.  Copy-ins queue on d->h2d, GEMMs on the compute stream, copy-outs on d->d2h.  Each
+// linear is computed exactly as envg_linear computes it from host pointers: from PIPE_MIN_M rows
+// on in row chunks of PIPE_CHUNK rows without split-K, else in one launch.  An input shared by
+// several linears (the same x, M and K) is copied once.  When one linear's output overlaps
+// another's output, or an input of a later linear (x, bias, gate), the linears run one call
+// after another instead.
+int batch_host(Dev* d, const envg_linear_desc* descs, int n, int flags) {
+  if (n < 0 || (n > 0 && !descs)) return fail(ENVG_ERR_ARG, "envg_linear_batch: bad descriptor array");
+  for (int i = 0; i < n; ++i) ENVG_TRY(check_linear_args(d, descs[i]));
+  auto n_out_of = [](const envg_linear_desc& q) { return q.W->layout == ENVG_LAYOUT_GATE_UP ? q.N / 2 : q.N; };
+  auto overlap = [](const void* a, size_t na, const void* b, size_t nb) {
+    const char* pa = static_cast<const char*>(a);
+    const char* pb = static_cast<const char*>(b);
+    return a && b && na && nb && pa < pb + nb && pb < pa + na;
+  };
+  bool sequential = !d->pipe_host;
+  for (int j = 0; j < n && !sequential; ++j) {
+    const envg_linear_desc& b = descs[j];
+    if (b.M == 0) continue;
+    const size_t yb = (size_t)(b.M * n_out_of(b)) * 4;
+    for (int i = 0; i < j && !sequential; ++i) {
+      const envg_linear_desc& a = descs[i];
+      if (a.M == 0) continue;
+      const size_t ya = (size_t)(a.M * n_out_of(a)) * 4;
+      sequential = overlap(a.dst, ya, b.dst, yb) || overlap(a.dst, ya, b.x, (size_t)(b.M * b.K) * 4) ||
+                   overlap(a.dst, ya, b.bias, b.bias ? (size_t)b.N * 4 : 0) ||
+                   overlap(a.dst, ya, b.gate, b.gate ? (size_t)b.N * 4 : 0);
+    }
+  }
+  if (sequential) {
+    for (int i = 0; i < n; ++i) {
+      const envg_linear_desc& q = descs[i];
+      ENVG_TRY(linear_core(d, q.dst, q.x, q.W, q.bias, q.M, q.K, q.N, q.epilogue, q.gate, ENVG_HOST_PTRS, Prologue{}));
+    }
+    return ENVG_OK;
+  }
+  // device copies: one per distinct input, an output, bias and gate per linear
+  auto a256 = [](size_t b) { return (b + 255) & ~size_t(255); };
+  std::vector<int> xsrc(n, -1);  // the descriptor whose copy of x this one reads
+  std::vector<size_t> xoff(n, 0), yoff(n, 0), boff(n, 0), goff(n, 0);
+  size_t total = 0;
+  for (int i = 0; i < n; ++i) {
+    const envg_linear_desc& q = descs[i];
+    if (q.M == 0) continue;
+    for (int k = 0; k < i && xsrc[i] < 0; ++k)
+      if (descs[k].M == q.M && descs[k].K == q.K && descs[k].x == q.x) xsrc[i] = xsrc[k];
+    if (xsrc[i] < 0) {
+      xsrc[i] = i;
+      xoff[i] = total;
+      total += a256((size_t)(q.M * q.K) * 4);
+    }
+    yoff[i] = total;
+    total += a256((size_t)(q.M * n_out_of(q)) * 4);
+    if (q.bias) {
+      boff[i] = total;
+      total += a256((size_t)q.N * 4);
+    }
+    if (q.epilogue == ENVG_EPI_GATED_RESIDUAL) {
+      goff[i] = total;
+      total += a256((size_t)q.N * 4);
+    }
+  }
+  if (total == 0) return ENVG_OK;
+  ENVG_TRY(ensure(d, d->hb, total));
+  uint8_t* base = reinterpret_cast<uint8_t*>(d->hb.p);
+  cudaStream_t s = stream_of(d);
+  if (!d->h2d) ENVG_CUDA(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
+  if (!d->d2h) ENVG_CUDA(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
+  // the copy streams start after the work already queued on s
+  size_t ev = 0;
+  ENVG_CUDA(cudaEventRecord(pipe_event(d, ev), s));
+  ENVG_CUDA(cudaStreamWaitEvent(d->h2d, pipe_event(d, ev), 0));
+  ENVG_CUDA(cudaStreamWaitEvent(d->d2h, pipe_event(d, ev), 0));
+  ++ev;
+  const uint64_t calls0 = d->st.calls;
+  for (int i = 0; i < n; ++i) {
+    const envg_linear_desc& q = descs[i];
+    if (q.M == 0) continue;
+    const int64_t n_out = n_out_of(q);
+    float* dx = reinterpret_cast<float*>(base + xoff[xsrc[i]]);
+    float* dy = reinterpret_cast<float*>(base + yoff[i]);
+    const float *dbias = nullptr, *dgate = nullptr;
+    if (q.bias) {
+      dbias = reinterpret_cast<float*>(base + boff[i]);
+      ENVG_CUDA(cudaMemcpyAsync(const_cast<float*>(dbias), q.bias, (size_t)q.N * 4, cudaMemcpyHostToDevice, d->h2d));
+      d->st.h2d_bytes += (double)q.N * 4;
+    }
+    if (q.epilogue == ENVG_EPI_GATED_RESIDUAL) {
+      dgate = reinterpret_cast<float*>(base + goff[i]);
+      ENVG_CUDA(cudaMemcpyAsync(const_cast<float*>(dgate), q.gate, (size_t)q.N * 4, cudaMemcpyHostToDevice, d->h2d));
+      d->st.h2d_bytes += (double)q.N * 4;
+    }
+    const bool chunked = q.M >= PIPE_MIN_M;
+    const int64_t nch = chunked ? std::max<int64_t>(1, q.M / PIPE_CHUNK) : 1;
+    for (int64_t c = 0; c < nch; ++c) {
+      const int64_t r0 = chunked ? c * PIPE_CHUNK : 0;
+      const int64_t rows = (c == nch - 1) ? q.M - r0 : PIPE_CHUNK;
+      if (xsrc[i] == i) {
+        ENVG_CUDA(cudaMemcpyAsync(dx + r0 * q.K, q.x + r0 * q.K, (size_t)(rows * q.K) * 4, cudaMemcpyHostToDevice,
+                                  d->h2d));
+        d->st.h2d_bytes += (double)(rows * q.K) * 4;
+      }
+      if (q.epilogue == ENVG_EPI_GATED_RESIDUAL) {
+        ENVG_CUDA(cudaMemcpyAsync(dy + r0 * n_out, q.dst + r0 * n_out, (size_t)(rows * n_out) * 4,
+                                  cudaMemcpyHostToDevice, d->h2d));
+        d->st.h2d_bytes += (double)(rows * n_out) * 4;
+      }
+      // every copy queued on h2d so far (this chunk's included) has landed
+      ENVG_CUDA(cudaEventRecord(pipe_event(d, ev), d->h2d));
+      ENVG_CUDA(cudaStreamWaitEvent(s, pipe_event(d, ev), 0));
+      ++ev;
+      {
+        struct NoSplit {
+          Dev* d;
+          bool prev;
+          ~NoSplit() { d->no_split = prev; }
+        } guard{d, d->no_split};
+        d->no_split = chunked;
+        ENVG_TRY(linear_core(d, dy + r0 * n_out, dx + r0 * q.K, q.W, dbias, rows, q.K, q.N, q.epilogue, dgate,
+                             ENVG_DEVICE_PTRS | ENVG_ASYNC, Prologue{}));
+      }
+      ENVG_CUDA(cudaEventRecord(pipe_event(d, ev), s));
+      ENVG_CUDA(cudaStreamWaitEvent(d->d2h, pipe_event(d, ev), 0));
+      ++ev;
+      ENVG_CUDA(cudaMemcpyAsync(q.dst + r0 * n_out, dy + r0 * n_out, (size_t)(rows * n_out) * 4,
+                                cudaMemcpyDeviceToHost, d->d2h));
+      d->st.d2h_bytes += (double)(rows * n_out) * 4;
+    }
+    d->st.calls = calls0 + (uint64_t)(i + 1);
+  }
+  ENVG_CUDA(cudaStreamSynchronize(d->d2h));
+  ENVG_CUDA(cudaStreamSynchronize(d->h2d));
+  return sync_and_check(d);
+}
+
 }  // namespace
 
 extern "C" {
@@ -2697,6 +2837,7 @@ int envg_linear_batch(const envg_linear_desc* descs, int n, int flags) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   Dev* d = cur();
   if (!d) return fail(ENVG_ERR_STATE, "envg_init has not been called");
+  if (!(flags & ENVG_DEVICE_PTRS)) return batch_host(d, descs, n, flags);
   return batch_core(d, descs, nullptr, n, flags);
 }
 

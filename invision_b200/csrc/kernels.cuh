@@ -1524,16 +1524,14 @@ __global__ void __launch_bounds__(K1_THREADS, 1)
           for (int m = 0; m < MPAD; m += 4)
             __stcg(reinterpret_cast<float4*>(p + m), make_float4(acc[r][m], acc[r][m + 1], acc[r][m + 2], acc[r][m + 3]));
         }
-        __threadfence();
         named_bar_sync(1, 128);
         if (et == 0) {
-          const int old = atomicAdd(args.counters + tile, 1);
+          const int old = atom_add_acq_rel_gpu(args.counters + tile, 1);
           *last_s = (old == args.splits - 1) ? 1 : 0;
         }
         named_bar_sync(1, 128);
         finalize = (*last_s != 0);
         if (finalize) {
-          __threadfence();
 #pragma unroll
           for (int r = 0; r < R; ++r) {
 #pragma unroll
@@ -2110,13 +2108,11 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
   if (a.splits > 1) {
     float* part = a.partial + ((int64_t)group * a.splits + split) * GEMV_PART;
     for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) __stcg(part + t, s_sum[t / 64][t % 64]);
-    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = (atomicAdd(a.counters + group, 1) == a.splits - 1) ? 1 : 0;
+    if (threadIdx.x == 0) s_last = (atom_add_acq_rel_gpu(a.counters + group, 1) == a.splits - 1) ? 1 : 0;
     __syncthreads();
     if (!s_last) continue;  // uniform across the block; s_sum is rewritten only after the next
                             // unit's __syncthreads
-    __threadfence();
     for (int t = threadIdx.x; t < MT * 64; t += blockDim.x) {
       float v = 0.0f;
 #pragma unroll 8
@@ -2151,8 +2147,9 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ GemvSet se
     }
   }
   if (e.nremote != 0) __threadfence_system();
-  if (a.done) __threadfence();  // this group's outputs are visible before it is counted
-  __syncthreads();  // every thread is done with s_sum before the next unit writes it
+  // every thread is done with s_sum before the next unit writes it, and (a.done) this group's
+  // outputs are ordered before the release that counts it
+  __syncthreads();
   if (a.done && threadIdx.x == 0) red_release_gpu_add(a.done, 1);
   }
 }

@@ -301,6 +301,14 @@ ENVG_DEV int ld_acquire_gpu(const int* p) {
 ENVG_DEV void red_release_gpu_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Arrival on a completion counter by one thread after its CTA's stores, which a barrier orders
+// before it: the release publishes them (cumulatively) at GPU scope, and the acquire lets the
+// thread that completes the count, and after a barrier its CTA, read every arriver's stores.
+ENVG_DEV int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 // 32-bit store into the shared memory of a CTA of this cluster (a shared::cluster address).
 ENVG_DEV void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");

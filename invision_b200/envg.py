@@ -393,21 +393,27 @@ def linear_noalloc(dst, x, W, bias=None, epilogue=None, gate=None, sync=True):
 
 
 def linear_batch(calls, sync=True):
-    """Several linears in one envg_linear_batch call (torch CUDA tensors only).  `calls` is a list
-    of dicts with keys dst, x, W and optionally bias, epilogue, gate; each distinct x is cast once
-    and the casts overlap the previous GEMM on a second stream."""
+    """Several linears in one envg_linear_batch call.  `calls` is a list of dicts with keys dst,
+    x, W and optionally bias, epilogue, gate, all torch CUDA tensors (each distinct x is cast once
+    and the casts overlap the previous GEMM on a second stream) or all numpy arrays (host
+    pointers: the linears' copies in and out overlap one another and the GEMMs; synchronous)."""
     arr = (LinearDesc * len(calls))()
     keep = []
+    modes = set()
     for i, c in enumerate(calls):
         W = c["W"]
         bias, gate = c.get("bias"), c.get("gate")
         epi = c.get("epilogue")
         if epi is None:
             epi = EPI_SILU_GATE if W.layout == LAYOUT_GATE_UP else (EPI_BIAS if bias is not None else EPI_NONE)
-        _mode(c["dst"], c["x"], bias, gate)
+        modes.add(_mode(c["dst"], c["x"], bias, gate))
         M, K = c["x"].shape
         arr[i] = LinearDesc(_ptr(c["dst"]), _ptr(c["x"]), W.h, _ptr(bias), M, K, W.N, epi, _ptr(gate))
         keep.append(c)
+    if len(modes) > 1:
+        raise TypeError("a batch's operands must be all numpy (host) or all torch CUDA tensors (device)")
+    if modes == {HOST_PTRS}:
+        return _check(lib().envg_linear_batch(arr, len(calls), HOST_PTRS))
     flags = DEVICE_PTRS | (0 if sync else ASYNC)
     return _check(lib().envg_linear_batch(arr, len(calls), flags))
 
