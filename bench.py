@@ -790,10 +790,14 @@ def run_ours(args, items, desc, world, rank, local):
 
 
 def run_e2e_nsplit(args, torch, dev, wl, step_flops, timed):
-    """N > 1: the N-split step through the public API (envg_linear_nsplit_batch), with every
-    step's inputs copied in from pinned host memory on every rank (each rank needs the whole X)
-    and each rank reading its part of the results back: its kept shard, and its block of rows
-    of every gathered output (together the ranks read each output once)."""
+    """N > 1: the N-split step through the public API (envg_linear_nsplit_batch) with every step's
+    inputs coming from pinned host memory and each rank reading its part of the results back: its
+    kept shard, and its block of rows of every gathered output (together the ranks read each
+    output once).  Every rank needs the whole X.  Headline: each rank copies only its block of
+    rows of each input over its own PCIe link and an NCCL all-gather over NVLink assembles the
+    whole input on every rank.  `replicated_copy`: every rank copies the whole input in."""
+    import torch.distributed as dist
+
     world, rank = wl.world, wl.rank
     hx, seen = {}, set()
     for k, v in wl.x.items():
@@ -814,26 +818,57 @@ def run_e2e_nsplit(args, torch, dev, wl, step_flops, timed):
             r1 = (rank + 1) * y.shape[0] // world
             src = y[r0:r1]
         outs.append((src, torch.empty(src.shape, dtype=torch.float32, pin_memory=True)))
-    h2d = sum(h.numel() * 4 for h in hx.values())
     d2h = sum(h.numel() * 4 for _, h in outs)
+    steps = max(2, min(args.steps, 5))
 
-    def step():
-        for k, h in hx.items():
-            wl.x[k].copy_(h, non_blocking=True)
-        wl.step()
+    def read_back():
         for src, h in outs:
             h.copy_(src, non_blocking=True)
 
-    steps = max(2, min(args.steps, 5))
+    def step_replicated():
+        for k, h in hx.items():
+            wl.x[k].copy_(h, non_blocking=True)
+        wl.step()
+        read_back()
+
+    # rows of each input this rank brings in (inputs whose rows do not split evenly are copied whole)
+    blocks = {}
+    for k, h in hx.items():
+        M = h.shape[0]
+        if M % world == 0 and wl.x[k].is_contiguous():
+            r0, r1 = rank * M // world, (rank + 1) * M // world
+            blocks[k] = (h[r0:r1], torch.empty((r1 - r0,) + tuple(h.shape[1:]), dtype=torch.float32, device=dev))
+
+    def step_split():
+        for k, h in hx.items():
+            if k in blocks:
+                hb, stage = blocks[k]
+                stage.copy_(hb, non_blocking=True)
+                dist.all_gather_into_tensor(wl.x[k], stage)
+            else:
+                wl.x[k].copy_(h, non_blocking=True)
+        wl.step()
+        read_back()
+
     for _ in range(2):
-        step()
+        step_split()
+        step_replicated()
     torch.cuda.synchronize()
-    ms = timed(step, steps)
+    ms = timed(step_split, steps)
+    ms_rep = timed(step_replicated, steps)
+    h2d_rep = sum(h.numel() * 4 for h in hx.values())
+    h2d = sum((blocks[k][0].numel() if k in blocks else h.numel()) * 4 for k, h in hx.items())
+    nvlink = sum((h.numel() - blocks[k][0].numel()) * 4 for k, h in hx.items() if k in blocks)
     return {"value": round(step_flops / (ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(ms, 3),
             "steps": steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "path": ("per rank: inputs from pinned host memory (torch copy), envg_linear_nsplit_batch step, its "
-                     "kept shards and its row block of every gathered output back to pinned host memory; max over "
-                     "ranks; bytes are this rank's")}
+            "nvlink_in_bytes_per_step": nvlink,
+            "path": ("per rank: its row block of each input from pinned host memory (torch copy), NCCL all-gather "
+                     "of the inputs over NVLink, envg_linear_nsplit_batch step, its kept shards and its row block "
+                     "of every gathered output back to pinned host memory; max over ranks; bytes are this rank's"),
+            "replicated_copy": {"value": round(step_flops / (ms_rep * 1e-3) / 1e12, 2), "unit": UNIT,
+                                "ms_per_step": round(ms_rep, 3), "h2d_bytes_per_step": h2d_rep,
+                                "d2h_bytes_per_step": d2h,
+                                "path": "per rank: the whole of every input from pinned host memory, then as above"}}
 
 
 def run_e2e(args, envg, torch, dev, wl, step_flops):
