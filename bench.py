@@ -152,7 +152,7 @@ def has_bias(it):
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per k1_gemm launch of one step of the
 # default workload at one GPU, from an ncu capture of the current kernels (one pass,
 # gpu__time_duration and the two dram counters; per-launch mean over the step's launches).
-K1_TRAFFIC_BYTES_PER_LAUNCH = {"c4": 4.071e9}
+K1_TRAFFIC_BYTES_PER_LAUNCH = {"c4": 3.886e9}
 
 
 def peaks(clocks=None, region_ms=0.0):

@@ -819,8 +819,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
   const uint32_t tempty0_leader = mapa_shared(tempty0, 0);
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
-  // Dynamic unit order: the even CTA's producer takes each next unit from set.sched[0] and writes
-  // it into slot it % UNIT_RING of both CTAs' rings (ufull); the consumers (the UMMA thread and the
+  // Dynamic unit order: the even CTA's producer takes each next unit from set.sched[0] (after the
+  // pair's first, its index) and writes it into slot it % UNIT_RING of both CTAs' rings (ufull); the consumers (the UMMA thread and the
   // four epilogue warps of the even CTA, the producer and the four epilogue warps of the odd one:
   // 10 arrivals) release the slot on the even CTA's uempty.  Consecutive units then run on
   // whichever pairs are free, so the pairs at work always hold a contiguous run of the raster and
@@ -879,7 +879,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
 
   // The it-th unit of this pair (set.total ends the sequence).  publish_unit: the even CTA's
   // producer; take_unit: every other role (one thread each); peek_unit reads a slot without
-  // releasing it.  false: a bounded wait gave up.
+  // releasing it.  false: a bounded wait gave up.  Dynamic order: a pair's first unit is its
+  // index; the counter hands out the units from npairs on, and the producer asks it for the
+  // pair's next unit as soon as it publishes one, so the atomic's round trip overlaps the
+  // current unit's loads instead of delaying the next unit's first one.
+  int next_raw = -1;  // the counter's value for the next unit; -1: the pair's first unit
   auto publish_unit = [&](int it, int& unit) -> bool {
     if (!dyn) {
       unit = min(pair + it * npairs, set.total);
@@ -887,11 +891,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(K1_THREADS, 1)
     }
     const int slot = it % UR;
     if (!wait_bounded_cluster(uempty0 + 8 * slot, ((it / UR) & 1) ^ 1, wc, 26)) return false;
-    const int u = min(atomicAdd(set.sched, 1), set.total);
+    const int u = min(next_raw < 0 ? pair : npairs + next_raw, set.total);
     uring[slot] = u;
     st_shared_cluster_u32(uring_peer + 4 * slot, (uint32_t)u);
     mbar_arrive(ufull0 + 8 * slot);
     mbar_arrive_cluster(ufull0_peer + 8 * slot);
+    if (u < set.total) next_raw = atomicAdd(set.sched, 1);  // read at the next publish_unit
     unit = u;
     return true;
   };

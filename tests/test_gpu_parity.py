@@ -398,9 +398,10 @@ np.savez(sys.argv[1], **out)
 
 
 def test_pair_unit_order_does_not_change_results(tmp_path):
-    """The CTA-pair GEMM hands out its units dynamically (the next free pair takes the next unit)
-    or statically (ENVG_PAIR_SCHED=static): every tile is computed the same way, so the outputs are
-    bit-identical, with and without split-K, for one tile wave and for many."""
+    """The CTA-pair GEMM hands out its units dynamically (the next free pair takes the next unit;
+    ENVG_PAIR_SCHED=dynamic forces it on launches of any length) or statically
+    (ENVG_PAIR_SCHED=static): every tile is computed the same way, so the outputs are bit-identical,
+    with and without split-K, for one tile wave and for many."""
     import os
     import subprocess
     import sys
@@ -409,9 +410,7 @@ def test_pair_unit_order_does_not_change_results(tmp_path):
     res = {}
     for mode in ("dynamic", "static"):
         env = dict(os.environ)
-        env.pop("ENVG_PAIR_SCHED", None)
-        if mode == "static":
-            env["ENVG_PAIR_SCHED"] = "static"
+        env["ENVG_PAIR_SCHED"] = mode
         f = str(tmp_path / f"{mode}.npz")
         r = subprocess.run([sys.executable, "-c", _SCHED_CASE, f], cwd=root, env=env, capture_output=True,
                            text=True, timeout=300)
