@@ -2778,7 +2778,7 @@ int batch_host(Dev* d, const envg_linear_desc* descs, int n, int flags) {
   ENVG_CUDA(cudaStreamWaitEvent(d->h2d, pipe_event(d, ev), 0));
   ENVG_CUDA(cudaStreamWaitEvent(d->d2h, pipe_event(d, ev), 0));
   ++ev;
-  const uint64_t calls0 = d->st.calls;
+  uint64_t calls = d->st.calls;  // one per linear, as envg_linear counts them (not one per chunk)
   for (int i = 0; i < n; ++i) {
     const envg_linear_desc& q = descs[i];
     if (q.M == 0) continue;
@@ -2832,7 +2832,7 @@ int batch_host(Dev* d, const envg_linear_desc* descs, int n, int flags) {
                                 cudaMemcpyDeviceToHost, d->d2h));
       d->st.d2h_bytes += (double)(rows * n_out) * 4;
     }
-    d->st.calls = calls0 + (uint64_t)(i + 1);
+    d->st.calls = ++calls;
   }
   ENVG_CUDA(cudaStreamSynchronize(d->d2h));
   ENVG_CUDA(cudaStreamSynchronize(d->h2d));
